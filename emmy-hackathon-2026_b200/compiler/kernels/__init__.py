@@ -1,0 +1,32 @@
+"""Hand-written sm_100a PTX templates, one per kernel family the IR lowers to."""
+
+from __future__ import annotations
+
+
+def _has(body, kinds) -> bool:
+    for s in body:
+        k = type(s).__name__
+        if k in kinds:
+            return True
+        for attr in ("body", "else_body"):
+            sub = getattr(s, attr, None)
+            if isinstance(sub, tuple) and _has(sub, kinds):
+                return True
+    return False
+
+
+def select(spec) -> str:
+    """Pick the template for ``spec`` and emit its module."""
+    body = spec.body
+    if _has(body, {"MmaSyncPtx"}):
+        if _has(body, {"FragmentRowReduce"}):
+            from .attention import emit_attention
+            return emit_attention(spec)
+        from .gemm import emit_gemm
+        return emit_gemm(spec)
+    if _has(body, {"WarpShuffle"}):
+        from .reduce import emit_reduction
+        return emit_reduction(spec)
+    raise NotImplementedError(
+        f"kernel {spec.name}: no sm_100a template for this IR family "
+        "(tensor-core GEMM, tensor-core attention and cooperative reductions are supported)")

@@ -1,0 +1,338 @@
+"""Statement registry and scalar lowering.
+
+Keeps the reference's dispatch surface (``compiler/stmts.py:23-41``): a module-level
+``HANDLERS`` table filled by the ``@handles("Kind")`` decorator, dispatched on
+``type(stmt).__name__``, with unknown kinds raising
+``NotImplementedError(f"statement {kind}")``.
+
+What differs is who owns the schedule.  The reference lowers every statement in
+emmy's sm_89 schedule.  Here a kernel template (``compiler/kernels``) owns the
+launch, the memory movement and the cross-thread combines, and calls
+:func:`lower_body` only for the IR's *scalar* statements -- the per-element map
+before an accumulation, the accumulator updates, the per-row tail and the
+per-element output expression.  Those statements are lowered exactly as the IR
+states them, so the template computes the IR's own arithmetic.
+
+Loads and writes are routed through hooks the template installs on the context,
+because the template decides how an element's address maps to registers (a
+vector lane of a 128-bit load, a value cached from an earlier pass, a constant
+folded to an immediate).
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+from typing import Callable
+
+from .ptx import Ptx, f32_hex
+
+HANDLERS: dict[str, Callable] = {}
+
+
+def handles(*kinds: str):
+    """Register ``fn(ctx, stmt)`` as the lowering of statement kind(s)."""
+    def deco(fn):
+        for k in kinds:
+            HANDLERS[k] = fn
+        return fn
+    return deco
+
+
+def lower_body(ctx, body) -> None:
+    for s in body:
+        kind = type(s).__name__
+        fn = HANDLERS.get(kind)
+        if fn is None:
+            raise NotImplementedError(f"statement {kind}")
+        fn(ctx, s)
+
+
+def dtype_name(dt) -> str | None:
+    if dt is None:
+        return None
+    return getattr(dt, "name", dt)
+
+
+# --------------------------------------------------------------------------
+# values and the scalar context
+
+
+@dataclass
+class Val:
+    text: str          # register name or immediate
+    kind: str          # "f32" | "s32" | "pred"
+    const: float | None = None
+
+
+@dataclass
+class ScalarCtx:
+    ptx: Ptx
+    env: dict = field(default_factory=dict)          # SSA name -> Val
+    mutable: set = field(default_factory=set)        # names updated in place (accumulators)
+    constants: dict = field(default_factory=dict)    # ConstantOp buffer -> value
+    on_load: Callable | None = None                  # fn(ctx, Load) -> None (binds names)
+    on_write: Callable | None = None                 # fn(ctx, Write) -> None
+    axis_regs: dict = field(default_factory=dict)    # axis name -> s32 register / immediate
+
+    def bind(self, name: str, val: Val) -> None:
+        if name in self.mutable and name in self.env:
+            dst = self.env[name]
+            if dst.text != val.text:
+                self.ptx.emit(f"mov.f32 {dst.text}, {val.text}" if dst.kind == "f32"
+                              else f"mov.b32 {dst.text}, {val.text}")
+            return
+        self.env[name] = val
+
+    def get(self, name: str) -> Val:
+        try:
+            return self.env[name]
+        except KeyError:
+            raise ValueError(f"IR name {name!r} is used before it is defined") from None
+
+    def f32(self, name: str) -> str:
+        v = self.get(name)
+        if v.kind != "f32":
+            raise NotImplementedError(f"{name!r} is {v.kind}, expected f32")
+        return v.text
+
+
+# --------------------------------------------------------------------------
+# f32 elementwise op table (the subset the hot-path kernels use: arithmetic,
+# max/min, exp, sqrt, rsqrt, reciprocal).  The reference's table is
+# compiler/ops.py:254-414.
+
+_LOG2E_HI = 1.4426950216293335       # float32(log2 e)
+_LOG2E_LO = 1.925963033500011e-08    # log2 e - _LOG2E_HI
+_LN2 = 0.6931471805599453
+
+
+def emit_exp(p: Ptx, dst: str, x: str) -> None:
+    """exp(x) = 2^(x log2 e) on the MUFU ``ex2.approx`` unit.
+
+    The product x*log2(e) is formed in two pieces (Cody-Waite style): ``t`` is the
+    rounded product with the f32 constant, ``e`` the exact residual of that product
+    plus x times the constant's own rounding error.  2^(t+e) = 2^t (1 + e ln 2) to
+    first order in e (|e| < 2^-23 |t|), so the result keeps ex2.approx's ~2 ulp
+    instead of losing |x log2 e| ulp to the rounding of the product."""
+    t, e, lo, r = p.reg("f32"), p.reg("f32"), p.reg("f32"), p.reg("f32")
+    p.emit(f"""
+        mul.rn.f32 {t}, {x}, {f32_hex(_LOG2E_HI)}
+        neg.f32 {e}, {t}
+        fma.rn.f32 {e}, {x}, {f32_hex(_LOG2E_HI)}, {e}
+        fma.rn.f32 {e}, {x}, {f32_hex(_LOG2E_LO)}, {e}
+        ex2.approx.f32 {r}, {t}
+        mul.rn.f32 {lo}, {e}, {f32_hex(_LN2)}
+        fma.rn.f32 {dst}, {r}, {lo}, {r}
+    """)
+
+
+def _unary(p: Ptx, op: str, dst: str, a: str) -> None:
+    if op == "copy":
+        p.emit(f"mov.f32 {dst}, {a}")
+    elif op == "negative":
+        p.emit(f"neg.f32 {dst}, {a}")
+    elif op == "abs":
+        p.emit(f"abs.f32 {dst}, {a}")
+    elif op == "exp":
+        emit_exp(p, dst, a)
+    elif op == "sqrt":
+        p.emit(f"sqrt.rn.f32 {dst}, {a}")
+    elif op == "reciprocal":
+        p.emit(f"rcp.rn.f32 {dst}, {a}")
+    elif op == "rsqrt":
+        # 1/sqrt(x) from the two IEEE-rounded instructions (both correctly rounded),
+        # as the reference lowers it (compiler/ops.py:88-92).
+        s = p.reg("f32")
+        p.emit(f"sqrt.rn.f32 {s}, {a}\nrcp.rn.f32 {dst}, {s}")
+    elif op == "relu":
+        p.emit(f"max.f32 {dst}, {a}, 0f00000000")
+    elif op == "square":
+        p.emit(f"mul.rn.f32 {dst}, {a}, {a}")
+    else:
+        raise NotImplementedError(f"elementwise op {op} (f32, unary)")
+
+
+def _binary(p: Ptx, op: str, dst: str, a: str, b: str) -> None:
+    if op == "add":
+        p.emit(f"add.rn.f32 {dst}, {a}, {b}")
+    elif op == "subtract":
+        p.emit(f"sub.rn.f32 {dst}, {a}, {b}")
+    elif op == "multiply":
+        p.emit(f"mul.rn.f32 {dst}, {a}, {b}")
+    elif op == "divide":
+        p.emit(f"div.rn.f32 {dst}, {a}, {b}")
+    elif op == "maximum":
+        p.emit(f"max.f32 {dst}, {a}, {b}")
+    elif op == "minimum":
+        p.emit(f"min.f32 {dst}, {a}, {b}")
+    else:
+        raise NotImplementedError(f"elementwise op {op} (f32, binary)")
+
+
+def compute_f32(ctx: ScalarCtx, op: str, args: list[str], dst: str | None = None) -> Val:
+    p = ctx.ptx
+    vals = [ctx.f32(a) for a in args]
+    out = dst or p.reg("f32")
+    if len(vals) == 1:
+        _unary(p, op, out, vals[0])
+    elif len(vals) == 2:
+        _binary(p, op, out, vals[0], vals[1])
+    else:
+        raise NotImplementedError(f"elementwise op {op} with {len(vals)} operands")
+    return Val(out, "f32")
+
+
+# --------------------------------------------------------------------------
+# handlers
+
+
+def _check_f32(dt, what: str) -> None:
+    n = dtype_name(dt)
+    if n not in (None, "f32"):
+        raise NotImplementedError(f"{what} of dtype {n}: this back end computes reductions in f32")
+
+
+@handles("Assign")
+def lower_assign(ctx: ScalarCtx, s) -> None:
+    _check_f32(s.dtype, "Assign")
+    target = ctx.env[s.name].text if (s.name in ctx.mutable and s.name in ctx.env) else None
+    val = compute_f32(ctx, s.op.name, list(s.args), dst=None)
+    if target is not None:
+        ctx.ptx.emit(f"mov.f32 {target}, {val.text}")
+    else:
+        ctx.env[s.name] = val
+
+
+@handles("Let")
+def lower_let(ctx: ScalarCtx, s) -> None:
+    v = s.value
+    if type(v).__name__ == "Literal":
+        if dtype_name(s.dtype) in (None, "f32") and isinstance(v.value, (int, float)):
+            ctx.env[s.name] = Val(f32_hex(float(v.value)), "f32", float(v.value))
+            return
+    raise NotImplementedError(f"Let of {type(v).__name__}")
+
+
+@handles("Init")
+def lower_init(ctx: ScalarCtx, s) -> None:
+    _check_f32(s.dtype, "Init")
+    r = ctx.ptx.reg("f32")
+    ctx.ptx.emit(f"mov.f32 {r}, {f32_hex(float(s.identity))}")
+    ctx.env[s.name] = Val(r, "f32")
+    ctx.mutable.add(s.name)
+
+
+@handles("Accum")
+def lower_accum(ctx: ScalarCtx, s) -> None:
+    """``acc = op(base or acc, value)`` into the accumulator's own register
+    (the reference: ``compiler/stmts.py:441-467``).  The template seeds the
+    accumulator register with the op's identity before the loop."""
+    _check_f32(s.dtype, "Accum")
+    acc = ctx.get(s.name)
+    left = s.base or s.name
+    a, b = ctx.f32(left), ctx.f32(s.value)
+    _binary(ctx.ptx, s.op.name, acc.text, a, b)
+
+
+@handles("Load")
+def lower_load(ctx: ScalarCtx, s) -> None:
+    if all(n in ctx.env for n in s.names):
+        return   # bound by the template (vector lane or cached value)
+    if len(s.names) == 1 and s.input in ctx.constants:
+        _check_f32(s.dtype, "constant Load")
+        v = float(ctx.constants[s.input])
+        ctx.env[s.names[0]] = Val(f32_hex(v), "f32", v)
+        return
+    if ctx.on_load is None:
+        raise NotImplementedError(f"Load of {s.input} outside a template stream")
+    ctx.on_load(ctx, s)
+
+
+@handles("Write")
+def lower_write(ctx: ScalarCtx, s) -> None:
+    if ctx.on_write is None:
+        raise NotImplementedError(f"Write to {s.output} outside a template stream")
+    ctx.on_write(ctx, s)
+
+
+# Structural statements are consumed by the kernel templates; reaching one
+# here means the IR nests it somewhere no template expects.
+def _structural(ctx, s):
+    raise NotImplementedError(f"statement {type(s).__name__} in an unsupported position")
+
+
+for _k in ("Tile", "Loop", "StridedLoop", "Cond", "WarpShuffle", "TreeHalve", "Smem", "Sync",
+           "CpAsyncCopy", "CpAsyncCommit", "CpAsyncWait", "RegFragment", "LdmatrixLoad",
+           "MmaSyncPtx", "RegStore", "FragmentApply", "FragmentRowReduce", "FragmentRepack"):
+    HANDLERS.setdefault(_k, _structural)
+
+
+# --------------------------------------------------------------------------
+# integer index expressions (Var / Literal / BinaryExpr / TernaryExpr)
+
+
+def eval_index(expr, env: dict) -> int:
+    """Evaluate an index expression with Python ints (C semantics for / and %)."""
+    k = type(expr).__name__
+    if k == "Var":
+        return env[expr.name]
+    if k == "Literal":
+        return int(expr.value)
+    if k == "BinaryExpr":
+        a, b = eval_index(expr.left, env), eval_index(expr.right, env)
+        op = expr.op
+        if op == "+":
+            return a + b
+        if op == "-":
+            return a - b
+        if op == "*":
+            return a * b
+        if op == "/":
+            q = abs(a) // abs(b)
+            return q if (a >= 0) == (b >= 0) else -q
+        if op == "%":
+            return a - b * eval_index_div(a, b)
+        if op == "<":
+            return int(a < b)
+        if op == "<=":
+            return int(a <= b)
+        if op == ">":
+            return int(a > b)
+        if op == ">=":
+            return int(a >= b)
+        if op == "==":
+            return int(a == b)
+        if op == "!=":
+            return int(a != b)
+        if op == "&&":
+            return int(bool(a) and bool(b))
+        if op == "||":
+            return int(bool(a) or bool(b))
+        raise NotImplementedError(f"index operator {op}")
+    if k == "TernaryExpr":
+        return eval_index(expr.if_true if eval_index(expr.cond, env) else expr.if_false, env)
+    raise NotImplementedError(f"index expression {k}")
+
+
+def eval_index_div(a: int, b: int) -> int:
+    q = abs(a) // abs(b)
+    return q if (a >= 0) == (b >= 0) else -q
+
+
+def expr_vars(expr) -> set:
+    k = type(expr).__name__
+    if k == "Var":
+        return {expr.name}
+    if k == "BinaryExpr":
+        return expr_vars(expr.left) | expr_vars(expr.right)
+    if k == "TernaryExpr":
+        return expr_vars(expr.cond) | expr_vars(expr.if_true) | expr_vars(expr.if_false)
+    return set()
+
+
+def flat_offset(index: tuple, shape: tuple, env: dict) -> int:
+    """Row-major element offset of ``buffer[index]`` (scalar buffers: ``()``)."""
+    off = 0
+    for e, d in zip(index, shape):
+        off = off * int(d) + eval_index(e, env)
+    return off

@@ -1,0 +1,258 @@
+"""CPU oracle for the hot path: numpy restatements of the reference harness's refs.
+
+TEST INFRASTRUCTURE ONLY.  Only tests/, __graft_entry__.smoke() and bench.py's
+CPU-baseline / ``--impl reference`` arm may import this module, and only as the
+checker or the timed CPU baseline -- never as a path that produces a product result.
+
+The reference computes every expected output with a numpy ``ref`` lambda over the
+seeded inputs (``tools/generate.py:169-176``: input ``i`` of the graph is
+``np.random.default_rng(i).standard_normal(shape)`` cast to its dtype).  The
+functions below restate those lambdas; each cites the line it follows.  They are
+pinned against the reference's own ``expected.npz`` golden vectors by
+``tests/test_oracle.py`` (``max |diff| == 0`` for most problems: same formula, same
+precision).
+"""
+
+from __future__ import annotations
+
+import numpy as np
+
+f64 = lambda a: np.asarray(a).astype(np.float64)   # noqa: E731
+f32 = lambda a: np.asarray(a).astype(np.float32)   # noqa: E731
+f16 = lambda a: np.asarray(a).astype(np.float16)   # noqa: E731
+
+
+# ---------------------------------------------------------------------------
+# inputs
+
+
+def seeded(seed: int, shape, dtype="f32") -> np.ndarray:
+    """``default_rng(seed).standard_normal(shape)`` cast to the buffer dtype
+    (``tools/generate.py:169-176``; ``docs/API.md:46``)."""
+    a = np.random.default_rng(seed).standard_normal(tuple(shape) or (1,))
+    if dtype == "f16":
+        return a.astype(np.float16)
+    if dtype == "f64":
+        return a
+    return a.astype(np.float32)
+
+
+# ---------------------------------------------------------------------------
+# reductions (category 2) -- tools/expressions_open.py:45-59,
+# tests/expressions_extra.py:186-205, 278-287
+
+
+def total_sum(x):
+    """``f32(f64(x).sum())`` (expressions_open.py:47-52; expressions_extra.py:187-190, 204-205)."""
+    return f32(f64(x).sum())
+
+
+def total_mean(x):
+    """``f32(f64(x).mean())`` (expressions_open.py:53-55)."""
+    return f32(f64(x).mean())
+
+
+def total_max(x):
+    """``x.max()`` (expressions_extra.py:191-192)."""
+    return np.asarray(x).max()
+
+
+def total_abs_max(x):
+    """``f32(abs(x).max())`` (expressions_extra.py:282-283)."""
+    return f32(np.abs(x).max())
+
+
+def total_sumsq(x):
+    """``f32((f64(x) ** 2).sum())`` (expressions_extra.py:193-194)."""
+    return f32((f64(x) ** 2).sum())
+
+
+def row_sum(x):
+    """``f32(f64(x).sum(-1))`` (expressions_open.py:56-58; expressions_extra.py:197-198)."""
+    return f32(f64(x).sum(-1))
+
+
+def row_mean(x):
+    """``f32(f64(x).mean(-1))`` (expressions_extra.py:195-196, 278-279)."""
+    return f32(f64(x).mean(-1))
+
+
+def row_max(x):
+    """``x.max(-1)`` (expressions_extra.py:199-200)."""
+    return np.asarray(x).max(-1)
+
+
+# ---------------------------------------------------------------------------
+# fused row kernels (category 4)
+
+
+def _softmax(x, axis=-1):
+    """Max-subtracted softmax in the input's precision (expressions_open.py:27-30)."""
+    m = x.max(axis=axis, keepdims=True)
+    e = np.exp(x - m)
+    return e / e.sum(axis=axis, keepdims=True)
+
+
+def softmax(x, scale=None):
+    """``f32(softmax(f64(x) [* scale]))`` (expressions_open.py:79-81;
+    expressions_extra.py:208-209, 249-250, 255-256)."""
+    xd = f64(x)
+    if scale is not None:
+        xd = xd * scale
+    return f32(_softmax(xd))
+
+
+def rmsnorm_sqrt(x, w, eps):
+    """``x / sqrt(mean(x^2) + eps) * w`` with the mean in f64
+    (expressions_open.py:73-78, problem f01_rmsnorm)."""
+    return f32(x / np.sqrt((f64(x) ** 2).mean(-1, keepdims=True) + eps) * w)
+
+
+def rmsnorm(x, w, eps=1e-6):
+    """``f32(f64(x) / sqrt(mean(f64(x)^2) + eps) * f64(w))`` -- the BASELINE formula
+    ``x * rsqrt(mean(x^2) + eps) * w`` (expressions_llm.py:76-78, x_l_rmsnorm_w)."""
+    return f32(f64(x) / np.sqrt((f64(x) ** 2).mean(-1, keepdims=True) + eps) * f64(w))
+
+
+def l2norm(x):
+    """``x / sqrt(sum(x^2))`` (expressions_open.py:82-84, problem f03_l2norm)."""
+    return f32(x / np.sqrt((f64(x) ** 2).sum(-1, keepdims=True)))
+
+
+# ---------------------------------------------------------------------------
+# tensor-core GEMM / attention (expressions_extra.py:48-63, 366-431;
+# expressions_quant.py:39-41)
+
+
+def mm_f16(a, b):
+    """torch's f16 matmul: exact products summed in f32, one rounding to f16
+    (``_mmh``, expressions_extra.py:50-51, computed in f64)."""
+    return f16(f64(a) @ f64(b))
+
+
+def attn_f16(q, kt, v, scale, causal=False, mask=None):
+    """torch's f16 attention with each op's result rounded to f16
+    (``_attn_h``, expressions_extra.py:54-63)."""
+    s = f16(f16(f64(q) @ f64(kt)) * scale)
+    if mask is not None:
+        s = f16(s + mask)
+    s = f64(s)
+    if causal:
+        s = np.where(np.tril(np.ones(s.shape[-2:], dtype=bool)), s, -np.inf)
+    return f16(f64(f16(_softmax(s))) @ f64(v))
+
+
+def gelu(x):
+    """Exact (erf) GELU, ``0.5 x (1 + erf(x / sqrt 2))`` (expressions_extra.py:66-67)."""
+    from math import erf, sqrt
+    v = np.vectorize(lambda t: 0.5 * t * (1.0 + erf(t / sqrt(2.0))))
+    return v(np.asarray(x, dtype=np.float64))
+
+
+def bf16_round(a) -> np.ndarray:
+    """Round f32 values to bf16 (nearest even) and return them as f32."""
+    u = np.ascontiguousarray(a, dtype=np.float32).view(np.uint32)
+    u = (u + (((u >> 16) & 1) + 0x7FFF)) & 0xFFFF0000
+    return u.view(np.float32)
+
+
+def mm_bf16(a, b):
+    """bf16 GEMM with f32 accumulation and a bf16 result, evaluated on the
+    bf16-valued operands in f64 (the BASELINE GEMM; x_q_bf16_mm's
+    ``a.bfloat16() @ b.bfloat16()``, expressions_quant.py:39-41)."""
+    return bf16_round(f32(f64(a) @ f64(b)))
+
+
+def attn_bf16(q, k, v, scale):
+    """Non-causal attention on bf16-valued inputs, softmax in f64, bf16 result:
+    ``softmax(q k^T * scale) v`` with ``[..., S, D]`` operands (the BASELINE
+    attention: F.scaled_dot_product_attention, as in x_h_sdpa)."""
+    s = f64(q) @ np.swapaxes(f64(k), -1, -2) * scale
+    return bf16_round(f32(_softmax(s) @ f64(v)))
+
+
+def e4m3_round(a) -> np.ndarray:
+    """Round to float8 e4m3fn with saturation to +-448 (torch's ``float8_e4m3fn``
+    cast, the semantics of the reference's dtypes.py:181-227), returned as f32."""
+    x = np.asarray(a, dtype=np.float64)
+    sign = np.sign(x)
+    m = np.minimum(np.abs(x), 448.0)
+    out = np.zeros_like(m)
+    nz = m > 0
+    e = np.floor(np.log2(m[nz]))
+    e = np.maximum(e, -6.0)                  # subnormals share the 2^-6 exponent
+    q = 2.0 ** (e - 3)                       # 3 mantissa bits
+    r = m[nz] / q
+    rn = np.round(r)                         # numpy rounds half to even
+    out[nz] = rn * q
+    out = np.minimum(out, 448.0)
+    return (sign * out).astype(np.float32)
+
+
+def mm_fp8(aq, bq, sa, sb):
+    """FP8 GEMM oracle: ``(A_q . B_q) * s_a * s_b`` in f64 from the e4m3-valued
+    operands, rounded to bf16 (no reference kernel: the reference has no FP8 GEMM)."""
+    return bf16_round(f32((f64(aq) @ f64(bq)) * sa * sb))
+
+
+# ---------------------------------------------------------------------------
+# per-problem table: which ref a golden fixture was generated with, with the
+# graph inputs in the order of meta.json's graph_inputs
+
+PROBLEM_REFS = {
+    "f01_rmsnorm": lambda x, w: [rmsnorm_sqrt(x, w, 1e-5)],
+    "f02_row_softmax": lambda x: [softmax(x)],
+    "f03_l2norm": lambda x: [l2norm(x)],
+    "r01_array_sum": lambda x: [total_sum(x)],
+    "r02_big_sum": lambda x: [total_sum(x)],
+    "r03_mean": lambda x: [total_mean(x)],
+    "r04_row_sum": lambda x: [row_sum(x)],
+    "x_l_rmsnorm_w": lambda x, w: [rmsnorm(x, w, 1e-6)],
+    "x_r_unpinned_sum": lambda x: [total_sum(x)],
+    "x_r_rowmax": lambda x: [row_max(x)],
+    "x_r_mean_rows": lambda x: [row_mean(x)],
+    "x_r_rowsum_wide": lambda x: [row_sum(x)],
+    "x_f_softmax_wide": lambda x: [softmax(x)],
+    "x_f_softmax_scaled": lambda x: [softmax(x, 0.125)],
+    "x_f_softmax_odd": lambda x: [softmax(x)],
+    "x_r_sumsq": lambda x: [total_sumsq(x)],
+    "x_r_max": lambda x: [total_max(x)],
+    "x_r_abs_max": lambda x: [total_abs_max(x)],
+    "x_r_sum100": lambda x: [total_sum(x)],
+    "x_r_sum1000": lambda x: [total_sum(x)],
+    "x_r_mean_3d": lambda x: [row_mean(x)],
+    "x_h_mm_1024": lambda a, b: [mm_f16(a, b)],
+    "x_h_mm_256": lambda a, b: [mm_f16(a, b)],
+    "x_h_mm_relu": lambda a, b: [np.maximum(mm_f16(a, b), f16(0))],
+    "x_h_mm_t_n8": lambda a, b: [mm_f16(a, b.T)],
+    "x_h_mm_t_odd": lambda a, b: [mm_f16(a, b.T)],
+    "x_h_linear": lambda x, w: [mm_f16(x, w.T)],
+    "x_h_bmm_t": lambda q, k: [mm_f16(q, np.swapaxes(k, -1, -2))],
+    "x_h_linear_bias_gelu": lambda x, w, b: [f16(gelu(f64(mm_f16(x, w.T) + b)))],
+    "x_h_mm_residual": lambda a, b, r: [mm_f16(a, b) + r],
+    "x_h_attn": lambda q, kt, v: [attn_f16(q, kt, v, 1 / 8)],
+    "x_h_attn_128": lambda q, kt, v: [attn_f16(q, kt, v, 1 / 8)],
+    "x_h_attn_b": lambda q, kt, v: [attn_f16(q, kt, v, 1 / 5.66)],
+    "x_h_sdpa": lambda q, k, v: [attn_f16(q, np.swapaxes(k, -1, -2), v, 1 / np.sqrt(32))],
+    "x_h_sdpa_causal": lambda q, k, v: [attn_f16(q, np.swapaxes(k, -1, -2), v, 1 / np.sqrt(32),
+                                                 causal=True)],
+    "x_h_sdpa_mask": lambda q, k, v, m: [attn_f16(q, np.swapaxes(k, -1, -2), v, 1 / np.sqrt(32),
+                                                  mask=m)],
+}
+
+
+def problem_inputs(meta: dict) -> list:
+    """The seeded graph inputs of a problem, in graph_inputs order."""
+    args = {a["name"]: a for k in meta["kernels"] for a in k["args"]}
+    out = []
+    for i, name in enumerate(meta["graph_inputs"]):
+        a = args[name]
+        out.append(seeded(a.get("seed", i), a["shape"], a["dtype"]))
+    return out
+
+
+def problem_expected(meta: dict) -> dict:
+    """Recompute a problem's expected outputs with the oracle."""
+    ref = PROBLEM_REFS[meta["id"]]
+    res = ref(*problem_inputs(meta))
+    return {name: np.asarray(r) for name, r in zip(meta["graph_outputs"], res)}

@@ -1,0 +1,62 @@
+#!/usr/bin/env python3
+"""Copy the hot-path known-answer problems out of the reference checkout.
+
+Each fixture is a problem folder of the reference (``problems/<id>`` or
+``tests/problems/<id>``) reduced to what a run needs: the kernels' IR json
+(``<entry>.ir.json``, the compiler input), ``meta.json`` (arg order, seeds,
+constants, tolerances) and ``expected.npz`` (the reference harness's golden
+outputs, computed by its numpy ``ref`` lambdas from the seeded inputs,
+``tools/generate.py:169-176``).  Emmy's rendered CUDA (``*.ref.cu``) and the
+pretty prints are not copied.
+
+Run from the repository root with the reference checked out at REFERENCE
+(default /root/reference):  python tests/golden/make_fixtures.py
+"""
+
+from __future__ import annotations
+
+import os
+import shutil
+import sys
+from pathlib import Path
+
+REFERENCE = Path(os.environ.get("REFERENCE", "/root/reference"))
+OUT = Path(__file__).resolve().parent / "problems"
+
+# the hot-path families (RMSNorm / softmax / L2 norm / row + global reductions,
+# tensor-core GEMM, tensor-core attention)
+FIXTURES = [
+    "problems/f01_rmsnorm", "problems/f02_row_softmax", "problems/f03_l2norm",
+    "problems/r01_array_sum", "problems/r02_big_sum", "problems/r03_mean", "problems/r04_row_sum",
+    "tests/problems/x_l_rmsnorm_w", "tests/problems/x_r_unpinned_sum", "tests/problems/x_r_rowmax",
+    "tests/problems/x_r_mean_rows", "tests/problems/x_r_rowsum_wide", "tests/problems/x_f_softmax_wide",
+    "tests/problems/x_f_softmax_scaled", "tests/problems/x_f_softmax_odd", "tests/problems/x_r_sumsq",
+    "tests/problems/x_r_max", "tests/problems/x_r_abs_max", "tests/problems/x_r_sum100",
+    "tests/problems/x_r_sum1000", "tests/problems/x_r_mean_3d",
+    "tests/problems/x_h_mm_1024", "tests/problems/x_h_mm_256", "tests/problems/x_h_mm_relu",
+    "tests/problems/x_h_mm_residual", "tests/problems/x_h_mm_t_n8", "tests/problems/x_h_mm_t_odd",
+    "tests/problems/x_h_bmm_t", "tests/problems/x_h_linear", "tests/problems/x_h_linear_bias_gelu",
+    "tests/problems/x_h_sdpa", "tests/problems/x_h_attn_128", "tests/problems/x_h_attn",
+    "tests/problems/x_h_attn_b", "tests/problems/x_h_sdpa_causal", "tests/problems/x_h_sdpa_mask",
+]
+
+
+def main() -> int:
+    if not REFERENCE.exists():
+        print(f"reference checkout not found at {REFERENCE}", file=sys.stderr)
+        return 1
+    for rel in FIXTURES:
+        src = REFERENCE / rel
+        dst = OUT / src.name
+        if dst.exists():
+            shutil.rmtree(dst)
+        dst.mkdir(parents=True)
+        for f in sorted(src.iterdir()):
+            if f.name == "meta.json" or f.name == "expected.npz" or f.name.endswith(".ir.json"):
+                shutil.copy(f, dst / f.name)
+        print(f"{rel} -> {dst.relative_to(OUT.parent.parent.parent)}")
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

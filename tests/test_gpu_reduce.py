@@ -1,0 +1,41 @@
+"""Parity of the streaming reduction kernels on the B200 (through the C-ABI runtime)."""
+
+import json
+
+import numpy as np
+import pytest
+
+from conftest import GOLDEN
+
+REDUCE = ["f01_rmsnorm", "f02_row_softmax", "f03_l2norm", "r01_array_sum", "r02_big_sum", "r03_mean",
+          "r04_row_sum", "x_l_rmsnorm_w", "x_r_unpinned_sum", "x_r_rowmax", "x_r_mean_rows",
+          "x_r_rowsum_wide", "x_f_softmax_wide", "x_f_softmax_scaled", "x_f_softmax_odd", "x_r_sumsq",
+          "x_r_max", "x_r_abs_max", "x_r_sum100", "x_r_sum1000", "x_r_mean_3d"]
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("pid", REDUCE)
+def test_reduction_matches_golden_and_oracle(runtime, pid):
+    from emmyrt.runner import run_problem
+    from oracle.refs import problem_expected
+    d = GOLDEN / pid
+    meta = json.loads((d / "meta.json").read_text())
+    res = run_problem(d)
+    exp = dict(np.load(d / "expected.npz"))
+    ora = problem_expected(meta)
+    for name, ref in exp.items():
+        got = res["outputs"][name].reshape(ref.shape)
+        assert np.allclose(got, ref, rtol=meta["rtol"], atol=meta["atol"]), \
+            f"{pid}:{name} max abs err {np.max(np.abs(got - ref))}"
+        # the BASELINE reduction bar: within 1e-5 relative of the f64 oracle
+        o = np.asarray(ora[name], dtype=np.float64).reshape(ref.shape)
+        tol = 1e-5 * np.maximum(np.abs(o), 1.0) if "sum" in pid or "mean" in pid else 1e-5 * np.abs(o) + 1e-6
+        assert np.all(np.abs(got - o) <= tol), f"{pid}:{name} oracle err {np.max(np.abs(got - o))}"
+
+
+@pytest.mark.gpu
+def test_rerun_is_deterministic(runtime):
+    from emmyrt.runner import run_problem
+    a = run_problem(GOLDEN / "x_r_unpinned_sum")["outputs"]["sum_1"]
+    b = run_problem(GOLDEN / "x_r_unpinned_sum")["outputs"]["sum_1"]
+    assert np.array_equal(a, b)
