@@ -1,5 +1,674 @@
-"""tcgen05 GEMM template (in progress)."""
+"""Dense GEMM on the 5th-generation tensor cores (tcgen05 + TMEM + TMA).
+
+Replaces the reference's register-fragment path for matmul kernels
+(``compiler/mma.py``: ``RegFragment`` m16n8k16 fragments, ``LdmatrixLoad`` from
+cp.async-filled shared memory, ``MmaSyncPtx``, ``RegStore``; ``compiler/coop.py``
+``CpAsyncCopy``; ``compiler/memory.py`` swizzles).  The IR's matmul family
+(``tests/problems/x_h_mm_1024`` and relatives) is recognised -- which buffer is A,
+which is B and in which major order, the output and its dtype -- and lowered to
+this template instead of emmy's 32x256 mma.sync schedule.
+
+Kernel structure (one CTA per SM, persistent over output tiles):
+
+* warp 0, lane 0 -- TMA producer: ``cp.async.bulk.tensor`` tiles of A (BM x 64 K,
+  K-major) and B (64 K x BN, MN- or K-major) into a ``STAGES``-deep ring of
+  128-byte-swizzled shared-memory stages, each guarded by a full/empty mbarrier pair;
+* warp 1 -- allocates TMEM (two BN-column f32 accumulators); lane 0 issues
+  ``tcgen05.mma.cta_group::1.kind::f16`` (M=128, N=BN, K=16) from shared-memory
+  descriptors and ``tcgen05.commit``\\ s each stage back to the producer and each
+  finished accumulator to the epilogue;
+* warps 2-5 -- epilogue: ``tcgen05.ld.32x32b.x32`` (one accumulator row per
+  thread), optional fused elementwise ops, ``cvt.rn.bf16x2.f32`` and 128-bit
+  stores; the accumulator buffer is released as soon as it is read, so the next
+  tile's MMAs overlap this tile's stores.
+
+Tiles are walked in groups of 8 M-tiles so CTAs running together share A and B
+panels in L2.  Every mbarrier wait is bounded (2 s of ``%globaltimer``): a stuck
+pipeline records a status bit and the CTA releases its TMEM and exits.
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass, field
+
+from ..ptx import Ptx, entry, f32_hex, module
+from .common import arg_params, load_pointer, param_symbol
+from .tc import Waits, instr_desc, smem_desc_hi, smem_desc_lo_const
+
+SMS = 148
+ELEM_BYTES = {"bf16": 2, "f16": 2, "e4m3": 1, "f32": 4}
+AB_FORMAT = {"f16": 0, "bf16": 1, "e4m3": 0, "e5m2": 1}
 
 
-def emit_gemm(spec):
-    raise NotImplementedError(f"kernel {spec.name}: tcgen05 GEMM template not built yet")
+@dataclass
+class GemmConfig:
+    M: int
+    N: int
+    K: int
+    batch: int = 1
+    ab: str = "bf16"              # operand type: bf16 | f16 | e4m3
+    c: str = "bf16"               # output type: bf16 | f16 | f32
+    b_kmajor: bool = False        # B stored [N, K] (else [K, N])
+    BN: int = 256
+    stages: int = 4
+    acc_bufs: int = 2
+    group_m: int = 8
+    epilogue: tuple = ()          # ("relu",) | ("bias", buf) | ("residual", buf) | ("scale2", sa, sb)
+    name: str = "k_gemm"
+    a_param: str = "a"
+    b_param: str = "b"
+    c_param: str = "c"
+    arg_params: list | None = None   # signature (meta.json arg_order) when compiled from IR
+    buffers: tuple = ()              # pointer params to load (name list) for IR kernels
+
+    BM = 128
+
+    @property
+    def kind(self) -> str:
+        return "f8f6f4" if self.ab in ("e4m3", "e5m2") else "f16"
+
+    @property
+    def BK(self) -> int:                 # K elements per stage: one 128-byte swizzle row
+        return 128 // ELEM_BYTES[self.ab]
+
+    @property
+    def UK(self) -> int:                 # K per tcgen05.mma instruction (32 bytes)
+        return 32 // ELEM_BYTES[self.ab]
+
+    @property
+    def tiles(self) -> tuple[int, int]:
+        return -(-self.M // self.BM), -(-self.N // self.BN)
+
+
+def choose_bn(M: int, N: int, batch: int) -> int:
+    """Largest N tile (<= 256, multiple of 16) that still gives every SM work when
+    possible; small problems trade per-tile efficiency for parallelism."""
+    bn = 256
+    while bn > 64 and batch * (-(-M // 128)) * (-(-N // bn)) < SMS:
+        bn //= 2
+    if N < bn:
+        bn = max(32, -(-N // 32) * 32)   # the epilogue reads TMEM 32 columns at a time
+    return bn
+
+
+def _tile_coords(p: Ptx, cfg: GemmConfig, t: str) -> tuple[str, str, str]:
+    """Grouped raster: tile index -> (batch, m tile, n tile), all u32 registers."""
+    tm, tn = cfg.tiles
+    per_batch = tm * tn
+    gsz = cfg.group_m * tn
+    bt, r, g, first, gm, w, mt, nt = p.regs("u32", 8)
+    p.emit(f"""
+        div.u32 {bt}, {t}, {per_batch}
+        rem.u32 {r}, {t}, {per_batch}
+        div.u32 {g}, {r}, {gsz}
+        mul.lo.u32 {first}, {g}, {cfg.group_m}
+        sub.u32 {gm}, {tm}, {first}
+        min.u32 {gm}, {gm}, {cfg.group_m}
+        rem.u32 {w}, {r}, {gsz}
+        rem.u32 {mt}, {w}, {gm}
+        add.u32 {mt}, {mt}, {first}
+        div.u32 {nt}, {w}, {gm}
+    """)
+    return bt, mt, nt
+
+
+def emit_gemm_module(cfg: GemmConfig) -> str:
+    p = Ptx()
+    M, N, K, BM, BN, BK, S = cfg.M, cfg.N, cfg.K, cfg.BM, cfg.BN, cfg.BK, cfg.stages
+    eb = ELEM_BYTES[cfg.ab]
+    cb = ELEM_BYTES[cfg.c]
+    tm, tn = cfg.tiles
+    ntiles = cfg.batch * tm * tn
+    kblocks = -(-K // BK)
+    a_bytes = BM * BK * eb                  # 16 KB
+    b_bytes = BN * BK * eb                  # 32 KB at BN = 256
+    stage_bytes = a_bytes + b_bytes
+    ncols = max(32, 1 << math.ceil(math.log2(BN * cfg.acc_bufs)))
+    if ncols > 512:
+        raise NotImplementedError("accumulators exceed TMEM")
+    smem = S * stage_bytes + 1024           # +1 KB to align the ring to 1024 B
+    if smem > 232448 - 256:
+        raise NotImplementedError("stage ring exceeds shared memory")
+    idesc = instr_desc(BM, BN, AB_FORMAT[cfg.ab], AB_FORMAT[cfg.ab], False, not cfg.b_kmajor)
+    a_hi = smem_desc_hi(1024)
+    a_lo = smem_desc_lo_const(16)
+    if cfg.b_kmajor:
+        b_hi, b_lo = smem_desc_hi(1024), smem_desc_lo_const(16)
+    else:
+        # MN-major: 64-element (128-byte) column blocks of BK K-rows each, BK*128 bytes apart
+        b_hi, b_lo = smem_desc_hi(1024), smem_desc_lo_const(BK * 128)
+    nb_mn = BN // (128 // eb)               # MN-major B: number of 128-byte column blocks
+    rank = 3 if cfg.batch > 1 else 2
+
+    p.comment(f"tcgen05 GEMM {cfg.batch}x{M}x{N}x{K} {cfg.ab}->{cfg.c}, tile {BM}x{BN}x{BK}, "
+              f"{S} stages, {cfg.acc_bufs} TMEM accumulators, B {'K' if cfg.b_kmajor else 'MN'}-major")
+    # ---------------------------------------------------------------- setup
+    ptr = {}
+    for name in cfg.buffers:
+        ptr[name] = load_pointer(p, name)
+    status = p.reg("b64")
+    p.emit(f"ld.param.u64 {status}, [param__status]\ncvta.to.global.u64 {status}, {status}")
+    tma_a, tma_b = p.reg("b64"), p.reg("b64")
+    p.emit(f"""
+        mov.u64 {tma_a}, param__tmap_a
+        cvta.param.u64 {tma_a}, {tma_a}
+        mov.u64 {tma_b}, param__tmap_b
+        cvta.param.u64 {tma_b}, {tma_b}
+    """)
+    tid, warp, lane = p.reg("u32"), p.reg("u32"), p.reg("u32")
+    p.emit(f"""
+        mov.u32 {tid}, %tid.x
+        shr.u32 {warp}, {tid}, 5
+        and.b32 {lane}, {tid}, 31
+    """)
+    ring, bars, abort, tslot = p.reg("u32"), p.reg("u32"), p.reg("u32"), p.reg("u32")
+    p.emit(f"""
+        mov.u32 {ring}, dsmem
+        add.u32 {ring}, {ring}, 1023
+        and.b32 {ring}, {ring}, -1024
+        mov.u32 {bars}, gbars
+        mov.u32 {abort}, gabort
+        mov.u32 {tslot}, gtmem
+    """)
+    # barrier layout: full[S], empty[S], tfull[A], tempty[A]
+    nbar = 2 * S + 2 * cfg.acc_bufs
+    full0, empty0, tfull0, tempty0 = 0, 8 * S, 16 * S, 16 * S + 8 * cfg.acc_bufs
+    p0 = p.reg("pred")
+    init_done = p.label("init_done")
+    p.emit(f"setp.ne.u32 {p0}, {tid}, 0\n@{p0} bra {init_done}")
+    for s in range(S):
+        p.emit(f"mbarrier.init.shared::cta.b64 [{bars}+{full0 + 8 * s}], 1")
+        p.emit(f"mbarrier.init.shared::cta.b64 [{bars}+{empty0 + 8 * s}], 1")
+    for b in range(cfg.acc_bufs):
+        p.emit(f"mbarrier.init.shared::cta.b64 [{bars}+{tfull0 + 8 * b}], 1")
+        p.emit(f"mbarrier.init.shared::cta.b64 [{bars}+{tempty0 + 8 * b}], 128")
+    p.emit(f"st.shared.u32 [{abort}], 0\nfence.mbarrier_init.release.cluster\nfence.proxy.async.shared::cta")
+    p.place(init_done)
+    # TMEM allocation by warp 1 (warp-collective)
+    p1 = p.reg("pred")
+    alloc_done = p.label("alloc_done")
+    p.emit(f"setp.ne.u32 {p1}, {warp}, 1\n@{p1} bra {alloc_done}")
+    p.emit(f"""
+        tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [{tslot}], {ncols}
+        tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned
+    """)
+    p.place(alloc_done)
+    tbase = p.reg("u32")
+    p.emit(f"""
+        tcgen05.fence::before_thread_sync
+        barrier.sync 0
+        tcgen05.fence::after_thread_sync
+        ld.shared.u32 {tbase}, [{tslot}]
+    """)
+    waits = Waits(p, status, abort)
+    finish = p.label("finish")
+    cta, nct = p.reg("u32"), p.reg("u32")
+    p.emit(f"mov.u32 {cta}, %ctaid.x\nmov.u32 {nct}, %nctaid.x")
+
+    # ------------------------------------------------------------ producer
+    role_mma, role_epi = p.label("role_mma"), p.label("role_epi")
+    pr = p.reg("pred")
+    p.emit(f"setp.ne.u32 {pr}, {warp}, 0\n@{pr} bra {role_mma}")
+    pl = p.reg("pred")
+    p.emit(f"setp.ne.u32 {pl}, {lane}, 0\n@{pl} bra {finish}")
+    p.emit(f"prefetch.tensormap [{tma_a}]\nprefetch.tensormap [{tma_b}]")
+    t, s, ph = p.reg("u32"), p.reg("u32"), p.reg("u32")
+    p.emit(f"mov.u32 {t}, {cta}\nmov.u32 {s}, 0\nmov.u32 {ph}, 0")
+    tl, td = p.label("p_tile"), p.label("p_done")
+    p.place(tl)
+    pt = p.reg("pred")
+    p.emit(f"setp.ge.u32 {pt}, {t}, {ntiles}\n@{pt} bra {td}")
+    bt, mt, nt = _tile_coords(p, cfg, t)
+    m0, n0 = p.reg("u32"), p.reg("u32")
+    p.emit(f"mul.lo.u32 {m0}, {mt}, {BM}\nmul.lo.u32 {n0}, {nt}, {BN}")
+    kb, kx = p.reg("u32"), p.reg("u32")
+    kl = p.label("p_k")
+    p.emit(f"mov.u32 {kb}, 0")
+    p.place(kl)
+    eaddr, faddr, sa, sbb, par = p.reg("u32"), p.reg("u32"), p.reg("u32"), p.reg("u32"), p.reg("u32")
+    p.emit(f"""
+        mad.lo.u32 {eaddr}, {s}, 8, {bars}
+        add.u32 {faddr}, {eaddr}, {full0}
+        add.u32 {eaddr}, {eaddr}, {empty0}
+        xor.b32 {par}, {ph}, 1
+    """)
+    waits.wait(eaddr, par, "producer", finish)
+    p.emit(f"""
+        mbarrier.arrive.expect_tx.shared::cta.b64 _, [{faddr}], {stage_bytes}
+        mad.lo.u32 {sa}, {s}, {stage_bytes}, {ring}
+        add.u32 {sbb}, {sa}, {a_bytes}
+        mul.lo.u32 {kx}, {kb}, {BK}
+    """)
+    zc = f", {bt}" if rank == 3 else ""
+    p.emit(f"cp.async.bulk.tensor.{rank}d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
+           f"[{sa}], [{tma_a}, {{{kx}, {m0}{zc}}}], [{faddr}]")
+    if cfg.b_kmajor:
+        p.emit(f"cp.async.bulk.tensor.{rank}d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
+               f"[{sbb}], [{tma_b}, {{{kx}, {n0}{zc}}}], [{faddr}]")
+    else:
+        blk = 128 // eb                      # 64 bf16 / 128 fp8 columns per box
+        for j in range(nb_mn):
+            nx, dst = p.reg("u32"), p.reg("u32")
+            p.emit(f"add.u32 {nx}, {n0}, {j * blk}\nadd.u32 {dst}, {sbb}, {j * BK * 128}")
+            p.emit(f"cp.async.bulk.tensor.{rank}d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
+                   f"[{dst}], [{tma_b}, {{{nx}, {kx}{zc}}}], [{faddr}]")
+    ps = p.reg("pred")
+    p.emit(f"""
+        add.u32 {s}, {s}, 1
+        setp.eq.u32 {ps}, {s}, {S}
+        @{ps} mov.u32 {s}, 0
+        @{ps} xor.b32 {ph}, {ph}, 1
+        add.u32 {kb}, {kb}, 1
+        setp.lt.u32 {ps}, {kb}, {kblocks}
+        @{ps} bra {kl}
+        add.u32 {t}, {t}, {nct}
+        bra {tl}
+    """)
+    p.place(td)
+    p.emit(f"bra {finish}")
+
+    # ----------------------------------------------------------------- MMA
+    p.place(role_mma)
+    p.emit(f"setp.ne.u32 {pr}, {warp}, 1\n@{pr} bra {role_epi}")
+    p.emit(f"setp.ne.u32 {pl}, {lane}, 0\n@{pl} bra {finish}")
+    t2, s2, ph2, tc = p.reg("u32"), p.reg("u32"), p.reg("u32"), p.reg("u32")
+    p.emit(f"mov.u32 {t2}, {cta}\nmov.u32 {s2}, 0\nmov.u32 {ph2}, 0\nmov.u32 {tc}, 0")
+    ml, md = p.label("m_tile"), p.label("m_done")
+    p.place(ml)
+    p.emit(f"setp.ge.u32 {pt}, {t2}, {ntiles}\n@{pt} bra {md}")
+    ab, aph, tea, tfa, dt = p.reg("u32"), p.reg("u32"), p.reg("u32"), p.reg("u32"), p.reg("u32")
+    p.emit(f"""
+        rem.u32 {ab}, {tc}, {cfg.acc_bufs}
+        div.u32 {aph}, {tc}, {cfg.acc_bufs}
+        and.b32 {aph}, {aph}, 1
+        xor.b32 {aph}, {aph}, 1
+        mad.lo.u32 {tea}, {ab}, 8, {bars}
+        add.u32 {tfa}, {tea}, {tfull0}
+        add.u32 {tea}, {tea}, {tempty0}
+        mad.lo.u32 {dt}, {ab}, {BN}, {tbase}
+    """)
+    waits.wait(tea, aph, "mma", finish)
+    p.emit("tcgen05.fence::after_thread_sync")
+    kb2 = p.reg("u32")
+    mk = p.label("m_k")
+    p.emit(f"mov.u32 {kb2}, 0")
+    p.place(mk)
+    fa2, ea2 = p.reg("u32"), p.reg("u32")
+    p.emit(f"""
+        mad.lo.u32 {fa2}, {s2}, 8, {bars}
+        add.u32 {ea2}, {fa2}, {empty0}
+        add.u32 {fa2}, {fa2}, {full0}
+    """)
+    waits.wait(fa2, ph2, "mma", finish)
+    p.emit("tcgen05.fence::after_thread_sync")
+    sa2, sb2 = p.reg("u32"), p.reg("u32")
+    p.emit(f"mad.lo.u32 {sa2}, {s2}, {stage_bytes}, {ring}\nadd.u32 {sb2}, {sa2}, {a_bytes}")
+    for kk in range(BK // cfg.UK):
+        alo, blo, ad, bd = p.reg("u32"), p.reg("u32"), p.reg("b64"), p.reg("b64")
+        a_off = kk * 32                                   # 32 bytes of K inside the swizzle row
+        b_off = kk * 32 if cfg.b_kmajor else kk * (cfg.UK * 128)   # MN-major: UK K-rows of 128 B
+        pacc = p.reg("pred")
+        p.emit(f"""
+            add.u32 {alo}, {sa2}, {a_off}
+            shr.u32 {alo}, {alo}, 4
+            or.b32 {alo}, {alo}, {a_lo}
+            mov.b64 {ad}, {{{alo}, {a_hi}}}
+            add.u32 {blo}, {sb2}, {b_off}
+            shr.u32 {blo}, {blo}, 4
+            or.b32 {blo}, {blo}, {b_lo}
+            mov.b64 {bd}, {{{blo}, {b_hi}}}
+        """)
+        if kk == 0:
+            p.emit(f"setp.ne.u32 {pacc}, {kb2}, 0")
+        else:
+            p.emit(f"setp.eq.u32 {pacc}, {kb2}, {kb2}")
+        p.emit(f"tcgen05.mma.cta_group::1.kind::{cfg.kind} [{dt}], {ad}, {bd}, {idesc}, {pacc}")
+    p.emit(f"tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [{ea2}]")
+    p.emit(f"""
+        add.u32 {s2}, {s2}, 1
+        setp.eq.u32 {ps}, {s2}, {S}
+        @{ps} mov.u32 {s2}, 0
+        @{ps} xor.b32 {ph2}, {ph2}, 1
+        add.u32 {kb2}, {kb2}, 1
+        setp.lt.u32 {ps}, {kb2}, {kblocks}
+        @{ps} bra {mk}
+        tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [{tfa}]
+        add.u32 {tc}, {tc}, 1
+        add.u32 {t2}, {t2}, {nct}
+        bra {ml}
+    """)
+    p.place(md)
+    p.emit(f"bra {finish}")
+
+    # ------------------------------------------------------------ epilogue
+    p.place(role_epi)
+    _emit_epilogue(p, cfg, ptr, bars, tfull0, tempty0, tbase, warp, lane, cta, nct, ntiles,
+                   waits, finish)
+
+    # -------------------------------------------------------------- finish
+    p.place(finish)
+    pw1 = p.reg("pred")
+    done = p.label("done")
+    p.emit(f"""
+        tcgen05.fence::before_thread_sync
+        barrier.sync 0
+        tcgen05.fence::after_thread_sync
+        setp.ne.u32 {pw1}, {warp}, 1
+        @{pw1} bra {done}
+        bar.warp.sync -1
+        tcgen05.dealloc.cta_group::1.sync.aligned.b32 {tbase}, {ncols}
+    """)
+    p.place(done)
+    p.emit("ret")
+
+    params = list(cfg.arg_params or [f".param .u64 {param_symbol(n)}" for n in cfg.buffers])
+    params += [".param .align 64 .b8 param__tmap_a[128]", ".param .align 64 .b8 param__tmap_b[128]",
+               ".param .u64 param__status"]
+    text = entry(cfg.name, params, p, maxntid=192)
+    statics = (f"\t.shared .align 8 .b64 gbars[{nbar}];\n\t.shared .align 4 .u32 gabort;\n"
+               f"\t.shared .align 4 .u32 gtmem;\n")
+    text = text.replace("{\n", "{\n" + statics, 1)
+    grid = min(ntiles, SMS)
+    a_dims = [K, M] + ([cfg.batch] if rank == 3 else [])
+    a_str = [K * eb] + ([M * K * eb] if rank == 3 else [])
+    if cfg.b_kmajor:
+        b_dims = [K, N] + ([cfg.batch] if rank == 3 else [])
+        b_str = [K * eb] + ([N * K * eb] if rank == 3 else [])
+        b_box = [BK, BN] + ([1] if rank == 3 else [])
+    else:
+        b_dims = [N, K] + ([cfg.batch] if rank == 3 else [])
+        b_str = [N * eb] + ([N * K * eb] if rank == 3 else [])
+        b_box = [128 // eb, BK] + ([1] if rank == 3 else [])
+    launch = {
+        "kind": "gemm", "grid": [grid, 1, 1], "block": [192, 1, 1], "cluster": [1, 1, 1],
+        "smem": smem, "flops": 2 * cfg.batch * M * N * K, "tiles": ntiles,
+        "extra_params": [
+            {"kind": "tmap", "buffer": cfg.a_param, "dtype": cfg.ab, "dims": a_dims, "strides": a_str,
+             "box": [BK, BM] + ([1] if rank == 3 else []), "swizzle": 128},
+            {"kind": "tmap", "buffer": cfg.b_param, "dtype": cfg.ab, "dims": b_dims, "strides": b_str,
+             "box": b_box, "swizzle": 128},
+            {"kind": "status"},
+        ],
+    }
+    return module([text], launch, globals_=[".extern .shared .align 1024 .b8 dsmem[];"])
+
+
+def _emit_epilogue(p: Ptx, cfg: GemmConfig, ptr: dict, bars, tfull0, tempty0, tbase, warp, lane,
+                   cta, nct, ntiles, waits: Waits, finish: str) -> None:
+    M, N, BM, BN = cfg.M, cfg.N, cfg.BM, cfg.BN
+    cb = ELEM_BYTES[cfg.c]
+    q, row_t = p.reg("u32"), p.reg("u32")
+    p.emit(f"and.b32 {q}, {warp}, 3\nmad.lo.u32 {row_t}, {q}, 32, {lane}")
+    lane_off = p.reg("u32")
+    p.emit(f"shl.b32 {lane_off}, {q}, 21")           # (q * 32) << 16: the warp's TMEM lane quarter
+    cptr = ptr[cfg.c_param]
+    extra = {}
+    for op in cfg.epilogue:
+        if op[0] in ("bias", "residual"):
+            extra[op[1]] = ptr[op[1]]
+    scale = None
+    for op in cfg.epilogue:
+        if op[0] == "scale2":
+            sa, sb, scale = p.reg("f32"), p.reg("f32"), p.reg("f32")
+            p.emit(f"ld.global.f32 {sa}, [{ptr[op[1]]}]\nld.global.f32 {sb}, [{ptr[op[2]]}]\n"
+                   f"mul.rn.f32 {scale}, {sa}, {sb}")
+    t, tc = p.reg("u32"), p.reg("u32")
+    p.emit(f"mov.u32 {t}, {cta}\nmov.u32 {tc}, 0")
+    el, ed = p.label("e_tile"), p.label("e_done")
+    p.place(el)
+    pt = p.reg("pred")
+    p.emit(f"setp.ge.u32 {pt}, {t}, {ntiles}\n@{pt} bra {ed}")
+    ab, aph, tfa, tea = p.reg("u32"), p.reg("u32"), p.reg("u32"), p.reg("u32")
+    p.emit(f"""
+        rem.u32 {ab}, {tc}, {cfg.acc_bufs}
+        div.u32 {aph}, {tc}, {cfg.acc_bufs}
+        and.b32 {aph}, {aph}, 1
+        mad.lo.u32 {tfa}, {ab}, 8, {bars}
+        add.u32 {tea}, {tfa}, {tempty0}
+        add.u32 {tfa}, {tfa}, {tfull0}
+    """)
+    waits.wait(tfa, aph, "epilogue", finish)
+    p.emit("bar.warp.sync -1\ntcgen05.fence::after_thread_sync")
+    bt, mt, nt = _tile_coords(p, cfg, t)
+    row, n0, taddr = p.reg("u32"), p.reg("u32"), p.reg("u32")
+    prow = p.reg("pred")
+    p.emit(f"""
+        mad.lo.u32 {row}, {mt}, {BM}, {row_t}
+        mul.lo.u32 {n0}, {nt}, {BN}
+        setp.lt.u32 {prow}, {row}, {M}
+        mad.lo.u32 {taddr}, {ab}, {BN}, {tbase}
+        add.u32 {taddr}, {taddr}, {lane_off}
+    """)
+    # element offset of (batch, row, n0) in C
+    off, cadr = p.reg("b64"), p.reg("b64")
+    wide = p.reg("b64")
+    p.emit(f"""
+        mul.wide.u32 {off}, {bt}, {M}
+        cvt.u64.u32 {wide}, {row}
+        add.s64 {off}, {off}, {wide}
+        mul.lo.s64 {off}, {off}, {N}
+        cvt.u64.u32 {wide}, {n0}
+        add.s64 {off}, {off}, {wide}
+        mad.lo.s64 {cadr}, {off}, {cb}, {cptr}
+    """)
+    res_adr = {}
+    for name, bp in extra.items():
+        a = p.reg("b64")
+        kind = [o[0] for o in cfg.epilogue if len(o) > 1 and o[1] == name][0]
+        if kind == "residual":
+            p.emit(f"mad.lo.s64 {a}, {off}, 2, {bp}")
+        else:   # bias over N: element n0
+            w2 = p.reg("b64")
+            p.emit(f"cvt.u64.u32 {w2}, {n0}\nmad.lo.s64 {a}, {w2}, 2, {bp}")
+        res_adr[name] = a
+    nchunks = BN // 32
+    regs = [p.reg("b32") for _ in range(32)]
+    for ch in range(nchunks):
+        p.emit(f"tcgen05.ld.sync.aligned.32x32b.x32.b32 {{{', '.join(regs)}}}, [{taddr}+{ch * 32}]")
+        p.emit("tcgen05.wait::ld.sync.aligned")
+        if ch == nchunks - 1:
+            # the accumulator is in registers: hand the buffer back to the MMA warp
+            p.emit(f"tcgen05.fence::before_thread_sync\nmbarrier.arrive.shared::cta.b64 _, [{tea}]")
+        vals = [p.reg("f32") for _ in range(32)]
+        for i in range(32):
+            p.emit(f"mov.b32 {vals[i]}, {regs[i]}")
+        vals = _apply_epilogue(p, cfg, vals, scale, res_adr, ch)
+        skip = p.label("st_skip")
+        col0 = ch * 32
+        p.emit(f"@!{prow} bra {skip}")
+        if cfg.c in ("bf16", "f16") and N % 8 == 0:
+            cvt = "cvt.rn.bf16x2.f32" if cfg.c == "bf16" else "cvt.rn.f16x2.f32"
+            packed = [p.reg("b32") for _ in range(16)]
+            for i in range(16):
+                # the first element of a pair goes to the low half (lower address)
+                p.emit(f"{cvt} {packed[i]}, {vals[2 * i + 1]}, {vals[2 * i]}")
+            for g in range(4):
+                pg = p.reg("pred")
+                colr = p.reg("u32")
+                p.emit(f"add.u32 {colr}, {n0}, {col0 + 8 * g}\nsetp.lt.u32 {pg}, {colr}, {N}")
+                p.emit(f"@{pg} st.global.v4.b32 [{cadr}+{(col0 + 8 * g) * 2}], "
+                       f"{{{', '.join(packed[4 * g:4 * g + 4])}}}")
+        elif cfg.c == "f32" and N % 4 == 0:
+            for g in range(8):
+                pg, colr = p.reg("pred"), p.reg("u32")
+                p.emit(f"add.u32 {colr}, {n0}, {col0 + 4 * g}\nsetp.lt.u32 {pg}, {colr}, {N}")
+                p.emit(f"@{pg} st.global.v4.f32 [{cadr}+{(col0 + 4 * g) * 4}], "
+                       f"{{{', '.join(vals[4 * g:4 * g + 4])}}}")
+        else:
+            for i in range(32):
+                pg, colr = p.reg("pred"), p.reg("u32")
+                p.emit(f"add.u32 {colr}, {n0}, {col0 + i}\nsetp.lt.u32 {pg}, {colr}, {N}")
+                if cfg.c == "f32":
+                    p.emit(f"@{pg} st.global.f32 [{cadr}+{(col0 + i) * 4}], {vals[i]}")
+                else:
+                    h = p.reg("b16")
+                    cvt = "cvt.rn.bf16.f32" if cfg.c == "bf16" else "cvt.rn.f16.f32"
+                    p.emit(f"{cvt} {h}, {vals[i]}\n@{pg} st.global.b16 [{cadr}+{(col0 + i) * 2}], {h}")
+        p.place(skip)
+    p.emit(f"""
+        add.u32 {tc}, {tc}, 1
+        add.u32 {t}, {t}, {nct}
+        bra {el}
+    """)
+    p.place(ed)
+    p.emit(f"bra {finish}")
+
+
+def _apply_epilogue(p: Ptx, cfg: GemmConfig, vals: list, scale, res_adr: dict, ch: int) -> list:
+    """Fused elementwise ops on one 32-column chunk of a row (f32 registers)."""
+    down = "cvt.rn.f16.f32" if cfg.c == "f16" else "cvt.rn.bf16.f32"
+    up = "cvt.f32.f16" if cfg.c == "f16" else "cvt.f32.bf16"
+    for op in cfg.epilogue:
+        kind = op[0]
+        if kind == "scale2":
+            for v in vals:
+                p.emit(f"mul.rn.f32 {v}, {v}, {scale}")
+        elif kind == "relu":
+            for v in vals:
+                p.emit(f"max.f32 {v}, {v}, 0f00000000")
+        elif kind == "round":
+            for v in vals:
+                h = p.reg("b16")
+                p.emit(f"{down} {h}, {v}\n{up} {v}, {h}")
+        elif kind in ("bias", "residual"):
+            a = res_adr[op[1]]
+            for i, v in enumerate(vals):
+                h, r = p.reg("b16"), p.reg("f32")
+                p.emit(f"ld.global.b16 {h}, [{a}+{(ch * 32 + i) * 2}]\n{up} {r}, {h}\n"
+                       f"add.rn.f32 {v}, {v}, {r}")
+        else:
+            raise NotImplementedError(f"GEMM epilogue {kind}")
+    return vals
+
+
+# ---------------------------------------------------------------------------
+# recognising the IR's matmul family
+
+
+def _walk(body):
+    for s in body:
+        yield s
+        for attr in ("body", "else_body"):
+            sub = getattr(s, attr, None)
+            if isinstance(sub, tuple):
+                yield from _walk(sub)
+
+
+def _vars(expr) -> set:
+    from ..stmts import expr_vars
+    return expr_vars(expr)
+
+
+def analyze(spec) -> GemmConfig:
+    """Identify A, B (and its major order), C and the epilogue of a matmul kernel."""
+    stmts = list(_walk(spec.body))
+    kinds = {type(s).__name__ for s in stmts}
+    if "MmaSyncPtx" not in kinds or "FragmentRowReduce" in kinds:
+        raise NotImplementedError("not a tensor-core matmul")
+    stores = [s for s in stmts if type(s).__name__ == "RegStore"]
+    if not stores or len({s.dst_buffer for s in stores}) != 1:
+        raise NotImplementedError("matmul without a single RegStore output")
+    if any(s.atomic for s in stores):
+        raise NotImplementedError("split-K partial matmul (atomic RegStore)")
+    cname = stores[0].dst_buffer
+    # the K loop: the Loop that (transitively) holds the MmaSyncPtx statements
+    kvar = None
+    for s in stmts:
+        if type(s).__name__ in ("Loop", "StridedLoop") and any(
+                type(x).__name__ == "MmaSyncPtx" for x in _walk(s.body)):
+            kvar = s.axis.name
+            break
+    # operand sources: smem staging (CpAsyncCopy / Write of loaded values) or gmem-direct
+    smem_src = {}
+    for s in stmts:
+        k = type(s).__name__
+        if k == "CpAsyncCopy":
+            smem_src[s.smem] = (s.src, s.src_index)
+    role_src = {}
+    for s in stmts:
+        if type(s).__name__ == "LdmatrixLoad":
+            buf = s.src_buffer
+            src = smem_src.get(buf, (buf, s.src_index) if buf in spec.buffers else None)
+            if src is None:
+                raise NotImplementedError(f"cannot trace operand {s.frag} to a buffer")
+            role_src.setdefault(s.role, src)
+    if set(role_src) != {"a", "b"}:
+        raise NotImplementedError("matmul operands not found")
+    (aname, aidx), (bname, bidx) = role_src["a"], role_src["b"]
+    A, B, C = spec.param(aname), spec.param(bname), spec.param(cname)
+    if A.dtype != B.dtype or A.dtype not in ("f16", "bf16"):
+        raise NotImplementedError(f"matmul operands {A.dtype}/{B.dtype}: TMA feeds 16-bit operands")
+    if C.dtype not in ("f16", "bf16", "f32"):
+        raise NotImplementedError(f"matmul output {C.dtype}")
+    if kvar is None:
+        raise NotImplementedError("no K loop")
+
+    def k_dim(index) -> int:
+        dims = [i for i, e in enumerate(index) if kvar in _vars(e)]
+        if len(dims) != 1:
+            raise NotImplementedError("K axis not identifiable in an operand index")
+        return dims[0]
+    if k_dim(aidx) != len(A.shape) - 1:
+        raise NotImplementedError("A operand is not K-major")
+    b_kmajor = k_dim(bidx) == len(B.shape) - 1
+    M, K = A.shape[-2], A.shape[-1]
+    N = B.shape[-2] if b_kmajor else B.shape[-1]
+    if (B.shape[-1] if b_kmajor else B.shape[-2]) != K or tuple(C.shape[-2:]) != (M, N):
+        raise NotImplementedError("operand shapes do not form a matmul")
+    batch = int(math.prod(C.shape[:-2])) if len(C.shape) > 2 else 1
+    if batch > 1 and (math.prod(A.shape[:-2]) != batch or math.prod(B.shape[:-2]) != batch):
+        raise NotImplementedError("broadcast batch operands")
+    eb = 2
+    if (K * eb) % 16 or (not b_kmajor and (N * eb) % 16):
+        raise NotImplementedError("operand rows are not 16-byte aligned (TMA)")
+    epi = _epilogue_ops(spec, stores[0])
+    bn = choose_bn(M, N, batch)
+    return GemmConfig(M=M, N=N, K=K, batch=batch, ab=A.dtype, c=C.dtype, b_kmajor=b_kmajor, BN=bn,
+                      epilogue=epi, name=spec.name, a_param=aname, b_param=bname, c_param=cname,
+                      arg_params=arg_params(spec), buffers=tuple(q.name for q in spec.params))
+
+
+def _epilogue_ops(spec, store) -> tuple:
+    """The RegStore epilogue Lambda (``mma.py:347-357`` in the reference) as fused ops,
+    in statement order: ``copy`` to a 16-bit dtype rounds the accumulator the way
+    torch's f16/bf16 matmul result is rounded before the next op; ``relu``; ``add`` of
+    a loaded operand (a C-shaped residual, or a bias over N)."""
+    lam = store.epilogue
+    if lam is None:
+        return ()
+    ops = []
+    loads = {}
+    for s in lam.body:
+        k = type(s).__name__
+        if k == "Load":
+            if s.input in spec.constants:
+                raise NotImplementedError("GEMM epilogue with constant operands")
+            loads[s.names[0]] = s.input
+        elif k == "Assign":
+            op = s.op.name
+            dt = getattr(s.dtype, "name", None)
+            if op == "copy":
+                if dt in ("f16", "bf16"):
+                    ops.append(("round",))
+            elif op == "relu":
+                ops.append(("relu",))
+            elif op == "add" and sum(a in loads for a in s.args) == 1:
+                buf = loads[[a for a in s.args if a in loads][0]]
+                shape = spec.param(buf).shape
+                cshape = spec.param(store.dst_buffer).shape
+                if tuple(shape) == tuple(cshape):
+                    ops.append(("residual", buf))
+                elif len(shape) == 1 and shape[0] == cshape[-1]:
+                    ops.append(("bias", buf))
+                else:
+                    raise NotImplementedError("GEMM epilogue operand shape")
+            else:
+                raise NotImplementedError(f"GEMM epilogue op {op}")
+        else:
+            raise NotImplementedError(f"GEMM epilogue statement {k}")
+    return tuple(ops)
+
+
+def emit_gemm(spec) -> str:
+    return emit_gemm_module(analyze(spec))

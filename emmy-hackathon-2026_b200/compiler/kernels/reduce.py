@@ -512,9 +512,9 @@ def _rename(expr, old: str, new: str):
 class FullReduce:
     """Every element of the tile's index space folds into one scalar per kernel."""
 
-    UNROLL = 4          # 128-bit loads in flight per thread per iteration
+    UNROLL = 8          # 128-bit loads in flight per thread per iteration
     CTA = 256
-    CTAS_PER_SM = 8
+    CTAS_PER_SM = 4     # one wave: 4 x 256 threads fit at the kernel's register count
 
     def __init__(self, spec):
         self.spec = spec
@@ -595,22 +595,33 @@ class FullReduce:
             accf = p.reg("f32")
             p.emit(f"mov.f32 {accf}, {f32_hex(ident)}")
 
+        body_wo_acc = [s for s in self.loop.body if s is not self.load and s is not self.acc]
+        combine_op = {"add": "add.rn.f32", "maximum": "max.f32", "minimum": "min.f32"}[self.op]
+
         def fold_elements(vals: list[str]):
-            """Run the IR's per-element statements on each value; return the f32
-            group partial (sum) or fold into accf (max/min)."""
-            grp = None
-            if is_add:
-                grp = p.reg("f32")
-                p.emit(f"mov.f32 {grp}, 0f00000000")
+            """Map each loaded value through the IR's per-element statements (the
+            Accum's operand), then fold the group as a balanced tree; sums return the
+            f32 group partial, max/min fold straight into ``accf``."""
+            mapped = []
             for v in vals:
                 saved = dict(ctx.env)
                 ctx.env[self.load.names[0]] = Val(v, "f32")
-                ctx.env[self.acc.name] = Val(grp if is_add else accf, "f32")
-                ctx.mutable.add(self.acc.name)
-                lower_body(ctx, [s for s in self.loop.body if s is not self.load])
+                lower_body(ctx, body_wo_acc)
+                mapped.append(ctx.f32(self.acc.value))
                 ctx.env = saved
-                ctx.mutable.discard(self.acc.name)
-            return grp
+            while len(mapped) > 1:
+                nxt = []
+                for i in range(0, len(mapped) - 1, 2):
+                    r = p.reg("f32")
+                    p.emit(f"{combine_op} {r}, {mapped[i]}, {mapped[i + 1]}")
+                    nxt.append(r)
+                if len(mapped) % 2:
+                    nxt.append(mapped[-1])
+                mapped = nxt
+            if is_add:
+                return mapped[0]
+            p.emit(f"{combine_op} {accf}, {accf}, {mapped[0]}")
+            return None
 
         # ---- main grid-stride loop over whole UNROLL x VEC groups (64-bit offsets)
         group = self.VEC * self.UNROLL

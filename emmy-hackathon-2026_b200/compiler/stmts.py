@@ -290,6 +290,8 @@ def eval_index(expr, env: dict) -> int:
         if op == "/":
             q = abs(a) // abs(b)
             return q if (a >= 0) == (b >= 0) else -q
+        if op == "//":
+            return a // b
         if op == "%":
             return a - b * eval_index_div(a, b)
         if op == "<":
