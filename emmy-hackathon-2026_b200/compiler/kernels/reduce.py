@@ -37,7 +37,7 @@ import math
 from dataclasses import dataclass, field
 
 from ..ptx import Ptx, entry, f32_hex, f64_hex, module
-from ..stmts import ScalarCtx, Val, dtype_name, expr_vars, lower_body
+from ..stmts import ScalarCtx, Val, dtype_name, emit_exp_nonpos, expr_vars, lower_body
 from .common import Affine, affine_offset, arg_params, load_pointer
 
 SMS = 148          # B200 multiprocessors (grid sizing for the streaming reduction)
@@ -347,6 +347,127 @@ class RowReduce:
         return pc
 
     # -- phases ------------------------------------------------------------------
+    def _match_online_softmax(self, loop):
+        """The online-softmax accumulator pair of one pass, if that is what it is:
+        ``m <- max(m, X)`` and ``l <- l * exp(m - G) + exp(X - G) [* 1]`` with
+        ``G = max(m, X)``.  Returns (X, m, l) or None."""
+        accs = _accums(loop.body)
+        if len(accs) != 2:
+            return None
+        am = [a for a in accs if a.op.name == "maximum" and a.base is None]
+        al = [a for a in accs if a.op.name == "add" and a.base is not None]
+        if len(am) != 1 or len(al) != 1:
+            return None
+        am, al = am[0], al[0]
+        X, m, l = am.value, am.name, al.name
+        defs, ones = {}, set()
+        for s in loop.body:
+            k = type(s).__name__
+            if k == "Assign":
+                defs[s.name] = (s.op.name, tuple(s.args))
+            elif k == "Let" and type(s.value).__name__ == "Literal" and float(s.value.value) == 1.0:
+                ones.add(s.name)
+
+        def is_op(name, op, args=None):
+            d = defs.get(name)
+            if d is None or d[0] != op:
+                return False
+            if args is None:
+                return True
+            if op in ("maximum", "multiply"):
+                return sorted(d[1]) == sorted(args)
+            return d[1] == tuple(args)
+
+        def strip_one(name):
+            d = defs.get(name)
+            if d and d[0] == "multiply":
+                a, b = d[1]
+                if b in ones:
+                    return a
+                if a in ones:
+                    return b
+            return name
+        gs = [n for n, d in defs.items() if d[0] == "maximum" and sorted(d[1]) == sorted((m, X))]
+        if len(gs) != 1:
+            return None
+        G = gs[0]
+        v = strip_one(al.value)
+        if not (is_op(v, "exp") and is_op(defs[v][1][0], "subtract", (X, G))):
+            return None
+        base = defs.get(al.base)
+        if base is None or base[0] != "multiply" or l not in base[1]:
+            return None
+        alpha = [a for a in base[1] if a != l][0]
+        if not (is_op(alpha, "exp") and is_op(defs[alpha][1][0], "subtract", (m, G))):
+            return None
+        return X, m, l
+
+    def _emit_online_softmax(self, ctx: ScalarCtx, loop, match, loads):
+        """Register-resident rewrite of the online pair: each thread takes the max of
+        its elements, then sums exp(X - max) -- one exp per element and no serial
+        dependency -- and folds that into (m, l) with the same online rule."""
+        p = ctx.ptx
+        X, m, l = match
+        # only the statements X depends on (the online update itself is replaced)
+        need, deps = {X}, {}
+        for s in loop.body:
+            k = type(s).__name__
+            if k == "Assign":
+                deps[s.name] = set(s.args)
+            elif k in ("Let", "Load"):
+                for n in (s.names if k == "Load" else (s.name,)):
+                    deps[n] = set()
+        changed = True
+        while changed:
+            changed = False
+            for n in list(need):
+                for d in deps.get(n, ()):
+                    if d not in need:
+                        need.add(d)
+                        changed = True
+        keep_stmts = [s for s in loop.body if type(s).__name__ in ("Assign", "Let") and
+                      s.name in need]
+        xs = []
+        for c in range(self.NCH):
+            for v in range(self.VEC):
+                saved = dict(ctx.env)
+                for s in loads:
+                    acc = self.accesses[id(s)]
+                    regs = self.val_cache[(acc.buffer, acc.aff, c if acc.col_coef else "row")]
+                    ctx.env[s.names[0]] = Val(regs[v] if acc.col_coef else regs[0], "f32")
+                lower_body(ctx, keep_stmts)
+                xs.append(ctx.f32(X))
+                keep = {n: ctx.env[n] for n in ctx.mutable if n in ctx.env}
+                ctx.env = saved
+                ctx.env.update(keep)
+
+        def tree(vals, op):
+            while len(vals) > 1:
+                nxt = []
+                for i in range(0, len(vals) - 1, 2):
+                    r = p.reg("f32")
+                    p.emit(f"{op} {r}, {vals[i]}, {vals[i + 1]}")
+                    nxt.append(r)
+                if len(vals) % 2:
+                    nxt.append(vals[-1])
+                vals = nxt
+            return vals[0]
+        mt = tree(list(xs), "max.f32")
+        es = []
+        for x in xs:
+            d, e = p.reg("f32"), p.reg("f32")
+            p.emit(f"sub.rn.f32 {d}, {x}, {mt}")
+            emit_exp_nonpos(p, e, d)
+            es.append(e)
+        lt = tree(es, "add.rn.f32")
+        mr, lr = ctx.f32(m), ctx.f32(l)
+        mn, d0, d1, a0, a1 = p.regs("f32", 5)
+        p.emit(f"max.f32 {mn}, {mr}, {mt}\nsub.rn.f32 {d0}, {mr}, {mn}\nsub.rn.f32 {d1}, {mt}, {mn}")
+        emit_exp_nonpos(p, a0, d0)
+        emit_exp_nonpos(p, a1, d1)
+        p.emit(f"mul.rn.f32 {a0}, {lr}, {a0}\nfma.rn.f32 {lr}, {lt}, {a1}, {a0}\nmov.f32 {mr}, {mn}")
+        ctx.max_states.add(m)
+
     def _emit_stream(self, ctx: ScalarCtx, loop):
         p = ctx.ptx
         span = self.TPR * self.VEC
@@ -380,8 +501,13 @@ class RowReduce:
                 r = p.reg("f32")
                 p.emit(f"ld.global.f32 {r}, [{self._row_base(acc.buffer, acc.aff)}]")
                 self.val_cache[key] = [r]
-        # 2. the IR's per-element statements, chunk by chunk, lane by lane
+        # 2a. the online-softmax accumulator pair over full chunks: register-resident rewrite
         writes = [s for s in loop.body if type(s).__name__ == "Write"]
+        match = self._match_online_softmax(loop)
+        if match and not writes and self.L % span == 0:
+            self._emit_online_softmax(ctx, loop, match, loads)
+            return
+        # 2b. the IR's per-element statements, chunk by chunk, lane by lane
         for c in range(self.NCH):
             pc = self._chunk_pred(c)
             skip = None

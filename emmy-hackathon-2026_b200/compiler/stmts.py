@@ -62,6 +62,7 @@ class Val:
     text: str          # register name or immediate
     kind: str          # "f32" | "s32" | "pred"
     const: float | None = None
+    nonpos: bool = False   # known <= 0 (an element minus the row maximum)
 
 
 @dataclass
@@ -73,6 +74,7 @@ class ScalarCtx:
     on_load: Callable | None = None                  # fn(ctx, Load) -> None (binds names)
     on_write: Callable | None = None                 # fn(ctx, Write) -> None
     axis_regs: dict = field(default_factory=dict)    # axis name -> s32 register / immediate
+    max_states: set = field(default_factory=set)     # accumulators holding a row maximum
 
     def bind(self, name: str, val: Val) -> None:
         if name in self.mutable and name in self.env:
@@ -104,6 +106,15 @@ class ScalarCtx:
 _LOG2E_HI = 1.4426950216293335       # float32(log2 e)
 _LOG2E_LO = 1.925963033500011e-08    # log2 e - _LOG2E_HI
 _LN2 = 0.6931471805599453
+
+
+def emit_exp_nonpos(p: Ptx, dst: str, x: str) -> None:
+    """exp(x) for x <= 0 (an element minus its row maximum): ``ex2.approx`` of the
+    rounded product x*log2(e).  The product's rounding adds at most |x| * 2^-24
+    relative error to the argument, so for x in [-20, 0] the result is within
+    ~1.5e-6 relative (plus ex2.approx's 2 ulp); arguments below -126 flush to 0."""
+    t = p.reg("f32")
+    p.emit(f"mul.rn.f32 {t}, {x}, {f32_hex(_LOG2E_HI)}\nex2.approx.ftz.f32 {dst}, {t}")
 
 
 def emit_exp(p: Ptx, dst: str, x: str) -> None:
@@ -173,6 +184,12 @@ def compute_f32(ctx: ScalarCtx, op: str, args: list[str], dst: str | None = None
     p = ctx.ptx
     vals = [ctx.f32(a) for a in args]
     out = dst or p.reg("f32")
+    if op == "subtract" and len(args) == 2 and args[1] in ctx.max_states:
+        _binary(p, op, out, vals[0], vals[1])
+        return Val(out, "f32", nonpos=True)
+    if op == "exp" and len(args) == 1 and ctx.get(args[0]).nonpos:
+        emit_exp_nonpos(p, out, vals[0])
+        return Val(out, "f32")
     if len(vals) == 1:
         _unary(p, op, out, vals[0])
     elif len(vals) == 2:
