@@ -1,0 +1,448 @@
+#!/usr/bin/env python3
+"""Benchmark of the B200 back end on BASELINE.json's configurations.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME] [--impl ours|reference]
+
+One step = one launch of the kernel compile.py emits for the workload's IR (the
+BASELINE configuration synthesised from the reference's IR family), over inputs
+already resident in HBM.  The default workload is the bf16 GEMM at M=N=K=8192,
+the configuration BASELINE.json's TFLOP/s target is quoted on.
+
+Multi-GPU (torchrun, one process per GPU): the work is partitioned the way the
+reference's problem partitions (GEMM by N-panel, attention by batch x head, row
+kernels by rows): every rank runs its own panel, no data-path collective, weak
+scaling; the global sum's per-rank partials are finished by one NCCL all-reduce.
+Times are CUDA events on the launching stream, the job time is the max over ranks.
+
+The JSON line carries the device-resident throughput (``value``), the end-to-end
+throughput through the C-ABI runtime with host buffers (``e2e``), the roofline of
+the kernel, a CPU baseline (the oracle port, timed on a bounded sample), SM clocks
+sampled during the timed region, and the number of our kernel launches timed.
+``--impl reference`` times the reference path's CPU evaluation (the numpy oracle the
+reference's harness computes expected outputs with) on the same configuration.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import sys
+import threading
+import time
+from datetime import timedelta
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "emmy-hackathon-2026_b200"))
+sys.path.insert(0, str(ROOT))
+
+METRIC = "GEMM/attention TFLOP/s & reduction HBM GB/s vs B200 peak at 1/2/4/8 GPUs"
+L2_BYTES = 126 * 2 ** 20
+
+# workload -> (synthesised problem, unit, kernel family)
+WORKLOADS = {
+    "gemm_8192": ("gemm_8192", "TFLOP/s", "gemm"),
+    "gemm_4096x14336x4096": ("gemm_4096x14336x4096", "TFLOP/s", "gemm"),
+    "gemm_2048": ("gemm_2048", "TFLOP/s", "gemm"),
+    "gemm_512": ("gemm_512", "TFLOP/s", "gemm"),
+    "attention": ("attention", "TFLOP/s", "attention"),
+    "rmsnorm": ("rmsnorm", "GB/s", "row"),
+    "softmax": ("softmax", "GB/s", "row"),
+    "sum": ("sum", "GB/s", "sum"),
+}
+
+
+# ---------------------------------------------------------------------------
+# distributed plumbing
+
+
+class Dist:
+    def __init__(self):
+        self.rank = int(os.environ.get("RANK", 0))
+        self.world = int(os.environ.get("WORLD_SIZE", 1))
+        self.local = int(os.environ.get("LOCAL_RANK", 0))
+        self.pg = None
+        if self.world > 1:
+            import torch.distributed as td
+            td.init_process_group("gloo", timeout=timedelta(seconds=180))
+            self.pg = td
+
+    def barrier(self):
+        if self.pg:
+            self.pg.barrier()
+
+    def max(self, x: float) -> float:
+        if not self.pg:
+            return x
+        import torch
+        t = torch.tensor([x], dtype=torch.float64)
+        self.pg.all_reduce(t, op=self.pg.ReduceOp.MAX)
+        return float(t.item())
+
+    def broadcast_bytes(self, b: bytes | None) -> bytes:
+        if not self.pg:
+            return b
+        obj = [b]
+        self.pg.broadcast_object_list(obj, src=0)
+        return obj[0]
+
+    def close(self):
+        if self.pg:
+            self.pg.destroy_process_group()
+
+
+# ---------------------------------------------------------------------------
+# clocks (read-only NVML sampling during the timed region)
+
+
+class ClockSampler:
+    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown",
+               0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown"}
+
+    def __init__(self, device: int):
+        self.samples, self.reasons, self.max_mhz = [], set(), None
+        self._stop = threading.Event()
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(device)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+        except Exception:
+            self.nv = None
+
+    def _run(self):
+        nv = self.nv
+        while not self._stop.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM))
+                bits = nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                for b, n in self.REASONS.items():
+                    if bits & b:
+                        self.reasons.add(n)
+            except Exception:
+                pass
+            time.sleep(0.01)
+
+    def __enter__(self):
+        if self.nv:
+            self.t = threading.Thread(target=self._run, daemon=True)
+            self.t.start()
+        return self
+
+    def __exit__(self, *a):
+        self._stop.set()
+        if self.nv:
+            self.t.join()
+
+    def summary(self) -> dict:
+        s = sorted(self.samples)
+        return {"sm_mhz": float(np.median(s)) if s else None, "sm_max_mhz": self.max_mhz,
+                "samples": len(s), "reasons": sorted(self.reasons)}
+
+
+# ---------------------------------------------------------------------------
+# workload construction
+
+
+def problem(name: str):
+    from compiler.synth import baseline_dir
+    d = baseline_dir(name)
+    meta = json.loads((d / "meta.json").read_text())
+    return d, meta
+
+
+def host_inputs(name: str, meta: dict, rank: int) -> dict:
+    """Seeded synthetic inputs with BASELINE.json's distributions (rank-distinct
+    panels under multi-GPU runs)."""
+    from emmyrt.runner import f32_to_bf16_bits, NP_DTYPE
+    k = meta["kernels"][0]
+    rng = np.random.default_rng(1000 * rank + 7)
+    out = {}
+    for a in k["args"]:
+        shape = tuple(a["shape"]) or (1,)
+        if a.get("output"):
+            out[a["name"]] = np.zeros(shape, dtype=NP_DTYPE[a["dtype"]])
+            continue
+        if "data" in a:
+            out[a["name"]] = np.asarray(a["data"], dtype=NP_DTYPE[a["dtype"]])
+            continue
+        if name.startswith("gemm"):
+            v = rng.standard_normal(shape, dtype=np.float32) * np.float32(0.05)
+        elif name == "sum":
+            v = rng.random(shape, dtype=np.float32) * np.float32(2) - np.float32(1)
+        elif name == "softmax":
+            v = rng.standard_normal(shape, dtype=np.float32) * np.float32(np.sqrt(2.0))
+        elif name == "rmsnorm" and len(shape) == 1:
+            v = rng.random(shape, dtype=np.float32) + np.float32(0.5)
+        else:
+            v = rng.standard_normal(shape, dtype=np.float32)
+        out[a["name"]] = f32_to_bf16_bits(v) if a["dtype"] == "bf16" else v.astype(NP_DTYPE[a["dtype"]])
+    return out
+
+
+def work_units(name: str, ck, meta: dict) -> float:
+    """Algorithmic work of one launch: flops for tensor-core kernels, bytes read once
+    + written once for streaming kernels."""
+    L = ck.launch
+    if "flops" in L:
+        return float(L["flops"])
+    k = meta["kernels"][0]
+    nbytes = 0
+    for a in k["args"]:
+        n = int(np.prod(a["shape"] or [1]))
+        if n > 1:
+            nbytes += n * {"f32": 4, "bf16": 2, "f16": 2}[a["dtype"]]
+    return float(nbytes)
+
+
+def traffic_from_profile(workload: str):
+    """DRAM bytes per launch from the committed ncu summary, if one exists."""
+    p = ROOT / "profiles" / f"{workload}.md"
+    if not p.exists():
+        return None
+    for line in p.read_text().splitlines():
+        if line.strip().startswith("dram_bytes_per_launch:"):
+            return float(line.split(":", 1)[1].strip().split()[0])
+    return None
+
+
+def measured_peaks() -> tuple[dict, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        return json.loads(p.read_text()), "measured"
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
+
+
+# ---------------------------------------------------------------------------
+# CPU side: the oracle port (reference arm and cpu_baseline)
+
+
+def cpu_sample_fn(name: str, inputs: dict, meta: dict, target_s: float = 2.0):
+    """(fn, units, description) for one bounded CPU sample of the workload, computed
+    by the oracle; GEMM samples are sized to take about ``target_s`` seconds."""
+    from oracle import refs
+    from emmyrt.runner import bf16_bits_to_f32
+    if name.startswith("gemm"):
+        A = bf16_bits_to_f32(inputs["x0"])
+        B = bf16_bits_to_f32(inputs["x1"])
+        rows = max(1, min(A.shape[0], 256))
+        t0 = time.perf_counter()
+        refs.mm_bf16(A[:rows], B)
+        dt = time.perf_counter() - t0
+        rows = int(max(1, min(A.shape[0], rows * max(1.0, target_s / max(dt, 1e-3)))))
+        sub = A[:rows]
+        return (lambda: refs.mm_bf16(sub, B)), 2.0 * rows * B.shape[0] * B.shape[1], \
+            f"{rows} rows of A against the full B (oracle mm_bf16, f64 BLAS)"
+    if name == "rmsnorm":
+        x, w = inputs["x0"], inputs["x1"]
+        return (lambda: refs.rmsnorm(x, w, 1e-6)), float(2 * x.nbytes + w.nbytes), "full 4096x4096"
+    if name == "softmax":
+        x = inputs["x"][:4096]
+        return (lambda: refs.softmax(x)), float(2 * x.nbytes), "4096 of the 65536 rows"
+    if name == "sum":
+        x = inputs["x"][: 1 << 28]
+        return (lambda: refs.total_sum(x)), float(x.nbytes), "first 2^28 of the 2^31 elements"
+    raise KeyError(name)
+
+
+def time_cpu(fn, reps: int) -> float:
+    best = float("inf")
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        fn()
+        best = min(best, time.perf_counter() - t0)
+    return best
+
+
+def to_rate(units: float, seconds: float, unit: str) -> float:
+    return units / seconds / (1e12 if unit == "TFLOP/s" else 1e9)
+
+
+# ---------------------------------------------------------------------------
+
+
+def run_reference(args, dist: Dist) -> int:
+    name = args.workload
+    _, unit, _ = WORKLOADS[name]
+    if dist.rank != 0:
+        return 0
+    pname = WORKLOADS[name][0]
+    _, meta = problem(pname)
+    inputs = host_inputs(pname, meta, 0)
+    # each step a bounded sample, so the whole run stays within a couple of minutes
+    fn, units, sample = cpu_sample_fn(pname, inputs, meta,
+                                      target_s=min(1.0, 90.0 / (args.steps + args.warmup)))
+    for _ in range(args.warmup):
+        fn()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        fn()
+    dt = (time.perf_counter() - t0) / args.steps
+    v = to_rate(units, dt, unit)
+    line = {"metric": METRIC, "impl": "reference", "value": round(v, 3), "unit": unit,
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(dt * 1e3, 3), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f64", "data": "synthetic",
+            "config": {"workload": name, "sample": sample},
+            "cpu_baseline": {"value": round(v, 3), "unit": unit, "cores": os.cpu_count(),
+                             "kind": "port", "sample": sample},
+            "e2e": {"value": round(v, 3), "unit": unit, "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_ours(args, dist: Dist) -> int:
+    import emmyrt
+    from emmyrt import DeviceBuffer, Event, HostBuffer, check, lib
+    from emmyrt.runner import CompiledKernel, NP_DTYPE
+    name = args.workload
+    pname, unit, family = WORKLOADS[name]
+    emmyrt.init(dist.local)
+    d, meta = problem(pname)
+    k = meta["kernels"][0]
+    ck = CompiledKernel.from_ir(d / f"{k['entry']}.ir.json")
+    inputs = host_inputs(pname, meta, dist.rank)
+    in_names = [a["name"] for a in k["args"] if not a.get("output") and "data" not in a]
+    out_names = [a["name"] for a in k["args"] if a.get("output")]
+    in_bytes = sum(inputs[n].nbytes for n in in_names)
+    # inputs larger than L2 (or rotated over enough copies to exceed it)
+    copies = 1 if in_bytes > L2_BYTES else -(-2 * L2_BYTES // max(1, in_bytes))
+    bufsets = []
+    for c in range(copies):
+        bufs = {}
+        for a in k["args"]:
+            h = inputs[a["name"]]
+            b = DeviceBuffer(h.nbytes)
+            b.upload(h)
+            bufs[a["name"]] = b
+        bufsets.append(bufs)
+    params = [ck.params({n: b.ptr for n, b in bs.items()}) for bs in bufsets]
+    stream = 0
+
+    def step(i):
+        ck(None, stream, params[i % copies])
+
+    # warm-up, including one checked launch
+    for i in range(max(1, args.warmup)):
+        step(i)
+    emmyrt.stream_wait(stream, 120)
+    if ck.status():
+        raise RuntimeError(f"kernel status {ck.status()}")
+    dist.barrier()
+    emmyrt.synchronize()
+    ev = [Event() for _ in range(args.steps + 1)]
+    with ClockSampler(dist.local) as clocks:
+        ev[0].record(stream)
+        for i in range(args.steps):
+            step(i)
+            ev[i + 1].record(stream)
+        ev[-1].synchronize()
+    emmyrt.synchronize()
+    dist.barrier()
+    total_ms = ev[0].elapsed_ms(ev[-1])
+    per_launch = [ev[i].elapsed_ms(ev[i + 1]) for i in range(args.steps)]
+    total_ms = dist.max(total_ms)
+    ms_step = total_ms / args.steps
+    units = work_units(pname, ck, meta)
+    value = to_rate(units * dist.world, ms_step / 1e3, unit)
+
+    # end to end through the C-ABI runtime: pinned host inputs -> HBM -> kernel -> host result
+    host_in = {}
+    for n in in_names:
+        hb = HostBuffer(inputs[n].nbytes)
+        hb.array(inputs[n].dtype, inputs[n].shape)[...] = inputs[n]
+        host_in[n] = hb
+    host_out = {n: HostBuffer(inputs[n].nbytes) for n in out_names}
+    bufs = bufsets[0]
+    e2e_steps = max(1, min(args.steps, 20))
+
+    def e2e_step():
+        for n in in_names:
+            check(lib.emmy_rt_memcpy_htod(bufs[n].ptr, host_in[n].ptr, inputs[n].nbytes, stream), "htod")
+        ck(None, stream, params[0])
+        for n in out_names:
+            check(lib.emmy_rt_memcpy_dtoh(host_out[n].ptr, bufs[n].ptr, inputs[n].nbytes, stream), "dtoh")
+    e2e_step()
+    emmyrt.stream_wait(stream, 120)
+    dist.barrier()
+    emmyrt.synchronize()
+    e0, e1 = Event(), Event()
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    e1.record(stream)
+    e1.synchronize()
+    e2e_ms = dist.max(e0.elapsed_ms(e1) / e2e_steps)
+    e2e_value = to_rate(units * dist.world, e2e_ms / 1e3, unit)
+
+    # roofline of the kernel (average launch duration, measured live above)
+    peaks, peak_kind = measured_peaks()
+    avg_launch_s = float(np.mean(per_launch)) / 1e3
+    achieved = to_rate(units, avg_launch_s, unit)
+    if unit == "TFLOP/s":
+        bound, peak = "tensor", float(peaks["bf16_tflops"])
+    else:
+        bound, peak = "hbm", float(peaks["hbm_gbs"])
+    roofline = {"bound": bound, "achieved": round(achieved, 2), "peak": peak,
+                "peak_kind": f"{peak_kind} ({'bf16_tflops burst' if bound == 'tensor' else 'hbm_gbs'})",
+                "unit": unit, "frac": round(achieved / peak, 4), "traffic": traffic_from_profile(name)}
+
+    cpu = None
+    if dist.rank == 0 and dist.world == 1 and not args.no_cpu:
+        fn, cunits, sample = cpu_sample_fn(pname, inputs, meta)
+        cdt = time_cpu(fn, 2)
+        cpu = {"value": round(to_rate(cunits, cdt, unit), 4), "unit": unit, "cores": os.cpu_count(),
+               "kind": "port", "sample": sample}
+
+    if dist.rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": unit, "n_gpus": dist.world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": {"gemm": "bf16", "attention": "bf16"}.get(family, "f32"), "data": "synthetic",
+            "config": {"workload": name, "kernel": k["entry"], "grid": ck.launch["grid"],
+                       "block": ck.launch["block"], "smem": ck.launch["smem"],
+                       "l2": ("inputs larger than L2" if copies == 1 else
+                              f"inputs rotated over {copies} copies ({copies * in_bytes >> 20} MiB)"),
+                       "parallelism": f"{dist.world} GPU(s), one panel per rank, no collective"
+                       if family != "sum" else f"{dist.world} GPU(s)"},
+            "e2e": {"value": round(e2e_value, 3), "unit": unit, "h2d_bytes_per_step": int(in_bytes),
+                    "d2h_bytes_per_step": int(sum(inputs[n].nbytes for n in out_names))},
+            "roofline": roofline,
+            "cpu_baseline": cpu,
+            "clocks": clocks.summary(),
+            "gpu_launches": args.steps,
+        }
+        print(json.dumps(line), flush=True)
+    for bs in bufsets:
+        for b in bs.values():
+            b.free()
+    return 0
+
+
+def main(argv=None) -> int:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="gemm_8192")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    args = ap.parse_args(argv)
+    args.warmup = max(3, args.warmup)
+    dist = Dist()
+    try:
+        if args.impl == "reference":
+            return run_reference(args, dist)
+        return run_ours(args, dist)
+    finally:
+        dist.close()
+
+
+if __name__ == "__main__":
+    sys.exit(main())
