@@ -1,5 +1,697 @@
-"""tcgen05 attention template (in progress)."""
+"""Fused attention O = softmax(Q K^T * scale) V on the tcgen05 tensor cores.
+
+Replaces the reference's register-fragment flash attention (``compiler/mma.py``:
+``MmaSyncPtx`` for S and O, ``FragmentApply`` scale/exp/rescale, ``FragmentRowReduce``
+row max / sum by 2-step shuffles, ``FragmentRepack`` P -> A fragment; K and V read
+straight from global memory, ``tests/problems/x_h_attn_128``, ``x_h_sdpa``).
+
+Kernel structure (one CTA per 2 x 128 query rows of one batch x head):
+
+* warp 0, lane 0 -- TMA: Q tiles once, then K_j and V_j (128 keys each) through a
+  3-slot ring of 128-byte-swizzled shared memory, full/empty mbarrier per slot;
+* warp 1 -- TMEM allocation (S0, S1: 128 f32 columns each; O0, O1: D columns each)
+  and, on lane 0, the MMA stream: ``S_t = Q_t K_j^T`` (kind::f16, M=128, N=128),
+  then per tile ``O_t += P_t V_j`` as soon as softmax warpgroup t hands P_t over,
+  immediately followed by ``S_t = Q_t K_{j+1}^T`` -- so one warpgroup's softmax
+  overlaps the other's matrix products;
+* warps 2-5 / 6-9 -- softmax warpgroup per query tile, one thread per query row:
+  pass A reads the S row from TMEM (``tcgen05.ld.32x32b.x32``) for its maximum,
+  pass B reads it again and forms ``p = 2^(s*scale*log2e - m)`` (one FFMA and one
+  ``ex2.approx``), accumulates the row sum in f32, packs P to bf16/f16 and stores it
+  into the 128B-swizzled K-major layout the PV MMA reads as its A operand;
+  the running max is updated lazily -- O (in TMEM) is rescaled only when the max
+  grows by more than 2^8, so most blocks skip the correction; the final
+  normalisation by 1/l makes the result exact either way;
+* epilogue (same warps): O row from TMEM, times 1/l, to bf16/f16, 128-bit stores.
+
+The online-softmax state (m, l) is f32.  Every mbarrier wait is bounded.
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+from ..ptx import Ptx, entry, f32_hex, module
+from .common import arg_params, load_pointer, param_symbol
+from .tc import Waits, instr_desc, smem_desc_hi, smem_desc_lo_const
+
+LOG2E = 1.4426950408889634
+AB_FORMAT = {"f16": 0, "bf16": 1}
+RESCALE_LOG2 = 8.0          # rescale O only when the row max grows by more than 2^8
 
 
-def emit_attention(spec):
-    raise NotImplementedError(f"kernel {spec.name}: tcgen05 attention template not built yet")
+@dataclass
+class AttnConfig:
+    BH: int                  # batch x heads
+    Sq: int
+    Sk: int
+    D: int
+    dtype: str = "bf16"
+    kt_layout: bool = False  # K given pre-transposed as [.., D, Sk]
+    scale: float = 1.0
+    name: str = "k_attention"
+    q_param: str = "q"
+    k_param: str = "k"
+    v_param: str = "v"
+    o_param: str = "o"
+    arg_params: list | None = None
+    buffers: tuple = ()
+    ring: int = 3
+
+    @property
+    def DP(self) -> int:                 # head dim padded to whole 64-element swizzle rows
+        return -(-self.D // 64) * 64
+
+    @property
+    def NQ(self) -> int:
+        return 2 if self.Sq > 128 else 1
+
+
+def emit_attention_module(cfg: AttnConfig) -> str:
+    if cfg.dtype not in AB_FORMAT:
+        raise NotImplementedError(f"attention in {cfg.dtype}")
+    if cfg.scale <= 0:
+        raise NotImplementedError("non-positive softmax scale")
+    if cfg.D % 8 or cfg.D > 128:
+        raise NotImplementedError(f"head dim {cfg.D}")
+    if cfg.kt_layout and cfg.Sk % 8:
+        raise NotImplementedError("pre-transposed K rows not 16-byte aligned")
+    p = Ptx()
+    NQ, DP, R = cfg.NQ, cfg.DP, cfg.ring
+    nblk = -(-cfg.Sk // 128)
+    tile_bytes = 128 * DP * 2             # a Q or K or V tile
+    p_bytes = 128 * 128 * 2
+    q_off, ring_off = 0, NQ * tile_bytes
+    p_off = ring_off + R * tile_bytes
+    smem = p_off + NQ * p_bytes + 1024
+    if smem > 232448 - 512:
+        raise NotImplementedError("attention tiles exceed shared memory")
+    ncols_used = NQ * (128 + DP)
+    ncols = max(32, 1 << math.ceil(math.log2(ncols_used)))
+    fmt = AB_FORMAT[cfg.dtype]
+    idesc_qk = instr_desc(128, 128, fmt, fmt, False, cfg.kt_layout)
+    idesc_pv = instr_desc(128, DP, fmt, fmt, False, True)
+    k_sw_hi = smem_desc_hi(1024)
+    kmaj_lo = smem_desc_lo_const(16)
+    kt_lo = smem_desc_lo_const(DP * 128)        # kt: 64-key blocks of DP d-rows
+    v_lo = smem_desc_lo_const(128 * 128)        # V: 64-d blocks of 128 key-rows
+    scale_log2 = cfg.scale * LOG2E
+    nthreads = 64 + 128 * NQ
+    masked = cfg.Sk % 128 != 0
+
+    p.comment(f"tcgen05 attention BH={cfg.BH} Sq={cfg.Sq} Sk={cfg.Sk} D={cfg.D} {cfg.dtype}, "
+              f"{NQ} query tiles per CTA, {nblk} key blocks, scale={cfg.scale}")
+    ptr = {n: load_pointer(p, n) for n in cfg.buffers}
+    status = p.reg("b64")
+    p.emit(f"ld.param.u64 {status}, [param__status]\ncvta.to.global.u64 {status}, {status}")
+    tq, tk, tv = p.reg("b64"), p.reg("b64"), p.reg("b64")
+    for r, n in ((tq, "q"), (tk, "k"), (tv, "v")):
+        p.emit(f"mov.u64 {r}, param__tmap_{n}\ncvta.param.u64 {r}, {r}")
+    tid, warp, lane = p.regs("u32", 3)
+    p.emit(f"mov.u32 {tid}, %tid.x\nshr.u32 {warp}, {tid}, 5\nand.b32 {lane}, {tid}, 31")
+    base, bars, abort, tslot = p.regs("u32", 4)
+    p.emit(f"""
+        mov.u32 {base}, dsmem
+        add.u32 {base}, {base}, 1023
+        and.b32 {base}, {base}, -1024
+        mov.u32 {bars}, gbars
+        mov.u32 {abort}, gabort
+        mov.u32 {tslot}, gtmem
+    """)
+    # barrier offsets
+    B_Q = 0
+    B_KVF = 8
+    B_KVE = B_KVF + 8 * R
+    B_S = B_KVE + 8 * R
+    B_P = B_S + 8 * NQ
+    B_O = B_P + 8 * NQ
+    nbar = 1 + 2 * R + 3 * NQ
+    p0 = p.reg("pred")
+    l_init = p.label("init_done")
+    p.emit(f"setp.ne.u32 {p0}, {tid}, 0\n@{p0} bra {l_init}")
+    p.emit(f"mbarrier.init.shared::cta.b64 [{bars}+{B_Q}], 1")
+    for s in range(R):
+        p.emit(f"mbarrier.init.shared::cta.b64 [{bars}+{B_KVF + 8 * s}], 1")
+        p.emit(f"mbarrier.init.shared::cta.b64 [{bars}+{B_KVE + 8 * s}], 1")
+    for t in range(NQ):
+        p.emit(f"mbarrier.init.shared::cta.b64 [{bars}+{B_S + 8 * t}], 1")
+        p.emit(f"mbarrier.init.shared::cta.b64 [{bars}+{B_P + 8 * t}], 128")
+        p.emit(f"mbarrier.init.shared::cta.b64 [{bars}+{B_O + 8 * t}], 1")
+    p.emit(f"st.shared.u32 [{abort}], 0\nfence.mbarrier_init.release.cluster\nfence.proxy.async.shared::cta")
+    p.place(l_init)
+    p1 = p.reg("pred")
+    l_alloc = p.label("alloc_done")
+    p.emit(f"setp.ne.u32 {p1}, {warp}, 1\n@{p1} bra {l_alloc}")
+    p.emit(f"tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [{tslot}], {ncols}\n"
+           f"tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned")
+    p.place(l_alloc)
+    tbase = p.reg("u32")
+    p.emit(f"""
+        tcgen05.fence::before_thread_sync
+        barrier.sync 0
+        tcgen05.fence::after_thread_sync
+        ld.shared.u32 {tbase}, [{tslot}]
+    """)
+    waits = Waits(p, status, abort)
+    finish = p.label("finish")
+    ptrue, pfalse, zr = p.reg("pred"), p.reg("pred"), p.reg("u32")
+    p.emit(f"mov.u32 {zr}, 0\nsetp.eq.u32 {ptrue}, {zr}, 0\nsetp.ne.u32 {pfalse}, {zr}, 0")
+    bh, q0 = p.reg("u32"), p.reg("u32")
+    p.emit(f"mov.u32 {bh}, %ctaid.y\nmov.u32 {q0}, %ctaid.x\nmul.lo.u32 {q0}, {q0}, {128 * NQ}")
+
+    def ring_advance(slot, ph):
+        ps = p.reg("pred")
+        p.emit(f"add.u32 {slot}, {slot}, 1\nsetp.eq.u32 {ps}, {slot}, {R}\n"
+               f"@{ps} mov.u32 {slot}, 0\n@{ps} xor.b32 {ph}, {ph}, 1")
+
+    # ------------------------------------------------------------------ producer
+    l_mma, l_soft = p.label("role_mma"), p.label("role_softmax")
+    pr, pl = p.reg("pred"), p.reg("pred")
+    p.emit(f"setp.ne.u32 {pr}, {warp}, 0\n@{pr} bra {l_mma}\nsetp.ne.u32 {pl}, {lane}, 0\n@{pl} bra {finish}")
+    p.emit(f"prefetch.tensormap [{tq}]\nprefetch.tensormap [{tk}]\nprefetch.tensormap [{tv}]")
+    qb = p.reg("u32")
+    p.emit(f"add.u32 {qb}, {bars}, {B_Q}\nmbarrier.arrive.expect_tx.shared::cta.b64 _, [{qb}], {NQ * tile_bytes}")
+    for t in range(NQ):
+        for db in range(DP // 64):
+            dst, y = p.reg("u32"), p.reg("u32")
+            p.emit(f"add.u32 {dst}, {base}, {q_off + t * tile_bytes + db * 16384}\nadd.u32 {y}, {q0}, {t * 128}")
+            p.emit(f"cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
+                   f"[{dst}], [{tq}, {{{db * 64}, {y}, {bh}}}], [{qb}]")
+    slot, ph, j = p.reg("u32"), p.reg("u32"), p.reg("u32")
+    p.emit(f"mov.u32 {slot}, 0\nmov.u32 {ph}, 0\nmov.u32 {j}, 0")
+    l_pk = p.label("p_kv")
+    p.place(l_pk)
+    key0 = p.reg("u32")
+    p.emit(f"mul.lo.u32 {key0}, {j}, 128")
+    for which in ("k", "v"):
+        ea, fa, par, dst0 = p.regs("u32", 4)
+        p.emit(f"""
+            mad.lo.u32 {ea}, {slot}, 8, {bars}
+            add.u32 {fa}, {ea}, {B_KVF}
+            add.u32 {ea}, {ea}, {B_KVE}
+            xor.b32 {par}, {ph}, 1
+        """)
+        waits.wait(ea, par, "producer", finish)
+        p.emit(f"mbarrier.arrive.expect_tx.shared::cta.b64 _, [{fa}], {tile_bytes}\n"
+               f"mad.lo.u32 {dst0}, {slot}, {tile_bytes}, {base}\nadd.u32 {dst0}, {dst0}, {ring_off}")
+        if which == "k" and cfg.kt_layout:
+            for kb in range(2):
+                dst, x = p.reg("u32"), p.reg("u32")
+                p.emit(f"add.u32 {dst}, {dst0}, {kb * DP * 128}\nadd.u32 {x}, {key0}, {kb * 64}")
+                p.emit(f"cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
+                       f"[{dst}], [{tk}, {{{x}, 0, {bh}}}], [{fa}]")
+        else:
+            tm = tk if which == "k" else tv
+            for db in range(DP // 64):
+                dst = p.reg("u32")
+                p.emit(f"add.u32 {dst}, {dst0}, {db * 16384}")
+                p.emit(f"cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
+                       f"[{dst}], [{tm}, {{{db * 64}, {key0}, {bh}}}], [{fa}]")
+        ring_advance(slot, ph)
+    pj = p.reg("pred")
+    p.emit(f"add.u32 {j}, {j}, 1\nsetp.lt.u32 {pj}, {j}, {nblk}\n@{pj} bra {l_pk}\nbra {finish}")
+
+    # ----------------------------------------------------------------------- MMA
+    p.place(l_mma)
+    p.emit(f"setp.ne.u32 {pr}, {warp}, 1\n@{pr} bra {l_soft}\nsetp.ne.u32 {pl}, {lane}, 0\n@{pl} bra {finish}")
+    zero = p.reg("u32")
+    p.emit(f"mov.u32 {zero}, 0")
+    waits.wait(_addr(p, bars, B_Q), zero, "mma", finish)
+    p.emit("tcgen05.fence::after_thread_sync")
+    cslot, cph = p.reg("u32"), p.reg("u32")
+    p.emit(f"mov.u32 {cslot}, 0\nmov.u32 {cph}, 0")
+
+    def wait_slot(sl, ph_):
+        fa = p.reg("u32")
+        p.emit(f"mad.lo.u32 {fa}, {sl}, 8, {bars}\nadd.u32 {fa}, {fa}, {B_KVF}")
+        waits.wait(fa, ph_, "mma", finish)
+        p.emit("tcgen05.fence::after_thread_sync")
+
+    def release_slot(sl):
+        ea = p.reg("u32")
+        p.emit(f"mad.lo.u32 {ea}, {sl}, 8, {bars}\nadd.u32 {ea}, {ea}, {B_KVE}")
+        p.emit(f"tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [{ea}]")
+
+    def desc(addr_reg, lo_const, hi_const):
+        lo, d = p.reg("u32"), p.reg("b64")
+        p.emit(f"shr.u32 {lo}, {addr_reg}, 4\nor.b32 {lo}, {lo}, {lo_const}\nmov.b64 {d}, {{{lo}, {hi_const}}}")
+        return d
+
+    def issue_qk(t, sl):
+        """S_t = Q_t K^T over the DP head-dim (K steps of 16)."""
+        kbase, qa, ka = p.reg("u32"), p.reg("u32"), p.reg("u32")
+        p.emit(f"mad.lo.u32 {kbase}, {sl}, {tile_bytes}, {base}\nadd.u32 {kbase}, {kbase}, {ring_off}")
+        st = p.reg("u32")
+        p.emit(f"add.u32 {st}, {tbase}, {t * 128}")
+        for kk in range(DP // 16):
+            p.emit(f"add.u32 {qa}, {base}, {q_off + t * tile_bytes + (kk // 4) * 16384 + (kk % 4) * 32}")
+            if cfg.kt_layout:
+                p.emit(f"add.u32 {ka}, {kbase}, {kk * 2048}")
+                kd = desc(ka, kt_lo, k_sw_hi)
+            else:
+                p.emit(f"add.u32 {ka}, {kbase}, {(kk // 4) * 16384 + (kk % 4) * 32}")
+                kd = desc(ka, kmaj_lo, k_sw_hi)
+            qd = desc(qa, kmaj_lo, k_sw_hi)
+            pe = pfalse if kk == 0 else ptrue
+            p.emit(f"tcgen05.mma.cta_group::1.kind::f16 [{st}], {qd}, {kd}, {idesc_qk}, {pe}")
+        sb = p.reg("u32")
+        p.emit(f"add.u32 {sb}, {bars}, {B_S + 8 * t}\n"
+               f"tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [{sb}]")
+
+    def issue_pv(t, sl, first_block_pred):
+        """O_t (+)= P_t V over the 128 keys of the block."""
+        vbase, pa, va = p.reg("u32"), p.reg("u32"), p.reg("u32")
+        p.emit(f"mad.lo.u32 {vbase}, {sl}, {tile_bytes}, {base}\nadd.u32 {vbase}, {vbase}, {ring_off}")
+        ot = p.reg("u32")
+        p.emit(f"add.u32 {ot}, {tbase}, {NQ * 128 + t * DP}")
+        for kk in range(128 // 16):
+            p.emit(f"add.u32 {pa}, {base}, {p_off + t * p_bytes + (kk // 4) * 16384 + (kk % 4) * 32}")
+            p.emit(f"add.u32 {va}, {vbase}, {kk * 2048}")
+            pd = desc(pa, kmaj_lo, k_sw_hi)
+            vd = desc(va, v_lo, k_sw_hi)
+            if kk == 0:
+                pe = p.reg("pred")
+                p.emit(f"not.pred {pe}, {first_block_pred}")
+            else:
+                pe = ptrue
+            p.emit(f"tcgen05.mma.cta_group::1.kind::f16 [{ot}], {pd}, {vd}, {idesc_pv}, {pe}")
+        ob = p.reg("u32")
+        p.emit(f"add.u32 {ob}, {bars}, {B_O + 8 * t}\n"
+               f"tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [{ob}]")
+
+    # prologue: S_t(0)
+    kslot, kph = p.reg("u32"), p.reg("u32")
+    p.emit(f"mov.u32 {kslot}, {cslot}\nmov.u32 {kph}, {cph}")
+    wait_slot(kslot, kph)
+    for t in range(NQ):
+        issue_qk(t, kslot)
+    release_slot(kslot)
+    ring_advance(cslot, cph)
+    jm = p.reg("u32")
+    p.emit(f"mov.u32 {jm}, 0")
+    l_mj = p.label("m_blk")
+    p.place(l_mj)
+    vslot, vph = p.reg("u32"), p.reg("u32")
+    p.emit(f"mov.u32 {vslot}, {cslot}\nmov.u32 {vph}, {cph}")
+    ring_advance(cslot, cph)
+    wait_slot(vslot, vph)
+    pfirst, pmore, pph = p.reg("pred"), p.reg("pred"), p.reg("u32")
+    nxt = p.reg("u32")
+    p.emit(f"setp.eq.u32 {pfirst}, {jm}, 0\nadd.u32 {nxt}, {jm}, 1\nsetp.lt.u32 {pmore}, {nxt}, {nblk}\n"
+           f"and.b32 {pph}, {jm}, 1")
+    p.emit(f"mov.u32 {kslot}, {cslot}\nmov.u32 {kph}, {cph}")
+    for t in range(NQ):
+        pb = p.reg("u32")
+        p.emit(f"add.u32 {pb}, {bars}, {B_P + 8 * t}")
+        waits.wait(pb, pph, "mma", finish)
+        p.emit("tcgen05.fence::after_thread_sync")
+        issue_pv(t, vslot, pfirst)
+        skip = p.label("m_noqk")
+        p.emit(f"@!{pmore} bra {skip}")
+        if t == 0:
+            wait_slot(kslot, kph)
+        issue_qk(t, kslot)
+        p.place(skip)
+    release_slot(vslot)
+    l_norel = p.label("m_norel")
+    p.emit(f"@!{pmore} bra {l_norel}")
+    release_slot(kslot)
+    ring_advance(cslot, cph)
+    p.place(l_norel)
+    p.emit(f"mov.u32 {jm}, {nxt}\n@{pmore} bra {l_mj}\nbra {finish}")
+
+    # ------------------------------------------------------------------ softmax
+    p.place(l_soft)
+    _emit_softmax(p, cfg, ptr, bars, B_S, B_P, B_O, tbase, base, p_off, p_bytes, warp, lane, tid,
+                  q0, bh, nblk, scale_log2, masked, waits, finish)
+
+    # ------------------------------------------------------------------- finish
+    p.place(finish)
+    pw1 = p.reg("pred")
+    done = p.label("done")
+    p.emit(f"""
+        tcgen05.fence::before_thread_sync
+        barrier.sync 0
+        tcgen05.fence::after_thread_sync
+        setp.ne.u32 {pw1}, {warp}, 1
+        @{pw1} bra {done}
+        bar.warp.sync -1
+        tcgen05.dealloc.cta_group::1.sync.aligned.b32 {tbase}, {ncols}
+    """)
+    p.place(done)
+    p.emit("ret")
+
+    params = list(cfg.arg_params or [f".param .u64 {param_symbol(n)}" for n in cfg.buffers])
+    params += [".param .align 64 .b8 param__tmap_q[128]", ".param .align 64 .b8 param__tmap_k[128]",
+               ".param .align 64 .b8 param__tmap_v[128]", ".param .u64 param__status"]
+    text = entry(cfg.name, params, p, maxntid=nthreads)
+    statics = (f"\t.shared .align 8 .b64 gbars[{nbar}];\n\t.shared .align 4 .u32 gabort;\n"
+               f"\t.shared .align 4 .u32 gtmem;\n")
+    text = text.replace("{\n", "{\n" + statics, 1)
+    eb = 2
+    kmap = ({"dims": [cfg.Sk, cfg.D, cfg.BH], "strides": [cfg.Sk * eb, cfg.D * cfg.Sk * eb],
+             "box": [64, DP, 1]} if cfg.kt_layout else
+            {"dims": [cfg.D, cfg.Sk, cfg.BH], "strides": [cfg.D * eb, cfg.Sk * cfg.D * eb],
+             "box": [64, 128, 1]})
+    launch = {
+        "kind": "attention", "grid": [-(-cfg.Sq // (128 * NQ)), cfg.BH, 1], "block": [nthreads, 1, 1],
+        "cluster": [1, 1, 1], "smem": smem, "flops": 4 * cfg.BH * cfg.Sq * cfg.Sk * cfg.D,
+        "exps": cfg.BH * cfg.Sq * cfg.Sk,
+        "extra_params": [
+            {"kind": "tmap", "buffer": cfg.q_param, "dtype": cfg.dtype, "dims": [cfg.D, cfg.Sq, cfg.BH],
+             "strides": [cfg.D * eb, cfg.Sq * cfg.D * eb], "box": [64, 128, 1], "swizzle": 128},
+            {"kind": "tmap", "buffer": cfg.k_param, "dtype": cfg.dtype, "swizzle": 128, **kmap},
+            {"kind": "tmap", "buffer": cfg.v_param, "dtype": cfg.dtype, "dims": [cfg.D, cfg.Sk, cfg.BH],
+             "strides": [cfg.D * eb, cfg.Sk * cfg.D * eb], "box": [64, 128, 1], "swizzle": 128},
+            {"kind": "status"},
+        ],
+    }
+    return module([text], launch, globals_=[".extern .shared .align 1024 .b8 dsmem[];"])
+
+
+def _addr(p: Ptx, base: str, off: int) -> str:
+    r = p.reg("u32")
+    p.emit(f"add.u32 {r}, {base}, {off}")
+    return r
+
+
+def _emit_softmax(p: Ptx, cfg: AttnConfig, ptr, bars, B_S, B_P, B_O, tbase, base, p_off, p_bytes,
+                  warp, lane, tid, q0, bh, nblk, scale_log2, masked, waits: Waits, finish):
+    NQ, DP = cfg.NQ, cfg.DP
+    t, q, row, lanebits = p.regs("u32", 4)
+    # warps 2..5 -> tile 0, 6..9 -> tile 1; TMEM lane quarter = warp % 4
+    p.emit(f"""
+        sub.u32 {t}, {warp}, 2
+        shr.u32 {t}, {t}, 2
+        and.b32 {q}, {warp}, 3
+        mad.lo.u32 {row}, {q}, 32, {lane}
+        shl.b32 {lanebits}, {q}, 21
+    """)
+    s_ta, o_ta = p.reg("u32"), p.reg("u32")
+    p.emit(f"""
+        mad.lo.u32 {s_ta}, {t}, 128, {tbase}
+        add.u32 {s_ta}, {s_ta}, {lanebits}
+        mad.lo.u32 {o_ta}, {t}, {DP}, {tbase}
+        add.u32 {o_ta}, {o_ta}, {NQ * 128}
+        add.u32 {o_ta}, {o_ta}, {lanebits}
+    """)
+    sbar, pbar, obar = p.regs("u32", 3)
+    p.emit(f"""
+        mad.lo.u32 {sbar}, {t}, 8, {bars}
+        add.u32 {pbar}, {sbar}, {B_P}
+        add.u32 {obar}, {sbar}, {B_O}
+        add.u32 {sbar}, {sbar}, {B_S}
+    """)
+    # this thread's P row in smem: tile t, row r; 16-byte chunk c of a 64-key block
+    # lives at chunk (c ^ (r % 8)) of the row (128-byte swizzle)
+    prow, rx = p.reg("u32"), p.reg("u32")
+    p.emit(f"""
+        mad.lo.u32 {prow}, {t}, {p_bytes}, {base}
+        add.u32 {prow}, {prow}, {p_off}
+        mad.lo.u32 {prow}, {row}, 128, {prow}
+        and.b32 {rx}, {row}, 7
+    """)
+    chunk_addr = {}
+    for c16 in range(16):            # 16 chunks of 8 keys = 128 keys
+        blk, c = c16 // 8, c16 % 8
+        a = p.reg("u32")
+        p.emit(f"xor.b32 {a}, {rx}, {c}\nmad.lo.u32 {a}, {a}, 16, {prow}\nadd.u32 {a}, {a}, {blk * 16384}")
+        chunk_addr[c16] = a
+    m, l = p.reg("f32"), p.reg("f32")
+    p.emit(f"mov.f32 {m}, 0fF149F2CA\nmov.f32 {l}, 0f00000000")     # m = -1e30 (log2 domain)
+    jj = p.reg("u32")
+    p.emit(f"mov.u32 {jj}, 0")
+    l_blk = p.label("s_blk")
+    p.place(l_blk)
+    par = p.reg("u32")
+    p.emit(f"and.b32 {par}, {jj}, 1")
+    waits.wait(sbar, par, "softmax", finish)
+    p.emit("bar.warp.sync -1\ntcgen05.fence::after_thread_sync")
+    vals = [p.reg("b32") for _ in range(32)]
+    fv = [p.reg("f32") for _ in range(32)]
+    keyb = None
+    if masked:
+        keyb = p.reg("u32")
+        p.emit(f"mul.lo.u32 {keyb}, {jj}, 128")
+
+    def load_chunk(c):
+        p.emit(f"tcgen05.ld.sync.aligned.32x32b.x32.b32 {{{', '.join(vals)}}}, [{s_ta}+{c * 32}]")
+        p.emit("tcgen05.wait::ld.sync.aligned")
+        for i in range(32):
+            p.emit(f"mov.b32 {fv[i]}, {vals[i]}")
+        if masked:
+            for i in range(32):
+                pk, kx = p.reg("pred"), p.reg("u32")
+                p.emit(f"add.u32 {kx}, {keyb}, {c * 32 + i}\nsetp.ge.u32 {pk}, {kx}, {cfg.Sk}\n"
+                       f"@{pk} mov.f32 {fv[i]}, 0fFF800000")
+    # pass A: row maximum of the raw scores
+    mx = p.reg("f32")
+    p.emit(f"mov.f32 {mx}, 0fFF800000")
+    for c in range(4):
+        load_chunk(c)
+        red = list(fv)
+        while len(red) > 1:
+            nxt = []
+            for i in range(0, len(red), 2):
+                r = p.reg("f32")
+                p.emit(f"max.f32 {r}, {red[i]}, {red[i + 1]}")
+                nxt.append(r)
+            red = nxt
+        p.emit(f"max.f32 {mx}, {mx}, {red[0]}")
+    mn, alpha, thr = p.reg("f32"), p.reg("f32"), p.reg("f32")
+    prs, pfirst = p.reg("pred"), p.reg("pred")
+    p.emit(f"""
+        mul.rn.f32 {mx}, {mx}, {f32_hex(scale_log2)}
+        max.f32 {mn}, {m}, {mx}
+        setp.eq.u32 {pfirst}, {jj}, 0
+        add.rn.f32 {thr}, {m}, {f32_hex(RESCALE_LOG2)}
+        setp.gt.f32 {prs}, {mn}, {thr}
+        @{pfirst} mov.f32 {m}, {mn}
+        mov.f32 {alpha}, 0f3F800000
+    """)
+    # (first block: m takes the block max; later blocks rescale only past the threshold)
+    d0, pnf = p.reg("f32"), p.reg("pred")
+    p.emit(f"""
+        not.pred {pnf}, {pfirst}
+        and.pred {prs}, {prs}, {pnf}
+        sub.rn.f32 {d0}, {m}, {mn}
+        @{prs} ex2.approx.ftz.f32 {alpha}, {d0}
+        @{prs} mov.f32 {m}, {mn}
+        mul.rn.f32 {l}, {l}, {alpha}
+    """)
+    # P buffer and O are free once the previous block's PV finished
+    l_nowait = p.label("s_nowait")
+    p.emit(f"@{pfirst} bra {l_nowait}")
+    par2 = p.reg("u32")
+    p.emit(f"sub.u32 {par2}, {jj}, 1\nand.b32 {par2}, {par2}, 1")
+    waits.wait(obar, par2, "softmax", finish)
+    p.emit("bar.warp.sync -1\ntcgen05.fence::after_thread_sync")
+    # lazy O correction: the whole warp takes part when any of its rows needs it
+    pany = p.reg("pred")
+    l_nores = p.label("s_nores")
+    p.emit(f"vote.sync.any.pred {pany}, {prs}, -1\n@!{pany} bra {l_nores}")
+    ov = [p.reg("b32") for _ in range(32)]
+    for c in range(DP // 32):
+        p.emit(f"tcgen05.ld.sync.aligned.32x32b.x32.b32 {{{', '.join(ov)}}}, [{o_ta}+{c * 32}]")
+        p.emit("tcgen05.wait::ld.sync.aligned")
+        for i in range(32):
+            f = p.reg("f32")
+            p.emit(f"mov.b32 {f}, {ov[i]}\nmul.rn.f32 {f}, {f}, {alpha}\nmov.b32 {ov[i]}, {f}")
+        p.emit(f"tcgen05.st.sync.aligned.32x32b.x32.b32 [{o_ta}+{c * 32}], {{{', '.join(ov)}}}")
+    p.emit("tcgen05.wait::st.sync.aligned")
+    p.place(l_nores)
+    p.place(l_nowait)
+    # pass B: p = 2^(s*scale*log2e - m), row sum, bf16/f16 pack into the swizzled P tile
+    negm = p.reg("f32")
+    p.emit(f"neg.f32 {negm}, {m}")
+    cvt = "cvt.rn.bf16x2.f32" if cfg.dtype == "bf16" else "cvt.rn.f16x2.f32"
+    for c in range(4):
+        load_chunk(c)
+        ps = []
+        for i in range(32):
+            e = p.reg("f32")
+            p.emit(f"fma.rn.f32 {e}, {fv[i]}, {f32_hex(scale_log2)}, {negm}\nex2.approx.ftz.f32 {e}, {e}")
+            ps.append(e)
+        red = list(ps)
+        while len(red) > 1:
+            nxt = []
+            for i in range(0, len(red), 2):
+                r = p.reg("f32")
+                p.emit(f"add.rn.f32 {r}, {red[i]}, {red[i + 1]}")
+                nxt.append(r)
+            red = nxt
+        p.emit(f"add.rn.f32 {l}, {l}, {red[0]}")
+        packed = [p.reg("b32") for _ in range(16)]
+        for i in range(16):
+            p.emit(f"{cvt} {packed[i]}, {ps[2 * i + 1]}, {ps[2 * i]}")
+        for g in range(4):
+            c16 = c * 4 + g
+            p.emit(f"st.shared.v4.b32 [{chunk_addr[c16]}], {{{', '.join(packed[4 * g:4 * g + 4])}}}")
+    p.emit(f"""
+        fence.proxy.async.shared::cta
+        tcgen05.fence::before_thread_sync
+        mbarrier.arrive.shared::cta.b64 _, [{pbar}]
+        add.u32 {jj}, {jj}, 1
+    """)
+    pj = p.reg("pred")
+    p.emit(f"setp.lt.u32 {pj}, {jj}, {nblk}\n@{pj} bra {l_blk}")
+    # epilogue: O / l
+    parf = p.reg("u32")
+    p.emit(f"mov.u32 {parf}, {(nblk - 1) & 1}")
+    waits.wait(obar, parf, "softmax", finish)
+    p.emit("bar.warp.sync -1\ntcgen05.fence::after_thread_sync")
+    inv = p.reg("f32")
+    p.emit(f"rcp.rn.f32 {inv}, {l}")
+    grow, prow_ok = p.reg("u32"), p.reg("pred")
+    p.emit(f"mad.lo.u32 {grow}, {t}, 128, {q0}\nadd.u32 {grow}, {grow}, {row}\nsetp.lt.u32 {prow_ok}, {grow}, {cfg.Sq}")
+    oadr, w64 = p.reg("b64"), p.reg("b64")
+    p.emit(f"""
+        mul.wide.u32 {oadr}, {bh}, {cfg.Sq}
+        cvt.u64.u32 {w64}, {grow}
+        add.s64 {oadr}, {oadr}, {w64}
+        mul.lo.s64 {oadr}, {oadr}, {cfg.D * 2}
+        add.s64 {oadr}, {oadr}, {ptr[cfg.o_param]}
+    """)
+    ov = [p.reg("b32") for _ in range(32)]
+    for c in range(DP // 32):
+        p.emit(f"tcgen05.ld.sync.aligned.32x32b.x32.b32 {{{', '.join(ov)}}}, [{o_ta}+{c * 32}]")
+        p.emit("tcgen05.wait::ld.sync.aligned")
+        if c * 32 >= cfg.D:
+            continue
+        fs = []
+        for i in range(32):
+            f = p.reg("f32")
+            p.emit(f"mov.b32 {f}, {ov[i]}\nmul.rn.f32 {f}, {f}, {inv}")
+            fs.append(f)
+        packed = [p.reg("b32") for _ in range(16)]
+        for i in range(16):
+            p.emit(f"{cvt} {packed[i]}, {fs[2 * i + 1]}, {fs[2 * i]}")
+        for g in range(4):
+            if c * 32 + 8 * g >= cfg.D:
+                break
+            p.emit(f"@{prow_ok} st.global.v4.b32 [{oadr}+{(c * 32 + 8 * g) * 2}], "
+                   f"{{{', '.join(packed[4 * g:4 * g + 4])}}}")
+    p.emit(f"bra {finish}")
+
+
+# ---------------------------------------------------------------------------
+# recognising the IR's attention family
+
+
+def _walk(body):
+    for s in body:
+        yield s
+        for attr in ("body", "else_body"):
+            sub = getattr(s, attr, None)
+            if isinstance(sub, tuple):
+                yield from _walk(sub)
+
+
+def _frag_base(name: str) -> str:
+    """``_qa0_[_r2]`` -> ``_qa0_``, ``_kb[_r0]`` -> ``_kb``."""
+    return name.split("[")[0]
+
+
+def analyze(spec) -> AttnConfig:
+    from ..stmts import expr_vars
+    stmts = list(_walk(spec.body))
+    kinds = {type(s).__name__ for s in stmts}
+    if "FragmentRowReduce" not in kinds or "MmaSyncPtx" not in kinds:
+        raise NotImplementedError("not a tensor-core attention")
+    ldm = [s for s in stmts if type(s).__name__ == "LdmatrixLoad"]
+    frag_src = {}
+    for s in ldm:
+        frag_src.setdefault(_frag_base(s.frag), s)
+        if s.pair_frag:
+            frag_src.setdefault(_frag_base(s.pair_frag), s)
+    repacked = {_frag_base(s.frag) for s in stmts if type(s).__name__ == "FragmentRepack"}
+    mmas = [s for s in stmts if type(s).__name__ == "MmaSyncPtx"]
+    qk = [s for s in mmas if _frag_base(s.a_frag) not in repacked]
+    pv = [s for s in mmas if _frag_base(s.a_frag) in repacked]
+    if not qk or not pv:
+        raise NotImplementedError("attention needs a score MMA and a PV MMA")
+    if any(s.src_buffer not in spec.buffers for s in ldm):
+        raise NotImplementedError("attention operands staged through shared memory")
+    qs = frag_src[_frag_base(qk[0].a_frag)]
+    ks = frag_src[_frag_base(qk[0].b_frag)]
+    vs = frag_src[_frag_base(pv[0].b_frag)]
+    Q, K, V = spec.param(qs.src_buffer), spec.param(ks.src_buffer), spec.param(vs.src_buffer)
+    stores = [s for s in stmts if type(s).__name__ == "RegStore"]
+    O = spec.param(stores[0].dst_buffer)
+    if len({Q.dtype, K.dtype, V.dtype, O.dtype}) != 1:
+        raise NotImplementedError("mixed attention dtypes")
+    for s in stmts:
+        if type(s).__name__ == "FragmentApply" and any(k in ("coord", "gmem") for k in (s.kinds or ())):
+            raise NotImplementedError("masked attention (causal / additive mask)")
+    # the key-chunk loop: the loop that holds the row reductions
+    ck = None
+    for s in stmts:
+        if type(s).__name__ in ("Loop", "StridedLoop") and \
+                any(type(x).__name__ == "FragmentRowReduce" for x in _walk(s.body)):
+            ck = s.axis.name
+            break
+    kdims = [i for i, e in enumerate(ks.src_index) if ck in expr_vars(e)]
+    if len(kdims) != 1:
+        raise NotImplementedError("key axis of K not identifiable")
+    kt_layout = kdims[0] == len(K.shape) - 1
+    Sq, D = Q.shape[-2], Q.shape[-1]
+    Sk = K.shape[-1] if kt_layout else K.shape[-2]
+    if (K.shape[-2] if kt_layout else K.shape[-1]) != D or tuple(V.shape[-2:]) != (Sk, D) \
+            or tuple(O.shape[-2:]) != (Sq, D):
+        raise NotImplementedError("attention operand shapes")
+    BH = math.prod(Q.shape[:-2]) if len(Q.shape) > 2 else 1
+    for X in (K, V, O):
+        if (math.prod(X.shape[:-2]) if len(X.shape) > 2 else 1) != BH:
+            raise NotImplementedError("grouped / broadcast heads")
+    scale = _score_scale(spec, stmts, {_frag_base(s.c_frag) for s in qk})
+    return AttnConfig(BH=BH, Sq=Sq, Sk=Sk, D=D, dtype=Q.dtype, kt_layout=kt_layout, scale=scale,
+                      name=spec.name, q_param=Q.name, k_param=K.name, v_param=V.name, o_param=O.name,
+                      arg_params=arg_params(spec), buffers=tuple(x.name for x in spec.params))
+
+
+def _score_scale(spec, stmts, score_frags) -> float:
+    """Product of the uniform multiplies / divides the IR applies to S before the
+    row max (``FragmentApply`` with a scalar operand from the constants)."""
+    env = {}
+    for s in stmts:
+        k = type(s).__name__
+        if k == "Load" and s.input in spec.constants and len(s.names) == 1:
+            env[s.names[0]] = float(spec.constants[s.input])
+        elif k == "Let" and type(s.value).__name__ == "Literal":
+            env[s.name] = float(s.value.value)
+        elif k == "Assign" and all(a in env for a in s.args):
+            a = [env[x] for x in s.args]
+            op = s.op.name
+            if op == "reciprocal":
+                env[s.name] = 1.0 / a[0]
+            elif op == "multiply":
+                env[s.name] = a[0] * a[1]
+            elif op == "divide":
+                env[s.name] = a[0] / a[1]
+            elif op == "copy":
+                env[s.name] = a[0]
+    scale = 1.0
+    derived = set(score_frags)
+    for s in stmts:
+        if type(s).__name__ != "FragmentApply":
+            continue
+        fr = [a for a, kd in zip(s.args, s.kinds) if kd == "frag"]
+        if not fr or _frag_base(fr[0]) not in derived:
+            continue
+        op = s.op.name
+        if op == "copy":
+            derived.add(s.out)
+            continue
+        unis = [a for a, kd in zip(s.args, s.kinds) if kd == "uniform"]
+        if op in ("multiply", "divide") and len(unis) == 1 and unis[0] in env:
+            v = env[unis[0]]
+            scale = scale * v if op == "multiply" else scale / v
+            derived.add(s.out)
+            continue
+        break   # the first non-scale op (the max subtraction) ends the score prologue
+    return scale
+
+
+def emit_attention(spec) -> str:
+    return emit_attention_module(analyze(spec))
