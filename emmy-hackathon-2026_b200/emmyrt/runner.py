@@ -105,6 +105,14 @@ class CompiledKernel:
         return cls.from_ptx(spec, ptx)
 
     @classmethod
+    def from_module(cls, ptx: str, entry: str, buffers) -> "CompiledKernel":
+        """A template module emitted directly (not from an IR file): its parameters
+        are the pointer ``buffers`` in order, then the descriptor's extras."""
+        from compiler.loader import KernelSpec, Param
+        spec = KernelSpec(entry, (), tuple(Param(b, "u64", ()) for b in buffers), None, None, {})
+        return cls.from_ptx(spec, ptx)
+
+    @classmethod
     def from_ptx(cls, spec, ptx: str) -> "CompiledKernel":
         desc = parse_launch(ptx)
         mod = Module(ptx)
