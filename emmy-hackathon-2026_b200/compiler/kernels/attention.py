@@ -671,25 +671,32 @@ def _score_scale(spec, stmts, score_frags) -> float:
                 env[s.name] = a[0] / a[1]
             elif op == "copy":
                 env[s.name] = a[0]
+    # follow the chain of one score fragment: S -> (copy) -> *scale -> ... -> max subtraction
+    applies = [s for s in stmts if type(s).__name__ == "FragmentApply"]
     scale = 1.0
-    derived = set(score_frags)
-    for s in stmts:
-        if type(s).__name__ != "FragmentApply":
-            continue
+    cur = None
+    for s in applies:
         fr = [a for a, kd in zip(s.args, s.kinds) if kd == "frag"]
-        if not fr or _frag_base(fr[0]) not in derived:
-            continue
-        op = s.op.name
+        if fr and _frag_base(fr[0]) in score_frags:
+            cur = s
+            break
+    while cur is not None:
+        op = cur.op.name
+        unis = [a for a, kd in zip(cur.args, cur.kinds) if kd == "uniform"]
         if op == "copy":
-            derived.add(s.out)
-            continue
-        unis = [a for a, kd in zip(s.args, s.kinds) if kd == "uniform"]
-        if op in ("multiply", "divide") and len(unis) == 1 and unis[0] in env:
+            pass
+        elif op in ("multiply", "divide") and len(unis) == 1 and unis[0] in env:
             v = env[unis[0]]
             scale = scale * v if op == "multiply" else scale / v
-            derived.add(s.out)
-            continue
-        break   # the first non-scale op (the max subtraction) ends the score prologue
+        else:
+            break
+        nxt = None
+        for s in applies:
+            fr = [a for a, kd in zip(s.args, s.kinds) if kd == "frag"]
+            if fr and fr[0].split("[")[0] == cur.out:
+                nxt = s
+                break
+        cur = nxt
     return scale
 
 

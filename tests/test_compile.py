@@ -98,3 +98,19 @@ def test_baseline_reductions_compile(name):
     ptx = compile_kernel(spec)
     from emmyrt import assemble
     assemble(ptx)
+
+
+@pytest.mark.parametrize("pid,scale,kt,d", [("x_h_sdpa", 32 ** -0.5, False, 32), ("x_h_attn", 1 / 8, True, 64),
+                                            ("x_h_attn_128", 1 / 8, True, 64)])
+def test_attention_recognizer(pid, scale, kt, d):
+    from compiler.kernels.attention import analyze
+    cfg = analyze(load(next((GOLDEN / pid).glob("*.ir.json"))))
+    assert abs(cfg.scale - scale) < 1e-12 and cfg.kt_layout == kt and cfg.D == d
+
+
+@pytest.mark.parametrize("pid,kmajor", [("x_h_mm_1024", False), ("x_h_linear", True), ("x_h_mm_t_odd", True),
+                                        ("x_h_bmm_t", True)])
+def test_gemm_recognizer(pid, kmajor):
+    from compiler.kernels.gemm import analyze
+    cfg = analyze(load(next((GOLDEN / pid).glob("*.ir.json"))))
+    assert cfg.b_kmajor == kmajor
