@@ -32,8 +32,25 @@ def build_runtime(verbose: bool = False) -> Path:
     return out
 
 
+def build_static_scratch(verbose: bool = False) -> Path:
+    """``emmyrt/libemmyrt_static.so``: the whole-array reduction entry point that takes
+    its scratch from a file-scope device array (csrc/emmyrt_static_scratch.cu), linked
+    against libemmyrt.so for the launch and against the static CUDA runtime."""
+    out = PKG / "emmyrt" / "libemmyrt_static.so"
+    src = PKG / "csrc" / "emmyrt_static_scratch.cu"
+    cmd = [str(CUDA / "bin" / "nvcc"), "-O2", "-shared", "-Xcompiler", "-fPIC",
+           "-Xcompiler", "-fvisibility=hidden", "-gencode", "arch=compute_100a,code=sm_100a",
+           "-lineinfo", f"-I{ROOT / 'include'}", str(src), "-o", str(out),
+           f"-L{PKG / 'emmyrt'}", "-lemmyrt", "-Xlinker", "-rpath,$ORIGIN", "-cudart", "static"]
+    if verbose:
+        print(" ".join(cmd))
+    subprocess.run(cmd, check=True)
+    return out
+
+
 def main() -> int:
     build_runtime(verbose=True)
+    build_static_scratch(verbose=True)
     print("built", PKG / "emmyrt" / "libemmyrt.so")
     return 0
 

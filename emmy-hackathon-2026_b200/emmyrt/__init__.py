@@ -322,3 +322,31 @@ def tensor_map(gaddr: int, dtype: str, dims, strides_bytes, box, swizzle: int = 
           "tensor map encode")
     view._keepalive = raw
     return view
+
+
+# ---------------------------------------------------------------------------
+# whole-array reductions with static scratch (libemmyrt_static.so)
+
+STATIC_LIB_PATH = _HERE / "libemmyrt_static.so"
+STATIC_SIGNATURES = {
+    "emmy_rt_full_reduce_static_scratch": ([_u64, ctypes.c_uint, ctypes.c_uint, _P(_u64), _int, _sz, _u64],
+                                           _int),
+}
+EMMY_RT_ESCRATCH = -6
+_static_lib = None
+
+
+def static_scratch_lib():
+    """The library whose single entry point launches a whole-array reduction with its
+    scratch taken from a static device array (for callers that cannot allocate)."""
+    global _static_lib
+    if _static_lib is None:
+        if not STATIC_LIB_PATH.exists():
+            raise ImportError(f"{STATIC_LIB_PATH} is not built; run __graft_entry__.build()")
+        lib2 = ctypes.CDLL(str(STATIC_LIB_PATH))
+        for name, (args, res) in STATIC_SIGNATURES.items():
+            fn = getattr(lib2, name)
+            fn.argtypes = args
+            fn.restype = res
+        _static_lib = lib2
+    return _static_lib

@@ -36,6 +36,7 @@ extern "C" {
 #define EMMY_RT_EINVAL    (-3)   /* bad argument                                  */
 #define EMMY_RT_ETIMEOUT  (-4)   /* emmy_rt_stream_wait deadline passed           */
 #define EMMY_RT_ENOINIT   (-5)   /* emmy_rt_init was not called                   */
+#define EMMY_RT_ESCRATCH  (-6)   /* scratch larger than the static array          */
 
 /* ---- errors ------------------------------------------------------------------ */
 
@@ -150,6 +151,28 @@ int emmy_rt_nccl_comm_init(uint64_t *comm, int nranks, const void *id, int rank)
 int emmy_rt_nccl_allreduce(uint64_t comm, uint64_t sendbuf, uint64_t recvbuf, size_t count,
                            int dtype, int op, uint64_t stream);
 int emmy_rt_nccl_comm_destroy(uint64_t comm);
+
+/* ---- whole-array reduction with static scratch (libemmyrt_static.so) ------------- */
+
+/* Size of the device array emmy_rt_full_reduce_static_scratch takes scratch from. */
+#define EMMY_RT_STATIC_SCRATCH_BYTES (64 * 1024)
+
+/* No counterpart in the reference: an addition for callers that cannot allocate device
+ * memory where they need a reduction (a process whose HBM is all handed to its own pool,
+ * an error path after an out-of-memory failure, a latency-bound loop that must not pay
+ * for cudaMalloc).  Launches a whole-array reduction kernel compiled by this back end
+ * (`function`, from emmy_rt_module_function; grid and block from its launch descriptor)
+ * with `args` = its nargs pointer arguments in meta.json arg_order and its scratch taken
+ * from a file-scope device array of EMMY_RT_STATIC_SCRATCH_BYTES instead of an allocation.
+ * Rejects scratch_bytes above that size with EMMY_RT_ESCRATCH.  The first call on a
+ * device looks the array up (cudaGetSymbolAddress) and should come before any stream
+ * capture.  Calls share the array: each clears its ticket word on `stream` first, and
+ * calls whose kernels overlap on the GPU race.  Returns 0, EMMY_RT_EINVAL /
+ * EMMY_RT_ESCRATCH, a cudaError_t from the set-up or the clear, or emmy_rt_launch's
+ * status. */
+int emmy_rt_full_reduce_static_scratch(uint64_t function, unsigned grid, unsigned block,
+                                       const uint64_t *args, int nargs, size_t scratch_bytes,
+                                       uint64_t stream);
 
 #ifdef __cplusplus
 }

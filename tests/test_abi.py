@@ -10,10 +10,23 @@ def test_exports_match_header():
     header = (ROOT / "include" / "emmyrt.h").read_text()
     declared = set(re.findall(r"\b(emmy_rt_\w+)\s*\(", header))
     assert declared, "no declarations found"
+    static = emmyrt.static_scratch_lib()
     for name in declared:
-        assert hasattr(emmyrt.lib, name), f"libemmyrt.so does not export {name}"
-    assert declared == set(emmyrt.SIGNATURES), "ctypes signatures out of sync with the header"
+        owner = static if name in emmyrt.STATIC_SIGNATURES else emmyrt.lib
+        assert hasattr(owner, name), f"{name} is not exported"
+    assert declared == set(emmyrt.SIGNATURES) | set(emmyrt.STATIC_SIGNATURES), \
+        "ctypes signatures out of sync with the header"
     assert emmyrt.lib.emmy_rt_version() == 1
+
+
+def test_static_scratch_rejects_oversize_without_touching_the_gpu():
+    import ctypes
+    import emmyrt
+    static = emmyrt.static_scratch_lib()
+    args = (ctypes.c_uint64 * 2)(0, 0)
+    # the size check comes before any CUDA call
+    rc = static.emmy_rt_full_reduce_static_scratch(0, 1, 32, args, 2, 64 * 1024 + 1, 0)
+    assert rc == emmyrt.EMMY_RT_ESCRATCH
 
 
 def test_calls_before_init_fail_cleanly():
