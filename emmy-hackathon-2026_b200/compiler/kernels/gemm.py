@@ -81,15 +81,16 @@ class GemmConfig:
         return -(-self.M // self.BM), -(-self.N // self.BN)
 
 
-def choose_bn(M: int, N: int, batch: int) -> int:
-    """Largest N tile (<= 256, multiple of 16) that still gives every SM work when
-    possible; small problems trade per-tile efficiency for parallelism."""
+def choose_bn(M: int, N: int, batch: int, min_bn: int = 64) -> int:
+    """Largest N tile (<= 256) that still gives every SM work when possible; small
+    problems trade per-tile efficiency for parallelism.  ``min_bn`` is the width of
+    one 128-byte TMA box of an MN-major B (64 16-bit or 128 8-bit elements)."""
     bn = 256
-    while bn > 64 and batch * (-(-M // 128)) * (-(-N // bn)) < SMS:
+    while bn > max(64, min_bn) and batch * (-(-M // 128)) * (-(-N // bn)) < SMS:
         bn //= 2
     if N < bn:
         bn = max(32, -(-N // 32) * 32)   # the epilogue reads TMEM 32 columns at a time
-    return bn
+    return max(bn, min_bn)
 
 
 def _tile_coords(p: Ptx, cfg: GemmConfig, t: str) -> tuple[str, str, str]:
@@ -139,6 +140,8 @@ def emit_gemm_module(cfg: GemmConfig) -> str:
         # MN-major: 64-element (128-byte) column blocks of BK K-rows each, BK*128 bytes apart
         b_hi, b_lo = smem_desc_hi(1024), smem_desc_lo_const(BK * 128)
     nb_mn = BN // (128 // eb)               # MN-major B: number of 128-byte column blocks
+    if not cfg.b_kmajor and BN % (128 // eb):
+        raise NotImplementedError(f"BN={BN} is not a whole number of 128-byte B boxes")
     rank = 3 if cfg.batch > 1 else 2
 
     p.comment(f"tcgen05 GEMM {cfg.batch}x{M}x{N}x{K} {cfg.ab}->{cfg.c}, tile {BM}x{BN}x{BK}, "
@@ -623,7 +626,7 @@ def analyze(spec) -> GemmConfig:
     if (K * eb) % 16 or (not b_kmajor and (N * eb) % 16):
         raise NotImplementedError("operand rows are not 16-byte aligned (TMA)")
     epi = _epilogue_ops(spec, stores[0])
-    bn = choose_bn(M, N, batch)
+    bn = choose_bn(M, N, batch, 32 if b_kmajor else 64)
     return GemmConfig(M=M, N=N, K=K, batch=batch, ab=A.dtype, c=C.dtype, b_kmajor=b_kmajor, BN=bn,
                       epilogue=epi, name=spec.name, a_param=aname, b_param=bname, c_param=cname,
                       arg_params=arg_params(spec), buffers=tuple(q.name for q in spec.params))

@@ -89,7 +89,7 @@ def emit_quantize_module(n: int, name: str = "k_quantize_e4m3") -> str:
 def fp8_gemm_config(M: int, N: int, K: int, name: str = "k_gemm_e4m3") -> GemmConfig:
     """C[M,N] (bf16) = (A_q[M,K] . B_q[K,N]) * s_a * s_b with e4m3 operands.
     Parameters: a, b (e4m3), c (bf16), sa, sb (f32 scalars)."""
-    return GemmConfig(M=M, N=N, K=K, ab="e4m3", c="bf16", b_kmajor=False, BN=choose_bn(M, N, 1),
+    return GemmConfig(M=M, N=N, K=K, ab="e4m3", c="bf16", b_kmajor=False, BN=choose_bn(M, N, 1, 128),
                       epilogue=(("scale2", "sa", "sb"),), name=name, a_param="a", b_param="b",
                       c_param="c", buffers=("a", "b", "c", "sa", "sb"))
 
