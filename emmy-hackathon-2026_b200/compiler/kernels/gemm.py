@@ -61,8 +61,13 @@ class GemmConfig:
     c_param: str = "c"
     arg_params: list | None = None   # signature (meta.json arg_order) when compiled from IR
     buffers: tuple = ()              # pointer params to load (name list) for IR kernels
+    pair: bool = False               # CTA pair (cta_group::2): 256-row tiles, B split by column
 
-    BM = 128
+    BM = 128                         # accumulator rows per CTA
+
+    @property
+    def MT(self) -> int:             # rows of one output tile
+        return 256 if self.pair else 128
 
     @property
     def kind(self) -> str:
@@ -78,7 +83,7 @@ class GemmConfig:
 
     @property
     def tiles(self) -> tuple[int, int]:
-        return -(-self.M // self.BM), -(-self.N // self.BN)
+        return -(-self.M // self.MT), -(-self.N // self.BN)
 
 
 def choose_bn(M: int, N: int, batch: int, min_bn: int = 64) -> int:
@@ -91,6 +96,14 @@ def choose_bn(M: int, N: int, batch: int, min_bn: int = 64) -> int:
     if N < bn:
         bn = max(32, -(-N // 32) * 32)   # the epilogue reads TMEM 32 columns at a time
     return max(bn, min_bn)
+
+
+def choose_tiling(M: int, N: int, batch: int, min_bn: int = 64) -> dict:
+    """CTA pairs with 256x256 tiles and 6 stages when there are enough such tiles to give
+    every SM pair work; otherwise single CTAs with ``choose_bn``'s tile width."""
+    if M >= 256 and N >= 256 and batch * (-(-M // 256)) * (-(-N // 256)) >= SMS // 2:
+        return {"pair": True, "BN": 256, "stages": 6}
+    return {"pair": False, "BN": choose_bn(M, N, batch, min_bn), "stages": 4}
 
 
 def _tile_coords(p: Ptx, cfg: GemmConfig, t: str) -> tuple[str, str, str]:
@@ -122,16 +135,19 @@ def emit_gemm_module(cfg: GemmConfig) -> str:
     tm, tn = cfg.tiles
     ntiles = cfg.batch * tm * tn
     kblocks = -(-K // BK)
+    pair = cfg.pair
+    BNc = BN // 2 if pair else BN           # B columns held by one CTA
     a_bytes = BM * BK * eb                  # 16 KB
-    b_bytes = BN * BK * eb                  # 32 KB at BN = 256
-    stage_bytes = a_bytes + b_bytes
+    b_bytes = BNc * BK * eb                 # 32 KB at BN = 256 (16 KB per CTA of a pair)
+    stage_bytes = a_bytes + b_bytes         # per CTA
     ncols = max(32, 1 << math.ceil(math.log2(BN * cfg.acc_bufs)))
     if ncols > 512:
         raise NotImplementedError("accumulators exceed TMEM")
     smem = S * stage_bytes + 1024           # +1 KB to align the ring to 1024 B
     if smem > 232448 - 256:
         raise NotImplementedError("stage ring exceeds shared memory")
-    idesc = instr_desc(BM, BN, AB_FORMAT[cfg.ab], AB_FORMAT[cfg.ab], False, not cfg.b_kmajor)
+    idesc = instr_desc(cfg.MT, BN, AB_FORMAT[cfg.ab], AB_FORMAT[cfg.ab], False, not cfg.b_kmajor)
+    cg = "cta_group::2" if pair else "cta_group::1"
     a_hi = smem_desc_hi(1024)
     a_lo = smem_desc_lo_const(16)
     if cfg.b_kmajor:
@@ -139,12 +155,13 @@ def emit_gemm_module(cfg: GemmConfig) -> str:
     else:
         # MN-major: 64-element (128-byte) column blocks of BK K-rows each, BK*128 bytes apart
         b_hi, b_lo = smem_desc_hi(1024), smem_desc_lo_const(BK * 128)
-    nb_mn = BN // (128 // eb)               # MN-major B: number of 128-byte column blocks
-    if not cfg.b_kmajor and BN % (128 // eb):
+    nb_mn = BNc // (128 // eb)              # MN-major B: number of 128-byte column blocks
+    if not cfg.b_kmajor and BNc % (128 // eb):
         raise NotImplementedError(f"BN={BN} is not a whole number of 128-byte B boxes")
     rank = 3 if cfg.batch > 1 else 2
 
-    p.comment(f"tcgen05 GEMM {cfg.batch}x{M}x{N}x{K} {cfg.ab}->{cfg.c}, tile {BM}x{BN}x{BK}, "
+    p.comment(f"tcgen05 GEMM {cfg.batch}x{M}x{N}x{K} {cfg.ab}->{cfg.c}, tile {cfg.MT}x{BN}x{BK}"
+              f"{' on a CTA pair (cta_group::2)' if pair else ''}, "
               f"{S} stages, {cfg.acc_bufs} TMEM accumulators, B {'K' if cfg.b_kmajor else 'MN'}-major")
     # ---------------------------------------------------------------- setup
     ptr = {}
@@ -185,16 +202,30 @@ def emit_gemm_module(cfg: GemmConfig) -> str:
         p.emit(f"mbarrier.init.shared::cta.b64 [{bars}+{empty0 + 8 * s}], 1")
     for b in range(cfg.acc_bufs):
         p.emit(f"mbarrier.init.shared::cta.b64 [{bars}+{tfull0 + 8 * b}], 1")
-        p.emit(f"mbarrier.init.shared::cta.b64 [{bars}+{tempty0 + 8 * b}], 128")
+        p.emit(f"mbarrier.init.shared::cta.b64 [{bars}+{tempty0 + 8 * b}], {256 if pair else 128}")
     p.emit(f"st.shared.u32 [{abort}], 0\nfence.mbarrier_init.release.cluster\nfence.proxy.async.shared::cta")
     p.place(init_done)
-    # TMEM allocation by warp 1 (warp-collective)
+    crank, lfull, ltempty = p.reg("u32"), p.reg("u32"), p.reg("u32")
+    pleader = p.reg("pred")
+    if pair:
+        # both CTAs' barriers are initialised before either CTA touches its peer's
+        p.emit(f"""
+            barrier.cluster.arrive.release
+            barrier.cluster.wait.acquire
+            mov.u32 {crank}, %cluster_ctarank
+            setp.eq.u32 {pleader}, {crank}, 0
+            add.u32 {lfull}, {bars}, {full0}
+            mapa.shared::cluster.u32 {lfull}, {lfull}, 0
+            add.u32 {ltempty}, {bars}, {tempty0}
+            mapa.shared::cluster.u32 {ltempty}, {ltempty}, 0
+        """)
+    # TMEM allocation by warp 1 (warp-collective; both CTAs of a pair)
     p1 = p.reg("pred")
     alloc_done = p.label("alloc_done")
     p.emit(f"setp.ne.u32 {p1}, {warp}, 1\n@{p1} bra {alloc_done}")
     p.emit(f"""
-        tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [{tslot}], {ncols}
-        tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned
+        tcgen05.alloc.{cg}.sync.aligned.shared::cta.b32 [{tslot}], {ncols}
+        tcgen05.relinquish_alloc_permit.{cg}.sync.aligned
     """)
     p.place(alloc_done)
     tbase = p.reg("u32")
@@ -207,7 +238,10 @@ def emit_gemm_module(cfg: GemmConfig) -> str:
     waits = Waits(p, status, abort)
     finish = p.label("finish")
     cta, nct = p.reg("u32"), p.reg("u32")
-    p.emit(f"mov.u32 {cta}, %ctaid.x\nmov.u32 {nct}, %nctaid.x")
+    if pair:    # tiles are walked per cluster
+        p.emit(f"mov.u32 {cta}, %clusterid.x\nmov.u32 {nct}, %nclusterid.x")
+    else:
+        p.emit(f"mov.u32 {cta}, %ctaid.x\nmov.u32 {nct}, %nctaid.x")
 
     # ------------------------------------------------------------ producer
     role_mma, role_epi = p.label("role_mma"), p.label("role_epi")
@@ -224,7 +258,9 @@ def emit_gemm_module(cfg: GemmConfig) -> str:
     p.emit(f"setp.ge.u32 {pt}, {t}, {ntiles}\n@{pt} bra {td}")
     bt, mt, nt = _tile_coords(p, cfg, t)
     m0, n0 = p.reg("u32"), p.reg("u32")
-    p.emit(f"mul.lo.u32 {m0}, {mt}, {BM}\nmul.lo.u32 {n0}, {nt}, {BN}")
+    p.emit(f"mul.lo.u32 {m0}, {mt}, {cfg.MT}\nmul.lo.u32 {n0}, {nt}, {BN}")
+    if pair:    # this CTA's rows of the 256-row tile and its half of the B columns
+        p.emit(f"mad.lo.u32 {m0}, {crank}, {BM}, {m0}\nmad.lo.u32 {n0}, {crank}, {BNc}, {n0}")
     kb, kx = p.reg("u32"), p.reg("u32")
     kl = p.label("p_k")
     p.emit(f"mov.u32 {kb}, 0")
@@ -237,25 +273,33 @@ def emit_gemm_module(cfg: GemmConfig) -> str:
         xor.b32 {par}, {ph}, 1
     """)
     waits.wait(eaddr, par, "producer", finish)
+    if pair:
+        # both CTAs' copies complete on the leader's full barrier; only the leader
+        # announces the stage's bytes (both halves)
+        p.emit(f"""
+            @{pleader} mbarrier.arrive.expect_tx.shared::cta.b64 _, [{faddr}], {2 * stage_bytes}
+            mad.lo.u32 {faddr}, {s}, 8, {lfull}
+        """)
+        tma = "cp.async.bulk.tensor.{r}d.cta_group::2.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+    else:
+        p.emit(f"mbarrier.arrive.expect_tx.shared::cta.b64 _, [{faddr}], {stage_bytes}")
+        tma = "cp.async.bulk.tensor.{r}d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+    tma = tma.format(r=rank)
     p.emit(f"""
-        mbarrier.arrive.expect_tx.shared::cta.b64 _, [{faddr}], {stage_bytes}
         mad.lo.u32 {sa}, {s}, {stage_bytes}, {ring}
         add.u32 {sbb}, {sa}, {a_bytes}
         mul.lo.u32 {kx}, {kb}, {BK}
     """)
     zc = f", {bt}" if rank == 3 else ""
-    p.emit(f"cp.async.bulk.tensor.{rank}d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
-           f"[{sa}], [{tma_a}, {{{kx}, {m0}{zc}}}], [{faddr}]")
+    p.emit(f"{tma} [{sa}], [{tma_a}, {{{kx}, {m0}{zc}}}], [{faddr}]")
     if cfg.b_kmajor:
-        p.emit(f"cp.async.bulk.tensor.{rank}d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
-               f"[{sbb}], [{tma_b}, {{{kx}, {n0}{zc}}}], [{faddr}]")
+        p.emit(f"{tma} [{sbb}], [{tma_b}, {{{kx}, {n0}{zc}}}], [{faddr}]")
     else:
         blk = 128 // eb                      # 64 bf16 / 128 fp8 columns per box
         for j in range(nb_mn):
             nx, dst = p.reg("u32"), p.reg("u32")
             p.emit(f"add.u32 {nx}, {n0}, {j * blk}\nadd.u32 {dst}, {sbb}, {j * BK * 128}")
-            p.emit(f"cp.async.bulk.tensor.{rank}d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
-                   f"[{dst}], [{tma_b}, {{{nx}, {kx}{zc}}}], [{faddr}]")
+            p.emit(f"{tma} [{dst}], [{tma_b}, {{{nx}, {kx}{zc}}}], [{faddr}]")
     ps = p.reg("pred")
     p.emit(f"""
         add.u32 {s}, {s}, 1
@@ -275,6 +319,14 @@ def emit_gemm_module(cfg: GemmConfig) -> str:
     p.place(role_mma)
     p.emit(f"setp.ne.u32 {pr}, {warp}, 1\n@{pr} bra {role_epi}")
     p.emit(f"setp.ne.u32 {pl}, {lane}, 0\n@{pl} bra {finish}")
+    if pair:
+        p.emit(f"@!{pleader} bra {finish}")
+        mask = p.reg("b16")
+        p.emit(f"mov.b16 {mask}, 3")
+        commit = ("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster"
+                  ".multicast::cluster.b64 [{a}], " + mask)
+    else:
+        commit = "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [{a}]"
     t2, s2, ph2, tc = p.reg("u32"), p.reg("u32"), p.reg("u32"), p.reg("u32")
     p.emit(f"mov.u32 {t2}, {cta}\nmov.u32 {s2}, 0\nmov.u32 {ph2}, 0\nmov.u32 {tc}, 0")
     ml, md = p.label("m_tile"), p.label("m_done")
@@ -326,8 +378,8 @@ def emit_gemm_module(cfg: GemmConfig) -> str:
             p.emit(f"setp.ne.u32 {pacc}, {kb2}, 0")
         else:
             p.emit(f"setp.eq.u32 {pacc}, {kb2}, {kb2}")
-        p.emit(f"tcgen05.mma.cta_group::1.kind::{cfg.kind} [{dt}], {ad}, {bd}, {idesc}, {pacc}")
-    p.emit(f"tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [{ea2}]")
+        p.emit(f"tcgen05.mma.{cg}.kind::{cfg.kind} [{dt}], {ad}, {bd}, {idesc}, {pacc}")
+    p.emit(commit.format(a=ea2))
     p.emit(f"""
         add.u32 {s2}, {s2}, 1
         setp.eq.u32 {ps}, {s2}, {S}
@@ -336,7 +388,7 @@ def emit_gemm_module(cfg: GemmConfig) -> str:
         add.u32 {kb2}, {kb2}, 1
         setp.lt.u32 {ps}, {kb2}, {kblocks}
         @{ps} bra {mk}
-        tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [{tfa}]
+        {commit.format(a=tfa)}
         add.u32 {tc}, {tc}, 1
         add.u32 {t2}, {t2}, {nct}
         bra {ml}
@@ -347,7 +399,7 @@ def emit_gemm_module(cfg: GemmConfig) -> str:
     # ------------------------------------------------------------ epilogue
     p.place(role_epi)
     _emit_epilogue(p, cfg, ptr, bars, tfull0, tempty0, tbase, warp, lane, cta, nct, ntiles,
-                   waits, finish)
+                   waits, finish, crank if pair else None, ltempty if pair else None)
 
     # -------------------------------------------------------------- finish
     p.place(finish)
@@ -356,11 +408,15 @@ def emit_gemm_module(cfg: GemmConfig) -> str:
     p.emit(f"""
         tcgen05.fence::before_thread_sync
         barrier.sync 0
+    """)
+    if pair:    # neither CTA leaves while its peer may still use its smem, TMEM or barriers
+        p.emit("barrier.cluster.arrive.release\nbarrier.cluster.wait.acquire")
+    p.emit(f"""
         tcgen05.fence::after_thread_sync
         setp.ne.u32 {pw1}, {warp}, 1
         @{pw1} bra {done}
         bar.warp.sync -1
-        tcgen05.dealloc.cta_group::1.sync.aligned.b32 {tbase}, {ncols}
+        tcgen05.dealloc.{cg}.sync.aligned.b32 {tbase}, {ncols}
     """)
     p.place(done)
     p.emit("ret")
@@ -372,19 +428,19 @@ def emit_gemm_module(cfg: GemmConfig) -> str:
     statics = (f"\t.shared .align 8 .b64 gbars[{nbar}];\n\t.shared .align 4 .u32 gabort;\n"
                f"\t.shared .align 4 .u32 gtmem;\n")
     text = text.replace("{\n", "{\n" + statics, 1)
-    grid = min(ntiles, SMS)
+    grid = 2 * min(ntiles, SMS // 2) if pair else min(ntiles, SMS)
     a_dims = [K, M] + ([cfg.batch] if rank == 3 else [])
     a_str = [K * eb] + ([M * K * eb] if rank == 3 else [])
     if cfg.b_kmajor:
         b_dims = [K, N] + ([cfg.batch] if rank == 3 else [])
         b_str = [K * eb] + ([N * K * eb] if rank == 3 else [])
-        b_box = [BK, BN] + ([1] if rank == 3 else [])
+        b_box = [BK, BNc] + ([1] if rank == 3 else [])
     else:
         b_dims = [N, K] + ([cfg.batch] if rank == 3 else [])
         b_str = [N * eb] + ([N * K * eb] if rank == 3 else [])
         b_box = [128 // eb, BK] + ([1] if rank == 3 else [])
     launch = {
-        "kind": "gemm", "grid": [grid, 1, 1], "block": [192, 1, 1], "cluster": [1, 1, 1],
+        "kind": "gemm", "grid": [grid, 1, 1], "block": [192, 1, 1], "cluster": [2 if pair else 1, 1, 1],
         "smem": smem, "flops": 2 * cfg.batch * M * N * K, "tiles": ntiles,
         "extra_params": [
             {"kind": "tmap", "buffer": cfg.a_param, "dtype": cfg.ab, "dims": a_dims, "strides": a_str,
@@ -398,7 +454,7 @@ def emit_gemm_module(cfg: GemmConfig) -> str:
 
 
 def _emit_epilogue(p: Ptx, cfg: GemmConfig, ptr: dict, bars, tfull0, tempty0, tbase, warp, lane,
-                   cta, nct, ntiles, waits: Waits, finish: str) -> None:
+                   cta, nct, ntiles, waits: Waits, finish: str, crank=None, ltempty=None) -> None:
     M, N, BM, BN = cfg.M, cfg.N, cfg.BM, cfg.BN
     cb = ELEM_BYTES[cfg.c]
     q, row_t = p.reg("u32"), p.reg("u32")
@@ -436,8 +492,13 @@ def _emit_epilogue(p: Ptx, cfg: GemmConfig, ptr: dict, bars, tfull0, tempty0, tb
     bt, mt, nt = _tile_coords(p, cfg, t)
     row, n0, taddr = p.reg("u32"), p.reg("u32"), p.reg("u32")
     prow = p.reg("pred")
+    if crank is not None:   # the CTA's 128 rows of the pair's 256-row tile
+        rt2 = p.reg("u32")
+        p.emit(f"mad.lo.u32 {rt2}, {crank}, {BM}, {row_t}")
+    else:
+        rt2 = row_t
     p.emit(f"""
-        mad.lo.u32 {row}, {mt}, {BM}, {row_t}
+        mad.lo.u32 {row}, {mt}, {cfg.MT}, {rt2}
         mul.lo.u32 {n0}, {nt}, {BN}
         setp.lt.u32 {prow}, {row}, {M}
         mad.lo.u32 {taddr}, {ab}, {BN}, {tbase}
@@ -472,7 +533,12 @@ def _emit_epilogue(p: Ptx, cfg: GemmConfig, ptr: dict, bars, tfull0, tempty0, tb
         p.emit("tcgen05.wait::ld.sync.aligned")
         if ch == nchunks - 1:
             # the accumulator is in registers: hand the buffer back to the MMA warp
-            p.emit(f"tcgen05.fence::before_thread_sync\nmbarrier.arrive.shared::cta.b64 _, [{tea}]")
+            if ltempty is not None:   # the leader CTA issues the MMAs: release to its barrier
+                ra = p.reg("u32")
+                p.emit(f"tcgen05.fence::before_thread_sync\nmad.lo.u32 {ra}, {ab}, 8, {ltempty}\n"
+                       f"mbarrier.arrive.release.cluster.shared::cluster.b64 _, [{ra}]")
+            else:
+                p.emit(f"tcgen05.fence::before_thread_sync\nmbarrier.arrive.shared::cta.b64 _, [{tea}]")
         vals = [p.reg("f32") for _ in range(32)]
         for i in range(32):
             p.emit(f"mov.b32 {vals[i]}, {regs[i]}")
@@ -626,8 +692,8 @@ def analyze(spec) -> GemmConfig:
     if (K * eb) % 16 or (not b_kmajor and (N * eb) % 16):
         raise NotImplementedError("operand rows are not 16-byte aligned (TMA)")
     epi = _epilogue_ops(spec, stores[0])
-    bn = choose_bn(M, N, batch, 32 if b_kmajor else 64)
-    return GemmConfig(M=M, N=N, K=K, batch=batch, ab=A.dtype, c=C.dtype, b_kmajor=b_kmajor, BN=bn,
+    tiling = choose_tiling(M, N, batch, 32 if b_kmajor else 64)
+    return GemmConfig(M=M, N=N, K=K, batch=batch, ab=A.dtype, c=C.dtype, b_kmajor=b_kmajor, **tiling,
                       epilogue=epi, name=spec.name, a_param=aname, b_param=bname, c_param=cname,
                       arg_params=arg_params(spec), buffers=tuple(q.name for q in spec.params))
 

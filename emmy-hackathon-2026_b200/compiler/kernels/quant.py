@@ -19,7 +19,7 @@ accumulation, dequantising in the epilogue: ``C = (A_q . B_q) * s_a * s_b`` in b
 from __future__ import annotations
 
 from ..ptx import Ptx, entry, f32_hex, module
-from .gemm import GemmConfig, choose_bn, emit_gemm_module
+from .gemm import GemmConfig, choose_tiling, emit_gemm_module
 
 FP8_MAX = 448.0
 SMS = 148
@@ -89,7 +89,7 @@ def emit_quantize_module(n: int, name: str = "k_quantize_e4m3") -> str:
 def fp8_gemm_config(M: int, N: int, K: int, name: str = "k_gemm_e4m3") -> GemmConfig:
     """C[M,N] (bf16) = (A_q[M,K] . B_q[K,N]) * s_a * s_b with e4m3 operands.
     Parameters: a, b (e4m3), c (bf16), sa, sb (f32 scalars)."""
-    return GemmConfig(M=M, N=N, K=K, ab="e4m3", c="bf16", b_kmajor=False, BN=choose_bn(M, N, 1, 128),
+    return GemmConfig(M=M, N=N, K=K, ab="e4m3", c="bf16", b_kmajor=False, **choose_tiling(M, N, 1, 128),
                       epilogue=(("scale2", "sa", "sb"),), name=name, a_param="a", b_param="b",
                       c_param="c", buffers=("a", "b", "c", "sa", "sb"))
 

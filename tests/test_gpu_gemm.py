@@ -30,3 +30,41 @@ def test_gemm_matches_golden(runtime, pid):
             f"{pid}:{name} max abs err {err}"
         o = np.asarray(ora[name], dtype=np.float32).reshape(ref.shape)
         assert np.allclose(got, o, rtol=meta["rtol"], atol=meta["atol"])
+
+
+def _direct_gemm(m, n, k, pair, b_kmajor, seed=0, batch=1):
+    from compiler.kernels.gemm import GemmConfig, emit_gemm_module
+    from emmyrt import DeviceBuffer
+    from emmyrt.runner import CompiledKernel, bf16_bits_to_f32, f32_to_bf16_bits
+    import emmyrt
+    cfg = GemmConfig(M=m, N=n, K=k, batch=batch, ab="bf16", c="bf16", b_kmajor=b_kmajor, BN=256,
+                     stages=6 if pair else 4, pair=pair, name="k_gemm_test", buffers=("a", "b", "c"))
+    ck = CompiledKernel.from_module(emit_gemm_module(cfg), "k_gemm_test", ["a", "b", "c"])
+    rng = np.random.default_rng(seed)
+    A = f32_to_bf16_bits(rng.standard_normal((batch, m, k), dtype=np.float32) * np.float32(0.05))
+    bshape = (batch, n, k) if b_kmajor else (batch, k, n)
+    B = f32_to_bf16_bits(rng.standard_normal(bshape, dtype=np.float32) * np.float32(0.05))
+    da, db, dc = DeviceBuffer(A.nbytes), DeviceBuffer(B.nbytes), DeviceBuffer(batch * m * n * 2)
+    da.upload(A)
+    db.upload(B)
+    dc.zero()
+    ck({"a": da.ptr, "b": db.ptr, "c": dc.ptr})
+    emmyrt.stream_wait(0, 60)
+    assert ck.status() == 0
+    out = np.zeros((batch, m, n), np.uint16)
+    dc.download(out)
+    Bf = bf16_bits_to_f32(B)
+    if b_kmajor:
+        Bf = np.swapaxes(Bf, -1, -2)
+    return bf16_bits_to_f32(out), bf16_bits_to_f32(A), Bf
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("m,n,k,pair,kmaj", [(512, 512, 512, True, False), (640, 384, 320, True, False),
+                                             (768, 512, 448, True, True), (512, 768, 256, False, False),
+                                             (300, 200, 136, False, True)])
+def test_gemm_direct_bf16(runtime, m, n, k, pair, kmaj):
+    from oracle.refs import mm_bf16
+    got, A, B = _direct_gemm(m, n, k, pair, kmaj)
+    ref = mm_bf16(A[0], B[0])
+    assert np.allclose(got[0], ref, rtol=1e-2, atol=1e-2), f"max abs err {np.max(np.abs(got[0] - ref))}"
