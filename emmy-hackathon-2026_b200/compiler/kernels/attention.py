@@ -58,6 +58,9 @@ class AttnConfig:
     arg_params: list | None = None
     buffers: tuple = ()
     ring: int = 3
+    s_group: int = 1         # S chunks (of 32 columns) per tcgen05.wait::ld; 4 = read S once
+    poly_every: int = 0      # every n-th probability from the FMA-pipe exp2 (0: all on MUFU)
+    p_tmem: bool = False     # P kept in TMEM over the consumed S columns (A operand from TMEM)
 
     @property
     def DP(self) -> int:                 # head dim padded to whole 64-element swizzle rows
@@ -84,7 +87,9 @@ def emit_attention_module(cfg: AttnConfig) -> str:
     p_bytes = 128 * 128 * 2
     q_off, ring_off = 0, NQ * tile_bytes
     p_off = ring_off + R * tile_bytes
-    smem = p_off + NQ * p_bytes + 1024
+    smem = p_off + (0 if cfg.p_tmem else NQ * p_bytes) + 1024
+    if cfg.p_tmem and cfg.s_group != 1:
+        raise NotImplementedError("P in TMEM overwrites S chunk by chunk: s_group must be 1")
     if smem > 232448 - 512:
         raise NotImplementedError("attention tiles exceed shared memory")
     ncols_used = NQ * (128 + DP)
@@ -266,16 +271,21 @@ def emit_attention_module(cfg: AttnConfig) -> str:
         ot = p.reg("u32")
         p.emit(f"add.u32 {ot}, {tbase}, {NQ * 128 + t * DP}")
         for kk in range(128 // 16):
-            p.emit(f"add.u32 {pa}, {base}, {p_off + t * p_bytes + (kk // 4) * 16384 + (kk % 4) * 32}")
             p.emit(f"add.u32 {va}, {vbase}, {kk * 2048}")
-            pd = desc(pa, kmaj_lo, k_sw_hi)
             vd = desc(va, v_lo, k_sw_hi)
             if kk == 0:
                 pe = p.reg("pred")
                 p.emit(f"not.pred {pe}, {first_block_pred}")
             else:
                 pe = ptrue
-            p.emit(f"tcgen05.mma.cta_group::1.kind::f16 [{ot}], {pd}, {vd}, {idesc_pv}, {pe}")
+            if cfg.p_tmem:
+                # A = P from TMEM: 16 keys of bf16/f16 pairs = 8 columns per K step
+                p.emit(f"add.u32 {pa}, {tbase}, {t * 128 + kk * 8}")
+                p.emit(f"tcgen05.mma.cta_group::1.kind::f16 [{ot}], [{pa}], {vd}, {idesc_pv}, {pe}")
+            else:
+                p.emit(f"add.u32 {pa}, {base}, {p_off + t * p_bytes + (kk // 4) * 16384 + (kk % 4) * 32}")
+                pd = desc(pa, kmaj_lo, k_sw_hi)
+                p.emit(f"tcgen05.mma.cta_group::1.kind::f16 [{ot}], {pd}, {vd}, {idesc_pv}, {pe}")
         ob = p.reg("u32")
         p.emit(f"add.u32 {ob}, {bars}, {B_O + 8 * t}\n"
                f"tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [{ob}]")
@@ -345,7 +355,13 @@ def emit_attention_module(cfg: AttnConfig) -> str:
     params = list(cfg.arg_params or [f".param .u64 {param_symbol(n)}" for n in cfg.buffers])
     params += [".param .align 64 .b8 param__tmap_q[128]", ".param .align 64 .b8 param__tmap_k[128]",
                ".param .align 64 .b8 param__tmap_v[128]", ".param .u64 param__status"]
-    text = entry(cfg.name, params, p, maxntid=nthreads)
+    # one CTA per SM (its shared memory allows no more): let ptxas use the whole register file
+    # registers come from 4 sub-partitions of 16K; warps are spread over them, so the
+    # busiest sub-partition (ceil(warps / 4) warps) sets the per-thread cap
+    warps = nthreads // 32
+    regcap = (16384 // (32 * -(-warps // 4))) // 8 * 8
+    text = entry(cfg.name, params, p, maxntid=nthreads,
+                 extra_directives=f"\n.maxnreg {min(regcap, 232)}")
     statics = (f"\t.shared .align 8 .b64 gbars[{nbar}];\n\t.shared .align 4 .u32 gabort;\n"
                f"\t.shared .align 4 .u32 gtmem;\n")
     text = text.replace("{\n", "{\n" + statics, 1)
@@ -368,6 +384,35 @@ def emit_attention_module(cfg: AttnConfig) -> str:
         ],
     }
     return module([text], launch, globals_=[".extern .shared .align 1024 .b8 dsmem[];"])
+
+
+# 2^f on f in [-1/2, 1/2]: cubic fitted here by least squares on the relative error
+# (iteratively reweighted towards minimax); max relative error 7.7e-5, far below the
+# bf16 rounding the probabilities get next.
+EXP2_POLY = (0.9999262094497681, 0.6932613253593445, 0.2426345944404602, 0.05518098175525665)
+
+
+def emit_exp2_poly(p: Ptx, dst: str, x: str) -> None:
+    """2^x on the FMA/ALU pipes (Cody-Waite split): j = round(x) by adding 1.5*2^23,
+    f = x - j in [-1/2, 1/2], 2^f by the cubic, and 2^j by adding j to the exponent
+    field.  x is clamped at -125 so the exponent arithmetic stays in range."""
+    xc, t, jf, f, q = p.regs("f32", 5)
+    tb, qb = p.reg("b32"), p.reg("b32")
+    c0, c1, c2, c3 = (f32_hex(c) for c in EXP2_POLY)
+    p.emit(f"""
+        max.f32 {xc}, {x}, 0fC2FA0000
+        add.rn.f32 {t}, {xc}, 0f4B400000
+        sub.rn.f32 {jf}, {t}, 0f4B400000
+        sub.rn.f32 {f}, {xc}, {jf}
+        fma.rn.f32 {q}, {f}, {c3}, {c2}
+        fma.rn.f32 {q}, {q}, {f}, {c1}
+        fma.rn.f32 {q}, {q}, {f}, {c0}
+        mov.b32 {tb}, {t}
+        shl.b32 {tb}, {tb}, 23
+        mov.b32 {qb}, {q}
+        add.s32 {qb}, {qb}, {tb}
+        mov.b32 {dst}, {qb}
+    """)
 
 
 def _addr(p: Ptx, base: str, off: int) -> str:
@@ -428,37 +473,54 @@ def _emit_softmax(p: Ptx, cfg: AttnConfig, ptr, bars, B_S, B_P, B_O, tbase, base
     p.emit(f"and.b32 {par}, {jj}, 1")
     waits.wait(sbar, par, "softmax", finish)
     p.emit("bar.warp.sync -1\ntcgen05.fence::after_thread_sync")
-    vals = [p.reg("b32") for _ in range(32)]
-    fv = [p.reg("f32") for _ in range(32)]
+    G = cfg.s_group
     keyb = None
     if masked:
         keyb = p.reg("u32")
         p.emit(f"mul.lo.u32 {keyb}, {jj}, 128")
+    regsets = [[p.reg("b32") for _ in range(32 * G)] for _ in range(1 if G < 4 else 1)]
+    fsets = [[p.reg("f32") for _ in range(32 * G)]]
 
-    def load_chunk(c):
-        p.emit(f"tcgen05.ld.sync.aligned.32x32b.x32.b32 {{{', '.join(vals)}}}, [{s_ta}+{c * 32}]")
+    def load_group(g):
+        """S chunks g*G .. g*G+G-1 into registers: G loads in flight, one wait."""
+        vals, fv = regsets[0], fsets[0]
+        for k in range(G):
+            c = g * G + k
+            p.emit(f"tcgen05.ld.sync.aligned.32x32b.x32.b32 {{{', '.join(vals[32 * k:32 * k + 32])}}}, "
+                   f"[{s_ta}+{c * 32}]")
         p.emit("tcgen05.wait::ld.sync.aligned")
-        for i in range(32):
+        for i in range(32 * G):
             p.emit(f"mov.b32 {fv[i]}, {vals[i]}")
         if masked:
-            for i in range(32):
+            for i in range(32 * G):
                 pk, kx = p.reg("pred"), p.reg("u32")
-                p.emit(f"add.u32 {kx}, {keyb}, {c * 32 + i}\nsetp.ge.u32 {pk}, {kx}, {cfg.Sk}\n"
+                p.emit(f"add.u32 {kx}, {keyb}, {g * G * 32 + i}\nsetp.ge.u32 {pk}, {kx}, {cfg.Sk}\n"
                        f"@{pk} mov.f32 {fv[i]}, 0fFF800000")
+        return fv
+
     # pass A: row maximum of the raw scores
     mx = p.reg("f32")
     p.emit(f"mov.f32 {mx}, 0fFF800000")
-    for c in range(4):
-        load_chunk(c)
-        red = list(fv)
-        while len(red) > 1:
+    for g in range(4 // G):
+        red = list(load_group(g)) + [mx]
+        while len(red) > 1:                  # three-input max tree
             nxt = []
-            for i in range(0, len(red), 2):
+            i = 0
+            while i < len(red):
                 r = p.reg("f32")
-                p.emit(f"max.f32 {r}, {red[i]}, {red[i + 1]}")
+                if len(red) - i >= 3:
+                    p.emit(f"max.f32 {r}, {red[i]}, {red[i + 1]}, {red[i + 2]}")
+                    i += 3
+                elif len(red) - i == 2:
+                    p.emit(f"max.f32 {r}, {red[i]}, {red[i + 1]}")
+                    i += 2
+                else:
+                    nxt.append(red[i])
+                    i += 1
+                    continue
                 nxt.append(r)
             red = nxt
-        p.emit(f"max.f32 {mx}, {mx}, {red[0]}")
+        p.emit(f"mov.f32 {mx}, {red[0]}")
     mn, alpha, thr = p.reg("f32"), p.reg("f32"), p.reg("f32")
     prs, pfirst = p.reg("pred"), p.reg("pred")
     p.emit(f"""
@@ -506,30 +568,58 @@ def _emit_softmax(p: Ptx, cfg: AttnConfig, ptr, bars, B_S, B_P, B_O, tbase, base
     negm = p.reg("f32")
     p.emit(f"neg.f32 {negm}, {m}")
     cvt = "cvt.rn.bf16x2.f32" if cfg.dtype == "bf16" else "cvt.rn.f16x2.f32"
+    fv = fsets[0]
+    # packed f32x2 operands: (scale*log2e, scale*log2e) and (-m, -m)
+    sl2, nm2 = p.reg("b64"), p.reg("b64")
+    slr = p.reg("f32")
+    p.emit(f"mov.f32 {slr}, {f32_hex(scale_log2)}\nmov.b64 {sl2}, {{{slr}, {slr}}}\n"
+           f"mov.b64 {nm2}, {{{negm}, {negm}}}")
     for c in range(4):
-        load_chunk(c)
+        if G < 4 and c % G == 0:
+            fv = load_group(c // G)          # read this group of S again
+        base_i = 32 * (c % G) if G < 4 else 32 * c
         ps = []
-        for i in range(32):
-            e = p.reg("f32")
-            p.emit(f"fma.rn.f32 {e}, {fv[i]}, {f32_hex(scale_log2)}, {negm}\nex2.approx.ftz.f32 {e}, {e}")
-            ps.append(e)
-        red = list(ps)
+        for i in range(0, 32, 2):
+            x2, e2 = p.reg("b64"), p.reg("b64")
+            ea, eb = p.reg("f32"), p.reg("f32")
+            p.emit(f"mov.b64 {x2}, {{{fv[base_i + i]}, {fv[base_i + i + 1]}}}\n"
+                   f"fma.rn.f32x2 {e2}, {x2}, {sl2}, {nm2}\nmov.b64 {{{ea}, {eb}}}, {e2}")
+            for k, e in ((i, ea), (i + 1, eb)):
+                if cfg.poly_every and not masked and k % cfg.poly_every == cfg.poly_every - 1:
+                    emit_exp2_poly(p, e, e)     # offload part of the exponentials from MUFU
+                else:
+                    p.emit(f"ex2.approx.ftz.f32 {e}, {e}")
+                ps.append(e)
+        # row sum: pairwise f32x2 adds, then the two halves
+        red = []
+        for i in range(0, 32, 2):
+            r = p.reg("b64")
+            p.emit(f"mov.b64 {r}, {{{ps[i]}, {ps[i + 1]}}}")
+            red.append(r)
         while len(red) > 1:
             nxt = []
             for i in range(0, len(red), 2):
-                r = p.reg("f32")
-                p.emit(f"add.rn.f32 {r}, {red[i]}, {red[i + 1]}")
+                r = p.reg("b64")
+                p.emit(f"add.rn.f32x2 {r}, {red[i]}, {red[i + 1]}")
                 nxt.append(r)
             red = nxt
-        p.emit(f"add.rn.f32 {l}, {l}, {red[0]}")
+        h0, h1 = p.reg("f32"), p.reg("f32")
+        p.emit(f"mov.b64 {{{h0}, {h1}}}, {red[0]}\nadd.rn.f32 {h0}, {h0}, {h1}\nadd.rn.f32 {l}, {l}, {h0}")
         packed = [p.reg("b32") for _ in range(16)]
         for i in range(16):
             p.emit(f"{cvt} {packed[i]}, {ps[2 * i + 1]}, {ps[2 * i]}")
-        for g in range(4):
-            c16 = c * 4 + g
-            p.emit(f"st.shared.v4.b32 [{chunk_addr[c16]}], {{{', '.join(packed[4 * g:4 * g + 4])}}}")
+        if cfg.p_tmem:
+            # P chunk c (32 keys = 16 packed columns) over S columns already read
+            p.emit(f"tcgen05.st.sync.aligned.32x32b.x16.b32 [{s_ta}+{c * 16}], {{{', '.join(packed)}}}")
+        else:
+            for g in range(4):
+                c16 = c * 4 + g
+                p.emit(f"st.shared.v4.b32 [{chunk_addr[c16]}], {{{', '.join(packed[4 * g:4 * g + 4])}}}")
+    if cfg.p_tmem:
+        p.emit("tcgen05.wait::st.sync.aligned")
+    else:
+        p.emit("fence.proxy.async.shared::cta")
     p.emit(f"""
-        fence.proxy.async.shared::cta
         tcgen05.fence::before_thread_sync
         mbarrier.arrive.shared::cta.b64 _, [{pbar}]
         add.u32 {jj}, {jj}, 1

@@ -13,7 +13,7 @@ import json
 import struct
 from collections import Counter
 
-PTX_VERSION = "8.7"      # tcgen05 needs >= 8.6; ptxas 12.9 accepts 8.6-8.8
+PTX_VERSION = "8.8"      # tcgen05 needs >= 8.6, three-input max 8.8; ptxas 12.9 accepts 8.6-8.8
 TARGET = "sm_100a"
 
 HEADER = f".version {PTX_VERSION}\n.target {TARGET}\n.address_size 64\n"

@@ -35,7 +35,7 @@ def test_module_contract(ir):
     assert time.time() - t0 < 1.0
     ptx.encode("ascii")
     lines = [l.strip() for l in ptx.splitlines() if l.strip() and not l.strip().startswith("//")]
-    assert lines[0] == ".version 8.7" and lines[1] == ".target sm_100a"
+    assert lines[0] == ".version 8.8" and lines[1] == ".target sm_100a"
     assert f".visible .entry {spec.name}(" in ptx
     launch = parse_launch(ptx)
     sig = ptx.split(f".visible .entry {spec.name}(")[1].split(")")[0]
