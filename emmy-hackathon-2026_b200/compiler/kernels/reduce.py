@@ -169,6 +169,7 @@ class RowReduce:
     """One row (all tile axes but the cooperative one) per ``TPR`` threads."""
 
     COL = "__col"
+    CHUNKS_PER_THREAD = 8    # VEC-wide column chunks each thread loads (loads in flight)
 
     def __init__(self, spec):
         self.spec = spec
@@ -223,7 +224,7 @@ class RowReduce:
                   and all(a.aff.const % 4 == 0 for a in col_accesses))
         self.VEC = 4 if vec_ok else 1
         chunks = -(-self.L // self.VEC)
-        tpr = 1 << max(0, math.ceil(math.log2(max(1, chunks / 4))))
+        tpr = 1 << max(0, math.ceil(math.log2(max(1, chunks / self.CHUNKS_PER_THREAD))))
         self.TPR = max(32, min(1024, tpr))
         self.NCH = -(-chunks // self.TPR)
         if self.NCH * self.VEC > 64:
@@ -278,6 +279,24 @@ class RowReduce:
         ctx = ScalarCtx(p, constants=dict(spec.constants))
         ctx.on_load = self._scalar_load
         ctx.on_write = self._leader_write
+        # exp(x - M) in a later pass, for an element x whose exp(x - m_t) the online
+        # rewrite already holds: e * exp(m_t - M), one exponential per thread, not per element
+        self.exp_cache, self.exp_base, self.exp_corr = {}, {}, {}
+
+        def exp_reuse(x_reg, state):
+            e = self.exp_cache.get(x_reg)
+            if e is None or state not in self.exp_base:
+                return None
+            corr = self.exp_corr.get(state)
+            if corr is None:
+                d, corr = p.reg("f32"), p.reg("f32")
+                p.emit(f"sub.rn.f32 {d}, {self.exp_base[state]}, {ctx.f32(state)}")
+                emit_exp_nonpos(p, corr, d)
+                self.exp_corr[state] = corr
+            r = p.reg("f32")
+            p.emit(f"mul.rn.f32 {r}, {e}, {corr}")
+            return r
+        ctx.exp_reuse = exp_reuse if self.L % (self.TPR * self.VEC) == 0 else None
         # every accumulator starts at its op's identity before the first pass
         for ph in self.phases:
             if ph.kind == "stream":
@@ -287,6 +306,11 @@ class RowReduce:
                         p.emit(f"mov.f32 {r}, {f32_hex(float(acc.op.identity))}")
                         ctx.env[acc.name] = Val(r, "f32")
                         ctx.mutable.add(acc.name)
+        # every pass's column loads are independent of the row results: issue them all up
+        # front so the second pass's operands (e.g. RMSNorm's weight) are in flight with x
+        for ph in self.phases:
+            if ph.kind == "stream":
+                self._issue_loads(p, ph.stmt)
         smem_decls = []
         for n, ph in enumerate(self.phases):
             if ph.kind == "stream":
@@ -459,6 +483,8 @@ class RowReduce:
             p.emit(f"sub.rn.f32 {d}, {x}, {mt}")
             emit_exp_nonpos(p, e, d)
             es.append(e)
+            self.exp_cache[x] = e
+        self.exp_base[m] = mt
         lt = tree(es, "add.rn.f32")
         mr, lr = ctx.f32(m), ctx.f32(l)
         mn, d0, d1, a0, a1 = p.regs("f32", 5)
@@ -468,11 +494,10 @@ class RowReduce:
         p.emit(f"mul.rn.f32 {a0}, {lr}, {a0}\nfma.rn.f32 {lr}, {lt}, {a1}, {a0}\nmov.f32 {mr}, {mn}")
         ctx.max_states.add(m)
 
-    def _emit_stream(self, ctx: ScalarCtx, loop):
-        p = ctx.ptx
+    def _issue_loads(self, p, loop):
+        """Issue the pass's column loads (values already cached are not reloaded)."""
         span = self.TPR * self.VEC
         loads = [s for s in loop.body if type(s).__name__ == "Load" and id(s) in self.accesses]
-        # 1. issue every load of the pass (cached values are reused, not reloaded)
         for s in loads:
             acc = self.accesses[id(s)]
             if not acc.col_coef:
@@ -491,6 +516,13 @@ class RowReduce:
                 else:
                     p.emit(f"{guard}ld.global.f32 {regs[0]}, [{addr}+{off}]")
                 self.val_cache[key] = regs
+
+    def _emit_stream(self, ctx: ScalarCtx, loop):
+        p = ctx.ptx
+        span = self.TPR * self.VEC
+        loads = [s for s in loop.body if type(s).__name__ == "Load" and id(s) in self.accesses]
+        # 1. every column load of the pass was issued up front (_issue_loads)
+        self._issue_loads(p, loop)
         # row-constant loads inside the loop: one scalar load per row
         for s in loads:
             acc = self.accesses[id(s)]
@@ -640,7 +672,7 @@ class FullReduce:
 
     UNROLL = 8          # 128-bit loads in flight per thread per iteration
     CTA = 256
-    CTAS_PER_SM = 4     # one wave: 4 x 256 threads fit at the kernel's register count
+    CTAS_PER_SM = 8     # one wave: 8 x 256 threads fit at the kernel's 32 registers
 
     def __init__(self, spec):
         self.spec = spec
@@ -749,34 +781,39 @@ class FullReduce:
             p.emit(f"{combine_op} {accf}, {accf}, {mapped[0]}")
             return None
 
-        # ---- main grid-stride loop over whole UNROLL x VEC groups (64-bit offsets)
+        # ---- main grid-stride loop over warp spans of 32 x UNROLL x VEC elements
+        # (64-bit offsets): load u of a warp reads 32 consecutive vectors, so every
+        # load instruction is one fully coalesced 512-byte (VEC=4) access
         group = self.VEC * self.UNROLL
-        ngroups = self.count // group
-        stride_g = total_thr
-        gi, pg = p.reg("b64"), p.reg("pred")
+        span = 32 * group                        # elements per warp per iteration
+        nspans = self.count // span
+        nwarps = total_thr // 32
+        wi, pg = p.reg("b64"), p.reg("pred")
         loop, done = p.label("grp"), p.label("grp_done")
-        p.emit(f"mov.u64 {gi}, {gtid}")
+        lane0, wid = p.reg("u32"), p.reg("b64")
+        p.emit(f"and.b32 {lane0}, {tid}, 31\nshr.u64 {wid}, {gtid}, 5\nmov.u64 {wi}, {wid}")
+        lane_off = p.reg("b64")
+        p.emit(f"mul.wide.u32 {lane_off}, {lane0}, {self.VEC * 4}")
         p.place(loop)
-        p.emit(f"setp.ge.u64 {pg}, {gi}, {ngroups}\n@{pg} bra {done}")
+        p.emit(f"setp.ge.u64 {pg}, {wi}, {nspans}\n@{pg} bra {done}")
         addr = p.reg("b64")
-        # group gi covers elements [gi*group, gi*group+group): UNROLL vectors spaced by VEC
-        p.emit(f"mad.lo.s64 {addr}, {gi}, {group * 4}, {x}")
+        p.emit(f"mad.lo.s64 {addr}, {wi}, {span * 4}, {x}\nadd.s64 {addr}, {addr}, {lane_off}")
         vals = []
         for u in range(self.UNROLL):
             regs = p.regs("f32", self.VEC)
             if self.VEC == 4:
-                p.emit(f"ld.global.nc.L1::no_allocate.v4.f32 {{{', '.join(regs)}}}, [{addr}+{u * 16}]")
+                p.emit(f"ld.global.nc.L1::no_allocate.v4.f32 {{{', '.join(regs)}}}, [{addr}+{u * 32 * 16}]")
             else:
-                p.emit(f"ld.global.nc.f32 {regs[0]}, [{addr}+{u * 4}]")
+                p.emit(f"ld.global.nc.f32 {regs[0]}, [{addr}+{u * 32 * 4}]")
             vals += regs
         grp = fold_elements(vals)
         if is_add:
             gd = p.reg("f64")
             p.emit(f"cvt.f64.f32 {gd}, {grp}\nadd.rn.f64 {accd}, {accd}, {gd}")
-        p.emit(f"add.s64 {gi}, {gi}, {stride_g}\nbra.uni {loop}")
+        p.emit(f"add.s64 {wi}, {wi}, {nwarps}\nbra.uni {loop}")
         p.place(done)
-        # ---- tail elements (count not a multiple of the group): one per thread
-        tail0 = ngroups * group
+        # ---- tail elements (count not a multiple of a warp span): one per thread
+        tail0 = nspans * span
         if tail0 < self.count:
             ti, pt = p.reg("b64"), p.reg("pred")
             tl, td = p.label("tail"), p.label("tail_done")

@@ -63,6 +63,7 @@ class Val:
     kind: str          # "f32" | "s32" | "pred"
     const: float | None = None
     nonpos: bool = False   # known <= 0 (an element minus the row maximum)
+    diff: tuple | None = None   # (element register, max state) when the value is their difference
 
 
 @dataclass
@@ -75,6 +76,7 @@ class ScalarCtx:
     on_write: Callable | None = None                 # fn(ctx, Write) -> None
     axis_regs: dict = field(default_factory=dict)    # axis name -> s32 register / immediate
     max_states: set = field(default_factory=set)     # accumulators holding a row maximum
+    exp_reuse: Callable | None = None                # fn(element register, max state) -> register
 
     def bind(self, name: str, val: Val) -> None:
         if name in self.mutable and name in self.env:
@@ -186,8 +188,13 @@ def compute_f32(ctx: ScalarCtx, op: str, args: list[str], dst: str | None = None
     out = dst or p.reg("f32")
     if op == "subtract" and len(args) == 2 and args[1] in ctx.max_states:
         _binary(p, op, out, vals[0], vals[1])
-        return Val(out, "f32", nonpos=True)
+        return Val(out, "f32", nonpos=True, diff=(vals[0], args[1]))
     if op == "exp" and len(args) == 1 and ctx.get(args[0]).nonpos:
+        v = ctx.get(args[0])
+        if ctx.exp_reuse is not None and v.diff is not None:
+            r = ctx.exp_reuse(*v.diff)
+            if r is not None:
+                return Val(r, "f32")
         emit_exp_nonpos(p, out, vals[0])
         return Val(out, "f32")
     if len(vals) == 1:
