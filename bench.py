@@ -364,8 +364,10 @@ def run_ours(args, dist: Dist) -> int:
         comm = NcclComm(uid, dist.world, dist.rank)
         out_ptrs = [bs[[a["name"] for a in k["args"] if a.get("output")][0]].ptr for bs in bufsets]
 
+    fire = [ck.prepare(pp) for pp in params]
+
     def step(i):
-        ck(None, stream, params[i % copies])
+        fire[i % copies](stream)
         if comm is not None:
             o = out_ptrs[i % copies]
             comm.allreduce(o, o, 1, stream=stream)

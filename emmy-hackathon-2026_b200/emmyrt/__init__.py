@@ -285,6 +285,27 @@ def function_attribute(fn: int, attr: int) -> int:
     return v.value
 
 
+class PreparedLaunch:
+    """A launch whose argument arrays are built once: each call is one C call (no
+    per-launch Python marshalling), so back-to-back launches keep the GPU fed."""
+
+    def __init__(self, fn: int, grid, block, cluster, smem: int, params: list):
+        self.fn, self.smem = fn, smem
+        self.g = (ctypes.c_uint * 3)(*grid)
+        self.b = (ctypes.c_uint * 3)(*block)
+        self.c = (ctypes.c_uint * 3)(*(cluster or (1, 1, 1)))
+        self.params = params
+        self.arr = (ctypes.c_void_p * max(1, len(params)))(
+            *[ctypes.cast(ctypes.pointer(p), ctypes.c_void_p) if not isinstance(p, ctypes.Array)
+              else ctypes.cast(p, ctypes.c_void_p) for p in params])
+        self._launch = lib.emmy_rt_launch
+
+    def __call__(self, stream: int = 0) -> None:
+        st = self._launch(self.fn, self.g, self.b, self.c, self.smem, stream, self.arr)
+        if st:
+            check(st, "launch")
+
+
 def launch(fn: int, grid, block, cluster, smem: int, stream: int, params: list) -> None:
     """``params``: one ctypes object per kernel parameter (c_uint64 pointers, tensor
     map byte arrays, scalars), in signature order."""

@@ -26,8 +26,8 @@ from pathlib import Path
 
 import numpy as np
 
-from . import (DeviceBuffer, Event, Module, function_attribute, init, launch, stream_wait,
-               tensor_map, CU_FUNC_ATTRIBUTE_NUM_REGS, lib, check)
+from . import (DeviceBuffer, Event, Module, PreparedLaunch, function_attribute, init, launch,
+               stream_wait, tensor_map, CU_FUNC_ATTRIBUTE_NUM_REGS, lib, check)
 
 _PKG = Path(__file__).resolve().parents[1]
 if str(_PKG) not in sys.path:
@@ -161,6 +161,12 @@ class CompiledKernel:
         launch(self.function, d["grid"], d["block"], d.get("cluster", [1, 1, 1]), d.get("smem", 0),
                stream, params if params is not None else self.params(ptrs))
 
+    def prepare(self, params: list) -> PreparedLaunch:
+        """A ready-to-fire launch of this kernel with fixed parameters."""
+        d = self.launch
+        return PreparedLaunch(self.function, d["grid"], d["block"], d.get("cluster", [1, 1, 1]),
+                              d.get("smem", 0), params)
+
     def status(self) -> int:
         """The kernel's device status word (0 = ok; non-zero = a bounded wait gave up)."""
         for i, extra in enumerate(self.launch.get("extra_params", [])):
@@ -217,17 +223,16 @@ def run_problem(pdir, iters: int = 0, timeout_s: float = 60.0, device: int = 0) 
             raise RuntimeError(f"{k['entry']}: kernel reported status {ck.status()}")
         us = None
         if iters:
+            fire = ck.prepare(params)
             e0, e1 = Event(), Event()
-            times = []
+            e0.record(0)
             for _ in range(iters):
                 for z in k.get("zero_outputs", []):
                     bufs[z].zero()
-                e0.record(0)
-                ck(ptrs, 0, params)
-                e1.record(0)
-                e1.synchronize()
-                times.append(e0.elapsed_ms(e1) * 1e3)
-            us = float(np.median(times))
+                fire(0)
+            e1.record(0)
+            e1.synchronize()
+            us = e0.elapsed_ms(e1) * 1e3 / iters
             for z in k.get("zero_outputs", []):   # leave the single-launch result
                 bufs[z].zero()
             ck(ptrs, 0, params)
