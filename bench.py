@@ -257,6 +257,18 @@ def cpu_sample_fn(name: str, inputs: dict, meta: dict, target_s: float = 2.0):
         sub = A[:rows]
         return (lambda: refs.mm_bf16(sub, B)), 2.0 * rows * B.shape[0] * B.shape[1], \
             f"{rows} rows of A against the full B (oracle mm_bf16, f64 BLAS)"
+    if name == "attention":
+        q, k, v = (bf16_bits_to_f32(inputs[n]) for n in ("x0", "x1", "x2"))
+        S, D = q.shape[-2], q.shape[-1]
+        scale = 1.0 / np.sqrt(D)
+        rows = 64
+        t0 = time.perf_counter()
+        refs.attn_bf16(q[0, 0, :rows], k[0, 0], v[0, 0], scale)
+        dt = time.perf_counter() - t0
+        rows = int(max(1, min(S, rows * max(1.0, target_s / max(dt, 1e-3)))))
+        sub = q[0, 0, :rows]
+        return (lambda: refs.attn_bf16(sub, k[0, 0], v[0, 0], scale)), 4.0 * rows * S * D, \
+            f"{rows} query rows of one batch x head pair against its {S} keys (oracle attn_bf16, f64)"
     if name == "rmsnorm":
         x, w = inputs["x0"], inputs["x1"]
         return (lambda: refs.rmsnorm(x, w, 1e-6)), float(2 * x.nbytes + w.nbytes), "full 4096x4096"

@@ -5,24 +5,33 @@ Replaces the reference's register-fragment flash attention (``compiler/mma.py``:
 row max / sum by 2-step shuffles, ``FragmentRepack`` P -> A fragment; K and V read
 straight from global memory, ``tests/problems/x_h_attn_128``, ``x_h_sdpa``).
 
-Kernel structure (one CTA per 2 x 128 query rows of one batch x head):
+Kernel structure (one CTA per NQ = 2 query tiles of 128 rows of one batch x head;
+128 * (NQ + 1) threads, one warpgroup per query tile plus a control warpgroup):
 
-* warp 0, lane 0 -- TMA: Q tiles once, then K_j and V_j (128 keys each) through a
-  3-slot ring of 128-byte-swizzled shared memory, full/empty mbarrier per slot;
-* warp 1 -- TMEM allocation (S0, S1: 128 f32 columns each; O0, O1: D columns each)
-  and, on lane 0, the MMA stream: ``S_t = Q_t K_j^T`` (kind::f16, M=128, N=128),
-  then per tile ``O_t += P_t V_j`` as soon as softmax warpgroup t hands P_t over,
-  immediately followed by ``S_t = Q_t K_{j+1}^T`` -- so one warpgroup's softmax
-  overlaps the other's matrix products;
-* warps 2-5 / 6-9 -- softmax warpgroup per query tile, one thread per query row:
-  pass A reads the S row from TMEM (``tcgen05.ld.32x32b.x32``) for its maximum,
-  pass B reads it again and forms ``p = 2^(s*scale*log2e - m)`` (one FFMA and one
-  ``ex2.approx``), accumulates the row sum in f32, packs P to bf16/f16 and stores it
-  into the 128B-swizzled K-major layout the PV MMA reads as its A operand;
-  the running max is updated lazily -- O (in TMEM) is rescaled only when the max
-  grows by more than 2^8, so most blocks skip the correction; the final
-  normalisation by 1/l makes the result exact either way;
-* epilogue (same warps): O row from TMEM, times 1/l, to bf16/f16, 128-bit stores.
+* softmax warpgroup t (warps 4t .. 4t+3), one thread per query row (TMEM lane):
+  reads its whole 128-key S row out of TMEM in one go (four ``tcgen05.ld.32x32b.x32``,
+  one wait), takes the row maximum with three-input ``max``, forms
+  ``p = 2^(s*scale*log2e - m)`` (packed ``fma.rn.f32x2`` and ``ex2.approx``, part of
+  them optionally on the FMA pipe by a cubic), accumulates the row sum in f32, packs P
+  to bf16/f16 and stores it into TMEM over the S columns it has consumed, where the PV
+  MMA reads it as its A operand (optionally into a 128B-swizzled K-major shared-memory
+  tile instead, which costs the ring two slots).  The running max is updated
+  lazily: O (in TMEM) is rescaled only when the max grows by more than 2^8, so most
+  blocks skip the correction; the final normalisation by 1/l makes the result exact
+  either way.  With two query tiles the control warpgroup hands its registers to the
+  softmax warpgroups (``setmaxnreg``), so the S row, the probabilities and the
+  addresses stay in registers;
+* control warpgroup: warp 4NQ, lane 0 -- TMA: Q tiles once, then K_j and V_j (128 keys
+  each) through a ring of 128-byte-swizzled shared-memory slots (as many as shared
+  memory holds: 5 at D = 128), full/empty mbarrier per slot; warp 4NQ+1 -- TMEM
+  allocation (S_t: 128 f32 columns, O_t: D columns per tile) and, on lane 0, the MMA
+  stream: ``S_t = Q_t K_j^T`` (kind::f16, M=128,
+  N=128); per tile ``O_t += P_t V_j`` as soon as softmax t hands P_t over, followed by
+  ``S_t = Q_t K_{j+1}^T``, so one warpgroup's softmax overlaps the other tile's
+  matrix products.  The commit that signals S_t(j+1) also covers O_t += P_t(j) V_j
+  (tcgen05 operations of one thread complete in order), so softmax t may reuse its P
+  buffer and rescale O_t as soon as it sees S_t(j+1);
+* epilogue (softmax warps): O row from TMEM, times 1/l, to bf16/f16, 128-bit stores.
 
 The online-softmax state (m, l) is f32.  Every mbarrier wait is bounded.
 """
@@ -39,6 +48,7 @@ from .tc import Waits, instr_desc, smem_desc_hi, smem_desc_lo_const
 LOG2E = 1.4426950408889634
 AB_FORMAT = {"f16": 0, "bf16": 1}
 RESCALE_LOG2 = 8.0          # rescale O only when the row max grows by more than 2^8
+REGS_CONTROL = 56           # registers per thread left to the control warpgroup (NQ = 2)
 
 
 @dataclass
@@ -57,10 +67,9 @@ class AttnConfig:
     o_param: str = "o"
     arg_params: list | None = None
     buffers: tuple = ()
-    ring: int = 3
-    s_group: int = 1         # S chunks (of 32 columns) per tcgen05.wait::ld; 4 = read S once
+    ring: int | None = None  # K/V ring slots (None: as many as shared memory holds, up to 6)
     poly_every: int = 0      # every n-th probability from the FMA-pipe exp2 (0: all on MUFU)
-    p_tmem: bool = False     # P kept in TMEM over the consumed S columns (A operand from TMEM)
+    p_tmem: bool = True      # P kept in TMEM over the consumed S columns (A operand from TMEM)
 
     @property
     def DP(self) -> int:                 # head dim padded to whole 64-element swizzle rows
@@ -69,6 +78,23 @@ class AttnConfig:
     @property
     def NQ(self) -> int:
         return 2 if self.Sq > 128 else 1
+
+
+def register_split(nq: int) -> tuple[int, int, int]:
+    """(launch cap, control warpgroup, softmax warpgroups) registers per thread.
+
+    The block is launched with ``cap`` registers per thread (all of the SM's 64K over
+    128 * (nq + 1) threads); with two query tiles the control warpgroup gives up all
+    but REGS_CONTROL and the softmax warpgroups take them over (``setmaxnreg``).  The
+    split never asks for more than the launch holds."""
+    nthreads = 128 * (nq + 1)
+    cap = min(65536 // nthreads // 8 * 8, 232)
+    if nq == 1:
+        return cap, cap, cap
+    freed = (cap - REGS_CONTROL) * 128
+    soft = min(cap + freed // (128 * nq) // 8 * 8, 248)
+    assert 128 * REGS_CONTROL + 128 * nq * soft <= nthreads * cap
+    return cap, REGS_CONTROL, soft
 
 
 def emit_attention_module(cfg: AttnConfig) -> str:
@@ -81,16 +107,19 @@ def emit_attention_module(cfg: AttnConfig) -> str:
     if cfg.kt_layout and cfg.Sk % 8:
         raise NotImplementedError("pre-transposed K rows not 16-byte aligned")
     p = Ptx()
-    NQ, DP, R = cfg.NQ, cfg.DP, cfg.ring
+    NQ, DP = cfg.NQ, cfg.DP
     nblk = -(-cfg.Sk // 128)
     tile_bytes = 128 * DP * 2             # a Q or K or V tile
     p_bytes = 128 * 128 * 2
+    smem_cap = 232448 - 512
+    R = cfg.ring
+    if R is None:
+        free = smem_cap - 1024 - NQ * tile_bytes - (0 if cfg.p_tmem else NQ * p_bytes)
+        R = max(2, min(6, free // tile_bytes))
     q_off, ring_off = 0, NQ * tile_bytes
     p_off = ring_off + R * tile_bytes
     smem = p_off + (0 if cfg.p_tmem else NQ * p_bytes) + 1024
-    if cfg.p_tmem and cfg.s_group != 1:
-        raise NotImplementedError("P in TMEM overwrites S chunk by chunk: s_group must be 1")
-    if smem > 232448 - 512:
+    if smem > smem_cap:
         raise NotImplementedError("attention tiles exceed shared memory")
     ncols_used = NQ * (128 + DP)
     ncols = max(32, 1 << math.ceil(math.log2(ncols_used)))
@@ -102,8 +131,10 @@ def emit_attention_module(cfg: AttnConfig) -> str:
     kt_lo = smem_desc_lo_const(DP * 128)        # kt: 64-key blocks of DP d-rows
     v_lo = smem_desc_lo_const(128 * 128)        # V: 64-d blocks of 128 key-rows
     scale_log2 = cfg.scale * LOG2E
-    nthreads = 64 + 128 * NQ
+    nthreads = 128 * (NQ + 1)
+    W_TMA, W_MMA = 4 * NQ, 4 * NQ + 1           # the control warpgroup's working warps
     masked = cfg.Sk % 128 != 0
+    cap, regs_ctl, regs_soft = register_split(NQ)
 
     p.comment(f"tcgen05 attention BH={cfg.BH} Sq={cfg.Sq} Sk={cfg.Sk} D={cfg.D} {cfg.dtype}, "
               f"{NQ} query tiles per CTA, {nblk} key blocks, scale={cfg.scale}")
@@ -147,7 +178,7 @@ def emit_attention_module(cfg: AttnConfig) -> str:
     p.place(l_init)
     p1 = p.reg("pred")
     l_alloc = p.label("alloc_done")
-    p.emit(f"setp.ne.u32 {p1}, {warp}, 1\n@{p1} bra {l_alloc}")
+    p.emit(f"setp.ne.u32 {p1}, {warp}, {W_MMA}\n@{p1} bra {l_alloc}")
     p.emit(f"tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [{tslot}], {ncols}\n"
            f"tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned")
     p.place(l_alloc)
@@ -170,10 +201,18 @@ def emit_attention_module(cfg: AttnConfig) -> str:
         p.emit(f"add.u32 {slot}, {slot}, 1\nsetp.eq.u32 {ps}, {slot}, {R}\n"
                f"@{ps} mov.u32 {slot}, 0\n@{ps} xor.b32 {ph}, {ph}, 1")
 
-    # ------------------------------------------------------------------ producer
-    l_mma, l_soft = p.label("role_mma"), p.label("role_softmax")
+    # -------------------------------------------------------------- role dispatch
+    l_ctl, l_soft = p.label("role_control"), p.label("role_softmax")
+    pc = p.reg("pred")
+    p.emit(f"setp.lt.u32 {pc}, {warp}, {4 * NQ}\n@{pc} bra {l_soft}")
+    p.place(l_ctl)
+    if NQ == 2:
+        p.emit(f"setmaxnreg.dec.sync.aligned.u32 {regs_ctl}")
+    l_mma = p.label("role_mma")
     pr, pl = p.reg("pred"), p.reg("pred")
-    p.emit(f"setp.ne.u32 {pr}, {warp}, 0\n@{pr} bra {l_mma}\nsetp.ne.u32 {pl}, {lane}, 0\n@{pl} bra {finish}")
+    p.emit(f"setp.ne.u32 {pr}, {warp}, {W_TMA}\n@{pr} bra {l_mma}\nsetp.ne.u32 {pl}, {lane}, 0\n@{pl} bra {finish}")
+
+    # ------------------------------------------------------------------ producer
     p.emit(f"prefetch.tensormap [{tq}]\nprefetch.tensormap [{tk}]\nprefetch.tensormap [{tv}]")
     qb = p.reg("u32")
     p.emit(f"add.u32 {qb}, {bars}, {B_Q}\nmbarrier.arrive.expect_tx.shared::cta.b64 _, [{qb}], {NQ * tile_bytes}")
@@ -219,7 +258,7 @@ def emit_attention_module(cfg: AttnConfig) -> str:
 
     # ----------------------------------------------------------------------- MMA
     p.place(l_mma)
-    p.emit(f"setp.ne.u32 {pr}, {warp}, 1\n@{pr} bra {l_soft}\nsetp.ne.u32 {pl}, {lane}, 0\n@{pl} bra {finish}")
+    p.emit(f"setp.ne.u32 {pr}, {warp}, {W_MMA}\n@{pr} bra {finish}\nsetp.ne.u32 {pl}, {lane}, 0\n@{pl} bra {finish}")
     zero = p.reg("u32")
     p.emit(f"mov.u32 {zero}, 0")
     waits.wait(_addr(p, bars, B_Q), zero, "mma", finish)
@@ -333,7 +372,9 @@ def emit_attention_module(cfg: AttnConfig) -> str:
 
     # ------------------------------------------------------------------ softmax
     p.place(l_soft)
-    _emit_softmax(p, cfg, ptr, bars, B_S, B_P, B_O, tbase, base, p_off, p_bytes, warp, lane, tid,
+    if NQ == 2:
+        p.emit(f"setmaxnreg.inc.sync.aligned.u32 {regs_soft}")
+    _emit_softmax(p, cfg, ptr, bars, B_S, B_P, B_O, tbase, base, p_off, p_bytes, warp, lane,
                   q0, bh, nblk, scale_log2, masked, waits, finish)
 
     # ------------------------------------------------------------------- finish
@@ -344,7 +385,7 @@ def emit_attention_module(cfg: AttnConfig) -> str:
         tcgen05.fence::before_thread_sync
         barrier.sync 0
         tcgen05.fence::after_thread_sync
-        setp.ne.u32 {pw1}, {warp}, 1
+        setp.ne.u32 {pw1}, {warp}, {W_MMA}
         @{pw1} bra {done}
         bar.warp.sync -1
         tcgen05.dealloc.cta_group::1.sync.aligned.b32 {tbase}, {ncols}
@@ -355,13 +396,9 @@ def emit_attention_module(cfg: AttnConfig) -> str:
     params = list(cfg.arg_params or [f".param .u64 {param_symbol(n)}" for n in cfg.buffers])
     params += [".param .align 64 .b8 param__tmap_q[128]", ".param .align 64 .b8 param__tmap_k[128]",
                ".param .align 64 .b8 param__tmap_v[128]", ".param .u64 param__status"]
-    # one CTA per SM (its shared memory allows no more): let ptxas use the whole register file
-    # registers come from 4 sub-partitions of 16K; warps are spread over them, so the
-    # busiest sub-partition (ceil(warps / 4) warps) sets the per-thread cap
-    warps = nthreads // 32
-    regcap = (16384 // (32 * -(-warps // 4))) // 8 * 8
-    text = entry(cfg.name, params, p, maxntid=nthreads,
-                 extra_directives=f"\n.maxnreg {min(regcap, 232)}")
+    # one CTA per SM (its shared memory allows no more): the launch takes the whole
+    # register file, which setmaxnreg then redistributes between the warpgroups
+    text = entry(cfg.name, params, p, maxntid=nthreads, extra_directives=f"\n.maxnreg {cap}")
     statics = (f"\t.shared .align 8 .b64 gbars[{nbar}];\n\t.shared .align 4 .u32 gabort;\n"
                f"\t.shared .align 4 .u32 gtmem;\n")
     text = text.replace("{\n", "{\n" + statics, 1)
@@ -421,14 +458,36 @@ def _addr(p: Ptx, base: str, off: int) -> str:
     return r
 
 
+def _max_tree(p: Ptx, vals: list) -> str:
+    """Maximum of ``vals`` by a tree of three-input ``max.f32``."""
+    red = list(vals)
+    while len(red) > 1:
+        nxt = []
+        i = 0
+        while i < len(red):
+            if len(red) - i >= 3:
+                r = p.reg("f32")
+                p.emit(f"max.f32 {r}, {red[i]}, {red[i + 1]}, {red[i + 2]}")
+                i += 3
+            elif len(red) - i == 2:
+                r = p.reg("f32")
+                p.emit(f"max.f32 {r}, {red[i]}, {red[i + 1]}")
+                i += 2
+            else:
+                r = red[i]
+                i += 1
+            nxt.append(r)
+        red = nxt
+    return red[0]
+
+
 def _emit_softmax(p: Ptx, cfg: AttnConfig, ptr, bars, B_S, B_P, B_O, tbase, base, p_off, p_bytes,
-                  warp, lane, tid, q0, bh, nblk, scale_log2, masked, waits: Waits, finish):
+                  warp, lane, q0, bh, nblk, scale_log2, masked, waits: Waits, finish):
     NQ, DP = cfg.NQ, cfg.DP
     t, q, row, lanebits = p.regs("u32", 4)
-    # warps 2..5 -> tile 0, 6..9 -> tile 1; TMEM lane quarter = warp % 4
+    # warps 0..3 -> tile 0, 4..7 -> tile 1; TMEM lane quarter = warp % 4
     p.emit(f"""
-        sub.u32 {t}, {warp}, 2
-        shr.u32 {t}, {t}, 2
+        shr.u32 {t}, {warp}, 2
         and.b32 {q}, {warp}, 3
         mad.lo.u32 {row}, {q}, 32, {lane}
         shl.b32 {lanebits}, {q}, 21
@@ -450,77 +509,52 @@ def _emit_softmax(p: Ptx, cfg: AttnConfig, ptr, bars, B_S, B_P, B_O, tbase, base
     """)
     # this thread's P row in smem: tile t, row r; 16-byte chunk c of a 64-key block
     # lives at chunk (c ^ (r % 8)) of the row (128-byte swizzle)
-    prow, rx = p.reg("u32"), p.reg("u32")
-    p.emit(f"""
-        mad.lo.u32 {prow}, {t}, {p_bytes}, {base}
-        add.u32 {prow}, {prow}, {p_off}
-        mad.lo.u32 {prow}, {row}, 128, {prow}
-        and.b32 {rx}, {row}, 7
-    """)
     chunk_addr = {}
-    for c16 in range(16):            # 16 chunks of 8 keys = 128 keys
-        blk, c = c16 // 8, c16 % 8
-        a = p.reg("u32")
-        p.emit(f"xor.b32 {a}, {rx}, {c}\nmad.lo.u32 {a}, {a}, 16, {prow}\nadd.u32 {a}, {a}, {blk * 16384}")
-        chunk_addr[c16] = a
+    if not cfg.p_tmem:
+        prow, rx = p.reg("u32"), p.reg("u32")
+        p.emit(f"""
+            mad.lo.u32 {prow}, {t}, {p_bytes}, {base}
+            add.u32 {prow}, {prow}, {p_off}
+            mad.lo.u32 {prow}, {row}, 128, {prow}
+            and.b32 {rx}, {row}, 7
+        """)
+        for c16 in range(16):            # 16 chunks of 8 keys = 128 keys
+            blk, c = c16 // 8, c16 % 8
+            a = p.reg("u32")
+            p.emit(f"xor.b32 {a}, {rx}, {c}\nmad.lo.u32 {a}, {a}, 16, {prow}\nadd.u32 {a}, {a}, {blk * 16384}")
+            chunk_addr[c16] = a
     m, l = p.reg("f32"), p.reg("f32")
     p.emit(f"mov.f32 {m}, 0fF149F2CA\nmov.f32 {l}, 0f00000000")     # m = -1e30 (log2 domain)
+    cvt = "cvt.rn.bf16x2.f32" if cfg.dtype == "bf16" else "cvt.rn.f16x2.f32"
+    sl2, slr = p.reg("b64"), p.reg("f32")
+    p.emit(f"mov.f32 {slr}, {f32_hex(scale_log2)}\nmov.b64 {sl2}, {{{slr}, {slr}}}")
     jj = p.reg("u32")
     p.emit(f"mov.u32 {jj}, 0")
     l_blk = p.label("s_blk")
     p.place(l_blk)
     par = p.reg("u32")
     p.emit(f"and.b32 {par}, {jj}, 1")
+    # S_t(j) complete; its commit also covers O_t += P_t(j-1) V_{j-1}, so the P buffer
+    # is free and O_t holds every earlier block
     waits.wait(sbar, par, "softmax", finish)
     p.emit("bar.warp.sync -1\ntcgen05.fence::after_thread_sync")
-    G = cfg.s_group
-    keyb = None
+    # the whole S row in registers: four loads in flight, one wait
+    sv = [p.reg("b32") for _ in range(128)]
+    for c in range(4):
+        p.emit(f"tcgen05.ld.sync.aligned.32x32b.x32.b32 {{{', '.join(sv[32 * c:32 * c + 32])}}}, "
+               f"[{s_ta}+{c * 32}]")
+    p.emit("tcgen05.wait::ld.sync.aligned")
+    fv = [p.reg("f32") for _ in range(128)]
+    for i in range(128):
+        p.emit(f"mov.b32 {fv[i]}, {sv[i]}")
     if masked:
         keyb = p.reg("u32")
         p.emit(f"mul.lo.u32 {keyb}, {jj}, 128")
-    regsets = [[p.reg("b32") for _ in range(32 * G)] for _ in range(1 if G < 4 else 1)]
-    fsets = [[p.reg("f32") for _ in range(32 * G)]]
-
-    def load_group(g):
-        """S chunks g*G .. g*G+G-1 into registers: G loads in flight, one wait."""
-        vals, fv = regsets[0], fsets[0]
-        for k in range(G):
-            c = g * G + k
-            p.emit(f"tcgen05.ld.sync.aligned.32x32b.x32.b32 {{{', '.join(vals[32 * k:32 * k + 32])}}}, "
-                   f"[{s_ta}+{c * 32}]")
-        p.emit("tcgen05.wait::ld.sync.aligned")
-        for i in range(32 * G):
-            p.emit(f"mov.b32 {fv[i]}, {vals[i]}")
-        if masked:
-            for i in range(32 * G):
-                pk, kx = p.reg("pred"), p.reg("u32")
-                p.emit(f"add.u32 {kx}, {keyb}, {g * G * 32 + i}\nsetp.ge.u32 {pk}, {kx}, {cfg.Sk}\n"
-                       f"@{pk} mov.f32 {fv[i]}, 0fFF800000")
-        return fv
-
-    # pass A: row maximum of the raw scores
-    mx = p.reg("f32")
-    p.emit(f"mov.f32 {mx}, 0fFF800000")
-    for g in range(4 // G):
-        red = list(load_group(g)) + [mx]
-        while len(red) > 1:                  # three-input max tree
-            nxt = []
-            i = 0
-            while i < len(red):
-                r = p.reg("f32")
-                if len(red) - i >= 3:
-                    p.emit(f"max.f32 {r}, {red[i]}, {red[i + 1]}, {red[i + 2]}")
-                    i += 3
-                elif len(red) - i == 2:
-                    p.emit(f"max.f32 {r}, {red[i]}, {red[i + 1]}")
-                    i += 2
-                else:
-                    nxt.append(red[i])
-                    i += 1
-                    continue
-                nxt.append(r)
-            red = nxt
-        p.emit(f"mov.f32 {mx}, {red[0]}")
+        for i in range(128):
+            pk, kx = p.reg("pred"), p.reg("u32")
+            p.emit(f"add.u32 {kx}, {keyb}, {i}\nsetp.ge.u32 {pk}, {kx}, {cfg.Sk}\n"
+                   f"@{pk} mov.f32 {fv[i]}, 0fFF800000")
+    mx = _max_tree(p, fv)
     mn, alpha, thr = p.reg("f32"), p.reg("f32"), p.reg("f32")
     prs, pfirst = p.reg("pred"), p.reg("pred")
     p.emit(f"""
@@ -542,13 +576,6 @@ def _emit_softmax(p: Ptx, cfg: AttnConfig, ptr, bars, B_S, B_P, B_O, tbase, base
         @{prs} mov.f32 {m}, {mn}
         mul.rn.f32 {l}, {l}, {alpha}
     """)
-    # P buffer and O are free once the previous block's PV finished
-    l_nowait = p.label("s_nowait")
-    p.emit(f"@{pfirst} bra {l_nowait}")
-    par2 = p.reg("u32")
-    p.emit(f"sub.u32 {par2}, {jj}, 1\nand.b32 {par2}, {par2}, 1")
-    waits.wait(obar, par2, "softmax", finish)
-    p.emit("bar.warp.sync -1\ntcgen05.fence::after_thread_sync")
     # lazy O correction: the whole warp takes part when any of its rows needs it
     pany = p.reg("pred")
     l_nores = p.label("s_nores")
@@ -563,26 +590,15 @@ def _emit_softmax(p: Ptx, cfg: AttnConfig, ptr, bars, B_S, B_P, B_O, tbase, base
         p.emit(f"tcgen05.st.sync.aligned.32x32b.x32.b32 [{o_ta}+{c * 32}], {{{', '.join(ov)}}}")
     p.emit("tcgen05.wait::st.sync.aligned")
     p.place(l_nores)
-    p.place(l_nowait)
-    # pass B: p = 2^(s*scale*log2e - m), row sum, bf16/f16 pack into the swizzled P tile
-    negm = p.reg("f32")
-    p.emit(f"neg.f32 {negm}, {m}")
-    cvt = "cvt.rn.bf16x2.f32" if cfg.dtype == "bf16" else "cvt.rn.f16x2.f32"
-    fv = fsets[0]
-    # packed f32x2 operands: (scale*log2e, scale*log2e) and (-m, -m)
-    sl2, nm2 = p.reg("b64"), p.reg("b64")
-    slr = p.reg("f32")
-    p.emit(f"mov.f32 {slr}, {f32_hex(scale_log2)}\nmov.b64 {sl2}, {{{slr}, {slr}}}\n"
-           f"mov.b64 {nm2}, {{{negm}, {negm}}}")
+    # p = 2^(s*scale*log2e - m), row sum, bf16/f16 pack into the swizzled P tile
+    negm, nm2 = p.reg("f32"), p.reg("b64")
+    p.emit(f"neg.f32 {negm}, {m}\nmov.b64 {nm2}, {{{negm}, {negm}}}")
     for c in range(4):
-        if G < 4 and c % G == 0:
-            fv = load_group(c // G)          # read this group of S again
-        base_i = 32 * (c % G) if G < 4 else 32 * c
         ps = []
-        for i in range(0, 32, 2):
+        for i in range(32 * c, 32 * c + 32, 2):
             x2, e2 = p.reg("b64"), p.reg("b64")
             ea, eb = p.reg("f32"), p.reg("f32")
-            p.emit(f"mov.b64 {x2}, {{{fv[base_i + i]}, {fv[base_i + i + 1]}}}\n"
+            p.emit(f"mov.b64 {x2}, {{{fv[i]}, {fv[i + 1]}}}\n"
                    f"fma.rn.f32x2 {e2}, {x2}, {sl2}, {nm2}\nmov.b64 {{{ea}, {eb}}}, {e2}")
             for k, e in ((i, ea), (i + 1, eb)):
                 if cfg.poly_every and not masked and k % cfg.poly_every == cfg.poly_every - 1:
@@ -626,7 +642,7 @@ def _emit_softmax(p: Ptx, cfg: AttnConfig, ptr, bars, B_S, B_P, B_O, tbase, base
     """)
     pj = p.reg("pred")
     p.emit(f"setp.lt.u32 {pj}, {jj}, {nblk}\n@{pj} bra {l_blk}")
-    # epilogue: O / l
+    # epilogue: O / l once the last O_t += P_t V has landed
     parf = p.reg("u32")
     p.emit(f"mov.u32 {parf}, {(nblk - 1) & 1}")
     waits.wait(obar, parf, "softmax", finish)
