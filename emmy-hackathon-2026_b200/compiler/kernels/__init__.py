@@ -25,6 +25,16 @@ def select(spec) -> str:
         from .gemm import emit_gemm
         return emit_gemm(spec)
     if _has(body, {"WarpShuffle"}):
+        # emmy's SIMT form of attention (an online softmax over streamed keys) runs on the
+        # tensor-core attention template; every other cooperative reduction on the
+        # streaming reduction template
+        from .attention import analyze_simt, emit_attention_module
+        try:
+            cfg = analyze_simt(spec)
+        except NotImplementedError:
+            cfg = None
+        if cfg is not None:
+            return emit_attention_module(cfg)
         from .reduce import emit_reduction
         return emit_reduction(spec)
     raise NotImplementedError(

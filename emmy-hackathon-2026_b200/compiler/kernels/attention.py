@@ -49,6 +49,7 @@ LOG2E = 1.4426950408889634
 AB_FORMAT = {"f16": 0, "bf16": 1}
 RESCALE_LOG2 = 8.0          # rescale O only when the row max grows by more than 2^8
 REGS_CONTROL = 56           # registers per thread left to the control warpgroup (NQ = 2)
+MASK_BYTES = {"f16": 2, "bf16": 2, "f32": 4}
 
 
 @dataclass
@@ -70,6 +71,10 @@ class AttnConfig:
     ring: int | None = None  # K/V ring slots (None: as many as shared memory holds, up to 6)
     poly_every: int = 0      # every n-th probability from the FMA-pipe exp2 (0: all on MUFU)
     p_tmem: bool = True      # P kept in TMEM over the consumed S columns (A operand from TMEM)
+    causal: bool = False     # key j > query i masked out (top-left aligned, as is_causal / tril)
+    mask_param: str | None = None   # additive score mask buffer, [.., Sq, Sk] row-major
+    mask_dtype: str = "f16"
+    mask_bh_stride: int = 0  # elements between the masks of consecutive batch x heads (0: shared)
 
     @property
     def DP(self) -> int:                 # head dim padded to whole 64-element swizzle rows
@@ -121,6 +126,11 @@ def emit_attention_module(cfg: AttnConfig) -> str:
     smem = p_off + (0 if cfg.p_tmem else NQ * p_bytes) + 1024
     if smem > smem_cap:
         raise NotImplementedError("attention tiles exceed shared memory")
+    if cfg.mask_param is not None:
+        if cfg.mask_dtype not in MASK_BYTES:
+            raise NotImplementedError(f"attention mask in {cfg.mask_dtype}")
+        if (cfg.Sk * MASK_BYTES[cfg.mask_dtype]) % 16:
+            raise NotImplementedError("attention mask rows not 16-byte aligned")
     ncols_used = NQ * (128 + DP)
     ncols = max(32, 1 << math.ceil(math.log2(ncols_used)))
     fmt = AB_FORMAT[cfg.dtype]
@@ -194,7 +204,22 @@ def emit_attention_module(cfg: AttnConfig) -> str:
     ptrue, pfalse, zr = p.reg("pred"), p.reg("pred"), p.reg("u32")
     p.emit(f"mov.u32 {zr}, 0\nsetp.eq.u32 {ptrue}, {zr}, 0\nsetp.ne.u32 {pfalse}, {zr}, 0")
     bh, q0 = p.reg("u32"), p.reg("u32")
-    p.emit(f"mov.u32 {bh}, %ctaid.y\nmov.u32 {q0}, %ctaid.x\nmul.lo.u32 {q0}, {q0}, {128 * NQ}")
+    p.emit(f"mov.u32 {bh}, %ctaid.y\nmov.u32 {q0}, %ctaid.x")
+    if cfg.causal:
+        # the last query tiles see the most keys: launch them first
+        p.emit(f"sub.u32 {q0}, {-(-cfg.Sq // (128 * NQ)) - 1}, {q0}")
+    p.emit(f"mul.lo.u32 {q0}, {q0}, {128 * NQ}")
+    # key blocks per query tile: all of them, or (causal) up to the tile's last query row
+    nbt = []
+    for t in range(NQ):
+        if cfg.causal:
+            r = p.reg("u32")
+            p.emit(f"add.u32 {r}, {q0}, {128 * t + 127}\nmin.u32 {r}, {r}, {cfg.Sq - 1}\n"
+                   f"shr.u32 {r}, {r}, 7\nadd.u32 {r}, {r}, 1\nmin.u32 {r}, {r}, {nblk}")
+            nbt.append(r)
+        else:
+            nbt.append(str(nblk))
+    nb_cta = nbt[-1]                      # the last tile needs the most blocks
 
     def ring_advance(slot, ph):
         ps = p.reg("pred")
@@ -254,7 +279,7 @@ def emit_attention_module(cfg: AttnConfig) -> str:
                        f"[{dst}], [{tm}, {{{db * 64}, {key0}, {bh}}}], [{fa}]")
         ring_advance(slot, ph)
     pj = p.reg("pred")
-    p.emit(f"add.u32 {j}, {j}, 1\nsetp.lt.u32 {pj}, {j}, {nblk}\n@{pj} bra {l_pk}\nbra {finish}")
+    p.emit(f"add.u32 {j}, {j}, 1\nsetp.lt.u32 {pj}, {j}, {nb_cta}\n@{pj} bra {l_pk}\nbra {finish}")
 
     # ----------------------------------------------------------------------- MMA
     p.place(l_mma)
@@ -347,21 +372,35 @@ def emit_attention_module(cfg: AttnConfig) -> str:
     wait_slot(vslot, vph)
     pfirst, pmore, pph = p.reg("pred"), p.reg("pred"), p.reg("u32")
     nxt = p.reg("u32")
-    p.emit(f"setp.eq.u32 {pfirst}, {jm}, 0\nadd.u32 {nxt}, {jm}, 1\nsetp.lt.u32 {pmore}, {nxt}, {nblk}\n"
+    p.emit(f"setp.eq.u32 {pfirst}, {jm}, 0\nadd.u32 {nxt}, {jm}, 1\nsetp.lt.u32 {pmore}, {nxt}, {nb_cta}\n"
            f"and.b32 {pph}, {jm}, 1")
     p.emit(f"mov.u32 {kslot}, {cslot}\nmov.u32 {kph}, {cph}")
+    kwait = p.reg("pred")                  # K_{j+1} not yet waited for in this block
+    p.emit(f"mov.pred {kwait}, {ptrue}")
     for t in range(NQ):
+        l_tdone = p.label("m_tdone")
+        if cfg.causal and t < NQ - 1:
+            pact = p.reg("pred")           # (causal) this tile may stop before the CTA does
+            p.emit(f"setp.lt.u32 {pact}, {jm}, {nbt[t]}\n@!{pact} bra {l_tdone}")
         pb = p.reg("u32")
         p.emit(f"add.u32 {pb}, {bars}, {B_P + 8 * t}")
         waits.wait(pb, pph, "mma", finish)
         p.emit("tcgen05.fence::after_thread_sync")
         issue_pv(t, vslot, pfirst)
+        pm_t = pmore
+        if cfg.causal and t < NQ - 1:
+            pm_t = p.reg("pred")
+            p.emit(f"setp.lt.u32 {pm_t}, {nxt}, {nbt[t]}")
         skip = p.label("m_noqk")
-        p.emit(f"@!{pmore} bra {skip}")
-        if t == 0:
-            wait_slot(kslot, kph)
+        p.emit(f"@!{pm_t} bra {skip}")
+        l_kw = p.label("m_kwaited")
+        p.emit(f"@!{kwait} bra {l_kw}")
+        wait_slot(kslot, kph)
+        p.emit(f"mov.pred {kwait}, {pfalse}")
+        p.place(l_kw)
         issue_qk(t, kslot)
         p.place(skip)
+        p.place(l_tdone)
     release_slot(vslot)
     l_norel = p.label("m_norel")
     p.emit(f"@!{pmore} bra {l_norel}")
@@ -375,7 +414,7 @@ def emit_attention_module(cfg: AttnConfig) -> str:
     if NQ == 2:
         p.emit(f"setmaxnreg.inc.sync.aligned.u32 {regs_soft}")
     _emit_softmax(p, cfg, ptr, bars, B_S, B_P, B_O, tbase, base, p_off, p_bytes, warp, lane,
-                  q0, bh, nblk, scale_log2, masked, waits, finish)
+                  q0, bh, nbt, scale_log2, masked, waits, finish)
 
     # ------------------------------------------------------------------- finish
     p.place(finish)
@@ -403,14 +442,16 @@ def emit_attention_module(cfg: AttnConfig) -> str:
                f"\t.shared .align 4 .u32 gtmem;\n")
     text = text.replace("{\n", "{\n" + statics, 1)
     eb = 2
+    # (query, key) pairs that take part: all of them, or (causal) key <= query
+    visible = (sum(min(r + 1, cfg.Sk) for r in range(cfg.Sq)) if cfg.causal else cfg.Sq * cfg.Sk)
     kmap = ({"dims": [cfg.Sk, cfg.D, cfg.BH], "strides": [cfg.Sk * eb, cfg.D * cfg.Sk * eb],
              "box": [64, DP, 1]} if cfg.kt_layout else
             {"dims": [cfg.D, cfg.Sk, cfg.BH], "strides": [cfg.D * eb, cfg.Sk * cfg.D * eb],
              "box": [64, 128, 1]})
     launch = {
         "kind": "attention", "grid": [-(-cfg.Sq // (128 * NQ)), cfg.BH, 1], "block": [nthreads, 1, 1],
-        "cluster": [1, 1, 1], "smem": smem, "flops": 4 * cfg.BH * cfg.Sq * cfg.Sk * cfg.D,
-        "exps": cfg.BH * cfg.Sq * cfg.Sk,
+        "cluster": [1, 1, 1], "smem": smem, "flops": 4 * cfg.BH * visible * cfg.D,
+        "exps": cfg.BH * visible,
         "extra_params": [
             {"kind": "tmap", "buffer": cfg.q_param, "dtype": cfg.dtype, "dims": [cfg.D, cfg.Sq, cfg.BH],
              "strides": [cfg.D * eb, cfg.Sq * cfg.D * eb], "box": [64, 128, 1], "swizzle": 128},
@@ -481,8 +522,47 @@ def _max_tree(p: Ptx, vals: list) -> str:
     return red[0]
 
 
+def _add_mask(p: Ptx, cfg: AttnConfig, fv: list, mrow: str, jj: str, scale_log2: float) -> None:
+    """fv[i] <- fv[i] * scale*log2e + mask[row, 128 jj + i] * log2e for the block's 128
+    keys; 16-byte loads, none past the row's end (keys >= Sk are masked afterwards)."""
+    esz = MASK_BYTES[cfg.mask_dtype]
+    per = 16 // esz                       # mask values per 16-byte load
+    a = p.reg("b64")
+    kb = p.reg("u32")
+    p.emit(f"mul.wide.u32 {a}, {jj}, {128 * esz}\nadd.s64 {a}, {a}, {mrow}\nmul.lo.u32 {kb}, {jj}, 128")
+    l2e = f32_hex(LOG2E)
+    sl = f32_hex(scale_log2)
+    for v in range(128 // per):
+        w = [p.reg("b32") for _ in range(4)]
+        pin, kx = p.reg("pred"), p.reg("u32")
+        p.emit(f"add.u32 {kx}, {kb}, {v * per}\nsetp.lt.u32 {pin}, {kx}, {cfg.Sk}")
+        for r in w:
+            p.emit(f"mov.b32 {r}, 0")
+        p.emit(f"@{pin} ld.global.nc.v4.b32 {{{', '.join(w)}}}, [{a}+{v * 16}]")
+        vals = []
+        for r in w:
+            if esz == 4:
+                f = p.reg("f32")
+                p.emit(f"mov.b32 {f}, {r}")
+                vals.append(f)
+                continue
+            lo, hi = p.reg("f32"), p.reg("f32")
+            if cfg.mask_dtype == "f16":
+                h0, h1 = p.reg("b16"), p.reg("b16")
+                p.emit(f"mov.b32 {{{h0}, {h1}}}, {r}\ncvt.f32.f16 {lo}, {h0}\ncvt.f32.f16 {hi}, {h1}")
+            else:                         # bf16: the high half of an f32
+                bl, bh_ = p.reg("b32"), p.reg("b32")
+                p.emit(f"shl.b32 {bl}, {r}, 16\nand.b32 {bh_}, {r}, -65536\n"
+                       f"mov.b32 {lo}, {bl}\nmov.b32 {hi}, {bh_}")
+            vals += [lo, hi]
+        for k, mval in enumerate(vals):
+            i = v * per + k
+            ms = p.reg("f32")
+            p.emit(f"mul.rn.f32 {ms}, {mval}, {l2e}\nfma.rn.f32 {fv[i]}, {fv[i]}, {sl}, {ms}")
+
+
 def _emit_softmax(p: Ptx, cfg: AttnConfig, ptr, bars, B_S, B_P, B_O, tbase, base, p_off, p_bytes,
-                  warp, lane, q0, bh, nblk, scale_log2, masked, waits: Waits, finish):
+                  warp, lane, q0, bh, nbt, scale_log2, masked, waits: Waits, finish):
     NQ, DP = cfg.NQ, cfg.DP
     t, q, row, lanebits = p.regs("u32", 4)
     # warps 0..3 -> tile 0, 4..7 -> tile 1; TMEM lane quarter = warp % 4
@@ -507,6 +587,26 @@ def _emit_softmax(p: Ptx, cfg: AttnConfig, ptr, bars, B_S, B_P, B_O, tbase, base
         add.u32 {obar}, {sbar}, {B_O}
         add.u32 {sbar}, {sbar}, {B_S}
     """)
+    # this tile's number of key blocks and this thread's query row
+    if len(set(nbt)) == 1:
+        nbm = nbt[0]
+    else:
+        nbm, pt0 = p.reg("u32"), p.reg("pred")
+        p.emit(f"setp.eq.u32 {pt0}, {t}, 0\nselp.b32 {nbm}, {nbt[0]}, {nbt[1]}, {pt0}")
+    qrow = p.reg("u32")
+    p.emit(f"mad.lo.u32 {qrow}, {t}, 128, {q0}\nadd.u32 {qrow}, {qrow}, {row}")
+    mrow = None
+    if cfg.mask_param is not None:
+        # this row of the additive mask: mask[bh, min(qrow, Sq - 1), :]
+        esz = MASK_BYTES[cfg.mask_dtype]
+        mrow, w64, qc = p.reg("b64"), p.reg("b64"), p.reg("u32")
+        p.emit(f"""
+            min.u32 {qc}, {qrow}, {cfg.Sq - 1}
+            mul.wide.u32 {mrow}, {bh}, {cfg.mask_bh_stride * esz}
+            mul.wide.u32 {w64}, {qc}, {cfg.Sk * esz}
+            add.s64 {mrow}, {mrow}, {w64}
+            add.s64 {mrow}, {mrow}, {ptr[cfg.mask_param]}
+        """)
     # this thread's P row in smem: tile t, row r; 16-byte chunk c of a 64-key block
     # lives at chunk (c ^ (r % 8)) of the row (128-byte swizzle)
     chunk_addr = {}
@@ -527,7 +627,8 @@ def _emit_softmax(p: Ptx, cfg: AttnConfig, ptr, bars, B_S, B_P, B_O, tbase, base
     p.emit(f"mov.f32 {m}, 0fF149F2CA\nmov.f32 {l}, 0f00000000")     # m = -1e30 (log2 domain)
     cvt = "cvt.rn.bf16x2.f32" if cfg.dtype == "bf16" else "cvt.rn.f16x2.f32"
     sl2, slr = p.reg("b64"), p.reg("f32")
-    p.emit(f"mov.f32 {slr}, {f32_hex(scale_log2)}\nmov.b64 {sl2}, {{{slr}, {slr}}}")
+    pre_scaled = cfg.mask_param is not None
+    p.emit(f"mov.f32 {slr}, {f32_hex(1.0 if pre_scaled else scale_log2)}\nmov.b64 {sl2}, {{{slr}, {slr}}}")
     jj = p.reg("u32")
     p.emit(f"mov.u32 {jj}, 0")
     l_blk = p.label("s_blk")
@@ -550,15 +651,34 @@ def _emit_softmax(p: Ptx, cfg: AttnConfig, ptr, bars, B_S, B_P, B_O, tbase, base
     if masked:
         keyb = p.reg("u32")
         p.emit(f"mul.lo.u32 {keyb}, {jj}, 128")
+    if cfg.mask_param is not None:
+        # scores in the log2 domain with the additive mask: s*scale*log2e + mask*log2e
+        _add_mask(p, cfg, fv, mrow, jj, scale_log2)
+    if masked:
         for i in range(128):
             pk, kx = p.reg("pred"), p.reg("u32")
             p.emit(f"add.u32 {kx}, {keyb}, {i}\nsetp.ge.u32 {pk}, {kx}, {cfg.Sk}\n"
                    f"@{pk} mov.f32 {fv[i]}, 0fFF800000")
+    if cfg.causal:
+        # keys past this thread's query row are out: key 128 jj + i > qrow <=> i > lim
+        lim, pneed, pany_c = p.reg("u32"), p.reg("pred"), p.reg("pred")
+        l_nocausal = p.label("s_nocausal")
+        p.emit(f"""
+            mad.lo.s32 {lim}, {jj}, -128, {qrow}
+            setp.lt.s32 {pneed}, {lim}, 127
+            vote.sync.any.pred {pany_c}, {pneed}, -1
+            @!{pany_c} bra {l_nocausal}
+        """)
+        for i in range(128):
+            pk = p.reg("pred")
+            p.emit(f"setp.lt.s32 {pk}, {lim}, {i}\n@{pk} mov.f32 {fv[i]}, 0fFF800000")
+        p.place(l_nocausal)
     mx = _max_tree(p, fv)
     mn, alpha, thr = p.reg("f32"), p.reg("f32"), p.reg("f32")
     prs, pfirst = p.reg("pred"), p.reg("pred")
+    if cfg.mask_param is None:
+        p.emit(f"mul.rn.f32 {mx}, {mx}, {f32_hex(scale_log2)}")
     p.emit(f"""
-        mul.rn.f32 {mx}, {mx}, {f32_hex(scale_log2)}
         max.f32 {mn}, {m}, {mx}
         setp.eq.u32 {pfirst}, {jj}, 0
         add.rn.f32 {thr}, {m}, {f32_hex(RESCALE_LOG2)}
@@ -641,16 +761,16 @@ def _emit_softmax(p: Ptx, cfg: AttnConfig, ptr, bars, B_S, B_P, B_O, tbase, base
         add.u32 {jj}, {jj}, 1
     """)
     pj = p.reg("pred")
-    p.emit(f"setp.lt.u32 {pj}, {jj}, {nblk}\n@{pj} bra {l_blk}")
+    p.emit(f"setp.lt.u32 {pj}, {jj}, {nbm}\n@{pj} bra {l_blk}")
     # epilogue: O / l once the last O_t += P_t V has landed
     parf = p.reg("u32")
-    p.emit(f"mov.u32 {parf}, {(nblk - 1) & 1}")
+    p.emit(f"sub.u32 {parf}, {nbm}, 1\nand.b32 {parf}, {parf}, 1")
     waits.wait(obar, parf, "softmax", finish)
     p.emit("bar.warp.sync -1\ntcgen05.fence::after_thread_sync")
     inv = p.reg("f32")
     p.emit(f"rcp.rn.f32 {inv}, {l}")
-    grow, prow_ok = p.reg("u32"), p.reg("pred")
-    p.emit(f"mad.lo.u32 {grow}, {t}, 128, {q0}\nadd.u32 {grow}, {grow}, {row}\nsetp.lt.u32 {prow_ok}, {grow}, {cfg.Sq}")
+    grow, prow_ok = qrow, p.reg("pred")
+    p.emit(f"setp.lt.u32 {prow_ok}, {grow}, {cfg.Sq}")
     oadr, w64 = p.reg("b64"), p.reg("b64")
     p.emit(f"""
         mul.wide.u32 {oadr}, {bh}, {cfg.Sq}
@@ -717,19 +837,6 @@ def analyze(spec) -> AttnConfig:
     pv = [s for s in mmas if _frag_base(s.a_frag) in repacked]
     if not qk or not pv:
         raise NotImplementedError("attention needs a score MMA and a PV MMA")
-    if any(s.src_buffer not in spec.buffers for s in ldm):
-        raise NotImplementedError("attention operands staged through shared memory")
-    qs = frag_src[_frag_base(qk[0].a_frag)]
-    ks = frag_src[_frag_base(qk[0].b_frag)]
-    vs = frag_src[_frag_base(pv[0].b_frag)]
-    Q, K, V = spec.param(qs.src_buffer), spec.param(ks.src_buffer), spec.param(vs.src_buffer)
-    stores = [s for s in stmts if type(s).__name__ == "RegStore"]
-    O = spec.param(stores[0].dst_buffer)
-    if len({Q.dtype, K.dtype, V.dtype, O.dtype}) != 1:
-        raise NotImplementedError("mixed attention dtypes")
-    for s in stmts:
-        if type(s).__name__ == "FragmentApply" and any(k in ("coord", "gmem") for k in (s.kinds or ())):
-            raise NotImplementedError("masked attention (causal / additive mask)")
     # the key-chunk loop: the loop that holds the row reductions
     ck = None
     for s in stmts:
@@ -737,7 +844,33 @@ def analyze(spec) -> AttnConfig:
                 any(type(x).__name__ == "FragmentRowReduce" for x in _walk(s.body)):
             ck = s.axis.name
             break
-    kdims = [i for i, e in enumerate(ks.src_index) if ck in expr_vars(e)]
+    # operands read straight from global memory, or staged through shared memory by
+    # cp.async (the staging copy inside the key loop names the global buffer and index)
+    copies = {}
+    for s in stmts:
+        if type(s).__name__ == "CpAsyncCopy":
+            copies.setdefault(s.smem, []).append(s)
+
+    def source(ld):
+        if ld.src_buffer in spec.buffers:
+            return ld.src_buffer, ld.src_index
+        cps = copies.get(ld.src_buffer)
+        if not cps or len({c.src for c in cps}) != 1 or cps[0].src not in spec.buffers:
+            raise NotImplementedError(f"attention operand {ld.src_buffer} not traceable to a buffer")
+        for c in cps:
+            if any(ck in expr_vars(e) for e in c.src_index):
+                return c.src, c.src_index
+        return cps[0].src, cps[0].src_index
+
+    q_name, _ = source(frag_src[_frag_base(qk[0].a_frag)])
+    k_name, k_index = source(frag_src[_frag_base(qk[0].b_frag)])
+    v_name, _ = source(frag_src[_frag_base(pv[0].b_frag)])
+    Q, K, V = spec.param(q_name), spec.param(k_name), spec.param(v_name)
+    stores = [s for s in stmts if type(s).__name__ == "RegStore"]
+    O = spec.param(stores[0].dst_buffer)
+    if len({Q.dtype, K.dtype, V.dtype, O.dtype}) != 1:
+        raise NotImplementedError("mixed attention dtypes")
+    kdims = [i for i, e in enumerate(k_index) if ck in expr_vars(e)]
     if len(kdims) != 1:
         raise NotImplementedError("key axis of K not identifiable")
     kt_layout = kdims[0] == len(K.shape) - 1
@@ -750,15 +883,16 @@ def analyze(spec) -> AttnConfig:
     for X in (K, V, O):
         if (math.prod(X.shape[:-2]) if len(X.shape) > 2 else 1) != BH:
             raise NotImplementedError("grouped / broadcast heads")
-    scale = _score_scale(spec, stmts, {_frag_base(s.c_frag) for s in qk})
+    scale, causal = _score_chain(spec, stmts, {_frag_base(s.c_frag) for s in qk})
     return AttnConfig(BH=BH, Sq=Sq, Sk=Sk, D=D, dtype=Q.dtype, kt_layout=kt_layout, scale=scale,
-                      name=spec.name, q_param=Q.name, k_param=K.name, v_param=V.name, o_param=O.name,
-                      arg_params=arg_params(spec), buffers=tuple(x.name for x in spec.params))
+                      causal=causal, name=spec.name, q_param=Q.name, k_param=K.name,
+                      v_param=V.name, o_param=O.name, arg_params=arg_params(spec),
+                      buffers=tuple(x.name for x in spec.params))
 
 
-def _score_scale(spec, stmts, score_frags) -> float:
-    """Product of the uniform multiplies / divides the IR applies to S before the
-    row max (``FragmentApply`` with a scalar operand from the constants)."""
+def _constants(spec, stmts) -> dict:
+    """Scalar values the body derives from constant buffers and literals (``Load`` of a
+    constant, ``Let`` of a literal, reciprocal / multiply / divide / copy of those)."""
     env = {}
     for s in stmts:
         k = type(s).__name__
@@ -777,33 +911,175 @@ def _score_scale(spec, stmts, score_frags) -> float:
                 env[s.name] = a[0] / a[1]
             elif op == "copy":
                 env[s.name] = a[0]
-    # follow the chain of one score fragment: S -> (copy) -> *scale -> ... -> max subtraction
+    return env
+
+
+def _is_causal_cond(cond) -> bool:
+    """``__frow < __fcol`` (or ``__fcol > __frow``): the query row is before the key."""
+    if type(cond).__name__ != "BinaryExpr":
+        return False
+    names = tuple(getattr(x, "name", None) for x in (cond.left, cond.right))
+    return (cond.op == "<" and names == ("__frow", "__fcol")) or \
+        (cond.op == ">" and names == ("__fcol", "__frow"))
+
+
+def _score_chain(spec, stmts, score_frags) -> tuple[float, bool]:
+    """Follow one score fragment from the QK MMA to the row-max subtraction and
+    return (scale, causal).  Accepted on the way (the reference's ``FragmentApply``
+    forms, ``compiler/mma.py:385-437``): copies; multiplies / divides by a constant
+    (the softmax scale); adds / subtracts of a constant (a uniform shift, which the
+    softmax cancels); ``where(__frow < __fcol, fill, s)`` with a very negative fill
+    (the causal mask).  Anything else raises ``NotImplementedError``."""
+    env = _constants(spec, stmts)
     applies = [s for s in stmts if type(s).__name__ == "FragmentApply"]
-    scale = 1.0
-    cur = None
-    for s in applies:
-        fr = [a for a, kd in zip(s.args, s.kinds) if kd == "frag"]
-        if fr and _frag_base(fr[0]) in score_frags:
-            cur = s
-            break
-    while cur is not None:
-        op = cur.op.name
-        unis = [a for a, kd in zip(cur.args, cur.kinds) if kd == "uniform"]
-        if op == "copy":
+
+    def frag_args(s):
+        return [a for a, kd in zip(s.args, s.kinds) if kd == "frag"]
+
+    start = next((i for i, s in enumerate(applies)
+                  if frag_args(s) and _frag_base(frag_args(s)[0]) in score_frags), None)
+    if start is None:
+        raise NotImplementedError("score fragment never reaches the softmax")
+    scale, causal, i = 1.0, False, start
+    for _ in range(len(applies)):
+        cur = applies[i]
+        op, kinds = cur.op.name, tuple(cur.kinds)
+        if cur.post:
+            raise NotImplementedError("score operation with a post-op")
+        unis = [a for a, kd in zip(cur.args, kinds) if kd == "uniform"]
+        if op == "copy" and kinds == ("frag",):
             pass
-        elif op in ("multiply", "divide") and len(unis) == 1 and unis[0] in env:
+        elif op in ("multiply", "divide") and sorted(kinds) == ["frag", "uniform"] and unis[0] in env:
+            if op == "divide" and kinds[0] != "frag":
+                raise NotImplementedError("constant divided by the scores")
             v = env[unis[0]]
             scale = scale * v if op == "multiply" else scale / v
+        elif op in ("add", "subtract") and sorted(kinds) == ["frag", "uniform"] and \
+                (op == "add" or kinds[0] == "frag"):
+            pass                               # a uniform shift: the softmax cancels it
+        elif op == "where" and kinds == ("coord", "uniform", "frag") and _is_causal_cond(cur.args[0]) \
+                and type(cur.args[1]).__name__ == "Literal" and float(cur.args[1].value) <= -1e4:
+            causal = True
+        elif op == "subtract" and "row" in kinds:
+            return scale, causal               # the row-max subtraction: the scores end here
         else:
-            break
-        nxt = None
-        for s in applies:
-            fr = [a for a, kd in zip(s.args, s.kinds) if kd == "frag"]
-            if fr and fr[0].split("[")[0] == cur.out:
-                nxt = s
-                break
-        cur = nxt
-    return scale
+            raise NotImplementedError(f"score operation {op}{kinds} before the softmax")
+        nxt = next((j for j in range(i + 1, len(applies))
+                    if frag_args(applies[j]) and _frag_base(frag_args(applies[j])[0]) == cur.out), None)
+        if nxt is None:
+            raise NotImplementedError("score chain does not reach the row maximum")
+        i = nxt
+    raise NotImplementedError("score chain does not reach the row maximum")
+
+
+def analyze_simt(spec) -> AttnConfig:
+    """Emmy's SIMT attention form: one cooperative tile per (head, query row, output
+    column) streams the keys, ``s = (q . k) * scale [+ mask[row, key]]`` over an inner
+    head-dim loop, and keeps an online softmax (running max, rescaled sums) of ``v``
+    (the reference lowers it statement by statement, ``compiler/stmts.py``; fixture
+    ``x_h_sdpa_mask``: sdpa with an additive ``attn_mask``).  Recognised strictly by its
+    index variables and its score chain; anything else raises ``NotImplementedError``."""
+    from ..stmts import expr_vars
+    if len(spec.body) != 1 or type(spec.body[0]).__name__ != "Tile":
+        raise NotImplementedError("not a single-tile kernel")
+    tile = spec.body[0]
+    loops = [x for x in tile.body if type(x).__name__ in ("Loop", "StridedLoop")]
+    if len(loops) != 1:
+        raise NotImplementedError("not a key-streaming attention")
+    kl = loops[0]
+    kv = kl.axis.name
+    inner = [x for x in kl.body if type(x).__name__ in ("Loop", "StridedLoop")]
+    if len(inner) != 1:
+        raise NotImplementedError("no head-dim loop")
+    dv = inner[0].axis.name
+    body_in = list(inner[0].body)
+    loads_in = {x.names[0]: x for x in body_in if type(x).__name__ == "Load" and len(x.names) == 1}
+    prods = [x for x in body_in if type(x).__name__ == "Assign" and x.op.name == "multiply"]
+    accs = [x for x in body_in if type(x).__name__ == "Accum" and x.op.name == "add"]
+    if len(prods) != 1 or len(accs) != 1 or accs[0].value != prods[0].name or \
+            len(body_in) != 4 or set(prods[0].args) != set(loads_in):
+        raise NotImplementedError("head-dim loop is not a dot product")
+    acc = accs[0].name
+
+    def ivars(ld):
+        return [expr_vars(e) for e in ld.index]
+
+    q_ld = [x for x in loads_in.values() if not any(kv in v for v in ivars(x))]
+    k_ld = [x for x in loads_in.values() if any(kv in v for v in ivars(x))]
+    if len(q_ld) != 1 or len(k_ld) != 1:
+        raise NotImplementedError("dot product is not query x key")
+    q_ld, k_ld = q_ld[0], k_ld[0]
+    qi = ivars(q_ld)
+    if qi[-1] != {dv} or len(qi[-2]) != 1:
+        raise NotImplementedError("query operand layout")
+    qvar = next(iter(qi[-2]))
+    ki = ivars(k_ld)
+    if ki[-2:] == [{kv}, {dv}]:
+        kt_layout = False
+    elif ki[-2:] == [{dv}, {kv}]:
+        kt_layout = True
+    else:
+        raise NotImplementedError("key operand layout")
+    env = _constants(spec, list(_walk(spec.body)))
+    stm = list(kl.body)
+    scaled = [x for x in stm if type(x).__name__ == "Assign" and acc in x.args]
+    if len(scaled) != 1 or scaled[0].op.name != "multiply" or \
+            not all(a == acc or a in env for a in scaled[0].args):
+        raise NotImplementedError("score is not a scaled dot product")
+    scale = math.prod(env[a] for a in scaled[0].args if a != acc)
+    score = scaled[0].name
+    loads = {x.names[0]: x for x in stm if type(x).__name__ == "Load" and len(x.names) == 1}
+    mask_ld = None
+    adds = [x for x in stm if type(x).__name__ == "Assign" and x.op.name == "add" and score in x.args]
+    if adds:
+        other = [a for a in adds[0].args if a != score]
+        if len(adds) != 1 or len(other) != 1 or other[0] not in loads:
+            raise NotImplementedError("score shifted by something other than a mask")
+        mask_ld = loads[other[0]]
+        mi = ivars(mask_ld)
+        if mi[-2:] != [{qvar}, {kv}]:
+            raise NotImplementedError("mask not indexed by (query, key)")
+        score = adds[0].name
+    # the running maximum is taken over exactly this score, and the softmax uses exp
+    maxes = [x for x in stm if type(x).__name__ == "Accum" and x.op.name == "maximum"]
+    if len(maxes) != 1 or maxes[0].value != score or \
+            not any(type(x).__name__ == "Assign" and x.op.name == "exp" for x in stm):
+        raise NotImplementedError("no online softmax over the score")
+    v_ld = [x for x in loads.values() if x is not mask_ld and any(kv in v for v in ivars(x))]
+    if len(v_ld) != 1:
+        raise NotImplementedError("value operand not identifiable")
+    vi = ivars(v_ld[0])
+    if vi[-2] != {kv} or len(vi[-1]) != 1:
+        raise NotImplementedError("value operand layout")
+    dout = next(iter(vi[-1]))
+    writes = [x for x in _walk(tile.body) if type(x).__name__ == "Write" and x.output in spec.buffers]
+    if len(writes) != 1 or [expr_vars(e) for e in writes[0].index][-2:] != [{qvar}, {dout}]:
+        raise NotImplementedError("output not written per (query, column)")
+    Q, K, V = spec.param(q_ld.input), spec.param(k_ld.input), spec.param(v_ld[0].input)
+    O = spec.param(writes[0].output)
+    if len({Q.dtype, K.dtype, V.dtype, O.dtype}) != 1:
+        raise NotImplementedError("mixed attention dtypes")
+    Sq, D = Q.shape[-2], Q.shape[-1]
+    Sk = K.shape[-1] if kt_layout else K.shape[-2]
+    if (K.shape[-2] if kt_layout else K.shape[-1]) != D or tuple(V.shape[-2:]) != (Sk, D) \
+            or tuple(O.shape[-2:]) != (Sq, D):
+        raise NotImplementedError("attention operand shapes")
+    BH = math.prod(Q.shape[:-2]) if len(Q.shape) > 2 else 1
+    for X in (K, V, O):
+        if (math.prod(X.shape[:-2]) if len(X.shape) > 2 else 1) != BH:
+            raise NotImplementedError("grouped / broadcast heads")
+    extra = {}
+    if mask_ld is not None:
+        M = spec.param(mask_ld.input)
+        if tuple(M.shape[-2:]) != (Sq, Sk):
+            raise NotImplementedError("mask shape")
+        lead = math.prod(M.shape[:-2]) if len(M.shape) > 2 else 1
+        if lead not in (1, BH):
+            raise NotImplementedError("mask broadcast over part of the batch x heads")
+        extra = dict(mask_param=M.name, mask_dtype=M.dtype, mask_bh_stride=0 if lead == 1 else Sq * Sk)
+    return AttnConfig(BH=BH, Sq=Sq, Sk=Sk, D=D, dtype=Q.dtype, kt_layout=kt_layout, scale=scale,
+                      name=spec.name, q_param=Q.name, k_param=K.name, v_param=V.name, o_param=O.name,
+                      arg_params=arg_params(spec), buffers=tuple(x.name for x in spec.params), **extra)
 
 
 def emit_attention(spec) -> str:

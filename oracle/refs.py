@@ -163,11 +163,18 @@ def mm_bf16(a, b):
     return bf16_round(f32(f64(a) @ f64(b)))
 
 
-def attn_bf16(q, k, v, scale):
-    """Non-causal attention on bf16-valued inputs, softmax in f64, bf16 result:
-    ``softmax(q k^T * scale) v`` with ``[..., S, D]`` operands (the BASELINE
-    attention: F.scaled_dot_product_attention, as in x_h_sdpa)."""
+def attn_bf16(q, k, v, scale, causal=False, mask=None, q_offset=0):
+    """Attention on bf16-valued inputs, softmax in f64, bf16 result:
+    ``softmax(q k^T * scale [+ mask]) v`` with ``[..., S, D]`` operands (the BASELINE
+    attention: F.scaled_dot_product_attention, as in x_h_sdpa).  ``causal`` drops keys
+    after the query (top-left aligned, ``is_causal``); ``q_offset`` is the absolute
+    index of the first query row when ``q`` holds a slice of the rows."""
     s = f64(q) @ np.swapaxes(f64(k), -1, -2) * scale
+    if mask is not None:
+        s = s + f64(mask)
+    if causal:
+        rows = np.arange(s.shape[-2])[:, None] + q_offset
+        s = np.where(np.arange(s.shape[-1])[None, :] <= rows, s, -np.inf)
     return bf16_round(f32(_softmax(s) @ f64(v)))
 
 

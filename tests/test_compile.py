@@ -114,3 +114,26 @@ def test_gemm_recognizer(pid, kmajor):
     from compiler.kernels.gemm import analyze
     cfg = analyze(load(next((GOLDEN / pid).glob("*.ir.json"))))
     assert cfg.b_kmajor == kmajor
+
+
+@pytest.mark.parametrize("pid,scale,kt,causal", [("x_h_sdpa_causal", 32 ** -0.5, False, True),
+                                                 ("x_h_attn_b", 1 / 5.66, True, False)])
+def test_attention_recognizer_staged_and_causal(pid, scale, kt, causal):
+    # operands staged through shared memory by cp.async are traced to their buffers;
+    # where(__frow < __fcol, -1e30, s) is the causal mask, a uniform add is a shift
+    from compiler.kernels.attention import analyze
+    cfg = analyze(load(next((GOLDEN / pid).glob("*.ir.json"))))
+    assert abs(cfg.scale - scale) < 1e-4 and cfg.kt_layout == kt and cfg.causal == causal
+
+
+def test_simt_attention_recognizer():
+    from compiler.kernels.attention import analyze_simt
+    cfg = analyze_simt(load(next((GOLDEN / "x_h_sdpa_mask").glob("*.ir.json"))))
+    assert (cfg.BH, cfg.Sq, cfg.Sk, cfg.D) == (2, 64, 64, 32)
+    assert cfg.mask_param == "x3" and cfg.mask_bh_stride == 0 and abs(cfg.scale - 32 ** -0.5) < 1e-12
+    assert (cfg.q_param, cfg.k_param, cfg.v_param) == ("x0", "x1", "x2")
+    # no reduction fixture is taken for attention
+    for ir in IRS:
+        if ir.parent.name != "x_h_sdpa_mask":
+            with pytest.raises(NotImplementedError):
+                analyze_simt(load(ir))
