@@ -84,8 +84,9 @@ def parse_cooperative(spec):
         raise NotThisTemplate("no cooperative axis")
     co = co[0]
     kinds = {type(s).__name__ for s in tile.body}
-    if "WarpShuffle" not in kinds or kinds & {"RegFragment", "MmaSyncPtx", "Loop"}:
+    if "WarpShuffle" not in kinds or kinds & {"RegFragment", "MmaSyncPtx"}:
         raise NotThisTemplate("no cross-thread combine")
+    row_len = {int(s.axis.extent.value) for s in tile.body if type(s).__name__ == "StridedLoop"}
     others = [a for a in tile.axes if a is not co]
     phases: list[Phase] = []
     body = list(tile.body)
@@ -130,9 +131,110 @@ def parse_cooperative(spec):
         elif k in ("Assign", "Let", "Load", "Init"):
             phases.append(Phase("scalar", s))
             i += 1
+        elif k == "Loop" and int(s.axis.extent.value) in row_len:
+            # a reduction every lane runs over the whole row (emmy's serial variance
+            # loop in LayerNorm): the same sum as a strided stream plus a combine
+            phases.extend(_serial_to_stream(s, co))
+            i += 1
         else:
             raise NotImplementedError(f"statement {k} in a cooperative reduction")
     return tile, co, others, phases
+
+
+def _serial_to_stream(loop, co) -> list:
+    """``for c in 0..L: acc <- op(acc, f(row[c]))`` run by every lane ->
+    ``for c in co..L:W`` per lane + a cross-lane combine of the accumulators with
+    the same op.  Only Load / Assign / Let / Accum (add, maximum, minimum) bodies."""
+    from ..ir import IR_CLASSES as C
+    accs = []
+    for st in loop.body:
+        k = type(st).__name__
+        if k == "Accum":
+            if st.op.name not in ("add", "maximum", "minimum") or st.base is not None:
+                raise NotImplementedError(f"serial row loop accumulating with {st.op.name}")
+            accs.append(st)
+        elif k not in ("Load", "Assign", "Let"):
+            raise NotImplementedError(f"{k} inside a serial row loop")
+    if not accs:
+        raise NotImplementedError("serial row loop without an accumulator")
+    width = int(co.extent.value)
+    stream = C["StridedLoop"](axis=loop.axis, start=C["Var"](name=co.name),
+                              step=C["Literal"](value=width, dtype="int"), body=loop.body,
+                              unroll=False, end=None, seed=True)
+    names = tuple(a.name for a in accs)
+    others = tuple(f"{n}__o" for n in names)
+    comb = tuple(C["Assign"](name=a.name, op=a.op, args=(a.name, f"{a.name}__o"), dtype=a.dtype)
+                 for a in accs)
+    return [Phase("stream", stream), Phase("combine", combine=Combine(names, others, comb))]
+
+
+def _zero_var(expr, name: str):
+    """Substitute Literal(0) for Var(name) in an index expression."""
+    from ..ir import IR_CLASSES as C
+    k = type(expr).__name__
+    if k == "Var":
+        return C["Literal"](value=0, dtype="int") if expr.name == name else expr
+    if k == "BinaryExpr":
+        return type(expr)(op=expr.op, left=_zero_var(expr.left, name), right=_zero_var(expr.right, name))
+    if k == "TernaryExpr":
+        return type(expr)(cond=_zero_var(expr.cond, name), if_true=_zero_var(expr.if_true, name),
+                          if_false=_zero_var(expr.if_false, name))
+    return expr
+
+
+def _mentions(obj, name: str) -> bool:
+    """Does any index expression inside ``obj`` (a statement or expression) use Var(name)?"""
+    if type(obj).__name__ == "Var":
+        return obj.name == name
+    if isinstance(obj, (tuple, list)):
+        return any(_mentions(x, name) for x in obj)
+    if hasattr(obj, "__dataclass_fields__"):
+        return any(_mentions(getattr(obj, f), name) for f in obj.__dataclass_fields__)
+    return False
+
+
+def fold_ksplit(spec, others, phases):
+    """Emmy's split rows (``Tile[_ksplit, rows.., co]``: each of S CTAs sums a C-wide
+    slice ``x[row, c + _ksplit * C]`` and adds it to the output atomically) as whole
+    rows: one stream over c in [0, S * C) with the same per-row combine and one
+    atomic add per row.  Checked on every access: the split offset must be exactly
+    C times the column stride."""
+    from ..ir import IR_CLASSES as C, Dim
+    ks = next(a for a in others if a.name == "_ksplit")
+    S = int(ks.extent.value)
+    rows = [a for a in others if a is not ks]
+    if not rows:
+        raise NotThisTemplate("split whole-array reduction")
+    ranges = {a.name: int(a.extent.value) for a in others}
+    out = []
+    for ph in phases:
+        if ph.kind != "stream":
+            if _mentions(ph.stmt, "_ksplit") or (ph.combine and _mentions(ph.combine, "_ksplit")):
+                raise NotImplementedError("_ksplit used outside the row streams")
+            out.append(ph)
+            continue
+        loop = ph.stmt
+        L = int(loop.axis.extent.value)
+        body = []
+        for st in loop.body:
+            k = type(st).__name__
+            if k in ("Load", "Write") and _mentions(st.index, "_ksplit"):
+                buf = st.input if k == "Load" else st.output
+                aff = affine_offset(tuple(st.index), spec.param(buf).shape,
+                                    {**ranges, loop.axis.name: L})
+                cf = dict(aff.coef)
+                if cf.get("_ksplit", 0) != L * cf.get(loop.axis.name, 0) or not cf.get(loop.axis.name):
+                    raise NotImplementedError("split offset is not a whole slice of the row")
+                st = type(st)(**{fn: (tuple(_zero_var(e, "_ksplit") for e in st.index)
+                                      if fn == "index" else getattr(st, fn))
+                                 for fn in st.__dataclass_fields__})
+            elif _mentions(st, "_ksplit"):
+                raise NotImplementedError("_ksplit used in a stream statement other than an access")
+            body.append(st)
+        axis = C["Axis"](name=loop.axis.name, extent=Dim(value=S * L), window=loop.axis.window)
+        out.append(Phase("stream", type(loop)(axis=axis, start=loop.start, step=loop.step, body=tuple(body),
+                                              unroll=loop.unroll, end=loop.end, seed=loop.seed)))
+    return rows, out
 
 
 def _stream_loads(stmts):
@@ -174,8 +276,10 @@ class RowReduce:
     def __init__(self, spec):
         self.spec = spec
         tile, co, others, phases = parse_cooperative(spec)
-        if not others or any(a.name == "_ksplit" for a in others):
+        if not others:
             raise NotThisTemplate("no row axes: whole-array reduction")
+        if any(a.name == "_ksplit" for a in others):
+            others, phases = fold_ksplit(spec, others, phases)
         self.tile, self.co, self.row_axes, self.phases = tile, co, others, phases
         self.row_ext = {a.name: int(a.extent.value) for a in others}
         self.rows = math.prod(self.row_ext.values())
@@ -510,7 +614,7 @@ class RowReduce:
                 addr = self._row_base(acc.buffer, acc.aff)
                 pc = self._chunk_pred(c)
                 guard = f"@{pc} " if pc else ""
-                off = c * span * 4
+                off = c * span * acc.col_coef * 4      # chunk c: span columns further on
                 if self.VEC == 4:
                     p.emit(f"{guard}ld.global.v4.f32 {{{', '.join(regs)}}}, [{addr}+{off}]")
                 else:
@@ -567,7 +671,7 @@ class RowReduce:
                 acc = self.accesses[id(w)]
                 addr = self._row_base(acc.buffer, acc.aff)
                 vals = outvals[id(w)]
-                off = c * span * 4
+                off = c * span * acc.col_coef * 4
                 if self.VEC == 4:
                     p.emit(f"@{self.pvalid} st.global.v4.f32 [{addr}+{off}], {{{', '.join(vals)}}}")
                 else:
@@ -642,11 +746,13 @@ class RowReduce:
     def _leader_write(self, ctx: ScalarCtx, w):
         """A Write in the leader section: one value per row."""
         _check_buffer(self.spec, w.output)
-        if len(w.values) != 1 or w.atomic:
-            raise NotImplementedError("vector or atomic leader Write")
+        if len(w.values) != 1:
+            raise NotImplementedError("vector leader Write")
         shape = self.spec.param(w.output).shape
         aff = affine_offset(tuple(w.index), shape, self.row_ext)
-        ctx.ptx.emit(f"st.global.f32 [{self._row_base(w.output, aff)}], {ctx.f32(w.values[0])}")
+        # an atomic (+=) output gets one add per row: the whole row is summed here
+        op = "red.global.add.f32" if w.atomic else "st.global.f32"
+        ctx.ptx.emit(f"{op} [{self._row_base(w.output, aff)}], {ctx.f32(w.values[0])}")
 
 
 def _rename(expr, old: str, new: str):
@@ -943,5 +1049,8 @@ def emit_reduction(spec):
     try:
         k = RowReduce(spec)
     except NotThisTemplate:
-        k = FullReduce(spec)
+        try:
+            k = FullReduce(spec)
+        except NotThisTemplate as e:
+            raise NotImplementedError(f"cooperative reduction outside both templates: {e}") from None
     return k.emit()

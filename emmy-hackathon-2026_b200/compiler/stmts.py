@@ -161,6 +161,11 @@ def _unary(p: Ptx, op: str, dst: str, a: str) -> None:
         p.emit(f"max.f32 {dst}, {a}, 0f00000000")
     elif op == "square":
         p.emit(f"mul.rn.f32 {dst}, {a}, {a}")
+    elif op == "log":
+        # ln x = log2(x) * ln 2 on the MUFU lg2 unit (about 2^-22 absolute error for
+        # x in [1/2, 2], a few ulp relative elsewhere)
+        l2 = p.reg("f32")
+        p.emit(f"lg2.approx.f32 {l2}, {a}\nmul.rn.f32 {dst}, {l2}, {f32_hex(_LN2)}")
     else:
         raise NotImplementedError(f"elementwise op {op} (f32, unary)")
 

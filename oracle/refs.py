@@ -82,6 +82,33 @@ def row_max(x):
     return np.asarray(x).max(-1)
 
 
+def axis_sum(x, axis):
+    """``f32(f64(x).sum(axis))`` (expressions_extra.py:201-202 x_r_colsum, 280-281
+    x_r_sum_dim0, 284-285 x_r_unpinned_rows)."""
+    return f32(f64(x).sum(axis))
+
+
+def axis_mean(x, axis):
+    """``f32(f64(x).mean(axis))`` (expressions_extra.py:286-287, x_r_mean_mid_3d)."""
+    return f32(f64(x).mean(axis))
+
+
+def f16_sum(x):
+    """``f16(f64(x).sum())`` (expressions_extra.py:307-308, x_d_f16_sum)."""
+    return f16(f64(x).sum())
+
+
+def f16_row_mean(x):
+    """``f16(f64(x).mean(-1))`` (expressions_extra.py:309-310, x_d_f16_mean)."""
+    return f16(f64(x).mean(-1))
+
+
+def f16_sq_mean(x):
+    """The f16 product rounded before the mean: ``f16(f64(f16(f32(x) * f32(x))).mean(-1))``
+    (expressions_extra.py:317-318, x_d_f16_sq_mean)."""
+    return f16(f64(f16(f32(x) * f32(x))).mean(-1))
+
+
 # ---------------------------------------------------------------------------
 # fused row kernels (category 4)
 
@@ -100,6 +127,44 @@ def softmax(x, scale=None):
     if scale is not None:
         xd = xd * scale
     return f32(_softmax(xd))
+
+
+def layernorm_ish(x):
+    """``f32(f64(x) - f64(x).mean(-1, keepdims=True))`` (expressions_extra.py:210-211)."""
+    return f32(f64(x) - f64(x).mean(-1, keepdims=True))
+
+
+def max_sub(x):
+    """``f32(f64(x) - f64(x).max(-1, keepdims=True))`` (expressions_extra.py:259-260)."""
+    return f32(f64(x) - f64(x).max(-1, keepdims=True))
+
+
+def layernorm(x, w, b, eps=1e-5):
+    """``(x - mean) / sqrt(var + eps) * w + b`` in f64 (expressions_extra.py:238-243)."""
+    xd = f64(x)
+    return f32((xd - xd.mean(-1, keepdims=True)) / np.sqrt(xd.var(-1, keepdims=True) + eps)
+               * f64(w) + f64(b))
+
+
+def log_softmax(x):
+    """``f32(log(softmax(f64(x))))`` (expressions_extra.py:245-250)."""
+    return f32(np.log(_softmax(f64(x))))
+
+
+def rmsnorm_silu(x, eps=1e-6):
+    """``silu(x / sqrt(mean(x^2) + eps))`` in f64 (expressions_extra.py:251-254)."""
+    y = f64(x) / np.sqrt((f64(x) ** 2).mean(-1, keepdims=True) + eps)
+    return f32(y / (1 + np.exp(-y)))
+
+
+def softmax_axis(x, axis):
+    """``f32(softmax(f64(x), axis))`` (expressions_extra.py:257-258, x_f_softmax_dim0)."""
+    return f32(_softmax(f64(x), axis=axis))
+
+
+def f16_softmax(x):
+    """``f16(softmax(f64(x)))`` (expressions_extra.py:305-306, x_d_f16_softmax)."""
+    return f16(_softmax(f64(x)))
 
 
 def rmsnorm_sqrt(x, w, eps):
@@ -228,6 +293,20 @@ PROBLEM_REFS = {
     "x_r_sum100": lambda x: [total_sum(x)],
     "x_r_sum1000": lambda x: [total_sum(x)],
     "x_r_mean_3d": lambda x: [row_mean(x)],
+    "x_r_colsum": lambda x: [axis_sum(x, 0)],
+    "x_r_sum_dim0": lambda x: [axis_sum(x, 0)],
+    "x_r_unpinned_rows": lambda x: [axis_sum(x, -1)],
+    "x_r_mean_mid_3d": lambda x: [axis_mean(x, 1)],
+    "x_f_layernorm_ish": lambda x: [layernorm_ish(x)],
+    "x_f_max_sub": lambda x: [max_sub(x)],
+    "x_f_layernorm": lambda x, w, b: [layernorm(x, w, b)],
+    "x_f_log_softmax": lambda x: [log_softmax(x)],
+    "x_f_rmsnorm_silu": lambda x: [rmsnorm_silu(x)],
+    "x_f_softmax_dim0": lambda x: [softmax_axis(x, 0)],
+    "x_d_f16_softmax": lambda x: [f16_softmax(x)],
+    "x_d_f16_sum": lambda x: [f16_sum(x)],
+    "x_d_f16_mean": lambda x: [f16_row_mean(x)],
+    "x_d_f16_sq_mean": lambda x: [f16_sq_mean(x)],
     "x_h_mm_1024": lambda a, b: [mm_f16(a, b)],
     "x_h_mm_256": lambda a, b: [mm_f16(a, b)],
     "x_h_mm_relu": lambda a, b: [np.maximum(mm_f16(a, b), f16(0))],

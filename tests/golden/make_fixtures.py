@@ -38,6 +38,14 @@ FIXTURES = [
     "tests/problems/x_h_bmm_t", "tests/problems/x_h_linear", "tests/problems/x_h_linear_bias_gelu",
     "tests/problems/x_h_sdpa", "tests/problems/x_h_attn_128", "tests/problems/x_h_attn",
     "tests/problems/x_h_attn_b", "tests/problems/x_h_sdpa_causal", "tests/problems/x_h_sdpa_mask",
+    # more reduction shapes: column / leading-axis sums, middle-axis mean, fused row ops
+    "tests/problems/x_f_layernorm_ish", "tests/problems/x_f_max_sub", "tests/problems/x_f_rmsnorm_silu",
+    "tests/problems/x_f_softmax_dim0", "tests/problems/x_r_colsum", "tests/problems/x_r_sum_dim0",
+    "tests/problems/x_r_mean_mid_3d", "tests/problems/x_r_unpinned_rows", "tests/problems/x_f_layernorm",
+    "tests/problems/x_f_log_softmax",
+    # f16-input reductions (f32 math, f16 result)
+    "tests/problems/x_d_f16_softmax", "tests/problems/x_d_f16_sum", "tests/problems/x_d_f16_mean",
+    "tests/problems/x_d_f16_sq_mean",
 ]
 
 

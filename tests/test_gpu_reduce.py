@@ -10,7 +10,10 @@ from conftest import GOLDEN
 REDUCE = ["f01_rmsnorm", "f02_row_softmax", "f03_l2norm", "r01_array_sum", "r02_big_sum", "r03_mean",
           "r04_row_sum", "x_l_rmsnorm_w", "x_r_unpinned_sum", "x_r_rowmax", "x_r_mean_rows",
           "x_r_rowsum_wide", "x_f_softmax_wide", "x_f_softmax_scaled", "x_f_softmax_odd", "x_r_sumsq",
-          "x_r_max", "x_r_abs_max", "x_r_sum100", "x_r_sum1000", "x_r_mean_3d"]
+          "x_r_max", "x_r_abs_max", "x_r_sum100", "x_r_sum1000", "x_r_mean_3d",
+          # leading / middle axes, split rows, fused row kernels
+          "x_r_colsum", "x_r_sum_dim0", "x_r_mean_mid_3d", "x_r_unpinned_rows", "x_f_layernorm_ish",
+          "x_f_max_sub", "x_f_rmsnorm_silu", "x_f_softmax_dim0", "x_f_layernorm", "x_f_log_softmax"]
 
 
 @pytest.mark.gpu
