@@ -37,6 +37,13 @@ def select(spec) -> str:
             return emit_attention_module(cfg)
         from .reduce import emit_reduction
         return emit_reduction(spec)
+    # no cooperative combine and no tensor-core work: one element per thread (the sum
+    # of split-K partial slices, elementwise tails)
+    from .pointwise import emit_map
+    try:
+        return emit_map(spec)
+    except NotImplementedError:
+        pass
     raise NotImplementedError(
         f"kernel {spec.name}: no sm_100a template for this IR family "
         "(tensor-core GEMM, tensor-core attention and cooperative reductions are supported)")

@@ -62,6 +62,8 @@ class GemmConfig:
     arg_params: list | None = None   # signature (meta.json arg_order) when compiled from IR
     buffers: tuple = ()              # pointer params to load (name list) for IR kernels
     pair: bool = False               # CTA pair (cta_group::2): 256-row tiles, B split by column
+    zero_slots: int = 0              # split-K partials: the full product goes to slice 0 of C and
+    slot_stride: int = 0             # these many further slices (slot_stride elements apart) are zeroed
 
     BM = 128                         # accumulator rows per CTA
 
@@ -528,6 +530,10 @@ def _emit_epilogue(p: Ptx, cfg: GemmConfig, ptr: dict, bars, tfull0, tempty0, tb
         res_adr[name] = a
     nchunks = BN // 32
     regs = [p.reg("b32") for _ in range(32)]
+    zf = p.reg("f32")
+    p.emit(f"mov.f32 {zf}, 0f00000000")
+    if cfg.zero_slots and cfg.c != "f32":
+        raise NotImplementedError("split-K partial slices other than f32")
     for ch in range(nchunks):
         p.emit(f"tcgen05.ld.sync.aligned.32x32b.x32.b32 {{{', '.join(regs)}}}, [{taddr}+{ch * 32}]")
         p.emit("tcgen05.wait::ld.sync.aligned")
@@ -564,12 +570,17 @@ def _emit_epilogue(p: Ptx, cfg: GemmConfig, ptr: dict, bars, tfull0, tempty0, tb
                 p.emit(f"add.u32 {colr}, {n0}, {col0 + 4 * g}\nsetp.lt.u32 {pg}, {colr}, {N}")
                 p.emit(f"@{pg} st.global.v4.f32 [{cadr}+{(col0 + 4 * g) * 4}], "
                        f"{{{', '.join(vals[4 * g:4 * g + 4])}}}")
+                for sl in range(1, cfg.zero_slots + 1):
+                    p.emit(f"@{pg} st.global.v4.f32 [{cadr}+{(sl * cfg.slot_stride + col0 + 4 * g) * 4}], "
+                           f"{{{zf}, {zf}, {zf}, {zf}}}")
         else:
             for i in range(32):
                 pg, colr = p.reg("pred"), p.reg("u32")
                 p.emit(f"add.u32 {colr}, {n0}, {col0 + i}\nsetp.lt.u32 {pg}, {colr}, {N}")
                 if cfg.c == "f32":
                     p.emit(f"@{pg} st.global.f32 [{cadr}+{(col0 + i) * 4}], {vals[i]}")
+                    for sl in range(1, cfg.zero_slots + 1):
+                        p.emit(f"@{pg} st.global.f32 [{cadr}+{(sl * cfg.slot_stride + col0 + i) * 4}], {zf}")
                 else:
                     h = p.reg("b16")
                     cvt = "cvt.rn.bf16.f32" if cfg.c == "bf16" else "cvt.rn.f16.f32"
@@ -641,6 +652,14 @@ def analyze(spec) -> GemmConfig:
     if any(s.atomic for s in stores):
         raise NotImplementedError("split-K partial matmul (atomic RegStore)")
     cname = stores[0].dst_buffer
+    # emmy's split-K schedule: a `*_ks` tile axis gives each CTA one K slice and the
+    # partial products go to slice ks of an f32 [S, ..., M, N] buffer that a second
+    # kernel sums; here the whole K runs in one pass into slice 0, the others are zeroed
+    tile = spec.body[0] if len(spec.body) == 1 and type(spec.body[0]).__name__ == "Tile" else None
+    ks_axes = [a for a in (tile.axes if tile else ()) if a.name.endswith("_ks")]
+    if len(ks_axes) > 1:
+        raise NotImplementedError("more than one split-K axis")
+    ks = ks_axes[0] if ks_axes else None
     # the K loop: the Loop that (transitively) holds the MmaSyncPtx statements
     kvar = None
     for s in stmts:
@@ -685,7 +704,18 @@ def analyze(spec) -> GemmConfig:
     N = B.shape[-2] if b_kmajor else B.shape[-1]
     if (B.shape[-1] if b_kmajor else B.shape[-2]) != K or tuple(C.shape[-2:]) != (M, N):
         raise NotImplementedError("operand shapes do not form a matmul")
-    batch = int(math.prod(C.shape[:-2])) if len(C.shape) > 2 else 1
+    split = {}
+    cdims = C.shape
+    if ks is not None:
+        S = int(ks.extent.value)
+        kloop = next(x for x in stmts if type(x).__name__ in ("Loop", "StridedLoop") and x.axis.name == kvar)
+        first = stores[0].dst_index[0] if stores[0].dst_index else None
+        if C.dtype != "f32" or cdims[0] != S or _vars(first) != {ks.name} or \
+                S * int(kloop.axis.extent.value) != K:
+            raise NotImplementedError("split-K partial that does not slice K exactly")
+        cdims = cdims[1:]
+        split = dict(zero_slots=S - 1, slot_stride=int(math.prod(cdims)))
+    batch = int(math.prod(cdims[:-2])) if len(cdims) > 2 else 1
     if batch > 1 and (math.prod(A.shape[:-2]) != batch or math.prod(B.shape[:-2]) != batch):
         raise NotImplementedError("broadcast batch operands")
     eb = 2
@@ -695,7 +725,7 @@ def analyze(spec) -> GemmConfig:
     tiling = choose_tiling(M, N, batch, 32 if b_kmajor else 64)
     return GemmConfig(M=M, N=N, K=K, batch=batch, ab=A.dtype, c=C.dtype, b_kmajor=b_kmajor, **tiling,
                       epilogue=epi, name=spec.name, a_param=aname, b_param=bname, c_param=cname,
-                      arg_params=arg_params(spec), buffers=tuple(q.name for q in spec.params))
+                      arg_params=arg_params(spec), buffers=tuple(q.name for q in spec.params), **split)
 
 
 def _epilogue_ops(spec, store) -> tuple:

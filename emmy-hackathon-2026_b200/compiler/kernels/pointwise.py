@@ -1,0 +1,173 @@
+"""Element-map kernels: one output element per thread, short serial loops unrolled.
+
+Emmy lowers the second half of a split-K matmul (``tests/problems/x_h_mm_rect``,
+``x_h_bmm``, ``x_h_mm_bias``: ``k_matmul`` / ``k_add``) as a tile over the output
+elements whose body sums the ``S`` partial slices in a serial ``Loop`` and applies the
+rest of the graph (a rounding to the output dtype, a bias add) before the ``Write``.
+The same shape covers elementwise kernels in general.  There is no cooperative axis,
+no combine and no tensor-core work: the template maps the tile's elements onto a
+grid-stride loop of threads, evaluates each ``Load`` index as an affine function of
+the tile axes (serial loop variables are unrolled to constants), and lowers the IR's
+scalar statements with per-op f16 / bf16 rounding where the IR types a result so.
+"""
+
+from __future__ import annotations
+
+import math
+
+from ..ptx import Ptx, entry, f32_hex, module
+from ..stmts import ScalarCtx, Val, lower_body
+from .common import affine_offset, arg_params, load_pointer
+
+ELEM = {"f32": 4, "f16": 2, "bf16": 2}
+MAX_UNROLL = 64          # serial loops up to this many iterations are unrolled
+CTA = 256
+
+
+class MapKernel:
+    def __init__(self, spec):
+        self.spec = spec
+        if len(spec.body) != 1 or type(spec.body[0]).__name__ != "Tile":
+            raise NotImplementedError("element map: body is not one Tile")
+        tile = spec.body[0]
+        if any(a.name.endswith("_co") for a in tile.axes):
+            raise NotImplementedError("element map: cooperative axis")
+        self.tile = tile
+        self.axes = list(tile.axes)
+        self.ext = {a.name: int(a.extent.value) for a in self.axes}
+        self.n = math.prod(self.ext.values())
+        self.writes = 0
+        self._check(tile.body)
+        if not self.writes:
+            raise NotImplementedError("element map: the kernel writes nothing")
+
+    def _check(self, body):
+        for s in body:
+            k = type(s).__name__
+            if k == "Loop":
+                if int(s.axis.extent.value) > MAX_UNROLL:
+                    raise NotImplementedError("element map: serial loop too long to unroll")
+                self._check(s.body)
+            elif k == "Write":
+                if s.atomic or len(s.values) != 1:
+                    raise NotImplementedError("element map: atomic or vector Write")
+                self._buffer(s.output)
+                self.writes += 1
+            elif k == "Load":
+                if s.input not in self.spec.constants:
+                    self._buffer(s.input)
+                if len(s.names) != 1:
+                    raise NotImplementedError("element map: multi-value Load")
+            elif k not in ("Assign", "Let", "Init", "Accum"):
+                raise NotImplementedError(f"element map: statement {k}")
+
+    def _buffer(self, name):
+        dt = self.spec.param(name).dtype
+        if dt not in ELEM:
+            raise NotImplementedError(f"element map: buffer {name} is {dt}")
+        return dt
+
+    # -- emission --------------------------------------------------------------
+    def emit(self) -> str:
+        spec = self.spec
+        p = Ptx()
+        p.comment(f"element map: {self.n} elements over {[a.name for a in self.axes]}")
+        self.ptrs = {q.name: load_pointer(p, q.name) for q in spec.params if not q.scalar}
+        i, step = p.reg("u32"), p.reg("u32")
+        p.emit(f"""
+            mov.u32 {i}, %ctaid.x
+            mov.u32 {step}, %tid.x
+            mad.lo.u32 {i}, {i}, {CTA}, {step}
+            mov.u32 {step}, %nctaid.x
+            mul.lo.u32 {step}, {step}, {CTA}
+        """)
+        top, done = p.label("elem"), p.label("elem_done")
+        p.place(top)
+        pe = p.reg("pred")
+        p.emit(f"setp.ge.u32 {pe}, {i}, {self.n}\n@{pe} bra {done}")
+        # the tile axes of element i, row-major
+        self.axis_reg = {}
+        rem = i
+        for a in reversed(self.axes):
+            r = p.reg("u32")
+            if a is self.axes[0]:
+                p.emit(f"mov.u32 {r}, {rem}")
+            else:
+                q = p.reg("u32")
+                p.emit(f"rem.u32 {r}, {rem}, {self.ext[a.name]}\ndiv.u32 {q}, {rem}, {self.ext[a.name]}")
+                rem = q
+            self.axis_reg[a.name] = r
+        ctx = ScalarCtx(p, constants=dict(spec.constants), half_results=True)
+        ctx.on_load = self._load
+        ctx.on_write = self._write
+        self.fixed = {}
+        self._lower(ctx, self.tile.body)
+        p.emit(f"add.u32 {i}, {i}, {step}\nbra {top}")
+        p.place(done)
+        p.emit("ret")
+        blocks = max(1, min(-(-self.n // CTA), 148 * 8))
+        launch = {"kind": "map", "grid": [blocks, 1, 1], "block": [CTA, 1, 1], "cluster": [1, 1, 1],
+                  "smem": 0, "extra_params": []}
+        return module([entry(spec.name, arg_params(spec), p, maxntid=CTA)], launch)
+
+    def _lower(self, ctx, body):
+        for s in body:
+            k = type(s).__name__
+            if k == "Loop":
+                # accumulators updated in the loop start at their op's identity
+                for st in s.body:
+                    if type(st).__name__ == "Accum" and st.name not in ctx.env:
+                        r = ctx.ptx.reg("f32")
+                        ctx.ptx.emit(f"mov.f32 {r}, {f32_hex(float(st.op.identity))}")
+                        ctx.env[st.name] = Val(r, "f32")
+                        ctx.mutable.add(st.name)
+                for v in range(int(s.axis.extent.value)):
+                    self.fixed[s.axis.name] = v
+                    saved = dict(ctx.env)
+                    self._lower(ctx, s.body)
+                    keep = {n: ctx.env[n] for n in ctx.mutable if n in ctx.env}
+                    ctx.env = saved
+                    ctx.env.update(keep)
+                del self.fixed[s.axis.name]
+            else:
+                lower_body(ctx, [s])
+
+    def _address(self, buffer: str, index) -> str:
+        shape = self.spec.param(buffer).shape
+        aff = affine_offset(tuple(index), shape, dict(self.ext), fixed=dict(self.fixed))
+        ptx = self._ptx
+        off = ptx.reg("b64")
+        ptx.emit(f"mov.u64 {off}, {aff.const}")
+        for var, c in aff.coef:
+            w = ptx.reg("b64")
+            ptx.emit(f"cvt.u64.u32 {w}, {self.axis_reg[var]}\nmad.lo.s64 {off}, {w}, {c}, {off}")
+        addr = ptx.reg("b64")
+        ptx.emit(f"mad.lo.s64 {addr}, {off}, {ELEM[self._buffer(buffer)]}, {self.ptrs[buffer]}")
+        return addr
+
+    def _load(self, ctx: ScalarCtx, s):
+        self._ptx = ctx.ptx
+        dt = self._buffer(s.input)
+        addr = self._address(s.input, s.index)
+        r = ctx.ptx.reg("f32")
+        if dt == "f32":
+            ctx.ptx.emit(f"ld.global.f32 {r}, [{addr}]")
+        else:
+            h = ctx.ptx.reg("b16")
+            ctx.ptx.emit(f"ld.global.b16 {h}, [{addr}]\ncvt.f32.{dt} {r}, {h}")
+        ctx.env[s.names[0]] = Val(r, "f32")
+
+    def _write(self, ctx: ScalarCtx, w):
+        self._ptx = ctx.ptx
+        dt = self._buffer(w.output)
+        addr = self._address(w.output, w.index)
+        v = ctx.f32(w.values[0])
+        if dt == "f32":
+            ctx.ptx.emit(f"st.global.f32 [{addr}], {v}")
+        else:
+            h = ctx.ptx.reg("b16")
+            ctx.ptx.emit(f"cvt.rn.{dt}.f32 {h}, {v}\nst.global.b16 [{addr}], {h}")
+
+
+def emit_map(spec) -> str:
+    return MapKernel(spec).emit()

@@ -77,6 +77,7 @@ class ScalarCtx:
     axis_regs: dict = field(default_factory=dict)    # axis name -> s32 register / immediate
     max_states: set = field(default_factory=set)     # accumulators holding a row maximum
     exp_reuse: Callable | None = None                # fn(element register, max state) -> register
+    half_results: bool = False                       # f16 / bf16 results rounded per op (else rejected)
 
     def bind(self, name: str, val: Val) -> None:
         if name in self.mutable and name in self.env:
@@ -215,17 +216,34 @@ def compute_f32(ctx: ScalarCtx, op: str, args: list[str], dst: str | None = None
 # handlers
 
 
-def _check_f32(dt, what: str) -> None:
+def _check_f32(dt, what: str, ctx: ScalarCtx | None = None) -> None:
     n = dtype_name(dt)
+    if n in ("f16", "bf16") and ctx is not None and ctx.half_results:
+        return
     if n not in (None, "f32"):
         raise NotImplementedError(f"{what} of dtype {n}: this back end computes reductions in f32")
 
 
+def round_half(ctx: ScalarCtx, dt, reg: str) -> str:
+    """A result of IR dtype f16 / bf16: the f32 value rounded to that type (nearest
+    even) and widened back, as the reference rounds every 16-bit op's result
+    (``compiler/dtypes.py:148-180``)."""
+    n = dtype_name(dt)
+    if n not in ("f16", "bf16"):
+        return reg
+    p = ctx.ptx
+    h, out = p.reg("b16"), p.reg("f32")
+    p.emit(f"cvt.rn.{n}.f32 {h}, {reg}\ncvt.f32.{n} {out}, {h}")
+    return out
+
+
 @handles("Assign")
 def lower_assign(ctx: ScalarCtx, s) -> None:
-    _check_f32(s.dtype, "Assign")
+    _check_f32(s.dtype, "Assign", ctx)
     target = ctx.env[s.name].text if (s.name in ctx.mutable and s.name in ctx.env) else None
     val = compute_f32(ctx, s.op.name, list(s.args), dst=None)
+    if dtype_name(s.dtype) in ("f16", "bf16"):
+        val = Val(round_half(ctx, s.dtype, val.text), "f32")
     if target is not None:
         ctx.ptx.emit(f"mov.f32 {target}, {val.text}")
     else:
@@ -256,11 +274,13 @@ def lower_accum(ctx: ScalarCtx, s) -> None:
     """``acc = op(base or acc, value)`` into the accumulator's own register
     (the reference: ``compiler/stmts.py:441-467``).  The template seeds the
     accumulator register with the op's identity before the loop."""
-    _check_f32(s.dtype, "Accum")
+    _check_f32(s.dtype, "Accum", ctx)
     acc = ctx.get(s.name)
     left = s.base or s.name
     a, b = ctx.f32(left), ctx.f32(s.value)
     _binary(ctx.ptx, s.op.name, acc.text, a, b)
+    if dtype_name(s.dtype) in ("f16", "bf16"):
+        ctx.ptx.emit(f"mov.f32 {acc.text}, {round_half(ctx, s.dtype, acc.text)}")
 
 
 @handles("Load")
@@ -268,8 +288,11 @@ def lower_load(ctx: ScalarCtx, s) -> None:
     if all(n in ctx.env for n in s.names):
         return   # bound by the template (vector lane or cached value)
     if len(s.names) == 1 and s.input in ctx.constants:
-        _check_f32(s.dtype, "constant Load")
+        _check_f32(s.dtype, "constant Load", ctx)
         v = float(ctx.constants[s.input])
+        if dtype_name(s.dtype) == "f16" and ctx.half_results:
+            import numpy as np
+            v = float(np.float16(v))       # the constant as the f16 buffer holds it
         ctx.env[s.names[0]] = Val(f32_hex(v), "f32", v)
         return
     if ctx.on_load is None:

@@ -316,6 +316,9 @@ PROBLEM_REFS = {
     "x_h_bmm_t": lambda q, k: [mm_f16(q, np.swapaxes(k, -1, -2))],
     "x_h_linear_bias_gelu": lambda x, w, b: [f16(gelu(f64(mm_f16(x, w.T) + b)))],
     "x_h_mm_residual": lambda a, b, r: [mm_f16(a, b) + r],
+    "x_h_mm_rect": lambda a, b: [mm_f16(a, b)],
+    "x_h_bmm": lambda a, b: [mm_f16(a, b)],
+    "x_h_mm_bias": lambda a, b, c: [mm_f16(a, b) + c],
     "x_h_attn": lambda q, kt, v: [attn_f16(q, kt, v, 1 / 8)],
     "x_h_attn_128": lambda q, kt, v: [attn_f16(q, kt, v, 1 / 8)],
     "x_h_attn_b": lambda q, kt, v: [attn_f16(q, kt, v, 1 / 5.66)],

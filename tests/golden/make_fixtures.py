@@ -46,6 +46,8 @@ FIXTURES = [
     # f16-input reductions (f32 math, f16 result)
     "tests/problems/x_d_f16_softmax", "tests/problems/x_d_f16_sum", "tests/problems/x_d_f16_mean",
     "tests/problems/x_d_f16_sq_mean",
+    # emmy's split-K matmul pairs (partial products + a kernel summing them)
+    "tests/problems/x_h_mm_rect", "tests/problems/x_h_bmm", "tests/problems/x_h_mm_bias",
 ]
 
 
