@@ -249,11 +249,62 @@ def _accums(stmts):
     return out
 
 
+ESZ = {"f32": 4, "f16": 2, "bf16": 2}
+
+
 def _check_buffer(spec, name):
+    """The buffer's IR dtype: f32, or f16 / bf16 (widened to f32 on load, rounded on
+    store; the arithmetic stays f32 with the IR's per-op 16-bit roundings)."""
     p = spec.param(name)
-    if p.dtype != "f32":
-        raise NotImplementedError(f"buffer {name} is {p.dtype}; reductions are f32")
-    return p
+    if p.dtype not in ESZ:
+        raise NotImplementedError(f"buffer {name} is {p.dtype}; reductions read f32, f16 or bf16")
+    return p.dtype
+
+
+def ld_vec(p, dt: str, regs: list, addr: str, guard: str = "", cache: str = "") -> None:
+    """Load len(regs) consecutive elements of type ``dt`` at [addr] into f32 registers."""
+    n = len(regs)
+    if dt == "f32":
+        if n == 1:
+            p.emit(f"{guard}ld.global{cache}.f32 {regs[0]}, [{addr}]")
+        else:
+            p.emit(f"{guard}ld.global{cache}.v{n}.f32 {{{', '.join(regs)}}}, [{addr}]")
+        return
+    if n == 1:
+        h = p.reg("b16")
+        p.emit(f"{guard}ld.global{cache}.b16 {h}, [{addr}]\ncvt.f32.{dt} {regs[0]}, {h}")
+        return
+    words = [p.reg("b32") for _ in range(n // 2)]
+    vec = f".v{len(words)}" if len(words) > 1 else ""
+    p.emit(f"{guard}ld.global{cache}{vec}.b32 {{{', '.join(words)}}}, [{addr}]" if vec else
+           f"{guard}ld.global{cache}.b32 {words[0]}, [{addr}]")
+    for i, w in enumerate(words):
+        lo, hi = p.reg("b16"), p.reg("b16")
+        # the lower address holds the first element
+        p.emit(f"mov.b32 {{{lo}, {hi}}}, {w}\ncvt.f32.{dt} {regs[2 * i]}, {lo}\n"
+               f"cvt.f32.{dt} {regs[2 * i + 1]}, {hi}")
+
+
+def st_vec(p, dt: str, vals: list, addr: str, guard: str = "") -> None:
+    """Store len(vals) f32 values as consecutive elements of type ``dt`` at [addr]."""
+    n = len(vals)
+    if dt == "f32":
+        if n == 1:
+            p.emit(f"{guard}st.global.f32 [{addr}], {vals[0]}")
+        else:
+            p.emit(f"{guard}st.global.v{n}.f32 [{addr}], {{{', '.join(vals)}}}")
+        return
+    if n == 1:
+        h = p.reg("b16")
+        p.emit(f"cvt.rn.{dt}.f32 {h}, {vals[0]}\n{guard}st.global.b16 [{addr}], {h}")
+        return
+    words = [p.reg("b32") for _ in range(n // 2)]
+    for i, w in enumerate(words):
+        p.emit(f"cvt.rn.{dt}x2.f32 {w}, {vals[2 * i + 1]}, {vals[2 * i]}")
+    if len(words) == 1:
+        p.emit(f"{guard}st.global.b32 [{addr}], {words[0]}")
+    else:
+        p.emit(f"{guard}st.global.v{len(words)}.b32 [{addr}], {{{', '.join(words)}}}")
 
 
 # ---------------------------------------------------------------------------
@@ -380,7 +431,7 @@ class RowReduce:
         self.base_cache = {}    # (buffer, aff) -> u64 address of chunk 0, lane 0
         self.val_cache = {}     # (buffer, aff, chunk) -> [regs]
 
-        ctx = ScalarCtx(p, constants=dict(spec.constants))
+        ctx = ScalarCtx(p, constants=dict(spec.constants), half_results=True)
         ctx.on_load = self._scalar_load
         ctx.on_write = self._leader_write
         # exp(x - M) in a later pass, for an element x whose exp(x - m_t) the online
@@ -452,7 +503,7 @@ class RowReduce:
             w = p.reg("b64")
             p.emit(f"cvt.u64.u32 {w}, {src}\nmad.lo.s64 {off}, {w}, {c}, {off}")
         addr = p.reg("b64")
-        p.emit(f"mad.lo.s64 {addr}, {off}, 4, {self.ptrs[buffer]}")
+        p.emit(f"mad.lo.s64 {addr}, {off}, {ESZ[_check_buffer(self.spec, buffer)]}, {self.ptrs[buffer]}")
         self.base_cache[key] = addr
         return addr
 
@@ -614,11 +665,9 @@ class RowReduce:
                 addr = self._row_base(acc.buffer, acc.aff)
                 pc = self._chunk_pred(c)
                 guard = f"@{pc} " if pc else ""
-                off = c * span * acc.col_coef * 4      # chunk c: span columns further on
-                if self.VEC == 4:
-                    p.emit(f"{guard}ld.global.v4.f32 {{{', '.join(regs)}}}, [{addr}+{off}]")
-                else:
-                    p.emit(f"{guard}ld.global.f32 {regs[0]}, [{addr}+{off}]")
+                dt = _check_buffer(self.spec, acc.buffer)
+                off = c * span * acc.col_coef * ESZ[dt]      # chunk c: span columns further on
+                ld_vec(p, dt, regs, f"{addr}+{off}", guard)
                 self.val_cache[key] = regs
 
     def _emit_stream(self, ctx: ScalarCtx, loop):
@@ -635,7 +684,7 @@ class RowReduce:
             key = (acc.buffer, acc.aff, "row")
             if key not in self.val_cache:
                 r = p.reg("f32")
-                p.emit(f"ld.global.f32 {r}, [{self._row_base(acc.buffer, acc.aff)}]")
+                ld_vec(p, _check_buffer(self.spec, acc.buffer), [r], self._row_base(acc.buffer, acc.aff))
                 self.val_cache[key] = [r]
         # 2a. the online-softmax accumulator pair over full chunks: register-resident rewrite
         writes = [s for s in loop.body if type(s).__name__ == "Write"]
@@ -671,11 +720,9 @@ class RowReduce:
                 acc = self.accesses[id(w)]
                 addr = self._row_base(acc.buffer, acc.aff)
                 vals = outvals[id(w)]
-                off = c * span * acc.col_coef * 4
-                if self.VEC == 4:
-                    p.emit(f"@{self.pvalid} st.global.v4.f32 [{addr}+{off}], {{{', '.join(vals)}}}")
-                else:
-                    p.emit(f"@{self.pvalid} st.global.f32 [{addr}+{off}], {vals[0]}")
+                dt = _check_buffer(self.spec, acc.buffer)
+                off = c * span * acc.col_coef * ESZ[dt]
+                st_vec(p, dt, vals, f"{addr}+{off}", f"@{self.pvalid} ")
             if skip:
                 p.place(skip)
 
@@ -734,25 +781,30 @@ class RowReduce:
 
     def _scalar_load(self, ctx: ScalarCtx, s):
         """A Load outside the streams: a row-constant value (e.g. a per-row bias)."""
-        _check_buffer(self.spec, s.input)
+        dt = _check_buffer(self.spec, s.input)
         if len(s.names) != 1:
             raise NotImplementedError("multi-value scalar Load")
         shape = self.spec.param(s.input).shape
         aff = affine_offset(tuple(s.index), shape, self.row_ext)
         r = ctx.ptx.reg("f32")
-        ctx.ptx.emit(f"ld.global.f32 {r}, [{self._row_base(s.input, aff)}]")
+        ld_vec(ctx.ptx, dt, [r], self._row_base(s.input, aff))
         ctx.env[s.names[0]] = Val(r, "f32")
 
     def _leader_write(self, ctx: ScalarCtx, w):
         """A Write in the leader section: one value per row."""
-        _check_buffer(self.spec, w.output)
+        dt = _check_buffer(self.spec, w.output)
         if len(w.values) != 1:
             raise NotImplementedError("vector leader Write")
         shape = self.spec.param(w.output).shape
         aff = affine_offset(tuple(w.index), shape, self.row_ext)
-        # an atomic (+=) output gets one add per row: the whole row is summed here
-        op = "red.global.add.f32" if w.atomic else "st.global.f32"
-        ctx.ptx.emit(f"{op} [{self._row_base(w.output, aff)}], {ctx.f32(w.values[0])}")
+        addr = self._row_base(w.output, aff)
+        if w.atomic:
+            # an atomic (+=) output gets one add per row: the whole row is summed here
+            if dt != "f32":
+                raise NotImplementedError("atomic 16-bit row result")
+            ctx.ptx.emit(f"red.global.add.f32 [{addr}], {ctx.f32(w.values[0])}")
+        else:
+            st_vec(ctx.ptx, dt, [ctx.f32(w.values[0])], addr)
 
 
 def _rename(expr, old: str, new: str):
@@ -814,7 +866,8 @@ class FullReduce:
         if len(loads) != 1 or len(loads[0].names) != 1:
             raise NotImplementedError("whole-array reduction must stream exactly one buffer")
         self.load = loads[0]
-        _check_buffer(spec, self.load.input)
+        self.dt = _check_buffer(spec, self.load.input)
+        self.esz = ESZ[self.dt]
         ranges = {"__i": self.L}
         if others:
             ranges["_ksplit"] = ks
@@ -824,7 +877,8 @@ class FullReduce:
             raise NotImplementedError("reduced elements are not one contiguous run")
         if ks > 1 and aff.get("_ksplit") != self.L:
             raise NotImplementedError("split axis is not the outer block of the run")
-        self.VEC = 4 if self.count % 4 == 0 else 1
+        vw = 16 // self.esz                      # elements in one 128-bit load
+        self.VEC = vw if self.count % vw == 0 else 1
         per_iter = self.CTA * self.VEC * self.UNROLL
         self.grid = max(1, min(SMS * self.CTAS_PER_SM, -(-self.count // per_iter)))
         self.scratch_bytes = 16 + 8 * self.grid
@@ -848,7 +902,7 @@ class FullReduce:
         """.replace("%r_cta", p.named_reg("%cta", "u32")))
         p.emit(f"cvt.u64.u32 {nthr}, {tid}\nadd.s64 {gtid}, {gtid}, {nthr}")
         total_thr = self.grid * self.CTA
-        ctx = ScalarCtx(p, constants=dict(spec.constants))
+        ctx = ScalarCtx(p, constants=dict(spec.constants), half_results=True)
 
         # per-thread accumulators: f64 for sums (f32 groups of VEC*UNROLL folded in),
         # f32 for max/min (exact)
@@ -899,18 +953,16 @@ class FullReduce:
         lane0, wid = p.reg("u32"), p.reg("b64")
         p.emit(f"and.b32 {lane0}, {tid}, 31\nshr.u64 {wid}, {gtid}, 5\nmov.u64 {wi}, {wid}")
         lane_off = p.reg("b64")
-        p.emit(f"mul.wide.u32 {lane_off}, {lane0}, {self.VEC * 4}")
+        p.emit(f"mul.wide.u32 {lane_off}, {lane0}, {self.VEC * self.esz}")
         p.place(loop)
         p.emit(f"setp.ge.u64 {pg}, {wi}, {nspans}\n@{pg} bra {done}")
         addr = p.reg("b64")
-        p.emit(f"mad.lo.s64 {addr}, {wi}, {span * 4}, {x}\nadd.s64 {addr}, {addr}, {lane_off}")
+        p.emit(f"mad.lo.s64 {addr}, {wi}, {span * self.esz}, {x}\nadd.s64 {addr}, {addr}, {lane_off}")
         vals = []
         for u in range(self.UNROLL):
             regs = p.regs("f32", self.VEC)
-            if self.VEC == 4:
-                p.emit(f"ld.global.nc.L1::no_allocate.v4.f32 {{{', '.join(regs)}}}, [{addr}+{u * 32 * 16}]")
-            else:
-                p.emit(f"ld.global.nc.f32 {regs[0]}, [{addr}+{u * 32 * 4}]")
+            ld_vec(p, self.dt, regs, f"{addr}+{u * 32 * self.VEC * self.esz}",
+                   cache=".nc.L1::no_allocate" if self.VEC > 1 else ".nc")
             vals += regs
         grp = fold_elements(vals)
         if is_add:
@@ -927,7 +979,8 @@ class FullReduce:
             p.place(tl)
             p.emit(f"setp.ge.u64 {pt}, {ti}, {self.count}\n@{pt} bra {td}")
             v, a2 = p.reg("f32"), p.reg("b64")
-            p.emit(f"mad.lo.s64 {a2}, {ti}, 4, {x}\nld.global.nc.f32 {v}, [{a2}]")
+            p.emit(f"mad.lo.s64 {a2}, {ti}, {self.esz}, {x}")
+            ld_vec(p, self.dt, [v], a2, cache=".nc")
             grp = fold_elements([v])
             if is_add:
                 gd = p.reg("f64")
@@ -1003,7 +1056,7 @@ class FullReduce:
         p.emit(f"st.global.u32 [{scratch}], 0")
         fin = p.reg("f32")
         p.emit(f"cvt.rn.f32.f64 {fin}, {tot}")
-        lctx = ScalarCtx(p, constants=dict(spec.constants))
+        lctx = ScalarCtx(p, constants=dict(spec.constants), half_results=True)
         lctx.env[self.acc.name] = Val(fin, "f32")
         lctx.on_write = self._final_write(ptrs)
         for ph in self.tail:
@@ -1030,7 +1083,7 @@ class FullReduce:
 
     def _final_write(self, ptrs):
         def on_write(ctx, w):
-            _check_buffer(self.spec, w.output)
+            dt = _check_buffer(self.spec, w.output)
             if len(w.values) != 1:
                 raise NotImplementedError("vector result write")
             shape = self.spec.param(w.output).shape
@@ -1040,7 +1093,7 @@ class FullReduce:
             off = flat_offset(tuple(w.index), shape, {})
             # the IR's atomic add into a zeroed scalar and this single store of the
             # full sum leave the same value (the runner re-zeroes atomic outputs)
-            ctx.ptx.emit(f"st.global.f32 [{ptrs[w.output]}+{off * 4}], {ctx.f32(w.values[0])}")
+            st_vec(ctx.ptx, dt, [ctx.f32(w.values[0])], f"{ptrs[w.output]}+{off * ESZ[dt]}")
         return on_write
 
 
