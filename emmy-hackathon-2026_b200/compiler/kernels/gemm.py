@@ -62,6 +62,7 @@ class GemmConfig:
     arg_params: list | None = None   # signature (meta.json arg_order) when compiled from IR
     buffers: tuple = ()              # pointer params to load (name list) for IR kernels
     pair: bool = False               # CTA pair (cta_group::2): 256-row tiles, B split by column
+    operand_dtypes: tuple = ()       # (buffer, dtype) of epilogue operands
     zero_slots: int = 0              # split-K partials: the full product goes to slice 0 of C and
     slot_stride: int = 0             # these many further slices (slot_stride elements apart) are zeroed
 
@@ -464,10 +465,15 @@ def _emit_epilogue(p: Ptx, cfg: GemmConfig, ptr: dict, bars, tfull0, tempty0, tb
     lane_off = p.reg("u32")
     p.emit(f"shl.b32 {lane_off}, {q}, 21")           # (q * 32) << 16: the warp's TMEM lane quarter
     cptr = ptr[cfg.c_param]
-    extra = {}
+    extra, kinds = {}, {}
     for op in cfg.epilogue:
         if op[0] in ("bias", "residual"):
             extra[op[1]] = ptr[op[1]]
+            kinds[op[1]] = op[0]
+        elif op[0] == "lambda":
+            for _, kind, buf in op[2]:
+                extra[buf] = ptr[buf]
+                kinds[buf] = kind
     scale = None
     for op in cfg.epilogue:
         if op[0] == "scale2":
@@ -521,7 +527,7 @@ def _emit_epilogue(p: Ptx, cfg: GemmConfig, ptr: dict, bars, tfull0, tempty0, tb
     res_adr = {}
     for name, bp in extra.items():
         a = p.reg("b64")
-        kind = [o[0] for o in cfg.epilogue if len(o) > 1 and o[1] == name][0]
+        kind = kinds[name]
         if kind == "residual":
             p.emit(f"mad.lo.s64 {a}, {off}, 2, {bp}")
         else:   # bias over N: element n0
@@ -617,9 +623,27 @@ def _apply_epilogue(p: Ptx, cfg: GemmConfig, vals: list, scale, res_adr: dict, c
                 h, r = p.reg("b16"), p.reg("f32")
                 p.emit(f"ld.global.b16 {h}, [{a}+{(ch * 32 + i) * 2}]\n{up} {r}, {h}\n"
                        f"add.rn.f32 {v}, {v}, {r}")
+        elif kind == "lambda":
+            from ..stmts import ScalarCtx, Val, lower_body
+            lam, operands, consts = op[1], op[2], dict(op[3])
+            for i, v in enumerate(vals):
+                ctx = ScalarCtx(p, constants=consts, half_results=True)
+                ctx.env[lam.params[0]] = Val(v, "f32")
+                for lname, _, buf in operands:
+                    h, r = p.reg("b16"), p.reg("f32")
+                    cv = "cvt.f32.f16" if _elem_dtype(cfg, buf) == "f16" else "cvt.f32.bf16"
+                    p.emit(f"ld.global.b16 {h}, [{res_adr[buf]}+{(ch * 32 + i) * 2}]\n{cv} {r}, {h}")
+                    ctx.env[lname] = Val(r, "f32")
+                lower_body(ctx, lam.body)
+                p.emit(f"mov.f32 {v}, {ctx.f32(lam.results[0])}")
         else:
             raise NotImplementedError(f"GEMM epilogue {kind}")
     return vals
+
+
+def _elem_dtype(cfg: GemmConfig, buf: str) -> str:
+    """A 16-bit epilogue operand's dtype (the IR's; the C type when not recorded)."""
+    return dict(cfg.operand_dtypes).get(buf, cfg.c)
 
 
 # ---------------------------------------------------------------------------
@@ -722,20 +746,52 @@ def analyze(spec) -> GemmConfig:
     if (K * eb) % 16 or (not b_kmajor and (N * eb) % 16):
         raise NotImplementedError("operand rows are not 16-byte aligned (TMA)")
     epi = _epilogue_ops(spec, stores[0])
+    od = tuple((q.name, q.dtype) for q in spec.params if q.dtype in ("f16", "bf16"))
     tiling = choose_tiling(M, N, batch, 32 if b_kmajor else 64)
     return GemmConfig(M=M, N=N, K=K, batch=batch, ab=A.dtype, c=C.dtype, b_kmajor=b_kmajor, **tiling,
                       epilogue=epi, name=spec.name, a_param=aname, b_param=bname, c_param=cname,
-                      arg_params=arg_params(spec), buffers=tuple(q.name for q in spec.params), **split)
+                      arg_params=arg_params(spec), buffers=tuple(q.name for q in spec.params),
+                      operand_dtypes=od, **split)
 
 
 def _epilogue_ops(spec, store) -> tuple:
     """The RegStore epilogue Lambda (``mma.py:347-357`` in the reference) as fused ops,
     in statement order: ``copy`` to a 16-bit dtype rounds the accumulator the way
     torch's f16/bf16 matmul result is rounded before the next op; ``relu``; ``add`` of
-    a loaded operand (a C-shaped residual, or a bias over N)."""
+    a loaded operand (a C-shaped residual, or a bias over N).  Any other Lambda (with
+    constants, erf, ...) is lowered statement by statement per element."""
     lam = store.epilogue
     if lam is None:
         return ()
+    try:
+        return _epilogue_patterns(spec, store)
+    except NotImplementedError:
+        return (("lambda", lam, _lambda_operands(spec, store), tuple(sorted(spec.constants.items()))),)
+
+
+def _lambda_operands(spec, store) -> tuple:
+    """(load name, kind, buffer) of each buffer the Lambda reads: a C-shaped residual
+    or a bias over N (``__N__``, the element's column, in its index)."""
+    out = []
+    cshape = spec.param(store.dst_buffer).shape
+    for s in store.epilogue.body:
+        if type(s).__name__ == "Load" and s.input not in spec.constants:
+            shape = spec.param(s.input).shape
+            if tuple(shape) == tuple(cshape):
+                out.append((s.names[0], "residual", s.input))
+            elif len(shape) == 1 and shape[0] == cshape[-1]:
+                out.append((s.names[0], "bias", s.input))
+            else:
+                raise NotImplementedError("GEMM epilogue operand shape")
+            if spec.param(s.input).dtype not in ("f16", "bf16"):
+                raise NotImplementedError("GEMM epilogue operand dtype")
+        elif type(s).__name__ not in ("Load", "Assign", "Let"):
+            raise NotImplementedError(f"GEMM epilogue statement {type(s).__name__}")
+    return tuple(out)
+
+
+def _epilogue_patterns(spec, store) -> tuple:
+    lam = store.epilogue
     ops = []
     loads = {}
     for s in lam.body:

@@ -140,6 +140,35 @@ def emit_exp(p: Ptx, dst: str, x: str) -> None:
     """)
 
 
+# erf by Abramowitz & Stegun, Handbook of Mathematical Functions, 7.1.26:
+# erf(x) = 1 - (a1 t + a2 t^2 + a3 t^3 + a4 t^4 + a5 t^5) exp(-x^2), t = 1 / (1 + p x),
+# x >= 0, |error| <= 1.5e-7; odd extension for x < 0
+_AS_P = 0.3275911
+_AS_A = (0.254829592, -0.284496736, 1.421413741, -1.453152027, 1.061405429)
+
+
+def emit_erf(p: Ptx, dst: str, x: str) -> None:
+    ax, t, q, e, x2, r = (p.reg("f32") for _ in range(6))
+    p.emit(f"""
+        abs.f32 {ax}, {x}
+        fma.rn.f32 {t}, {ax}, {f32_hex(_AS_P)}, 0f3F800000
+        rcp.rn.f32 {t}, {t}
+        fma.rn.f32 {q}, {t}, {f32_hex(_AS_A[4])}, {f32_hex(_AS_A[3])}
+        fma.rn.f32 {q}, {q}, {t}, {f32_hex(_AS_A[2])}
+        fma.rn.f32 {q}, {q}, {t}, {f32_hex(_AS_A[1])}
+        fma.rn.f32 {q}, {q}, {t}, {f32_hex(_AS_A[0])}
+        mul.rn.f32 {q}, {q}, {t}
+        mul.rn.f32 {x2}, {ax}, {ax}
+        neg.f32 {x2}, {x2}
+    """)
+    emit_exp(p, e, x2)
+    p.emit(f"""
+        neg.f32 {q}, {q}
+        fma.rn.f32 {r}, {q}, {e}, 0f3F800000
+        copysign.f32 {dst}, {x}, {r}
+    """)
+
+
 def _unary(p: Ptx, op: str, dst: str, a: str) -> None:
     if op == "copy":
         p.emit(f"mov.f32 {dst}, {a}")
@@ -162,6 +191,8 @@ def _unary(p: Ptx, op: str, dst: str, a: str) -> None:
         p.emit(f"max.f32 {dst}, {a}, 0f00000000")
     elif op == "square":
         p.emit(f"mul.rn.f32 {dst}, {a}, {a}")
+    elif op == "erf":
+        emit_erf(p, dst, a)
     elif op == "log":
         # ln x = log2(x) * ln 2 on the MUFU lg2 unit (about 2^-22 absolute error for
         # x in [1/2, 2], a few ulp relative elsewhere)
