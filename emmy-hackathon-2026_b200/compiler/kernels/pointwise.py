@@ -16,7 +16,7 @@ from __future__ import annotations
 import math
 
 from ..ptx import Ptx, entry, f32_hex, module
-from ..stmts import ScalarCtx, Val, lower_body
+from ..stmts import ScalarCtx, Val, load_index_vars, lower_body, matmul_kernel
 from .common import affine_offset, arg_params, load_pointer
 
 ELEM = {"f32": 4, "f16": 2, "bf16": 2}
@@ -97,7 +97,8 @@ class MapKernel:
                 p.emit(f"rem.u32 {r}, {rem}, {self.ext[a.name]}\ndiv.u32 {q}, {rem}, {self.ext[a.name]}")
                 rem = q
             self.axis_reg[a.name] = r
-        ctx = ScalarCtx(p, constants=dict(spec.constants), half_results=True)
+        ctx = ScalarCtx(p, constants=dict(spec.constants), half_results=True,
+                        exact_products=matmul_kernel(spec.name), index_vars=load_index_vars(spec.body))
         ctx.on_load = self._load
         ctx.on_write = self._write
         self.fixed = {}

@@ -37,7 +37,8 @@ import math
 from dataclasses import dataclass, field
 
 from ..ptx import Ptx, entry, f32_hex, f64_hex, module
-from ..stmts import ScalarCtx, Val, dtype_name, emit_exp_nonpos, expr_vars, lower_body
+from ..stmts import (ScalarCtx, Val, dtype_name, emit_exp_nonpos, expr_vars, load_index_vars,
+                     lower_body, matmul_kernel)
 from .common import Affine, affine_offset, arg_params, load_pointer
 
 SMS = 148          # B200 multiprocessors (grid sizing for the streaming reduction)
@@ -431,7 +432,8 @@ class RowReduce:
         self.base_cache = {}    # (buffer, aff) -> u64 address of chunk 0, lane 0
         self.val_cache = {}     # (buffer, aff, chunk) -> [regs]
 
-        ctx = ScalarCtx(p, constants=dict(spec.constants), half_results=True)
+        ctx = ScalarCtx(p, constants=dict(spec.constants), half_results=True,
+                        exact_products=matmul_kernel(spec.name), index_vars=load_index_vars(spec.body))
         ctx.on_load = self._scalar_load
         ctx.on_write = self._leader_write
         # exp(x - M) in a later pass, for an element x whose exp(x - m_t) the online
@@ -902,7 +904,8 @@ class FullReduce:
         """.replace("%r_cta", p.named_reg("%cta", "u32")))
         p.emit(f"cvt.u64.u32 {nthr}, {tid}\nadd.s64 {gtid}, {gtid}, {nthr}")
         total_thr = self.grid * self.CTA
-        ctx = ScalarCtx(p, constants=dict(spec.constants), half_results=True)
+        ctx = ScalarCtx(p, constants=dict(spec.constants), half_results=True,
+                        exact_products=matmul_kernel(spec.name), index_vars=load_index_vars(spec.body))
 
         # per-thread accumulators: f64 for sums (f32 groups of VEC*UNROLL folded in),
         # f32 for max/min (exact)

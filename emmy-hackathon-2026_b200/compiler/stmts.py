@@ -21,6 +21,7 @@ folded to an immediate).
 
 from __future__ import annotations
 
+import re
 from dataclasses import dataclass, field
 from typing import Callable
 
@@ -78,6 +79,8 @@ class ScalarCtx:
     max_states: set = field(default_factory=set)     # accumulators holding a row maximum
     exp_reuse: Callable | None = None                # fn(element register, max state) -> register
     half_results: bool = False                       # f16 / bf16 results rounded per op (else rejected)
+    exact_products: bool = False                     # a matmul kernel: 16-bit products stay exact
+    index_vars: dict = field(default_factory=dict)   # loaded name -> index variables of its Load
 
     def bind(self, name: str, val: Val) -> None:
         if name in self.mutable and name in self.env:
@@ -268,12 +271,58 @@ def round_half(ctx: ScalarCtx, dt, reg: str) -> str:
     return out
 
 
+# torch ops whose 16-bit products are summed exactly in f32 (cuBLAS, flash attention):
+# the reference tells them from an elementwise product-sum by the kernel's name
+# (``compiler/__init__.py:16-32``); the op list has to be the same to round alike
+_MATMUL_OPS = re.compile(r"(?:^|_)(?:matmul|mm|bmm|addmm|baddbmm|addbmm|mv|addmv|dot|inner|"
+                         r"tensordot|linear|bilinear|sdpa|einsum)(?:_|$)")
+
+
+def matmul_kernel(name: str) -> bool:
+    """Does the kernel compute a torch matmul (its 16-bit products are not rounded)?"""
+    return bool(_MATMUL_OPS.search(name.removeprefix("k_")))
+
+
+def load_index_vars(body) -> dict:
+    """Loaded name -> the index variables of its Load, over a whole kernel body."""
+    out = {}
+
+    def walk(stmts):
+        for s in stmts:
+            if type(s).__name__ == "Load":
+                vs = set()
+                for e in s.index:
+                    vs |= expr_vars(e)
+                for n in s.names:
+                    out[n] = vs
+            for attr in ("body", "else_body"):
+                sub = getattr(s, attr, None)
+                if isinstance(sub, tuple):
+                    walk(sub)
+    walk(body)
+    return out
+
+
+def _contraction(ctx: ScalarCtx, args) -> bool:
+    """``a * b`` as a matmul step by its indexing: each operand is indexed by a variable
+    the other lacks (an outer product summed over the shared one), as the reference
+    decides it (``compiler/stmts.py:421-430``)."""
+    if len(args) != 2:
+        return False
+    a, b = (ctx.index_vars.get(n) for n in args)
+    return bool(a and b and a - b and b - a)
+
+
 @handles("Assign")
 def lower_assign(ctx: ScalarCtx, s) -> None:
     _check_f32(s.dtype, "Assign", ctx)
     target = ctx.env[s.name].text if (s.name in ctx.mutable and s.name in ctx.env) else None
     val = compute_f32(ctx, s.op.name, list(s.args), dst=None)
-    if dtype_name(s.dtype) in ("f16", "bf16"):
+    if s.op.name == "copy" and len(s.args) == 1 and s.args[0] in ctx.index_vars:
+        ctx.index_vars[s.name] = ctx.index_vars[s.args[0]]     # `f16 v0 = copy(in0)`
+    exact = s.op.name == "multiply" and (ctx.exact_products or _contraction(ctx, s.args))
+    if dtype_name(s.dtype) in ("f16", "bf16") and not exact:
+        # (a product of two 16-bit values is exact in f32: kept as is in a matmul)
         val = Val(round_half(ctx, s.dtype, val.text), "f32")
     if target is not None:
         ctx.ptx.emit(f"mov.f32 {target}, {val.text}")

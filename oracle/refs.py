@@ -207,6 +207,20 @@ def attn_f16(q, kt, v, scale, causal=False, mask=None):
     return f16(f64(f16(_softmax(s))) @ f64(v))
 
 
+def f16_dot(a, b, out):
+    """Row dot products of f16 vectors whose elementwise products are rounded to f16
+    first (their own torch op), summed in f64: ``out(f64(f16(f32(a) * f32(b))).sum(-1))``
+    (expressions_extra.py:313-316, x_d_f16_dot / x_d_f16_dot_f32)."""
+    return out(f64(f16(f32(a) * f32(b))).sum(-1))
+
+
+def swiglu(x, w1, w3):
+    """``silu(x @ w1) * (x @ w3)`` in f64, ``silu(y) = y / (1 + exp(-y))``
+    (expressions_llm.py:66-68, x_l_swiglu)."""
+    g = f64(x) @ f64(w1)
+    return f32(g / (1 + np.exp(-g)) * (f64(x) @ f64(w3)))
+
+
 def gelu(x):
     """Exact (erf) GELU, ``0.5 x (1 + erf(x / sqrt 2))`` (expressions_extra.py:66-67)."""
     from math import erf, sqrt
@@ -317,6 +331,17 @@ PROBLEM_REFS = {
     "x_h_linear_bias_gelu": lambda x, w, b: [f16(gelu(f64(mm_f16(x, w.T) + b)))],
     "x_h_mm_residual": lambda a, b, r: [mm_f16(a, b) + r],
     "x_h_mm_rect": lambda a, b: [mm_f16(a, b)],
+    "x_h_mm_16": lambda a, b: [mm_f16(a, b)],
+    "x_h_mm_64": lambda a, b: [mm_f16(a, b)],
+    "x_h_mm_128": lambda a, b: [mm_f16(a, b)],
+    "x_h_mm_t": lambda a, b: [mm_f16(a, b.T)],
+    "x_h_mm_vec": lambda a, b: [mm_f16(a, b)],
+    "x_q_f16_mm_t": lambda a, b: [f32(mm_f16(f16(a), f16(b).T))],
+    "x_d_f16_dot": lambda a, b: [f16_dot(a, b, f16)],
+    "x_d_f16_dot_f32": lambda a, b: [f16_dot(a, b, f32)],
+    "x_l_swiglu": lambda x, w1, w3: [swiglu(x, w1, w3)],
+    "x_p_odd7": lambda a, b: [a + b],
+    "x_p_odd1001": lambda a, b: [a * b],
     "x_h_bmm": lambda a, b: [mm_f16(a, b)],
     "x_h_mm_bias": lambda a, b, c: [mm_f16(a, b) + c],
     "x_h_attn": lambda q, kt, v: [attn_f16(q, kt, v, 1 / 8)],

@@ -48,6 +48,12 @@ FIXTURES = [
     "tests/problems/x_d_f16_sq_mean",
     # emmy's split-K matmul pairs (partial products + a kernel summing them)
     "tests/problems/x_h_mm_rect", "tests/problems/x_h_bmm", "tests/problems/x_h_mm_bias",
+    # more GEMM shapes (small, transposed B, vector x matrix), f16 dot rows, an f32 SwiGLU,
+    # elementwise kernels of odd length
+    "tests/problems/x_h_mm_16", "tests/problems/x_h_mm_64", "tests/problems/x_h_mm_128",
+    "tests/problems/x_h_mm_t", "tests/problems/x_h_mm_vec", "tests/problems/x_q_f16_mm_t",
+    "tests/problems/x_d_f16_dot", "tests/problems/x_d_f16_dot_f32", "tests/problems/x_l_swiglu",
+    "tests/problems/x_p_odd7", "tests/problems/x_p_odd1001",
 ]
 
 
