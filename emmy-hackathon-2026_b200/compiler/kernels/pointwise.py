@@ -49,15 +49,15 @@ class MapKernel:
                     raise NotImplementedError("element map: serial loop too long to unroll")
                 self._check(s.body)
             elif k == "Write":
-                if s.atomic or len(s.values) != 1:
-                    raise NotImplementedError("element map: atomic or vector Write")
+                if s.atomic:
+                    raise NotImplementedError("element map: atomic Write")
                 self._buffer(s.output)
                 self.writes += 1
             elif k == "Load":
                 if s.input not in self.spec.constants:
                     self._buffer(s.input)
-                if len(s.names) != 1:
-                    raise NotImplementedError("element map: multi-value Load")
+                elif len(s.names) != 1:
+                    raise NotImplementedError("element map: multi-value constant Load")
             elif k not in ("Assign", "Let", "Init", "Accum"):
                 raise NotImplementedError(f"element map: statement {k}")
 
@@ -147,27 +147,33 @@ class MapKernel:
         return addr
 
     def _load(self, ctx: ScalarCtx, s):
+        """``names[k]`` of a multi-value Load is the element k after the index."""
         self._ptx = ctx.ptx
         dt = self._buffer(s.input)
         addr = self._address(s.input, s.index)
-        r = ctx.ptx.reg("f32")
-        if dt == "f32":
-            ctx.ptx.emit(f"ld.global.f32 {r}, [{addr}]")
-        else:
-            h = ctx.ptx.reg("b16")
-            ctx.ptx.emit(f"ld.global.b16 {h}, [{addr}]\ncvt.f32.{dt} {r}, {h}")
-        ctx.env[s.names[0]] = Val(r, "f32")
+        for k, name in enumerate(s.names):
+            r = ctx.ptx.reg("f32")
+            off = k * ELEM[dt]
+            if dt == "f32":
+                ctx.ptx.emit(f"ld.global.f32 {r}, [{addr}+{off}]")
+            else:
+                h = ctx.ptx.reg("b16")
+                ctx.ptx.emit(f"ld.global.b16 {h}, [{addr}+{off}]\ncvt.f32.{dt} {r}, {h}")
+            ctx.env[name] = Val(r, "f32")
 
     def _write(self, ctx: ScalarCtx, w):
+        """``values[k]`` of a multi-value Write goes to the element k after the index."""
         self._ptx = ctx.ptx
         dt = self._buffer(w.output)
         addr = self._address(w.output, w.index)
-        v = ctx.f32(w.values[0])
-        if dt == "f32":
-            ctx.ptx.emit(f"st.global.f32 [{addr}], {v}")
-        else:
-            h = ctx.ptx.reg("b16")
-            ctx.ptx.emit(f"cvt.rn.{dt}.f32 {h}, {v}\nst.global.b16 [{addr}], {h}")
+        for k, name in enumerate(w.values):
+            v = ctx.f32(name)
+            off = k * ELEM[dt]
+            if dt == "f32":
+                ctx.ptx.emit(f"st.global.f32 [{addr}+{off}], {v}")
+            else:
+                h = ctx.ptx.reg("b16")
+                ctx.ptx.emit(f"cvt.rn.{dt}.f32 {h}, {v}\nst.global.b16 [{addr}+{off}], {h}")
 
 
 def emit_map(spec) -> str:

@@ -250,23 +250,34 @@ def compute_f32(ctx: ScalarCtx, op: str, args: list[str], dst: str | None = None
 # handlers
 
 
+NARROW = ("f16", "bf16", "f8e4m3")     # result types rounded per op (values stay f32)
+
+
 def _check_f32(dt, what: str, ctx: ScalarCtx | None = None) -> None:
     n = dtype_name(dt)
-    if n in ("f16", "bf16") and ctx is not None and ctx.half_results:
+    if n in NARROW and ctx is not None and ctx.half_results:
         return
     if n not in (None, "f32"):
         raise NotImplementedError(f"{what} of dtype {n}: this back end computes reductions in f32")
 
 
 def round_half(ctx: ScalarCtx, dt, reg: str) -> str:
-    """A result of IR dtype f16 / bf16: the f32 value rounded to that type (nearest
-    even) and widened back, as the reference rounds every 16-bit op's result
-    (``compiler/dtypes.py:148-180``)."""
+    """A result of IR dtype f16 / bf16 / f8e4m3: the f32 value rounded to that type
+    (nearest even; e4m3 saturating at +-448 like torch's float8_e4m3fn cast) and widened
+    back, as the reference rounds every narrow op's result (``compiler/dtypes.py:148-227``)."""
     n = dtype_name(dt)
-    if n not in ("f16", "bf16"):
+    if n not in NARROW:
         return reg
     p = ctx.ptx
-    h, out = p.reg("b16"), p.reg("f32")
+    out = p.reg("f32")
+    if n == "f8e4m3":
+        # e4m3 pair (value, 0) -> f16 pair -> the value's half -> f32; every e4m3 value is
+        # exact in f16
+        q, hh, lo, hi = p.reg("b16"), p.reg("b32"), p.reg("b16"), p.reg("b16")
+        p.emit(f"cvt.rn.satfinite.e4m3x2.f32 {q}, 0f00000000, {reg}\n"
+               f"cvt.rn.f16x2.e4m3x2 {hh}, {q}\nmov.b32 {{{lo}, {hi}}}, {hh}\ncvt.f32.f16 {out}, {lo}")
+        return out
+    h = p.reg("b16")
     p.emit(f"cvt.rn.{n}.f32 {h}, {reg}\ncvt.f32.{n} {out}, {h}")
     return out
 
@@ -321,7 +332,7 @@ def lower_assign(ctx: ScalarCtx, s) -> None:
     if s.op.name == "copy" and len(s.args) == 1 and s.args[0] in ctx.index_vars:
         ctx.index_vars[s.name] = ctx.index_vars[s.args[0]]     # `f16 v0 = copy(in0)`
     exact = s.op.name == "multiply" and (ctx.exact_products or _contraction(ctx, s.args))
-    if dtype_name(s.dtype) in ("f16", "bf16") and not exact:
+    if dtype_name(s.dtype) in NARROW and not exact:
         # (a product of two 16-bit values is exact in f32: kept as is in a matmul)
         val = Val(round_half(ctx, s.dtype, val.text), "f32")
     if target is not None:
@@ -359,7 +370,7 @@ def lower_accum(ctx: ScalarCtx, s) -> None:
     left = s.base or s.name
     a, b = ctx.f32(left), ctx.f32(s.value)
     _binary(ctx.ptx, s.op.name, acc.text, a, b)
-    if dtype_name(s.dtype) in ("f16", "bf16"):
+    if dtype_name(s.dtype) in NARROW:
         ctx.ptx.emit(f"mov.f32 {acc.text}, {round_half(ctx, s.dtype, acc.text)}")
 
 
@@ -370,9 +381,6 @@ def lower_load(ctx: ScalarCtx, s) -> None:
     if len(s.names) == 1 and s.input in ctx.constants:
         _check_f32(s.dtype, "constant Load", ctx)
         v = float(ctx.constants[s.input])
-        if dtype_name(s.dtype) == "f16" and ctx.half_results:
-            import numpy as np
-            v = float(np.float16(v))       # the constant as the f16 buffer holds it
         ctx.env[s.names[0]] = Val(f32_hex(v), "f32", v)
         return
     if ctx.on_load is None:

@@ -48,11 +48,15 @@ def _rewrite_body(text: str, dims: dict, dtypes: dict) -> str:
 
 
 def rescale(src_dir: Path, dims: dict, dtypes: dict | None = None, constants: dict | None = None,
-            shapes: dict | None = None, problem_id: str | None = None) -> tuple[dict, dict]:
-    """Rescale one fixture problem; returns (ir_json_by_entry, meta)."""
+            shapes: dict | None = None, problem_id: str | None = None,
+            const_dtypes: dict | None = None) -> tuple[dict, dict]:
+    """Rescale one fixture problem; returns (ir_json_by_entry, meta).  ``const_dtypes``
+    gives named constant buffers their own dtype (e.g. an exact f32 softmax scale in a
+    bf16 problem)."""
     dtypes = dtypes or {}
     constants = constants or {}
     shapes = shapes or {}
+    const_dtypes = const_dtypes or {}
     meta = json.loads((src_dir / "meta.json").read_text())
     irs = {}
     for k in meta["kernels"]:
@@ -60,7 +64,7 @@ def rescale(src_dir: Path, dims: dict, dtypes: dict | None = None, constants: di
         for node in ir["nodes"].values():
             for o in node["outputs"]:
                 o["shape"] = shapes.get(o["name"], [dims.get(int(d), int(d)) for d in o["shape"]])
-                o["dtype"] = dtypes.get(o["dtype"], o["dtype"])
+                o["dtype"] = const_dtypes.get(o["name"], dtypes.get(o["dtype"], o["dtype"]))
             if node["op"] == "ConstantOp":
                 nid = node["op_fields"]["name"]
                 if nid in constants:
@@ -71,7 +75,7 @@ def rescale(src_dir: Path, dims: dict, dtypes: dict | None = None, constants: di
         irs[k["entry"]] = ir
         for a in k["args"]:
             a["shape"] = shapes.get(a["name"], [dims.get(int(d), int(d)) for d in a["shape"]])
-            a["dtype"] = dtypes.get(a["dtype"], a["dtype"])
+            a["dtype"] = const_dtypes.get(a["name"], dtypes.get(a["dtype"], a["dtype"]))
             if a["name"] in constants:
                 a["data"] = [constants[a["name"]]]
     meta = copy.deepcopy(meta)
@@ -115,6 +119,7 @@ def baseline_problem(name: str, golden: Path = GOLDEN) -> tuple[dict, dict]:
         return rescale(golden / "x_h_sdpa", {}, dtypes={"f16": "bf16"},
                        shapes={"x0": shp, "x1": shp, "x2": shp, "scaled_dot_product_attention": shp},
                        constants={"scaled_dot_product_attention_scale": 128 ** -0.5},
+                       const_dtypes={"scaled_dot_product_attention_scale": "f32"},
                        problem_id="attention_b8h32s4096d128")
     raise KeyError(name)
 

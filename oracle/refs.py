@@ -235,6 +235,13 @@ def bf16_round(a) -> np.ndarray:
     return u.view(np.float32)
 
 
+def bf16_math(a, b):
+    """``(a.bf16() * b.bf16() + a.bf16()).float()``: each bf16 op computed in f32 and
+    rounded to bf16 (expressions_quant.py:31-33, x_q_bf16_math)."""
+    A, B = bf16_round(a), bf16_round(b)
+    return bf16_round(bf16_round(A * B) + A)
+
+
 def mm_bf16(a, b):
     """bf16 GEMM with f32 accumulation and a bf16 result, evaluated on the
     bf16-valued operands in f64 (the BASELINE GEMM; x_q_bf16_mm's
@@ -341,6 +348,13 @@ PROBLEM_REFS = {
     "x_d_f16_dot_f32": lambda a, b: [f16_dot(a, b, f32)],
     "x_l_swiglu": lambda x, w1, w3: [swiglu(x, w1, w3)],
     "x_p_odd7": lambda a, b: [a + b],
+    "x_q_fp8_e4m3": lambda x: [e4m3_round(x)],
+    "x_q_fp8_e4m3_sat": lambda x: [e4m3_round(f32(x * f32(300.0)))],
+    "x_q_fp8_scaled": lambda x: [e4m3_round(f32(x * f32(64.0))) / f32(64.0)],
+    "x_q_bf16_cast": lambda x: [bf16_round(x)],
+    "x_q_bf16_math": lambda a, b: [bf16_math(a, b)],
+    # the scalar stays f32 (torch's opmath; the kernel folds the constant buffer's value)
+    "x_q_f16_scalar": lambda x: [f32(f16(f32(f16(x)) * f32(0.1)))],
     "x_p_odd1001": lambda a, b: [a * b],
     "x_h_bmm": lambda a, b: [mm_f16(a, b)],
     "x_h_mm_bias": lambda a, b, c: [mm_f16(a, b) + c],

@@ -54,6 +54,9 @@ FIXTURES = [
     "tests/problems/x_h_mm_t", "tests/problems/x_h_mm_vec", "tests/problems/x_q_f16_mm_t",
     "tests/problems/x_d_f16_dot", "tests/problems/x_d_f16_dot_f32", "tests/problems/x_l_swiglu",
     "tests/problems/x_p_odd7", "tests/problems/x_p_odd1001",
+    # low-precision casts inside kernels: e4m3 (saturating), bf16, f16 with a constant
+    "tests/problems/x_q_fp8_e4m3", "tests/problems/x_q_fp8_e4m3_sat", "tests/problems/x_q_fp8_scaled",
+    "tests/problems/x_q_bf16_cast", "tests/problems/x_q_bf16_math", "tests/problems/x_q_f16_scalar",
 ]
 
 

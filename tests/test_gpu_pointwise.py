@@ -1,4 +1,5 @@
-"""Element-map kernels on the B200 against the golden vectors (exact for f32 add / mul)."""
+"""Element-map kernels on the B200 against the golden vectors: f32 add / mul, e4m3 / bf16 / f16
+casts inside a kernel (all exact: rtol = atol = 0 in the fixtures)."""
 
 import json
 
@@ -7,7 +8,8 @@ import pytest
 
 from conftest import GOLDEN
 
-MAP = ["x_p_odd7", "x_p_odd1001"]
+MAP = ["x_p_odd7", "x_p_odd1001", "x_q_fp8_e4m3", "x_q_fp8_e4m3_sat", "x_q_fp8_scaled", "x_q_bf16_cast",
+       "x_q_bf16_math", "x_q_f16_scalar"]
 
 
 @pytest.mark.gpu
