@@ -20,7 +20,7 @@ from ..stmts import ScalarCtx, Val, load_index_vars, lower_body, matmul_kernel
 from .common import affine_offset, arg_params, load_pointer
 
 ELEM = {"f32": 4, "f16": 2, "bf16": 2}
-MAX_UNROLL = 64          # serial loops up to this many iterations are unrolled
+UNROLL = 8               # serial loops up to this many iterations are unrolled, longer ones loop
 CTA = 256
 
 
@@ -34,7 +34,7 @@ class MapKernel:
             raise NotImplementedError("element map: cooperative axis")
         self.tile = tile
         self.axes = list(tile.axes)
-        self.ext = {a.name: int(a.extent.value) for a in self.axes}
+        self.ext = {a.name: int(a.extent.value) for a in self.axes}   # + serial loop axes in scope
         self.n = math.prod(self.ext.values())
         self.writes = 0
         self._check(tile.body)
@@ -45,8 +45,6 @@ class MapKernel:
         for s in body:
             k = type(s).__name__
             if k == "Loop":
-                if int(s.axis.extent.value) > MAX_UNROLL:
-                    raise NotImplementedError("element map: serial loop too long to unroll")
                 self._check(s.body)
             elif k == "Write":
                 if s.atomic:
@@ -112,26 +110,48 @@ class MapKernel:
         return module([entry(spec.name, arg_params(spec), p, maxntid=CTA)], launch)
 
     def _lower(self, ctx, body):
+        p = ctx.ptx
         for s in body:
             k = type(s).__name__
-            if k == "Loop":
-                # accumulators updated in the loop start at their op's identity
-                for st in s.body:
-                    if type(st).__name__ == "Accum" and st.name not in ctx.env:
-                        r = ctx.ptx.reg("f32")
-                        ctx.ptx.emit(f"mov.f32 {r}, {f32_hex(float(st.op.identity))}")
-                        ctx.env[st.name] = Val(r, "f32")
-                        ctx.mutable.add(st.name)
-                for v in range(int(s.axis.extent.value)):
-                    self.fixed[s.axis.name] = v
-                    saved = dict(ctx.env)
-                    self._lower(ctx, s.body)
-                    keep = {n: ctx.env[n] for n in ctx.mutable if n in ctx.env}
-                    ctx.env = saved
-                    ctx.env.update(keep)
-                del self.fixed[s.axis.name]
-            else:
+            if k != "Loop":
                 lower_body(ctx, [s])
+                continue
+            # a seeding loop starts the accumulators it folds into at their op's identity
+            # every time it runs (the reference's _seed_accumulators, stmts.py:131-139)
+            if s.seed:
+                for st in s.body:
+                    if type(st).__name__ == "Accum":
+                        if st.name in ctx.env and st.name in ctx.mutable:
+                            r = ctx.env[st.name].text
+                        else:
+                            r = p.reg("f32")
+                            ctx.env[st.name] = Val(r, "f32")
+                            ctx.mutable.add(st.name)
+                        p.emit(f"mov.f32 {r}, {f32_hex(float(st.op.identity))}")
+            ext, name = int(s.axis.extent.value), s.axis.name
+            if ext <= UNROLL:
+                for v in range(ext):
+                    self.fixed[name] = v
+                    self._body_scope(ctx, s.body)
+                del self.fixed[name]
+                continue
+            r, pl = p.reg("u32"), p.reg("pred")
+            top = p.label("serial")
+            p.emit(f"mov.u32 {r}, 0")
+            p.place(top)
+            self.axis_reg[name], self.ext[name] = r, ext
+            self._body_scope(ctx, s.body)
+            del self.axis_reg[name], self.ext[name]
+            p.emit(f"add.u32 {r}, {r}, 1\nsetp.lt.u32 {pl}, {r}, {ext}\n@{pl} bra {top}")
+
+    def _body_scope(self, ctx, body):
+        """Lower a loop body once; its element-local names do not outlive it, the
+        accumulators it updates do."""
+        saved = dict(ctx.env)
+        self._lower(ctx, body)
+        keep = {n: ctx.env[n] for n in ctx.mutable if n in ctx.env}
+        ctx.env = saved
+        ctx.env.update(keep)
 
     def _address(self, buffer: str, index) -> str:
         shape = self.spec.param(buffer).shape

@@ -221,6 +221,13 @@ def swiglu(x, w1, w3):
     return f32(g / (1 + np.exp(-g)) * (f64(x) @ f64(w3)))
 
 
+def linattn(q, k, v):
+    """Causal linear attention ``y_t = q_t . sum_{s<=t} k_s v_s^T`` in f64
+    (expressions_llm.py:38-41)."""
+    state = np.cumsum(f64(k)[:, :, None] * f64(v)[:, None, :], 0)
+    return f32((f64(q)[:, :, None] * state).sum(1))
+
+
 def gelu(x):
     """Exact (erf) GELU, ``0.5 x (1 + erf(x / sqrt 2))`` (expressions_extra.py:66-67)."""
     from math import erf, sqrt
@@ -353,6 +360,50 @@ PROBLEM_REFS = {
     "x_q_fp8_scaled": lambda x: [e4m3_round(f32(x * f32(64.0))) / f32(64.0)],
     "x_q_bf16_cast": lambda x: [bf16_round(x)],
     "x_q_bf16_math": lambda a, b: [bf16_math(a, b)],
+    # -- elementwise (tools/expressions_open.py:33-46, tests/expressions_extra.py:77-175, 295-322)
+    "p00_scalar_add": lambda a, b: [a + b],
+    "p01_vector_add": lambda a, b: [a + b],
+    "p02_scale_shift": lambda x: [x * np.float32(2.0) + np.float32(1.0)],
+    "p03_relu_mul": lambda x, y: [np.maximum(x, 0) * y],
+    "x_p_short_launch": lambda a, b: [a + b],
+    "x_p_sub1000": lambda a, b: [a - b],
+    "x_p_big": lambda a, b: [a + b],
+    "x_p_bcast_row": lambda a, b: [a + b],
+    "x_p_bcast_col": lambda a, b: [a * b],
+    "x_p_3d": lambda a, b: [a * b],
+    "x_p_3d_bcast": lambda a, b: [a + b],
+    "x_p_odd_2d": lambda a, b: [a + b],
+    "x_p_div": lambda x, y: [x / y],
+    "x_p_neg_abs": lambda x: [-np.abs(x)],
+    "x_p_maxmin": lambda x, y: [np.maximum(x, y) - np.minimum(x, y)],
+    "x_p_clamp": lambda x: [np.clip(x, np.float32(-0.5), np.float32(0.5))],
+    "x_p_square": lambda x: [x * x],
+    "x_p_sub_const": lambda x: [np.float32(3.0) - x],
+    "x_p_sqrt": lambda x: [np.sqrt(np.abs(x))],
+    "x_p_chain3": lambda x, y, z: [f32((f64(x) * 1.5 + f64(y)) * f64(z) - 0.25 * f64(x))],
+    "x_p_exp": lambda x: [f32(np.exp(f64(x)))],
+    "x_p_exp_wide": lambda x: [f32(np.exp(f64(np.float32(20.0) * x)))],
+    "x_p_log": lambda x: [f32(np.log(f64(np.abs(x) + np.float32(0.5))))],
+    "x_p_rsqrt": lambda x: [f32(1.0 / np.sqrt(f64(np.abs(x) + np.float32(0.1))))],
+    "x_p_recip": lambda x: [f32(1.0 / f64(np.abs(x) + np.float32(1.0)))],
+    "x_p_silu": lambda x: [f32(f64(x) / (1.0 + np.exp(-f64(x))))],
+    "x_p_gelu": lambda x: [f32(gelu(x))],
+    "x_p_pow_half": lambda x: [f32(np.sqrt(f64(np.abs(x))))],
+    "x_p_softplus": lambda x: [f32(np.logaddexp(0.0, f64(x)))],
+    "x_p_hardtanh_clamp": lambda x: [np.clip(x * np.float32(2), np.float32(-1), np.float32(1))],
+    "x_p_softsign": lambda x: [f32(f64(x) / (1 + np.abs(f64(x))))],
+    "x_p_mul_add_exact": lambda a, b, c: [a * b + c],
+    "x_d_f16_add": lambda a, b: [a + b],
+    "x_d_f16_bcast_mul": lambda a, b: [a * b],
+    "x_d_f16_div_sqrt": lambda x: [x / np.sqrt(np.abs(x) + f16(1))],
+    "x_d_f16_exp": lambda x: [f16(np.exp(f64(x)))],
+    "x_d_f16_gelu": lambda x: [f16(gelu(x))],
+    "x_d_f32_to_f16": lambda x: [f16(x) * f16(2)],
+    "x_d_f16_to_f32": lambda x: [f32(x) * np.float32(3)],
+    # -- f32 attention and causal linear attention (expressions_open.py:93-98,
+    #    expressions_llm.py:38-41, 62-64)
+    "a01_attention": lambda q, kt, v: [f32(_softmax(f64(q) @ f64(kt) / 8.0) @ f64(v))],
+    "x_l_linattn": lambda q, k, v: [linattn(q, k, v)],
     # the scalar stays f32 (torch's opmath; the kernel folds the constant buffer's value)
     "x_q_f16_scalar": lambda x: [f32(f16(f32(f16(x)) * f32(0.1)))],
     "x_p_odd1001": lambda a, b: [a * b],

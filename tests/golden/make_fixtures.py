@@ -57,6 +57,22 @@ FIXTURES = [
     # low-precision casts inside kernels: e4m3 (saturating), bf16, f16 with a constant
     "tests/problems/x_q_fp8_e4m3", "tests/problems/x_q_fp8_e4m3_sat", "tests/problems/x_q_fp8_scaled",
     "tests/problems/x_q_bf16_cast", "tests/problems/x_q_bf16_math", "tests/problems/x_q_f16_scalar",
+    # element maps of the reference's elementwise set (f32 / f16), its f32 attention and linear
+    # attention problems (emmy lowers them as row reductions)
+    "problems/a01_attention", "problems/p00_scalar_add", "problems/p01_vector_add",
+    "problems/p02_scale_shift", "problems/p03_relu_mul", "tests/problems/x_d_f16_add",
+    "tests/problems/x_d_f16_bcast_mul", "tests/problems/x_d_f16_div_sqrt",
+    "tests/problems/x_d_f16_exp", "tests/problems/x_d_f16_gelu", "tests/problems/x_d_f16_to_f32",
+    "tests/problems/x_d_f32_to_f16", "tests/problems/x_l_linattn", "tests/problems/x_p_3d",
+    "tests/problems/x_p_3d_bcast", "tests/problems/x_p_bcast_col", "tests/problems/x_p_bcast_row",
+    "tests/problems/x_p_big", "tests/problems/x_p_chain3", "tests/problems/x_p_clamp",
+    "tests/problems/x_p_div", "tests/problems/x_p_exp", "tests/problems/x_p_exp_wide",
+    "tests/problems/x_p_gelu", "tests/problems/x_p_hardtanh_clamp", "tests/problems/x_p_log",
+    "tests/problems/x_p_maxmin", "tests/problems/x_p_mul_add_exact", "tests/problems/x_p_neg_abs",
+    "tests/problems/x_p_odd_2d", "tests/problems/x_p_pow_half", "tests/problems/x_p_recip",
+    "tests/problems/x_p_rsqrt", "tests/problems/x_p_short_launch", "tests/problems/x_p_silu",
+    "tests/problems/x_p_softplus", "tests/problems/x_p_softsign", "tests/problems/x_p_sqrt",
+    "tests/problems/x_p_square", "tests/problems/x_p_sub1000", "tests/problems/x_p_sub_const",
 ]
 
 
