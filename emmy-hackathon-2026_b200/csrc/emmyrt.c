@@ -77,6 +77,7 @@ static struct {
     CUresult (*StreamDestroy)(CUstream);
     CUresult (*StreamSynchronize)(CUstream);
     CUresult (*StreamQuery)(CUstream);
+    CUresult (*StreamWaitEvent)(CUstream, CUevent, unsigned);
     CUresult (*EventCreate)(CUevent *, unsigned);
     CUresult (*EventDestroy)(CUevent);
     CUresult (*EventRecord)(CUevent, CUstream);
@@ -126,7 +127,8 @@ static int load_driver(void) {
         E(cuMemcpyDtoHAsync, MemcpyDtoHAsync), E(cuMemcpyDtoDAsync, MemcpyDtoDAsync),
         E(cuMemsetD8Async, MemsetD8Async), E(cuStreamCreate, StreamCreate),
         E(cuStreamDestroy, StreamDestroy), E(cuStreamSynchronize, StreamSynchronize),
-        E(cuStreamQuery, StreamQuery), E(cuEventCreate, EventCreate),
+        E(cuStreamQuery, StreamQuery), E(cuStreamWaitEvent, StreamWaitEvent),
+        E(cuEventCreate, EventCreate),
         E(cuEventDestroy, EventDestroy), E(cuEventRecord, EventRecord),
         E(cuEventSynchronize, EventSynchronize), E(cuEventElapsedTime, EventElapsedTime),
 #undef E
@@ -398,6 +400,12 @@ EXPORT int emmy_rt_stream_wait(uint64_t stream, double timeout_s) {
         struct timespec ts = {0, 200000};
         nanosleep(&ts, NULL);
     }
+}
+
+EXPORT int emmy_rt_stream_wait_event(uint64_t stream, uint64_t event) {
+    NEED_INIT();
+    CU(cu.StreamWaitEvent((CUstream)(uintptr_t)stream, (CUevent)(uintptr_t)event, 0), "cuStreamWaitEvent");
+    return 0;
 }
 
 EXPORT int emmy_rt_event_create(uint64_t *event) {

@@ -63,6 +63,7 @@ SIGNATURES = {
     "emmy_rt_stream_destroy": ([_u64], _int),
     "emmy_rt_stream_synchronize": ([_u64], _int),
     "emmy_rt_stream_wait": ([_u64, ctypes.c_double], _int),
+    "emmy_rt_stream_wait_event": ([_u64, _u64], _int),
     "emmy_rt_event_create": ([_P(_u64)], _int),
     "emmy_rt_event_destroy": ([_u64], _int),
     "emmy_rt_event_record": ([_u64, _u64], _int),
@@ -192,6 +193,25 @@ class HostBuffer:
     def __del__(self):
         try:
             self.free()
+        except Exception:
+            pass
+
+
+class Stream:
+    """A non-blocking stream of the current context (its handle is ``.handle``)."""
+
+    def __init__(self):
+        s = _u64()
+        check(lib.emmy_rt_stream_create(ctypes.byref(s)), "stream create")
+        self.handle = s.value
+
+    def wait(self, event: "Event") -> None:
+        """Later work on this stream waits for ``event``'s latest recording."""
+        check(lib.emmy_rt_stream_wait_event(self.handle, event.handle), "stream wait event")
+
+    def __del__(self):
+        try:
+            lib.emmy_rt_stream_destroy(self.handle)
         except Exception:
             pass
 

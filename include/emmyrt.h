@@ -132,6 +132,11 @@ int emmy_rt_stream_synchronize(uint64_t stream);
 /* Poll the stream until it is idle or `timeout_s` seconds pass (EMMY_RT_ETIMEOUT):
  * the runner's 20 s launch limit (docs/API.md:69) without blocking forever. */
 int emmy_rt_stream_wait(uint64_t stream, double timeout_s);
+/* Work queued on `stream` after this call starts once `event`'s latest recording has
+ * completed (cuStreamWaitEvent): copies of the next step overlap the current kernel.
+ * The runner ran one launch at a time (submit.py:126-135); this orders streams of a
+ * pipelined run instead. */
+int emmy_rt_stream_wait_event(uint64_t stream, uint64_t event);
 int emmy_rt_event_create(uint64_t *event);
 int emmy_rt_event_destroy(uint64_t event);
 int emmy_rt_event_record(uint64_t event, uint64_t stream);
