@@ -78,6 +78,13 @@ static struct {
     CUresult (*StreamSynchronize)(CUstream);
     CUresult (*StreamQuery)(CUstream);
     CUresult (*StreamWaitEvent)(CUstream, CUevent, unsigned);
+    CUresult (*StreamBeginCapture)(CUstream, CUstreamCaptureMode);
+    CUresult (*StreamEndCapture)(CUstream, CUgraph *);
+    CUresult (*GraphInstantiateWithFlags)(CUgraphExec *, CUgraph, unsigned long long);
+    CUresult (*GraphLaunch)(CUgraphExec, CUstream);
+    CUresult (*GraphUpload)(CUgraphExec, CUstream);
+    CUresult (*GraphExecDestroy)(CUgraphExec);
+    CUresult (*GraphDestroy)(CUgraph);
     CUresult (*EventCreate)(CUevent *, unsigned);
     CUresult (*EventDestroy)(CUevent);
     CUresult (*EventRecord)(CUevent, CUstream);
@@ -128,6 +135,10 @@ static int load_driver(void) {
         E(cuMemsetD8Async, MemsetD8Async), E(cuStreamCreate, StreamCreate),
         E(cuStreamDestroy, StreamDestroy), E(cuStreamSynchronize, StreamSynchronize),
         E(cuStreamQuery, StreamQuery), E(cuStreamWaitEvent, StreamWaitEvent),
+        E(cuStreamBeginCapture, StreamBeginCapture), E(cuStreamEndCapture, StreamEndCapture),
+        E(cuGraphInstantiateWithFlags, GraphInstantiateWithFlags), E(cuGraphLaunch, GraphLaunch),
+        E(cuGraphUpload, GraphUpload),
+        E(cuGraphExecDestroy, GraphExecDestroy), E(cuGraphDestroy, GraphDestroy),
         E(cuEventCreate, EventCreate),
         E(cuEventDestroy, EventDestroy), E(cuEventRecord, EventRecord),
         E(cuEventSynchronize, EventSynchronize), E(cuEventElapsedTime, EventElapsedTime),
@@ -405,6 +416,46 @@ EXPORT int emmy_rt_stream_wait(uint64_t stream, double timeout_s) {
 EXPORT int emmy_rt_stream_wait_event(uint64_t stream, uint64_t event) {
     NEED_INIT();
     CU(cu.StreamWaitEvent((CUstream)(uintptr_t)stream, (CUevent)(uintptr_t)event, 0), "cuStreamWaitEvent");
+    return 0;
+}
+
+/* ------------------------------------------------------------------ graphs */
+
+EXPORT int emmy_rt_graph_begin(uint64_t stream) {
+    NEED_INIT();
+    if (stream == 0) return fail(EMMY_RT_EINVAL, "the legacy default stream cannot be captured");
+    CU(cu.StreamBeginCapture((CUstream)(uintptr_t)stream, CU_STREAM_CAPTURE_MODE_THREAD_LOCAL),
+       "cuStreamBeginCapture");
+    return 0;
+}
+
+EXPORT int emmy_rt_graph_end(uint64_t stream, uint64_t *graph) {
+    NEED_INIT();
+    CUgraph g = NULL;
+    CUgraphExec e = NULL;
+    CU(cu.StreamEndCapture((CUstream)(uintptr_t)stream, &g), "cuStreamEndCapture");
+    CUresult r = cu.GraphInstantiateWithFlags(&e, g, 0);
+    cu.GraphDestroy(g);
+    if (r != CUDA_SUCCESS) return cu_fail(r, "cuGraphInstantiateWithFlags");
+    *graph = (uint64_t)(uintptr_t)e;
+    return 0;
+}
+
+EXPORT int emmy_rt_graph_launch(uint64_t graph, uint64_t stream) {
+    NEED_INIT();
+    CU(cu.GraphLaunch((CUgraphExec)(uintptr_t)graph, (CUstream)(uintptr_t)stream), "cuGraphLaunch");
+    return 0;
+}
+
+EXPORT int emmy_rt_graph_upload(uint64_t graph, uint64_t stream) {
+    NEED_INIT();
+    CU(cu.GraphUpload((CUgraphExec)(uintptr_t)graph, (CUstream)(uintptr_t)stream), "cuGraphUpload");
+    return 0;
+}
+
+EXPORT int emmy_rt_graph_destroy(uint64_t graph) {
+    NEED_INIT();
+    CU(cu.GraphExecDestroy((CUgraphExec)(uintptr_t)graph), "cuGraphExecDestroy");
     return 0;
 }
 

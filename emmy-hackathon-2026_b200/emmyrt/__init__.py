@@ -64,6 +64,11 @@ SIGNATURES = {
     "emmy_rt_stream_synchronize": ([_u64], _int),
     "emmy_rt_stream_wait": ([_u64, ctypes.c_double], _int),
     "emmy_rt_stream_wait_event": ([_u64, _u64], _int),
+    "emmy_rt_graph_begin": ([_u64], _int),
+    "emmy_rt_graph_end": ([_u64, _P(_u64)], _int),
+    "emmy_rt_graph_launch": ([_u64, _u64], _int),
+    "emmy_rt_graph_upload": ([_u64, _u64], _int),
+    "emmy_rt_graph_destroy": ([_u64], _int),
     "emmy_rt_event_create": ([_P(_u64)], _int),
     "emmy_rt_event_destroy": ([_u64], _int),
     "emmy_rt_event_record": ([_u64, _u64], _int),
@@ -212,6 +217,40 @@ class Stream:
     def __del__(self):
         try:
             lib.emmy_rt_stream_destroy(self.handle)
+        except Exception:
+            pass
+
+
+class Graph:
+    """Launches captured from a stream once and replayed as one CUDA graph::
+
+        g = Graph.capture(stream, lambda: [fire(stream.handle) for fire in launches])
+        g.launch(0)
+    """
+
+    def __init__(self, handle: int):
+        self.handle = handle
+
+    @classmethod
+    def capture(cls, stream: "Stream", enqueue) -> "Graph":
+        check(lib.emmy_rt_graph_begin(stream.handle), "graph begin")
+        try:
+            enqueue()
+        finally:
+            g = _u64()
+            check(lib.emmy_rt_graph_end(stream.handle, ctypes.byref(g)), "graph end")
+        return cls(g.value)
+
+    def launch(self, stream: int = 0) -> None:
+        check(lib.emmy_rt_graph_launch(self.handle, stream), "graph launch")
+
+    def upload(self, stream: int = 0) -> None:
+        """Stage the graph on the device without running it."""
+        check(lib.emmy_rt_graph_upload(self.handle, stream), "graph upload")
+
+    def __del__(self):
+        try:
+            lib.emmy_rt_graph_destroy(self.handle)
         except Exception:
             pass
 

@@ -143,6 +143,20 @@ int emmy_rt_event_record(uint64_t event, uint64_t stream);
 int emmy_rt_event_synchronize(uint64_t event);
 int emmy_rt_event_elapsed_ms(uint64_t start, uint64_t end, float *ms);
 
+/* ---- CUDA graphs (new: the runner launched one kernel per request, submit.py:126-135;
+ *      a sequence of short launches replays as one graph without per-launch host cost) */
+
+/* Start capturing the work queued on `stream` (not the legacy stream 0; thread-local
+ * capture mode).  Launches made on it until emmy_rt_graph_end are recorded, not run. */
+int emmy_rt_graph_begin(uint64_t stream);
+/* Stop capturing and instantiate the recorded work: *graph receives the executable. */
+int emmy_rt_graph_end(uint64_t stream, uint64_t *graph);
+/* Run the captured work on `stream` (any stream, 0 included). */
+int emmy_rt_graph_launch(uint64_t graph, uint64_t stream);
+/* Stage the graph on the device ahead of its first launch (nothing runs). */
+int emmy_rt_graph_upload(uint64_t graph, uint64_t stream);
+int emmy_rt_graph_destroy(uint64_t graph);
+
 /* ---- NCCL (new: the reference has no collective; one all-reduce finishes the
  *      sharded global sum) ------------------------------------------------------- */
 
