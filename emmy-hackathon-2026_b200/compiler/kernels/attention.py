@@ -75,6 +75,12 @@ class AttnConfig:
     mask_param: str | None = None   # additive score mask buffer, [.., Sq, Sk] row-major
     mask_dtype: str = "f16"
     mask_bh_stride: int = 0  # elements between the masks of consecutive batch x heads (0: shared)
+    heads: int = 0           # query heads per batch entry (grouped-query attention; 0: no groups)
+    kv_group: int = 1        # query heads per key / value head: head h reads K / V head h // kv_group
+
+    @property
+    def BHKV(self) -> int:               # batch x key / value heads
+        return self.BH // self.kv_group
 
     @property
     def DP(self) -> int:                 # head dim padded to whole 64-element swizzle rows
@@ -111,6 +117,8 @@ def emit_attention_module(cfg: AttnConfig) -> str:
         raise NotImplementedError(f"head dim {cfg.D}")
     if cfg.kt_layout and cfg.Sk % 8:
         raise NotImplementedError("pre-transposed K rows not 16-byte aligned")
+    if cfg.kv_group > 1 and (not cfg.heads or cfg.heads % cfg.kv_group or cfg.BH % cfg.heads):
+        raise NotImplementedError("grouped-query attention needs heads divisible by the group")
     p = Ptx()
     NQ, DP = cfg.NQ, cfg.DP
     nblk = -(-cfg.Sk // 128)
@@ -247,6 +255,12 @@ def emit_attention_module(cfg: AttnConfig) -> str:
             p.emit(f"add.u32 {dst}, {base}, {q_off + t * tile_bytes + db * 16384}\nadd.u32 {y}, {q0}, {t * 128}")
             p.emit(f"cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
                    f"[{dst}], [{tq}, {{{db * 64}, {y}, {bh}}}], [{qb}]")
+    kvbh = bh
+    if cfg.kv_group > 1:
+        # query head h of batch entry b reads key / value head h // g of b
+        kvbh, hq = p.reg("u32"), p.reg("u32")
+        p.emit(f"div.u32 {kvbh}, {bh}, {cfg.heads}\nrem.u32 {hq}, {bh}, {cfg.heads}\n"
+               f"div.u32 {hq}, {hq}, {cfg.kv_group}\nmad.lo.u32 {kvbh}, {kvbh}, {cfg.heads // cfg.kv_group}, {hq}")
     slot, ph, j = p.reg("u32"), p.reg("u32"), p.reg("u32")
     p.emit(f"mov.u32 {slot}, 0\nmov.u32 {ph}, 0\nmov.u32 {j}, 0")
     l_pk = p.label("p_kv")
@@ -269,14 +283,14 @@ def emit_attention_module(cfg: AttnConfig) -> str:
                 dst, x = p.reg("u32"), p.reg("u32")
                 p.emit(f"add.u32 {dst}, {dst0}, {kb * DP * 128}\nadd.u32 {x}, {key0}, {kb * 64}")
                 p.emit(f"cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
-                       f"[{dst}], [{tk}, {{{x}, 0, {bh}}}], [{fa}]")
+                       f"[{dst}], [{tk}, {{{x}, 0, {kvbh}}}], [{fa}]")
         else:
             tm = tk if which == "k" else tv
             for db in range(DP // 64):
                 dst = p.reg("u32")
                 p.emit(f"add.u32 {dst}, {dst0}, {db * 16384}")
                 p.emit(f"cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
-                       f"[{dst}], [{tm}, {{{db * 64}, {key0}, {bh}}}], [{fa}]")
+                       f"[{dst}], [{tm}, {{{db * 64}, {key0}, {kvbh}}}], [{fa}]")
         ring_advance(slot, ph)
     pj = p.reg("pred")
     p.emit(f"add.u32 {j}, {j}, 1\nsetp.lt.u32 {pj}, {j}, {nb_cta}\n@{pj} bra {l_pk}\nbra {finish}")
@@ -444,9 +458,9 @@ def emit_attention_module(cfg: AttnConfig) -> str:
     eb = 2
     # (query, key) pairs that take part: all of them, or (causal) key <= query
     visible = (sum(min(r + 1, cfg.Sk) for r in range(cfg.Sq)) if cfg.causal else cfg.Sq * cfg.Sk)
-    kmap = ({"dims": [cfg.Sk, cfg.D, cfg.BH], "strides": [cfg.Sk * eb, cfg.D * cfg.Sk * eb],
+    kmap = ({"dims": [cfg.Sk, cfg.D, cfg.BHKV], "strides": [cfg.Sk * eb, cfg.D * cfg.Sk * eb],
              "box": [64, DP, 1]} if cfg.kt_layout else
-            {"dims": [cfg.D, cfg.Sk, cfg.BH], "strides": [cfg.D * eb, cfg.Sk * cfg.D * eb],
+            {"dims": [cfg.D, cfg.Sk, cfg.BHKV], "strides": [cfg.D * eb, cfg.Sk * cfg.D * eb],
              "box": [64, 128, 1]})
     launch = {
         "kind": "attention", "grid": [-(-cfg.Sq // (128 * NQ)), cfg.BH, 1], "block": [nthreads, 1, 1],
@@ -456,7 +470,7 @@ def emit_attention_module(cfg: AttnConfig) -> str:
             {"kind": "tmap", "buffer": cfg.q_param, "dtype": cfg.dtype, "dims": [cfg.D, cfg.Sq, cfg.BH],
              "strides": [cfg.D * eb, cfg.Sq * cfg.D * eb], "box": [64, 128, 1], "swizzle": 128},
             {"kind": "tmap", "buffer": cfg.k_param, "dtype": cfg.dtype, "swizzle": 128, **kmap},
-            {"kind": "tmap", "buffer": cfg.v_param, "dtype": cfg.dtype, "dims": [cfg.D, cfg.Sk, cfg.BH],
+            {"kind": "tmap", "buffer": cfg.v_param, "dtype": cfg.dtype, "dims": [cfg.D, cfg.Sk, cfg.BHKV],
              "strides": [cfg.D * eb, cfg.Sk * cfg.D * eb], "box": [64, 128, 1], "swizzle": 128},
             {"kind": "status"},
         ],

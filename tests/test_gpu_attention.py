@@ -132,3 +132,26 @@ def test_attention_additive_mask_bf16(runtime, bh, sq, sk, d, per_head):
     f = {n: bf16_bits_to_f32(a) for n, a in host.items()}
     ref = attn_bf16(f["q"], f["k"], f["v"], cfg.scale, mask=f["mask"])
     assert np.allclose(got, ref, rtol=1e-2, atol=1e-2), f"max abs err {np.max(np.abs(got - ref))}"
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("b,hq,g,s,d,causal", [(2, 8, 4, 256, 128, False), (1, 6, 3, 384, 64, True)])
+def test_attention_grouped_query_bf16(runtime, b, hq, g, s, d, causal):
+    """Grouped-query attention: query head h reads key / value head h // g (the
+    repeat_interleave semantics of x_l_gqa), plain and causal."""
+    from compiler.kernels.attention import AttnConfig
+    from emmyrt.runner import bf16_bits_to_f32, f32_to_bf16_bits
+    from oracle.refs import attn_bf16
+    hk = hq // g
+    cfg = AttnConfig(BH=b * hq, Sq=s, Sk=s, D=d, dtype="bf16", scale=1 / math.sqrt(d), causal=causal,
+                     heads=hq, kv_group=g, name="k_attn_gqa", buffers=("q", "k", "v", "o"))
+    rng = np.random.default_rng(7)
+    host = {"q": f32_to_bf16_bits(rng.standard_normal((b * hq, s, d), dtype=np.float32)),
+            "k": f32_to_bf16_bits(rng.standard_normal((b * hk, s, d), dtype=np.float32)),
+            "v": f32_to_bf16_bits(rng.standard_normal((b * hk, s, d), dtype=np.float32))}
+    got = _run_cfg(cfg, host)
+    f = {n: bf16_bits_to_f32(a) for n, a in host.items()}
+    kk = np.repeat(f["k"].reshape(b, hk, s, d), g, axis=1).reshape(b * hq, s, d)
+    vv = np.repeat(f["v"].reshape(b, hk, s, d), g, axis=1).reshape(b * hq, s, d)
+    ref = attn_bf16(f["q"], kk, vv, cfg.scale, causal=causal)
+    assert np.allclose(got, ref, rtol=1e-2, atol=1e-2), f"max abs err {np.max(np.abs(got - ref))}"
