@@ -155,16 +155,76 @@ class MapKernel:
 
     def _address(self, buffer: str, index) -> str:
         shape = self.spec.param(buffer).shape
-        aff = affine_offset(tuple(index), shape, dict(self.ext), fixed=dict(self.fixed))
         ptx = self._ptx
         off = ptx.reg("b64")
-        ptx.emit(f"mov.u64 {off}, {aff.const}")
-        for var, c in aff.coef:
-            w = ptx.reg("b64")
-            ptx.emit(f"cvt.u64.u32 {w}, {self.axis_reg[var]}\nmad.lo.s64 {off}, {w}, {c}, {off}")
+        try:
+            aff = affine_offset(tuple(index), shape, dict(self.ext), fixed=dict(self.fixed))
+        except NotImplementedError:
+            aff = None
+        if aff is not None:
+            ptx.emit(f"mov.u64 {off}, {aff.const}")
+            for var, c in aff.coef:
+                w = ptx.reg("b64")
+                ptx.emit(f"cvt.u64.u32 {w}, {self.axis_reg[var]}\nmad.lo.s64 {off}, {w}, {c}, {off}")
+        else:
+            # not affine (a grouped head a0 / 4, a clamp): each coordinate evaluated as
+            # written, then the row-major offset
+            if len(index) != len(shape):
+                raise NotImplementedError("element map: index rank differs from the buffer's")
+            ptx.emit(f"mov.u64 {off}, 0")
+            for e, extent in zip(index, shape):
+                v, w = self._index(ptx, e), ptx.reg("b64")
+                ptx.emit(f"mul.lo.s64 {off}, {off}, {int(extent)}\ncvt.s64.s32 {w}, {v}\nadd.s64 {off}, {off}, {w}")
         addr = ptx.reg("b64")
         ptx.emit(f"mad.lo.s64 {addr}, {off}, {ELEM[self._buffer(buffer)]}, {self.ptrs[buffer]}")
         return addr
+
+    _CMP = {"<": "lt", "<=": "le", ">": "gt", ">=": "ge", "==": "eq", "!=": "ne"}
+
+    def _index(self, ptx, e) -> str:
+        """An s32 index expression (C semantics for / and %, floor for //)."""
+        k = type(e).__name__
+        if k == "Literal":
+            r = ptx.reg("s32")
+            ptx.emit(f"mov.s32 {r}, {int(e.value)}")
+            return r
+        if k == "Var":
+            if e.name in self.fixed:
+                r = ptx.reg("s32")
+                ptx.emit(f"mov.s32 {r}, {int(self.fixed[e.name])}")
+                return r
+            return self.axis_reg[e.name]
+        if k == "TernaryExpr":
+            c, a, b = self._index(ptx, e.cond), self._index(ptx, e.if_true), self._index(ptx, e.if_false)
+            pc, r = ptx.reg("pred"), ptx.reg("s32")
+            ptx.emit(f"setp.ne.s32 {pc}, {c}, 0\nselp.b32 {r}, {a}, {b}, {pc}")
+            return r
+        if k != "BinaryExpr":
+            raise NotImplementedError(f"element map: index expression {k}")
+        a, b, r = self._index(ptx, e.left), self._index(ptx, e.right), ptx.reg("s32")
+        op = e.op
+        if op in ("+", "-", "*"):
+            ptx.emit(f"{ {'+': 'add', '-': 'sub', '*': 'mul.lo'}[op]}.s32 {r}, {a}, {b}")
+        elif op == "/":
+            ptx.emit(f"div.s32 {r}, {a}, {b}")
+        elif op == "%":
+            ptx.emit(f"rem.s32 {r}, {a}, {b}")
+        elif op == "//":
+            # floor: the truncated quotient, one less when the signs differ and it is inexact
+            q, m, pn = ptx.reg("s32"), ptx.reg("s32"), ptx.reg("pred")
+            ptx.emit(f"div.s32 {q}, {a}, {b}\nmul.lo.s32 {m}, {q}, {b}\nxor.b32 {r}, {a}, {b}\n"
+                     f"setp.lt.s32 {pn}, {r}, 0\nsetp.ne.and.s32 {pn}, {m}, {a}, {pn}\n"
+                     f"selp.s32 {r}, 1, 0, {pn}\nsub.s32 {r}, {q}, {r}")
+        elif op in self._CMP:
+            pc = ptx.reg("pred")
+            ptx.emit(f"setp.{self._CMP[op]}.s32 {pc}, {a}, {b}\nselp.s32 {r}, 1, 0, {pc}")
+        elif op in ("&&", "||"):
+            pa, pb = ptx.reg("pred"), ptx.reg("pred")
+            ptx.emit(f"setp.ne.s32 {pa}, {a}, 0\nsetp.ne.s32 {pb}, {b}, 0\n"
+                     f"{'and' if op == '&&' else 'or'}.pred {pa}, {pa}, {pb}\nselp.s32 {r}, 1, 0, {pa}")
+        else:
+            raise NotImplementedError(f"element map: index operator {op}")
+        return r
 
     def _load(self, ctx: ScalarCtx, s):
         """``names[k]`` of a multi-value Load is the element k after the index."""

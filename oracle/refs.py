@@ -404,6 +404,9 @@ PROBLEM_REFS = {
     #    expressions_llm.py:38-41, 62-64)
     "a01_attention": lambda q, kt, v: [f32(_softmax(f64(q) @ f64(kt) / 8.0) @ f64(v))],
     "x_l_linattn": lambda q, k, v: [linattn(q, k, v)],
+    # grouped-query sdpa: key / value heads repeated 4 times (expressions_llm.py:49-51, 81-84)
+    "x_l_gqa": lambda q, k, v: [f32(_softmax(f64(q) @ np.swapaxes(np.repeat(f64(k), 4, 1), -1, -2)
+                                             / np.sqrt(q.shape[-1])) @ np.repeat(f64(v), 4, 1))],
     # the scalar stays f32 (torch's opmath; the kernel folds the constant buffer's value)
     "x_q_f16_scalar": lambda x: [f32(f16(f32(f16(x)) * f32(0.1)))],
     "x_p_odd1001": lambda a, b: [a * b],
