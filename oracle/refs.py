@@ -404,6 +404,12 @@ PROBLEM_REFS = {
     #    expressions_llm.py:38-41, 62-64)
     "a01_attention": lambda q, kt, v: [f32(_softmax(f64(q) @ f64(kt) / 8.0) @ f64(v))],
     "x_l_linattn": lambda q, k, v: [linattn(q, k, v)],
+    "a02_attention_128": lambda q, kt, v: [f32(_softmax(f64(q) @ f64(kt) / 5.656854) @ f64(v))],
+    "x_a_rect": lambda q, kt, v: [f32(_softmax((f64(q) @ f64(kt)) * 0.17677669) @ f64(v))],
+    # scans (expressions_extra.py:288-291; expressions_llm.py:27-29, 56-58)
+    "x_r_cumsum": lambda x: [f32(np.cumsum(f64(x)))],
+    "x_r_cumsum_rows": lambda x: [f32(np.cumsum(f64(x), -1))],
+    "x_l_ssm_decay": lambda a, x: [f32(np.exp(np.cumsum(-np.abs(f64(a)) * 0.1, -1)) * f64(x))],
     # grouped-query sdpa: key / value heads repeated 4 times (expressions_llm.py:49-51, 81-84)
     "x_l_gqa": lambda q, k, v: [f32(_softmax(f64(q) @ np.swapaxes(np.repeat(f64(k), 4, 1), -1, -2)
                                              / np.sqrt(q.shape[-1])) @ np.repeat(f64(v), 4, 1))],

@@ -57,7 +57,9 @@ FIXTURES = [
     # low-precision casts inside kernels: e4m3 (saturating), bf16, f16 with a constant
     "tests/problems/x_q_fp8_e4m3", "tests/problems/x_q_fp8_e4m3_sat", "tests/problems/x_q_fp8_scaled",
     "tests/problems/x_q_bf16_cast", "tests/problems/x_q_bf16_math", "tests/problems/x_q_f16_scalar",
-    "tests/problems/x_l_gqa",
+    "tests/problems/x_l_gqa", "problems/a02_attention_128", "tests/problems/x_a_rect",
+    # serial scans emmy writes as per-element loops (element maps)
+    "tests/problems/x_r_cumsum", "tests/problems/x_r_cumsum_rows", "tests/problems/x_l_ssm_decay",
     # element maps of the reference's elementwise set (f32 / f16), its f32 attention and linear
     # attention problems (emmy lowers them as row reductions)
     "problems/a01_attention", "problems/p00_scalar_add", "problems/p01_vector_add",

@@ -18,7 +18,9 @@ MAP = ["x_p_odd7", "x_p_odd1001", "x_q_fp8_e4m3", "x_q_fp8_e4m3_sat", "x_q_fp8_s
        "x_p_mul_add_exact", "x_d_f16_add", "x_d_f16_bcast_mul", "x_d_f16_div_sqrt", "x_d_f16_exp",
        "x_d_f16_gelu", "x_d_f32_to_f16", "x_d_f16_to_f32",
        # f32 attention / causal linear attention lowered as row reductions and element maps
-       "a01_attention", "x_l_linattn", "x_l_gqa"]
+       "a01_attention", "x_l_linattn", "x_l_gqa", "a02_attention_128", "x_a_rect",
+       # scans written as per-element serial loops
+       "x_r_cumsum", "x_r_cumsum_rows", "x_l_ssm_decay"]
 
 
 @pytest.mark.gpu
