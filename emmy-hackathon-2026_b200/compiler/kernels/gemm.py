@@ -89,24 +89,40 @@ class GemmConfig:
         return -(-self.M // self.MT), -(-self.N // self.BN)
 
 
+# Relative work rate of one SM per tile shape (bf16, 2048^3 .. 8192^3 on B200): a CTA
+# pair's 256x256 tile halves each SM's shared-memory reads of B; a 128-wide N tile
+# makes every MMA instruction re-read the whole A slice for half the columns.
+_TILE_RATE = {("pair", 256): 1.05, (1, 256): 1.0, (1, 128): 0.75, (1, 64): 0.5}
+
+
 def choose_bn(M: int, N: int, batch: int, min_bn: int = 64) -> int:
-    """Largest N tile (<= 256) that still gives every SM work when possible; small
-    problems trade per-tile efficiency for parallelism.  ``min_bn`` is the width of
-    one 128-byte TMA box of an MN-major B (64 16-bit or 128 8-bit elements)."""
-    bn = 256
-    while bn > max(64, min_bn) and batch * (-(-M // 128)) * (-(-N // bn)) < SMS:
-        bn //= 2
-    if N < bn:
-        bn = max(32, -(-N // 32) * 32)   # the epilogue reads TMEM 32 columns at a time
-    return max(bn, min_bn)
+    """N tile width (<= 256) of single-CTA tiles: ``choose_tiling``'s estimate over
+    the single-CTA shapes.  ``min_bn`` is the width of one 128-byte TMA box of an
+    MN-major B (64 16-bit or 128 8-bit elements)."""
+    return choose_tiling(M, N, batch, min_bn, pairs=False)["BN"]
 
 
-def choose_tiling(M: int, N: int, batch: int, min_bn: int = 64) -> dict:
-    """CTA pairs with 256x256 tiles and 6 stages when there are enough such tiles to give
-    every SM pair work; otherwise single CTAs with ``choose_bn``'s tile width."""
-    if M >= 256 and N >= 256 and batch * (-(-M // 256)) * (-(-N // 256)) >= SMS // 2:
-        return {"pair": True, "BN": 256, "stages": 6}
-    return {"pair": False, "BN": choose_bn(M, N, batch, min_bn), "stages": 4}
+def choose_tiling(M: int, N: int, batch: int, min_bn: int = 64, pairs: bool = True) -> dict:
+    """The tiling with the least estimated time: persistent waves over the SMs (or SM
+    pairs) times one tile's MACs per SM divided by that shape's work rate.  Single
+    CTAs run 128 x BN tiles (BN 256, 128 or 64) with 4 stages, CTA pairs 256 x 256
+    tiles with 6 stages (M and N of 256 or more)."""
+    cands = []
+    if pairs and M >= 256 and N >= 256:
+        tiles = batch * (-(-M // 256)) * (-(-N // 256))
+        cands.append(((-(-tiles // (SMS // 2))) * 128 * 256 / _TILE_RATE[("pair", 256)],
+                      0, {"pair": True, "BN": 256, "stages": 6}))
+    for bn in (256, 128, 64):
+        if bn < min_bn:
+            continue
+        tiles = batch * (-(-M // 128)) * (-(-N // bn))
+        cands.append(((-(-tiles // SMS)) * 128 * bn / _TILE_RATE[(1, bn)], 1,
+                      {"pair": False, "BN": bn, "stages": 4}))
+    best = min(cands, key=lambda c: (c[0], c[1], -c[2]["BN"]))[2]
+    if not best["pair"] and N < best["BN"]:
+        bn = max(32, -(-N // 32) * 32)       # the epilogue reads TMEM 32 columns at a time
+        best = dict(best, BN=max(bn, min_bn))
+    return best
 
 
 def _tile_coords(p: Ptx, cfg: GemmConfig, t: str) -> tuple[str, str, str]:
