@@ -37,6 +37,15 @@ def select(spec) -> str:
             return emit_attention_module(cfg)
         from .reduce import emit_reduction
         return emit_reduction(spec)
+    # emmy's SIMT f32 matmuls (FMA over cp.async-staged tiles) run on the tensor cores
+    # as 3xTF32
+    from .gemm import analyze_f32, emit_gemm_module
+    try:
+        cfg = analyze_f32(spec)
+    except NotImplementedError:
+        cfg = None
+    if cfg is not None:
+        return emit_gemm_module(cfg)
     # no cooperative combine and no tensor-core work: one element per thread (the sum
     # of split-K partial slices, elementwise tails)
     from .pointwise import emit_map

@@ -37,8 +37,10 @@ from .common import arg_params, load_pointer, param_symbol
 from .tc import Waits, instr_desc, smem_desc_hi, smem_desc_lo_const
 
 SMS = 148
+GEMM_THREADS = 192       # warp 0 TMA, warp 1 MMA, warps 2-5 epilogue
+CONV_THREADS = 128       # warps 6-9 with 3xTF32 operands: the hi/lo split
 ELEM_BYTES = {"bf16": 2, "f16": 2, "e4m3": 1, "f32": 4}
-AB_FORMAT = {"f16": 0, "bf16": 1, "e4m3": 0, "e5m2": 1}
+AB_FORMAT = {"f16": 0, "bf16": 1, "e4m3": 0, "e5m2": 1, "f32": 2}   # f32 operands are read as tf32
 
 
 @dataclass
@@ -47,7 +49,7 @@ class GemmConfig:
     N: int
     K: int
     batch: int = 1
-    ab: str = "bf16"              # operand type: bf16 | f16 | e4m3
+    ab: str = "bf16"              # operand type: bf16 | f16 | e4m3 | f32 (3xTF32, see split3)
     c: str = "bf16"               # output type: bf16 | f16 | f32
     b_kmajor: bool = False        # B stored [N, K] (else [K, N])
     BN: int = 256
@@ -74,7 +76,13 @@ class GemmConfig:
 
     @property
     def kind(self) -> str:
-        return "f8f6f4" if self.ab in ("e4m3", "e5m2") else "f16"
+        return {"e4m3": "f8f6f4", "e5m2": "f8f6f4", "f32": "tf32"}.get(self.ab, "f16")
+
+    @property
+    def split3(self) -> bool:
+        """f32 operands: each is split into tf32 hi + lo parts in shared memory and the
+        product accumulates hi*hi + hi*lo + lo*hi (three kind::tf32 MMAs per K step)."""
+        return self.ab == "f32"
 
     @property
     def BK(self) -> int:                 # K elements per stage: one 128-byte swizzle row
@@ -158,18 +166,27 @@ def emit_gemm_module(cfg: GemmConfig) -> str:
     BNc = BN // 2 if pair else BN           # B columns held by one CTA
     a_bytes = BM * BK * eb                  # 16 KB
     b_bytes = BNc * BK * eb                 # 32 KB at BN = 256 (16 KB per CTA of a pair)
-    stage_bytes = a_bytes + b_bytes         # per CTA
+    raw_bytes = a_bytes + b_bytes           # what the TMA copies write per stage and CTA
+    split = cfg.split3
+    if split and pair:
+        raise NotImplementedError("3xTF32 operands on CTA pairs")
+    # 3xTF32: the stage holds the tf32 hi parts (in place of the loaded f32 values)
+    # followed by the lo parts
+    stage_bytes = raw_bytes * (2 if split else 1)
     ncols = max(32, 1 << math.ceil(math.log2(BN * cfg.acc_bufs)))
     if ncols > 512:
         raise NotImplementedError("accumulators exceed TMEM")
     smem = S * stage_bytes + 1024           # +1 KB to align the ring to 1024 B
     if smem > 232448 - 256:
         raise NotImplementedError("stage ring exceeds shared memory")
-    idesc = instr_desc(cfg.MT, BN, AB_FORMAT[cfg.ab], AB_FORMAT[cfg.ab], False, not cfg.b_kmajor)
+    # tf32 operands read MN-major need the 32-byte-atom swizzle; the 3xTF32 converter writes
+    # B K-major instead (the layout A has), so the MMAs read both operands K-major
+    mma_b_kmajor = cfg.b_kmajor or cfg.split3
+    idesc = instr_desc(cfg.MT, BN, AB_FORMAT[cfg.ab], AB_FORMAT[cfg.ab], False, not mma_b_kmajor)
     cg = "cta_group::2" if pair else "cta_group::1"
     a_hi = smem_desc_hi(1024)
     a_lo = smem_desc_lo_const(16)
-    if cfg.b_kmajor:
+    if mma_b_kmajor:
         b_hi, b_lo = smem_desc_hi(1024), smem_desc_lo_const(16)
     else:
         # MN-major: 64-element (128-byte) column blocks of BK K-rows each, BK*128 bytes apart
@@ -211,8 +228,12 @@ def emit_gemm_module(cfg: GemmConfig) -> str:
         mov.u32 {tslot}, gtmem
     """)
     # barrier layout: full[S], empty[S], tfull[A], tempty[A]
-    nbar = 2 * S + 2 * cfg.acc_bufs
+    # ... and with 3xTF32 conv[S]: the stage's hi/lo parts are written
+    # and cread: every converter has read the stage's B before any overwrites it
+    nbar = 2 * S + 2 * cfg.acc_bufs + (S + 1 if split else 0)
     full0, empty0, tfull0, tempty0 = 0, 8 * S, 16 * S, 16 * S + 8 * cfg.acc_bufs
+    conv0 = 16 * S + 16 * cfg.acc_bufs
+    cread = conv0 + 8 * S
     p0 = p.reg("pred")
     init_done = p.label("init_done")
     p.emit(f"setp.ne.u32 {p0}, {tid}, 0\n@{p0} bra {init_done}")
@@ -222,6 +243,9 @@ def emit_gemm_module(cfg: GemmConfig) -> str:
     for b in range(cfg.acc_bufs):
         p.emit(f"mbarrier.init.shared::cta.b64 [{bars}+{tfull0 + 8 * b}], 1")
         p.emit(f"mbarrier.init.shared::cta.b64 [{bars}+{tempty0 + 8 * b}], {256 if pair else 128}")
+    if split:
+        for st in range(S + 1):
+            p.emit(f"mbarrier.init.shared::cta.b64 [{bars}+{conv0 + 8 * st}], {CONV_THREADS}")
     p.emit(f"st.shared.u32 [{abort}], 0\nfence.mbarrier_init.release.cluster\nfence.proxy.async.shared::cta")
     p.place(init_done)
     crank, lfull, ltempty = p.reg("u32"), p.reg("u32"), p.reg("u32")
@@ -296,12 +320,12 @@ def emit_gemm_module(cfg: GemmConfig) -> str:
         # both CTAs' copies complete on the leader's full barrier; only the leader
         # announces the stage's bytes (both halves)
         p.emit(f"""
-            @{pleader} mbarrier.arrive.expect_tx.shared::cta.b64 _, [{faddr}], {2 * stage_bytes}
+            @{pleader} mbarrier.arrive.expect_tx.shared::cta.b64 _, [{faddr}], {2 * raw_bytes}
             mad.lo.u32 {faddr}, {s}, 8, {lfull}
         """)
         tma = "cp.async.bulk.tensor.{r}d.cta_group::2.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
     else:
-        p.emit(f"mbarrier.arrive.expect_tx.shared::cta.b64 _, [{faddr}], {stage_bytes}")
+        p.emit(f"mbarrier.arrive.expect_tx.shared::cta.b64 _, [{faddr}], {raw_bytes}")
         tma = "cp.async.bulk.tensor.{r}d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
     tma = tma.format(r=rank)
     p.emit(f"""
@@ -372,32 +396,35 @@ def emit_gemm_module(cfg: GemmConfig) -> str:
     p.emit(f"""
         mad.lo.u32 {fa2}, {s2}, 8, {bars}
         add.u32 {ea2}, {fa2}, {empty0}
-        add.u32 {fa2}, {fa2}, {full0}
+        add.u32 {fa2}, {fa2}, {conv0 if split else full0}
     """)
     waits.wait(fa2, ph2, "mma", finish)
     p.emit("tcgen05.fence::after_thread_sync")
     sa2, sb2 = p.reg("u32"), p.reg("u32")
     p.emit(f"mad.lo.u32 {sa2}, {s2}, {stage_bytes}, {ring}\nadd.u32 {sb2}, {sa2}, {a_bytes}")
+    # operand pairs per K step: (A, B), or with 3xTF32 (A hi, B hi), (A hi, B lo), (A lo, B hi)
+    pairs_ab = [(0, 0), (0, raw_bytes), (raw_bytes, 0)] if split else [(0, 0)]
     for kk in range(BK // cfg.UK):
-        alo, blo, ad, bd = p.reg("u32"), p.reg("u32"), p.reg("b64"), p.reg("b64")
         a_off = kk * 32                                   # 32 bytes of K inside the swizzle row
-        b_off = kk * 32 if cfg.b_kmajor else kk * (cfg.UK * 128)   # MN-major: UK K-rows of 128 B
-        pacc = p.reg("pred")
-        p.emit(f"""
-            add.u32 {alo}, {sa2}, {a_off}
-            shr.u32 {alo}, {alo}, 4
-            or.b32 {alo}, {alo}, {a_lo}
-            mov.b64 {ad}, {{{alo}, {a_hi}}}
-            add.u32 {blo}, {sb2}, {b_off}
-            shr.u32 {blo}, {blo}, 4
-            or.b32 {blo}, {blo}, {b_lo}
-            mov.b64 {bd}, {{{blo}, {b_hi}}}
-        """)
-        if kk == 0:
-            p.emit(f"setp.ne.u32 {pacc}, {kb2}, 0")
-        else:
-            p.emit(f"setp.eq.u32 {pacc}, {kb2}, {kb2}")
-        p.emit(f"tcgen05.mma.{cg}.kind::{cfg.kind} [{dt}], {ad}, {bd}, {idesc}, {pacc}")
+        b_off = kk * 32 if mma_b_kmajor else kk * (cfg.UK * 128)   # MN-major: UK K-rows of 128 B
+        for j, (ax, bx) in enumerate(pairs_ab):
+            alo, blo, ad, bd = p.reg("u32"), p.reg("u32"), p.reg("b64"), p.reg("b64")
+            pacc = p.reg("pred")
+            p.emit(f"""
+                add.u32 {alo}, {sa2}, {a_off + ax}
+                shr.u32 {alo}, {alo}, 4
+                or.b32 {alo}, {alo}, {a_lo}
+                mov.b64 {ad}, {{{alo}, {a_hi}}}
+                add.u32 {blo}, {sb2}, {b_off + bx}
+                shr.u32 {blo}, {blo}, 4
+                or.b32 {blo}, {blo}, {b_lo}
+                mov.b64 {bd}, {{{blo}, {b_hi}}}
+            """)
+            if kk == 0 and j == 0:
+                p.emit(f"setp.ne.u32 {pacc}, {kb2}, 0")
+            else:
+                p.emit(f"setp.eq.u32 {pacc}, {kb2}, {kb2}")
+            p.emit(f"tcgen05.mma.{cg}.kind::{cfg.kind} [{dt}], {ad}, {bd}, {idesc}, {pacc}")
     p.emit(commit.format(a=ea2))
     p.emit(f"""
         add.u32 {s2}, {s2}, 1
@@ -417,8 +444,15 @@ def emit_gemm_module(cfg: GemmConfig) -> str:
 
     # ------------------------------------------------------------ epilogue
     p.place(role_epi)
+    if split:
+        role_conv = p.label("role_conv")
+        p.emit(f"setp.ge.u32 {pr}, {warp}, {GEMM_THREADS // 32}\n@{pr} bra {role_conv}")
     _emit_epilogue(p, cfg, ptr, bars, tfull0, tempty0, tbase, warp, lane, cta, nct, ntiles,
                    waits, finish, crank if pair else None, ltempty if pair else None)
+    if split:
+        p.place(role_conv)
+        _emit_split_tf32(p, cfg, tid, ring, bars, full0, conv0, cread, a_bytes, raw_bytes, stage_bytes,
+                         kblocks, cta, nct, ntiles, waits, finish)
 
     # -------------------------------------------------------------- finish
     p.place(finish)
@@ -443,7 +477,8 @@ def emit_gemm_module(cfg: GemmConfig) -> str:
     params = list(cfg.arg_params or [f".param .u64 {param_symbol(n)}" for n in cfg.buffers])
     params += [".param .align 64 .b8 param__tmap_a[128]", ".param .align 64 .b8 param__tmap_b[128]",
                ".param .u64 param__status"]
-    text = entry(cfg.name, params, p, maxntid=192)
+    nthreads = GEMM_THREADS + (CONV_THREADS if split else 0)
+    text = entry(cfg.name, params, p, maxntid=nthreads)
     statics = (f"\t.shared .align 8 .b64 gbars[{nbar}];\n\t.shared .align 4 .u32 gabort;\n"
                f"\t.shared .align 4 .u32 gtmem;\n")
     text = text.replace("{\n", "{\n" + statics, 1)
@@ -459,7 +494,7 @@ def emit_gemm_module(cfg: GemmConfig) -> str:
         b_str = [N * eb] + ([N * K * eb] if rank == 3 else [])
         b_box = [128 // eb, BK] + ([1] if rank == 3 else [])
     launch = {
-        "kind": "gemm", "grid": [grid, 1, 1], "block": [192, 1, 1], "cluster": [2 if pair else 1, 1, 1],
+        "kind": "gemm", "grid": [grid, 1, 1], "block": [nthreads, 1, 1], "cluster": [2 if pair else 1, 1, 1],
         "smem": smem, "flops": 2 * cfg.batch * M * N * K, "tiles": ntiles,
         "extra_params": [
             {"kind": "tmap", "buffer": cfg.a_param, "dtype": cfg.ab, "dims": a_dims, "strides": a_str,
@@ -470,6 +505,144 @@ def emit_gemm_module(cfg: GemmConfig) -> str:
         ],
     }
     return module([text], launch, globals_=[".extern .shared .align 1024 .b8 dsmem[];"])
+
+
+def _tf32_split(p: Ptx, x: str) -> tuple[str, str]:
+    """hi = tf32(x), lo = tf32(x - hi), both as f32 bit patterns with the low 13 bits clear."""
+    hi, lo = p.reg("b32"), p.reg("b32")
+    p.emit(f"""
+        cvt.rna.tf32.f32 {hi}, {x}
+        and.b32 {hi}, {hi}, -8192
+        sub.rn.f32 {lo}, {x}, {hi}
+        cvt.rna.tf32.f32 {lo}, {lo}
+        and.b32 {lo}, {lo}, -8192
+    """)
+    return hi, lo
+
+
+def _emit_split_tf32(p: Ptx, cfg: GemmConfig, tid, ring, bars, full0, conv0, cread, a_bytes, raw_bytes,
+                     stage_bytes, kblocks, cta, nct, ntiles, waits: Waits, finish: str) -> None:
+    """Converter warps of the 3xTF32 GEMM.  Once a stage's f32 tiles have landed, each
+    value x becomes hi = tf32(x) and lo = tf32(x - hi), both exact tf32 values, so the
+    tensor core's reading of tf32 operands adds no rounding of its own, and
+    hi*hi + hi*lo + lo*hi misses x*y by the lo*lo term and the rounding of lo: about
+    2^-21 relative per product.  hi replaces x; lo goes ``raw_bytes`` further on.
+
+    A (K-major, and B when stored [N, K]) is split element by element: the 128-byte
+    swizzle is kept as it is.  An MN-major B tile (32-column blocks of BK K-rows, as the
+    TMA boxes land) is transposed on the way into the K-major layout A has, because
+    tf32 operands read MN-major need the 32-byte-atom swizzle: every converter reads
+    its values first and arrives on ``cread``; after that barrier's (bounded) wait the
+    transposed hi values overwrite the raw tile.  Generic-proxy stores are made visible
+    to the tensor core (async proxy) by ``fence.proxy.async`` before the arrival on
+    conv[stage] that the MMA warp waits for."""
+    BK, BNc = cfg.BK, cfg.BN
+    ctid = p.reg("u32")
+    p.emit(f"sub.u32 {ctid}, {tid}, {GEMM_THREADS}")
+    flat = raw_bytes if cfg.b_kmajor else a_bytes     # bytes split element by element
+    per = flat // 16 // CONV_THREADS                   # 16-byte vectors per thread and stage
+    assert flat % (16 * CONV_THREADS) == 0
+    rd, wr = [], []
+    if not cfg.b_kmajor:
+        # (row n of the K-major tile, 16-byte K chunk c) items; n fastest across threads
+        assert BNc & (BNc - 1) == 0 and BNc >= 32 and (BNc * (BK // 4)) % CONV_THREADS == 0
+        lg = BNc.bit_length() - 1
+        for j in range(BNc * (BK // 4) // CONV_THREADS):
+            it, n, c, w, t1, t2 = (p.reg("u32") for _ in range(6))
+            p.emit(f"""
+                add.u32 {it}, {ctid}, {j * CONV_THREADS}
+                and.b32 {n}, {it}, {BNc - 1}
+                shr.u32 {c}, {it}, {lg}
+                and.b32 {w}, {n}, 31
+            """)
+            offs = []
+            for i in range(4):
+                # element (K row 4c+i, column n) of the MN-major tile: block n/32, row
+                # 4c+i, 16-byte chunk (n%32)/4 swizzled by the row, word n%4
+                o = p.reg("u32")
+                p.emit(f"""
+                    shr.u32 {t1}, {n}, 5
+                    mul.lo.u32 {o}, {t1}, {BK * 128}
+                    mad.lo.u32 {o}, {c}, 512, {o}
+                    add.u32 {o}, {o}, {i * 128}
+                    shr.u32 {t1}, {w}, 2
+                    and.b32 {t2}, {c}, 1
+                    mad.lo.u32 {t2}, {t2}, 4, {i}
+                    xor.b32 {t1}, {t1}, {t2}
+                    mad.lo.u32 {o}, {t1}, 16, {o}
+                    and.b32 {t2}, {w}, 3
+                    mad.lo.u32 {o}, {t2}, 4, {o}
+                """)
+                offs.append(o)
+            rd.append(offs)
+            o = p.reg("u32")
+            p.emit(f"""
+                and.b32 {t1}, {n}, 7
+                xor.b32 {t1}, {t1}, {c}
+                shl.b32 {t1}, {t1}, 4
+                mad.lo.u32 {o}, {n}, 128, {t1}
+            """)
+            wr.append(o)
+    t, s, ph, kb, rph = p.reg("u32"), p.reg("u32"), p.reg("u32"), p.reg("u32"), p.reg("u32")
+    p.emit(f"mov.u32 {t}, {cta}\nmov.u32 {s}, 0\nmov.u32 {ph}, 0\nmov.u32 {rph}, 0")
+    tl, kl = p.label("c_tile"), p.label("c_k")
+    pt, ps = p.reg("pred"), p.reg("pred")
+    p.place(tl)
+    p.emit(f"setp.ge.u32 {pt}, {t}, {ntiles}\n@{pt} bra {finish}\nmov.u32 {kb}, 0")
+    p.place(kl)
+    fa, ca, base, vb, ra = p.reg("u32"), p.reg("u32"), p.reg("u32"), p.reg("u32"), p.reg("u32")
+    p.emit(f"""
+        mad.lo.u32 {fa}, {s}, 8, {bars}
+        add.u32 {ca}, {fa}, {conv0}
+        add.u32 {fa}, {fa}, {full0}
+        add.u32 {ra}, {bars}, {cread}
+    """)
+    waits.wait(fa, ph, "convert", finish)
+    p.emit(f"mad.lo.u32 {base}, {s}, {stage_bytes}, {ring}\nmad.lo.u32 {vb}, {ctid}, 16, {base}")
+    group = 4
+    for g0 in range(0, per, group):
+        xs = []
+        for j in range(g0, min(per, g0 + group)):
+            x = [p.reg("b32") for _ in range(4)]
+            p.emit(f"ld.shared.v4.b32 {{{', '.join(x)}}}, [{vb}+{j * 16 * CONV_THREADS}]")
+            xs.append((j, x))
+        for j, x in xs:
+            parts = [_tf32_split(p, e) for e in x]
+            p.emit(f"st.shared.v4.b32 [{vb}+{j * 16 * CONV_THREADS}], {{{', '.join(h for h, _ in parts)}}}")
+            p.emit(f"st.shared.v4.b32 [{vb}+{j * 16 * CONV_THREADS + raw_bytes}], "
+                   f"{{{', '.join(lo for _, lo in parts)}}}")
+    if rd:
+        bb = p.reg("u32")
+        p.emit(f"add.u32 {bb}, {base}, {a_bytes}")
+        vals = []
+        for offs in rd:
+            v = [p.reg("b32") for _ in range(4)]
+            for i in range(4):
+                ad = p.reg("u32")
+                p.emit(f"add.u32 {ad}, {bb}, {offs[i]}\nld.shared.b32 {v[i]}, [{ad}]")
+            vals.append(v)
+        p.emit(f"mbarrier.arrive.shared::cta.b64 _, [{ra}]")
+        waits.wait(ra, rph, "convert", finish)
+        p.emit(f"xor.b32 {rph}, {rph}, 1")
+        for v, o in zip(vals, wr):
+            parts = [_tf32_split(p, e) for e in v]
+            ad = p.reg("u32")
+            p.emit(f"add.u32 {ad}, {bb}, {o}")
+            p.emit(f"st.shared.v4.b32 [{ad}], {{{', '.join(h for h, _ in parts)}}}")
+            p.emit(f"st.shared.v4.b32 [{ad}+{raw_bytes}], {{{', '.join(lo for _, lo in parts)}}}")
+    p.emit(f"""
+        fence.proxy.async.shared::cta
+        mbarrier.arrive.shared::cta.b64 _, [{ca}]
+        add.u32 {s}, {s}, 1
+        setp.eq.u32 {ps}, {s}, {cfg.stages}
+        @{ps} mov.u32 {s}, 0
+        @{ps} xor.b32 {ph}, {ph}, 1
+        add.u32 {kb}, {kb}, 1
+        setp.lt.u32 {ps}, {kb}, {kblocks}
+        @{ps} bra {kl}
+        add.u32 {t}, {t}, {nct}
+        bra {tl}
+    """)
 
 
 def _emit_epilogue(p: Ptx, cfg: GemmConfig, ptr: dict, bars, tfull0, tempty0, tbase, warp, lane,
@@ -544,11 +717,12 @@ def _emit_epilogue(p: Ptx, cfg: GemmConfig, ptr: dict, bars, tfull0, tempty0, tb
     for name, bp in extra.items():
         a = p.reg("b64")
         kind = kinds[name]
+        esz = ELEM_BYTES[_elem_dtype(cfg, name)]
         if kind == "residual":
-            p.emit(f"mad.lo.s64 {a}, {off}, 2, {bp}")
+            p.emit(f"mad.lo.s64 {a}, {off}, {esz}, {bp}")
         else:   # bias over N: element n0
             w2 = p.reg("b64")
-            p.emit(f"cvt.u64.u32 {w2}, {n0}\nmad.lo.s64 {a}, {w2}, 2, {bp}")
+            p.emit(f"cvt.u64.u32 {w2}, {n0}\nmad.lo.s64 {a}, {w2}, {esz}, {bp}")
         res_adr[name] = a
     nchunks = BN // 32
     regs = [p.reg("b32") for _ in range(32)]
@@ -570,7 +744,7 @@ def _emit_epilogue(p: Ptx, cfg: GemmConfig, ptr: dict, bars, tfull0, tempty0, tb
         vals = [p.reg("f32") for _ in range(32)]
         for i in range(32):
             p.emit(f"mov.b32 {vals[i]}, {regs[i]}")
-        vals = _apply_epilogue(p, cfg, vals, scale, res_adr, ch)
+        vals = _apply_epilogue(p, cfg, vals, scale, res_adr, ch, prow, n0)
         skip = p.label("st_skip")
         col0 = ch * 32
         p.emit(f"@!{prow} bra {skip}")
@@ -617,7 +791,23 @@ def _emit_epilogue(p: Ptx, cfg: GemmConfig, ptr: dict, bars, tfull0, tempty0, tb
     p.emit(f"bra {finish}")
 
 
-def _apply_epilogue(p: Ptx, cfg: GemmConfig, vals: list, scale, res_adr: dict, ch: int) -> list:
+def _load_operand(p: Ptx, cfg: GemmConfig, buf: str, adr: str, ch: int, i: int, prow, n0) -> str:
+    """Element (row, n0 + 32 ch + i) of an epilogue operand as f32; 0 outside C."""
+    dt = _elem_dtype(cfg, buf)
+    pin, col, r = p.reg("pred"), p.reg("u32"), p.reg("f32")
+    p.emit(f"add.u32 {col}, {n0}, {ch * 32 + i}\nsetp.lt.and.u32 {pin}, {col}, {cfg.N}, {prow}\n"
+           f"mov.f32 {r}, 0f00000000")
+    if dt == "f32":
+        p.emit(f"@{pin} ld.global.f32 {r}, [{adr}+{(ch * 32 + i) * 4}]")
+    else:
+        h = p.reg("b16")
+        up = "cvt.f32.f16" if dt == "f16" else "cvt.f32.bf16"
+        p.emit(f"mov.b16 {h}, 0\n@{pin} ld.global.b16 {h}, [{adr}+{(ch * 32 + i) * 2}]\n{up} {r}, {h}")
+    return r
+
+
+def _apply_epilogue(p: Ptx, cfg: GemmConfig, vals: list, scale, res_adr: dict, ch: int,
+                    prow, n0) -> list:
     """Fused elementwise ops on one 32-column chunk of a row (f32 registers)."""
     down = "cvt.rn.f16.f32" if cfg.c == "f16" else "cvt.rn.bf16.f32"
     up = "cvt.f32.f16" if cfg.c == "f16" else "cvt.f32.bf16"
@@ -634,11 +824,9 @@ def _apply_epilogue(p: Ptx, cfg: GemmConfig, vals: list, scale, res_adr: dict, c
                 h = p.reg("b16")
                 p.emit(f"{down} {h}, {v}\n{up} {v}, {h}")
         elif kind in ("bias", "residual"):
-            a = res_adr[op[1]]
             for i, v in enumerate(vals):
-                h, r = p.reg("b16"), p.reg("f32")
-                p.emit(f"ld.global.b16 {h}, [{a}+{(ch * 32 + i) * 2}]\n{up} {r}, {h}\n"
-                       f"add.rn.f32 {v}, {v}, {r}")
+                r = _load_operand(p, cfg, op[1], res_adr[op[1]], ch, i, prow, n0)
+                p.emit(f"add.rn.f32 {v}, {v}, {r}")
         elif kind == "lambda":
             from ..stmts import ScalarCtx, Val, lower_body
             lam, operands, consts = op[1], op[2], dict(op[3])
@@ -646,10 +834,7 @@ def _apply_epilogue(p: Ptx, cfg: GemmConfig, vals: list, scale, res_adr: dict, c
                 ctx = ScalarCtx(p, constants=consts, half_results=True)
                 ctx.env[lam.params[0]] = Val(v, "f32")
                 for lname, _, buf in operands:
-                    h, r = p.reg("b16"), p.reg("f32")
-                    cv = "cvt.f32.f16" if _elem_dtype(cfg, buf) == "f16" else "cvt.f32.bf16"
-                    p.emit(f"ld.global.b16 {h}, [{res_adr[buf]}+{(ch * 32 + i) * 2}]\n{cv} {r}, {h}")
-                    ctx.env[lname] = Val(r, "f32")
+                    ctx.env[lname] = Val(_load_operand(p, cfg, buf, res_adr[buf], ch, i, prow, n0), "f32")
                 lower_body(ctx, lam.body)
                 p.emit(f"mov.f32 {v}, {ctx.f32(lam.results[0])}")
         else:
@@ -841,5 +1026,194 @@ def _epilogue_patterns(spec, store) -> tuple:
     return tuple(ops)
 
 
+_F32_RATE = {128: 1.0, 64: 0.7, 32: 0.45}
+
+
+def choose_tiling_f32(M: int, N: int, batch: int) -> dict:
+    """Tiling of the 3xTF32 GEMM: single CTAs, BN of 128, 64 or 32 by the same
+    waves x tile-work estimate as ``choose_tiling``; as many stages as fit (a stage
+    holds the f32 tiles and their lo parts: 2 x (16 KB + BN x 128 B))."""
+    best = None
+    for bn in (128, 64, 32):
+        tiles = batch * (-(-M // 128)) * (-(-N // bn))
+        cost = (-(-tiles // SMS)) * 128 * bn / _F32_RATE[bn]
+        if best is None or cost < best[0]:
+            best = (cost, bn)
+    bn = best[1]
+    stage = 2 * (128 * 128 + bn * 128)
+    return {"pair": False, "BN": bn, "stages": min(4, (232448 - 256 - 1024) // stage)}
+
+
+def analyze_f32(spec) -> GemmConfig:
+    """emmy's SIMT matmul family with f32 operands: ``problems/m01_matmul_512`` (a
+    cp.async-staged 32x64 CTA tile, ``k_matmul_2967be.ir.txt:1-38``), the split-K form
+    with atomic partial sums (``problems/m02_matmul_rect/k_matmul.ir.txt:1-24``), and
+    ``tests/problems/x_m_*`` (batched, bias + relu and constant-scale tails).  Each
+    accumulator adds products of two values loaded -- from global memory or from a
+    shared buffer that a ``CpAsyncCopy`` filled -- from the operands A [.., M, K] and
+    B [.., K, N] (or [.., N, K]); the statements between the accumulator and the Write
+    of C become the epilogue.  The whole K runs in one pass (a split-K ``*_ks`` axis and
+    its atomic adds into the zeroed C give the same sum), on the 3xTF32 template."""
+    stmts = list(_walk(spec.body))
+    kinds = {type(s).__name__ for s in stmts}
+    if kinds & {"MmaSyncPtx", "WarpShuffle", "FragmentRowReduce"}:
+        raise NotImplementedError("not the SIMT matmul form")
+    accs = [s for s in stmts if type(s).__name__ == "Accum"]
+    if not accs:
+        raise NotImplementedError("no accumulation")
+    order = {id(s): i for i, s in enumerate(stmts)}
+    defs = {}
+    for s in stmts:
+        k = type(s).__name__
+        if k == "Load":
+            for n in s.names:
+                defs[n] = s
+        elif k == "Assign":
+            defs[s.name] = s
+    staged = {}
+    for s in stmts:
+        if type(s).__name__ == "CpAsyncCopy":
+            if staged.setdefault(s.smem, s.src) != s.src:
+                raise NotImplementedError("a shared buffer staged from two sources")
+
+    def source(name):
+        d = defs.get(name)
+        while d is not None and type(d).__name__ == "Assign" and d.op.name == "copy" and len(d.args) == 1:
+            d = defs.get(d.args[0])
+        if d is None or type(d).__name__ != "Load":
+            raise NotImplementedError(f"matmul operand {name} is not a loaded value")
+        if d.input in staged:
+            return staged[d.input], d
+        if d.input in spec.buffers and d.input not in spec.constants:
+            return d.input, d
+        raise NotImplementedError(f"cannot trace operand {name} to a buffer")
+
+    acc_names = {a.name for a in accs}
+    kvars, loads = set(), {}
+    for a in accs:
+        v = defs.get(a.value)
+        if a.op.name != "add" or v is None or type(v).__name__ != "Assign" or \
+                v.op.name != "multiply" or len(v.args) != 2:
+            raise NotImplementedError("an accumulation that is not a sum of products")
+        kvars |= set(a.axes or ())
+        for x in v.args:
+            buf, ld = source(x)
+            loads.setdefault(buf, ld)
+    if len(loads) != 2 or not kvars:
+        raise NotImplementedError("products of other than two operands")
+
+    writes = [s for s in stmts if type(s).__name__ == "Write"]
+    if not writes or len({w.output for w in writes}) != 1:
+        raise NotImplementedError("matmul without a single output")
+    first = writes[0]
+    cname = first.output
+    C = spec.param(cname)
+    rvars, cvars = _vars(first.index[-2]), _vars(first.index[-1])
+
+    def backslice(name):
+        """(statements, accumulators) the value ``name`` is computed from."""
+        out, seeds, seen = [], set(), set()
+
+        def visit(n):
+            if n in acc_names:
+                seeds.add(n)
+                return
+            d = defs.get(n)
+            if d is None:
+                raise NotImplementedError(f"{n} is not defined in the kernel")
+            if id(d) in seen:
+                return
+            seen.add(id(d))
+            if type(d).__name__ == "Assign":
+                for x in d.args:
+                    visit(x)
+            elif d.input not in spec.constants and d.input not in spec.buffers:
+                raise NotImplementedError(f"epilogue reads {d.input}")
+            out.append(d)
+        visit(name)
+        return sorted(out, key=lambda d: order[id(d)]), seeds
+
+    # the epilogue: what the written value is computed from, back to one accumulator;
+    # every output element must be computed the same way
+    chain, lam_seeds = backslice(first.values[0])
+
+    def signature(c):
+        return [(type(d).__name__, getattr(getattr(d, "op", None), "name", None)) for d in c]
+    sig = signature(chain)
+    for w in writes:
+        for val in w.values:
+            c, seeds = backslice(val)
+            if len(seeds) != 1 or signature(c) != sig:
+                raise NotImplementedError("outputs computed from several accumulators or differently")
+
+    def dims(buf, ld):
+        """(K dim, free dim) of an operand, as dims of the global buffer."""
+        shape = spec.param(buf).shape
+        idx = ld.index
+        kd = [i for i, e in enumerate(idx) if _vars(e) & kvars]
+        if len(kd) != 1 or len(idx) < 2:
+            raise NotImplementedError("K axis not identifiable in an operand index")
+        fd = len(idx) - 1 if kd[0] == len(idx) - 2 else len(idx) - 2
+        # a staged operand: shared dims are the buffer's trailing dims
+        off = len(shape) - len(idx)
+        return kd[0] + off, fd + off, _vars(idx[fd])
+
+    (b0, l0), (b1, l1) = loads.items()
+    d0, d1 = dims(b0, l0), dims(b1, l1)
+    row_only, col_only = rvars - cvars, cvars - rvars
+    if d0[2] & row_only and d1[2] & col_only:
+        (aname, (ak, af, _)), (bname, (bk, bf, _)) = (b0, d0), (b1, d1)
+    elif d1[2] & row_only and d0[2] & col_only:
+        (aname, (ak, af, _)), (bname, (bk, bf, _)) = (b1, d1), (b0, d0)
+    else:
+        raise NotImplementedError("operand roles not identifiable")
+    A, B = spec.param(aname), spec.param(bname)
+    if A.dtype != "f32" or B.dtype != "f32" or C.dtype != "f32":
+        raise NotImplementedError(f"SIMT matmul {A.dtype} x {B.dtype} -> {C.dtype}")
+    if ak != len(A.shape) - 1:
+        raise NotImplementedError("A operand is not K-major")
+    b_kmajor = bk == len(B.shape) - 1
+    M, K = A.shape[-2], A.shape[-1]
+    N = B.shape[bf]
+    if B.shape[bk] != K or tuple(C.shape[-2:]) != (M, N):
+        raise NotImplementedError("operand shapes do not form a matmul")
+    batch = int(math.prod(C.shape[:-2])) if len(C.shape) > 2 else 1
+    if batch > 1 and (math.prod(A.shape[:-2]) != batch or math.prod(B.shape[:-2]) != batch):
+        raise NotImplementedError("broadcast batch operands")
+    if any(w.atomic for w in writes) and cname not in spec.zero_outputs:
+        raise NotImplementedError("atomic partial sums into an output that is not zeroed")
+    if (K * 4) % 16 or (not b_kmajor and (N * 4) % 16):
+        raise NotImplementedError("operand rows are not 16-byte aligned (TMA)")
+
+    epi = ()
+    if chain:
+        from types import SimpleNamespace
+        operands = []
+        for d in chain:
+            if type(d).__name__ != "Load" or d.input in spec.constants:
+                continue
+            shape = tuple(spec.param(d.input).shape)
+            iv = set().union(*(_vars(e) for e in d.index))
+            if shape == tuple(C.shape) and _vars(d.index[-2]) <= rvars and _vars(d.index[-1]) <= cvars:
+                operands.append((d.names[0], "residual", d.input))
+            elif len(shape) == 1 and shape[0] == N and iv <= cvars:
+                operands.append((d.names[0], "bias", d.input))
+            else:
+                raise NotImplementedError("epilogue operand that is neither a bias over N nor C-shaped")
+            if spec.param(d.input).dtype not in ("f32", "f16", "bf16"):
+                raise NotImplementedError("epilogue operand dtype")
+        lam = SimpleNamespace(params=tuple(lam_seeds), body=tuple(chain), results=(first.values[0],))
+        epi = (("lambda", lam, tuple(operands), tuple(sorted(spec.constants.items()))),)
+    od = tuple((q.name, q.dtype) for q in spec.params)
+    return GemmConfig(M=M, N=N, K=K, batch=batch, ab="f32", c="f32", b_kmajor=b_kmajor,
+                      **choose_tiling_f32(M, N, batch), epilogue=epi, name=spec.name,
+                      a_param=aname, b_param=bname, c_param=cname, arg_params=arg_params(spec),
+                      buffers=tuple(q.name for q in spec.params), operand_dtypes=od)
+
+
 def emit_gemm(spec) -> str:
     return emit_gemm_module(analyze(spec))
+
+
+def emit_gemm_f32(spec) -> str:
+    return emit_gemm_module(analyze_f32(spec))

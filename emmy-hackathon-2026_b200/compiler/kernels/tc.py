@@ -30,7 +30,7 @@ from __future__ import annotations
 TIMEOUT_NS = 2_000_000_000     # every mbarrier wait gives up after 2 s
 
 # status codes written to the kernel's status word when a wait gives up
-STATUS = {"producer": 1, "mma": 2, "epilogue": 4, "softmax": 8, "correction": 16}
+STATUS = {"producer": 1, "mma": 2, "epilogue": 4, "softmax": 8, "correction": 16, "convert": 32}
 
 
 def smem_desc_hi(sbo: int, layout: int = 2) -> int:

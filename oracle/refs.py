@@ -289,6 +289,13 @@ def e4m3_round(a) -> np.ndarray:
     return (sign * out).astype(np.float32)
 
 
+def mm_f32(a, b):
+    """f32 matmul: the product in f64, rounded once to f32 (the reference's refs for
+    ``m01_matmul_512`` / ``m02_matmul_rect``, tools/expressions_open.py:66-73, and the
+    ``x_m_*`` family, tests/expressions_extra.py:215-233)."""
+    return f32(f64(a) @ f64(b))
+
+
 def mm_fp8(aq, bq, sa, sb):
     """FP8 GEMM oracle: ``(A_q . B_q) * s_a * s_b`` in f64 from the e4m3-valued
     operands, rounded to bf16 (no reference kernel: the reference has no FP8 GEMM)."""
@@ -300,6 +307,16 @@ def mm_fp8(aq, bq, sa, sb):
 # graph inputs in the order of meta.json's graph_inputs
 
 PROBLEM_REFS = {
+    "m01_matmul_512": lambda a, b: [mm_f32(a, b)],
+    "m02_matmul_rect": lambda a, b: [mm_f32(a, b)],
+    "x_m_small": lambda a, b: [mm_f32(a, b)],
+    "x_m_tall": lambda a, b: [mm_f32(a, b)],
+    "x_m_wide": lambda a, b: [mm_f32(a, b)],
+    "x_m_longk": lambda a, b: [mm_f32(a, b)],
+    "x_m_256": lambda a, b: [mm_f32(a, b)],
+    "x_m_batched": lambda a, b: [mm_f32(a, b)],
+    "x_m_bias_relu": lambda a, b, c: [f32(np.maximum(f64(a) @ f64(b) + f64(c), 0))],
+    "x_m_scaled": lambda a, b: [f32((f64(a) @ f64(b)) * 0.5)],
     "f01_rmsnorm": lambda x, w: [rmsnorm_sqrt(x, w, 1e-5)],
     "f02_row_softmax": lambda x: [softmax(x)],
     "f03_l2norm": lambda x: [l2norm(x)],

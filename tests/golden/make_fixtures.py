@@ -76,6 +76,11 @@ FIXTURES = [
     "tests/problems/x_p_rsqrt", "tests/problems/x_p_short_launch", "tests/problems/x_p_silu",
     "tests/problems/x_p_softplus", "tests/problems/x_p_softsign", "tests/problems/x_p_sqrt",
     "tests/problems/x_p_square", "tests/problems/x_p_sub1000", "tests/problems/x_p_sub_const",
+    # f32 matmuls (emmy's SIMT FMA schedule; split-K atomics in m02 / x_m_scaled)
+    "problems/m01_matmul_512", "problems/m02_matmul_rect", "tests/problems/x_m_small",
+    "tests/problems/x_m_tall", "tests/problems/x_m_wide", "tests/problems/x_m_longk",
+    "tests/problems/x_m_256", "tests/problems/x_m_batched", "tests/problems/x_m_bias_relu",
+    "tests/problems/x_m_scaled",
 ]
 
 

@@ -137,3 +137,39 @@ def test_simt_attention_recognizer():
         if ir.parent.name != "x_h_sdpa_mask":
             with pytest.raises(NotImplementedError):
                 analyze_simt(load(ir))
+
+
+@pytest.mark.parametrize("pid,mnk,batch,a,b,epi", [
+    ("m01_matmul_512", (512, 512, 512), 1, "x0", "x1", None),
+    ("m02_matmul_rect", (128, 64, 256), 1, "x0", "x1", None),      # split-K atomics: one pass
+    ("x_m_batched", (64, 48, 32), 4, "x0", "x1", None),
+    ("x_m_bias_relu", (128, 96, 64), 1, "a", "b", ("add", "relu")),
+    ("x_m_scaled", (64, 64, 128), 1, "x0", "x1", ("multiply",)),
+])
+def test_f32_matmul_recognizer(pid, mnk, batch, a, b, epi):
+    # emmy's SIMT f32 matmul (operands staged by cp.async, FMA accumulators) goes to the
+    # tcgen05 GEMM with 3xTF32 operands
+    from compiler.kernels.gemm import analyze_f32
+    cfg = analyze_f32(load(next((GOLDEN / pid).glob("*.ir.json"))))
+    assert (cfg.M, cfg.N, cfg.K) == mnk and cfg.batch == batch and cfg.ab == "f32" and cfg.split3
+    assert (cfg.a_param, cfg.b_param) == (a, b) and not cfg.b_kmajor and not cfg.pair
+    if epi is None:
+        assert cfg.epilogue == ()
+    else:
+        lam = cfg.epilogue[0][1]
+        assert tuple(s.op.name for s in lam.body if type(s).__name__ == "Assign") == epi
+    ptx = compile_kernel(load(next((GOLDEN / pid).glob("*.ir.json"))))
+    assert "kind::tf32" in ptx and "cvt.rna.tf32.f32" in ptx
+
+
+def test_f32_matmul_recognizer_rejects_other_kernels():
+    from compiler.kernels.gemm import analyze_f32
+    taken = set()
+    for ir in IRS:
+        try:
+            analyze_f32(load(ir))
+            taken.add(ir.parent.name)
+        except NotImplementedError:
+            pass
+    assert taken == {"m01_matmul_512", "m02_matmul_rect", "x_m_small", "x_m_tall", "x_m_wide", "x_m_longk",
+                     "x_m_256", "x_m_batched", "x_m_bias_relu", "x_m_scaled"}

@@ -1,0 +1,90 @@
+"""f32 matmuls on the B200: emmy's SIMT FMA schedule (``problems/m01_matmul_512``,
+``problems/m02_matmul_rect``, ``tests/problems/x_m_*``) lowered to the tcgen05 GEMM
+with 3xTF32 operands, against the golden vectors and the f64 oracle."""
+
+import json
+
+import numpy as np
+import pytest
+
+from conftest import GOLDEN
+
+F32_MM = ["m01_matmul_512", "m02_matmul_rect", "x_m_small", "x_m_tall", "x_m_wide", "x_m_longk",
+          "x_m_256", "x_m_batched", "x_m_bias_relu", "x_m_scaled"]
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("pid", F32_MM)
+def test_f32_matmul_matches_golden(runtime, pid):
+    from emmyrt.runner import run_problem
+    from oracle.refs import problem_expected
+    d = GOLDEN / pid
+    meta = json.loads((d / "meta.json").read_text())
+    res = run_problem(d)
+    exp = dict(np.load(d / "expected.npz"))
+    ora = problem_expected(meta)
+    for name, ref in exp.items():
+        got = res["outputs"][name].reshape(ref.shape)
+        err = np.max(np.abs(got - ref))
+        assert np.allclose(got, ref, rtol=meta["rtol"], atol=meta["atol"]), f"{pid}:{name} max abs err {err}"
+        assert np.allclose(got, np.asarray(ora[name]).reshape(ref.shape), rtol=meta["rtol"], atol=meta["atol"])
+
+
+def _run_f32(m, n, k, b_kmajor=False, batch=1, bias=False, seed=0, BN=None):
+    import emmyrt
+    from compiler.kernels.gemm import GemmConfig, choose_tiling_f32, emit_gemm_module
+    from emmyrt import DeviceBuffer
+    from emmyrt.runner import CompiledKernel
+    tiling = choose_tiling_f32(m, n, batch)
+    if BN is not None:
+        tiling = dict(tiling, BN=BN, stages=min(4, (232448 - 256 - 1024) // (2 * (128 * 128 + BN * 128))))
+    epi = (("bias", "bias"),) if bias else ()
+    cfg = GemmConfig(M=m, N=n, K=k, batch=batch, ab="f32", c="f32", b_kmajor=b_kmajor, **tiling,
+                     epilogue=epi, name="k_gemm_f32_test", buffers=("a", "b", "c", "bias"),
+                     operand_dtypes=(("bias", "f32"),))
+    ck = CompiledKernel.from_module(emit_gemm_module(cfg), "k_gemm_f32_test", ["a", "b", "c", "bias"])
+    rng = np.random.default_rng(seed)
+    A = rng.standard_normal((batch, m, k)).astype(np.float32)
+    B = rng.standard_normal((batch, n, k) if b_kmajor else (batch, k, n)).astype(np.float32)
+    bv = rng.standard_normal(n).astype(np.float32)
+    da, db, dc, dbias = DeviceBuffer(A.nbytes), DeviceBuffer(B.nbytes), DeviceBuffer(batch * m * n * 4), \
+        DeviceBuffer(bv.nbytes)
+    da.upload(A)
+    db.upload(B)
+    dbias.upload(bv)
+    dc.zero()
+    ck({"a": da.ptr, "b": db.ptr, "c": dc.ptr, "bias": dbias.ptr})
+    emmyrt.stream_wait(0, 60)
+    assert ck.status() == 0
+    out = np.zeros((batch, m, n), np.float32)
+    dc.download(out)
+    Bm = np.swapaxes(B, -1, -2) if b_kmajor else B
+    ref = A.astype(np.float64) @ Bm.astype(np.float64)
+    scale = np.abs(A.astype(np.float64)) @ np.abs(Bm.astype(np.float64))
+    if bias:
+        ref = ref + bv
+        scale = scale + np.abs(bv)
+    return out, ref, scale
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("m,n,k,b_kmajor,batch,BN", [
+    (512, 512, 512, False, 1, None),
+    (1000, 600, 300, False, 1, None),       # partial M and N tiles, K not a multiple of 32
+    (384, 256, 1024, True, 1, None),        # B stored [N, K]
+    (200, 96, 64, False, 3, 64),            # batched, partial M tile
+    (2048, 2048, 2048, False, 1, 128),
+])
+def test_3xtf32_accuracy(runtime, m, n, k, b_kmajor, batch, BN):
+    out, ref, scale = _run_f32(m, n, k, b_kmajor, batch, BN=BN)
+    # hi*hi + hi*lo + lo*hi misses each product by about 2^-21 of its size and the f32
+    # accumulation adds about 2^-24 per step: 2^-16 of sum |a||b| holds with room, while
+    # single tf32 products (2^-11 each) would miss it
+    err = np.abs(out - ref) / scale
+    assert np.max(err) <= 2.0 ** -16, f"max error {np.max(err)} of sum |a||b|"
+
+
+@pytest.mark.gpu
+def test_3xtf32_bias_on_ragged_tiles(runtime):
+    out, ref, scale = _run_f32(130, 100, 64, bias=True, BN=64)
+    assert np.max(np.abs(out - ref) / scale) <= 2.0 ** -16
