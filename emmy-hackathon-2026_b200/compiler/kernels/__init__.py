@@ -35,6 +35,14 @@ def select(spec) -> str:
             cfg = None
         if cfg is not None:
             return emit_attention_module(cfg)
+        # a dot product per output element, reduced across the warp: a matmul
+        from .gemm import analyze_f32, emit_gemm_module
+        try:
+            gcfg = analyze_f32(spec)
+        except NotImplementedError:
+            gcfg = None
+        if gcfg is not None:
+            return emit_gemm_module(gcfg)
         from .reduce import emit_reduction
         return emit_reduction(spec)
     # emmy's SIMT f32 matmuls (FMA over cp.async-staged tiles) run on the tensor cores

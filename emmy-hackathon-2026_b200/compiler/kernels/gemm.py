@@ -67,6 +67,8 @@ class GemmConfig:
     operand_dtypes: tuple = ()       # (buffer, dtype) of epilogue operands
     zero_slots: int = 0              # split-K partials: the full product goes to slice 0 of C and
     slot_stride: int = 0             # these many further slices (slot_stride elements apart) are zeroed
+    operand_round: str | None = None  # f32 operands cast to "bf16" / "f16" before the product: one
+                                      # exact tf32 MMA on the rounded values instead of 3xTF32
 
     BM = 128                         # accumulator rows per CTA
 
@@ -79,10 +81,15 @@ class GemmConfig:
         return {"e4m3": "f8f6f4", "e5m2": "f8f6f4", "f32": "tf32"}.get(self.ab, "f16")
 
     @property
+    def converts(self) -> bool:
+        """f32 operands pass through the converter warps before the tf32 MMAs."""
+        return self.ab == "f32"
+
+    @property
     def split3(self) -> bool:
         """f32 operands: each is split into tf32 hi + lo parts in shared memory and the
         product accumulates hi*hi + hi*lo + lo*hi (three kind::tf32 MMAs per K step)."""
-        return self.ab == "f32"
+        return self.ab == "f32" and self.operand_round is None
 
     @property
     def BK(self) -> int:                 # K elements per stage: one 128-byte swizzle row
@@ -167,9 +174,9 @@ def emit_gemm_module(cfg: GemmConfig) -> str:
     a_bytes = BM * BK * eb                  # 16 KB
     b_bytes = BNc * BK * eb                 # 32 KB at BN = 256 (16 KB per CTA of a pair)
     raw_bytes = a_bytes + b_bytes           # what the TMA copies write per stage and CTA
-    split = cfg.split3
-    if split and pair:
-        raise NotImplementedError("3xTF32 operands on CTA pairs")
+    split, conv = cfg.split3, cfg.converts
+    if conv and pair:
+        raise NotImplementedError("converted f32 operands on CTA pairs")
     # 3xTF32: the stage holds the tf32 hi parts (in place of the loaded f32 values)
     # followed by the lo parts
     stage_bytes = raw_bytes * (2 if split else 1)
@@ -181,7 +188,7 @@ def emit_gemm_module(cfg: GemmConfig) -> str:
         raise NotImplementedError("stage ring exceeds shared memory")
     # tf32 operands read MN-major need the 32-byte-atom swizzle; the 3xTF32 converter writes
     # B K-major instead (the layout A has), so the MMAs read both operands K-major
-    mma_b_kmajor = cfg.b_kmajor or cfg.split3
+    mma_b_kmajor = cfg.b_kmajor or cfg.converts
     idesc = instr_desc(cfg.MT, BN, AB_FORMAT[cfg.ab], AB_FORMAT[cfg.ab], False, not mma_b_kmajor)
     cg = "cta_group::2" if pair else "cta_group::1"
     a_hi = smem_desc_hi(1024)
@@ -230,7 +237,7 @@ def emit_gemm_module(cfg: GemmConfig) -> str:
     # barrier layout: full[S], empty[S], tfull[A], tempty[A]
     # ... and with 3xTF32 conv[S]: the stage's hi/lo parts are written
     # and cread: every converter has read the stage's B before any overwrites it
-    nbar = 2 * S + 2 * cfg.acc_bufs + (S + 1 if split else 0)
+    nbar = 2 * S + 2 * cfg.acc_bufs + (S + 1 if conv else 0)
     full0, empty0, tfull0, tempty0 = 0, 8 * S, 16 * S, 16 * S + 8 * cfg.acc_bufs
     conv0 = 16 * S + 16 * cfg.acc_bufs
     cread = conv0 + 8 * S
@@ -243,7 +250,7 @@ def emit_gemm_module(cfg: GemmConfig) -> str:
     for b in range(cfg.acc_bufs):
         p.emit(f"mbarrier.init.shared::cta.b64 [{bars}+{tfull0 + 8 * b}], 1")
         p.emit(f"mbarrier.init.shared::cta.b64 [{bars}+{tempty0 + 8 * b}], {256 if pair else 128}")
-    if split:
+    if conv:
         for st in range(S + 1):
             p.emit(f"mbarrier.init.shared::cta.b64 [{bars}+{conv0 + 8 * st}], {CONV_THREADS}")
     p.emit(f"st.shared.u32 [{abort}], 0\nfence.mbarrier_init.release.cluster\nfence.proxy.async.shared::cta")
@@ -396,7 +403,7 @@ def emit_gemm_module(cfg: GemmConfig) -> str:
     p.emit(f"""
         mad.lo.u32 {fa2}, {s2}, 8, {bars}
         add.u32 {ea2}, {fa2}, {empty0}
-        add.u32 {fa2}, {fa2}, {conv0 if split else full0}
+        add.u32 {fa2}, {fa2}, {conv0 if conv else full0}
     """)
     waits.wait(fa2, ph2, "mma", finish)
     p.emit("tcgen05.fence::after_thread_sync")
@@ -444,12 +451,12 @@ def emit_gemm_module(cfg: GemmConfig) -> str:
 
     # ------------------------------------------------------------ epilogue
     p.place(role_epi)
-    if split:
+    if conv:
         role_conv = p.label("role_conv")
         p.emit(f"setp.ge.u32 {pr}, {warp}, {GEMM_THREADS // 32}\n@{pr} bra {role_conv}")
     _emit_epilogue(p, cfg, ptr, bars, tfull0, tempty0, tbase, warp, lane, cta, nct, ntiles,
                    waits, finish, crank if pair else None, ltempty if pair else None)
-    if split:
+    if conv:
         p.place(role_conv)
         _emit_split_tf32(p, cfg, tid, ring, bars, full0, conv0, cread, a_bytes, raw_bytes, stage_bytes,
                          kblocks, cta, nct, ntiles, waits, finish)
@@ -477,7 +484,7 @@ def emit_gemm_module(cfg: GemmConfig) -> str:
     params = list(cfg.arg_params or [f".param .u64 {param_symbol(n)}" for n in cfg.buffers])
     params += [".param .align 64 .b8 param__tmap_a[128]", ".param .align 64 .b8 param__tmap_b[128]",
                ".param .u64 param__status"]
-    nthreads = GEMM_THREADS + (CONV_THREADS if split else 0)
+    nthreads = GEMM_THREADS + (CONV_THREADS if conv else 0)
     text = entry(cfg.name, params, p, maxntid=nthreads)
     statics = (f"\t.shared .align 8 .b64 gbars[{nbar}];\n\t.shared .align 4 .u32 gabort;\n"
                f"\t.shared .align 4 .u32 gtmem;\n")
@@ -507,6 +514,18 @@ def emit_gemm_module(cfg: GemmConfig) -> str:
     return module([text], launch, globals_=[".extern .shared .align 1024 .b8 dsmem[];"])
 
 
+def _tf32_round(p: Ptx, x: str, mode: str) -> str:
+    """x rounded to bf16 / f16 (nearest even, as the IR's cast), as an f32 bit pattern: a
+    value a tf32 operand holds exactly, so the MMA's products are the 16-bit products."""
+    h, r = p.reg("b16"), p.reg("b32")
+    if mode == "bf16":
+        z = p.reg("b16")
+        p.emit(f"cvt.rn.bf16.f32 {h}, {x}\nmov.b16 {z}, 0\nmov.b32 {r}, {{{z}, {h}}}")
+    else:
+        p.emit(f"cvt.rn.f16.f32 {h}, {x}\ncvt.f32.f16 {r}, {h}")
+    return r
+
+
 def _tf32_split(p: Ptx, x: str) -> tuple[str, str]:
     """hi = tf32(x), lo = tf32(x - hi), both as f32 bit patterns with the low 13 bits clear."""
     hi, lo = p.reg("b32"), p.reg("b32")
@@ -518,6 +537,13 @@ def _tf32_split(p: Ptx, x: str) -> tuple[str, str]:
         and.b32 {lo}, {lo}, -8192
     """)
     return hi, lo
+
+
+def _convert(p: Ptx, cfg: GemmConfig, xs: list) -> list:
+    """(hi, lo) per value: the 3xTF32 split, or (rounded, None) for cast operands."""
+    if cfg.operand_round:
+        return [(_tf32_round(p, x, cfg.operand_round), None) for x in xs]
+    return [_tf32_split(p, x) for x in xs]
 
 
 def _emit_split_tf32(p: Ptx, cfg: GemmConfig, tid, ring, bars, full0, conv0, cread, a_bytes, raw_bytes,
@@ -535,7 +561,8 @@ def _emit_split_tf32(p: Ptx, cfg: GemmConfig, tid, ring, bars, full0, conv0, cre
     its values first and arrives on ``cread``; after that barrier's (bounded) wait the
     transposed hi values overwrite the raw tile.  Generic-proxy stores are made visible
     to the tensor core (async proxy) by ``fence.proxy.async`` before the arrival on
-    conv[stage] that the MMA warp waits for."""
+    conv[stage] that the MMA warp waits for.  Operands the IR casts to bf16 / f16 are
+    rounded instead (``operand_round``): one value, no lo part, one MMA per K step."""
     BK, BNc = cfg.BK, cfg.BN
     ctid = p.reg("u32")
     p.emit(f"sub.u32 {ctid}, {tid}, {GEMM_THREADS}")
@@ -607,10 +634,11 @@ def _emit_split_tf32(p: Ptx, cfg: GemmConfig, tid, ring, bars, full0, conv0, cre
             p.emit(f"ld.shared.v4.b32 {{{', '.join(x)}}}, [{vb}+{j * 16 * CONV_THREADS}]")
             xs.append((j, x))
         for j, x in xs:
-            parts = [_tf32_split(p, e) for e in x]
+            parts = _convert(p, cfg, x)
             p.emit(f"st.shared.v4.b32 [{vb}+{j * 16 * CONV_THREADS}], {{{', '.join(h for h, _ in parts)}}}")
-            p.emit(f"st.shared.v4.b32 [{vb}+{j * 16 * CONV_THREADS + raw_bytes}], "
-                   f"{{{', '.join(lo for _, lo in parts)}}}")
+            if cfg.split3:
+                p.emit(f"st.shared.v4.b32 [{vb}+{j * 16 * CONV_THREADS + raw_bytes}], "
+                       f"{{{', '.join(lo for _, lo in parts)}}}")
     if rd:
         bb = p.reg("u32")
         p.emit(f"add.u32 {bb}, {base}, {a_bytes}")
@@ -625,11 +653,12 @@ def _emit_split_tf32(p: Ptx, cfg: GemmConfig, tid, ring, bars, full0, conv0, cre
         waits.wait(ra, rph, "convert", finish)
         p.emit(f"xor.b32 {rph}, {rph}, 1")
         for v, o in zip(vals, wr):
-            parts = [_tf32_split(p, e) for e in v]
+            parts = _convert(p, cfg, v)
             ad = p.reg("u32")
             p.emit(f"add.u32 {ad}, {bb}, {o}")
             p.emit(f"st.shared.v4.b32 [{ad}], {{{', '.join(h for h, _ in parts)}}}")
-            p.emit(f"st.shared.v4.b32 [{ad}+{raw_bytes}], {{{', '.join(lo for _, lo in parts)}}}")
+            if cfg.split3:
+                p.emit(f"st.shared.v4.b32 [{ad}+{raw_bytes}], {{{', '.join(lo for _, lo in parts)}}}")
     p.emit(f"""
         fence.proxy.async.shared::cta
         mbarrier.arrive.shared::cta.b64 _, [{ca}]
@@ -809,8 +838,6 @@ def _load_operand(p: Ptx, cfg: GemmConfig, buf: str, adr: str, ch: int, i: int, 
 def _apply_epilogue(p: Ptx, cfg: GemmConfig, vals: list, scale, res_adr: dict, ch: int,
                     prow, n0) -> list:
     """Fused elementwise ops on one 32-column chunk of a row (f32 registers)."""
-    down = "cvt.rn.f16.f32" if cfg.c == "f16" else "cvt.rn.bf16.f32"
-    up = "cvt.f32.f16" if cfg.c == "f16" else "cvt.f32.bf16"
     for op in cfg.epilogue:
         kind = op[0]
         if kind == "scale2":
@@ -820,9 +847,12 @@ def _apply_epilogue(p: Ptx, cfg: GemmConfig, vals: list, scale, res_adr: dict, c
             for v in vals:
                 p.emit(f"max.f32 {v}, {v}, 0f00000000")
         elif kind == "round":
+            rdt = op[1] if len(op) > 1 else cfg.c
+            rdown = "cvt.rn.f16.f32" if rdt == "f16" else "cvt.rn.bf16.f32"
+            rup = "cvt.f32.f16" if rdt == "f16" else "cvt.f32.bf16"
             for v in vals:
                 h = p.reg("b16")
-                p.emit(f"{down} {h}, {v}\n{up} {v}, {h}")
+                p.emit(f"{rdown} {h}, {v}\n{rup} {v}, {h}")
         elif kind in ("bias", "residual"):
             for i, v in enumerate(vals):
                 r = _load_operand(p, cfg, op[1], res_adr[op[1]], ch, i, prow, n0)
@@ -893,12 +923,30 @@ def analyze(spec) -> GemmConfig:
             kvar = s.axis.name
             break
     # operand sources: smem staging (CpAsyncCopy / Write of loaded values) or gmem-direct
-    smem_src = {}
+    smem_src, smem_cast = {}, {}
+    defs = {}
+    for s in stmts:
+        k = type(s).__name__
+        if k == "Load":
+            for n in s.names:
+                defs[n] = s
+        elif k == "Assign":
+            defs[s.name] = s
     for s in stmts:
         k = type(s).__name__
         if k == "CpAsyncCopy":
             smem_src[s.smem] = (s.src, s.src_index)
-    role_src = {}
+        elif k == "Write" and s.output not in spec.buffers and s.values:
+            # a shared tile written from loaded values, possibly cast (``x.to(bf16)``)
+            d, cast = defs.get(s.values[0]), None
+            while d is not None and type(d).__name__ == "Assign" and d.op.name == "copy":
+                dt = getattr(d.dtype, "name", None)
+                cast = dt if dt in ("bf16", "f16") else cast
+                d = defs.get(d.args[0])
+            if d is not None and type(d).__name__ == "Load" and d.input in spec.buffers:
+                smem_src[s.output] = (d.input, d.index)
+                smem_cast[s.output] = cast
+    role_src, role_cast = {}, {}
     for s in stmts:
         if type(s).__name__ == "LdmatrixLoad":
             buf = s.src_buffer
@@ -906,11 +954,16 @@ def analyze(spec) -> GemmConfig:
             if src is None:
                 raise NotImplementedError(f"cannot trace operand {s.frag} to a buffer")
             role_src.setdefault(s.role, src)
+            role_cast.setdefault(s.role, smem_cast.get(buf))
     if set(role_src) != {"a", "b"}:
         raise NotImplementedError("matmul operands not found")
     (aname, aidx), (bname, bidx) = role_src["a"], role_src["b"]
     A, B, C = spec.param(aname), spec.param(bname), spec.param(cname)
-    if A.dtype != B.dtype or A.dtype not in ("f16", "bf16"):
+    # f32 operands cast to a 16-bit type on the way into shared memory: the tf32 template
+    # with the same rounding (the 16-bit products are exact either way)
+    f32_cast = A.dtype == B.dtype == "f32" and role_cast["a"] == role_cast["b"] and \
+        role_cast["a"] in ("bf16", "f16")
+    if not f32_cast and (A.dtype != B.dtype or A.dtype not in ("f16", "bf16")):
         raise NotImplementedError(f"matmul operands {A.dtype}/{B.dtype}: TMA feeds 16-bit operands")
     if C.dtype not in ("f16", "bf16", "f32"):
         raise NotImplementedError(f"matmul output {C.dtype}")
@@ -943,10 +996,19 @@ def analyze(spec) -> GemmConfig:
     batch = int(math.prod(cdims[:-2])) if len(cdims) > 2 else 1
     if batch > 1 and (math.prod(A.shape[:-2]) != batch or math.prod(B.shape[:-2]) != batch):
         raise NotImplementedError("broadcast batch operands")
-    eb = 2
+    eb = 4 if f32_cast else 2
     if (K * eb) % 16 or (not b_kmajor and (N * eb) % 16):
         raise NotImplementedError("operand rows are not 16-byte aligned (TMA)")
     epi = _epilogue_ops(spec, stores[0])
+    if f32_cast:
+        if C.dtype != "f32":
+            raise NotImplementedError("cast-operand matmul with a 16-bit output")
+        od = tuple((q.name, q.dtype) for q in spec.params)
+        return GemmConfig(M=M, N=N, K=K, batch=batch, ab="f32", c="f32", b_kmajor=b_kmajor,
+                          **choose_tiling_f32(M, N, batch, split3=False), epilogue=epi, name=spec.name,
+                          a_param=aname, b_param=bname, c_param=cname, arg_params=arg_params(spec),
+                          buffers=tuple(q.name for q in spec.params), operand_dtypes=od,
+                          operand_round=role_cast["a"], **split)
     od = tuple((q.name, q.dtype) for q in spec.params if q.dtype in ("f16", "bf16"))
     tiling = choose_tiling(M, N, batch, 32 if b_kmajor else 64)
     return GemmConfig(M=M, N=N, K=K, batch=batch, ab=A.dtype, c=C.dtype, b_kmajor=b_kmajor, **tiling,
@@ -1006,7 +1068,7 @@ def _epilogue_patterns(spec, store) -> tuple:
             dt = getattr(s.dtype, "name", None)
             if op == "copy":
                 if dt in ("f16", "bf16"):
-                    ops.append(("round",))
+                    ops.append(("round", dt))
             elif op == "relu":
                 ops.append(("relu",))
             elif op == "add" and sum(a in loads for a in s.args) == 1:
@@ -1029,10 +1091,10 @@ def _epilogue_patterns(spec, store) -> tuple:
 _F32_RATE = {128: 1.0, 64: 0.7, 32: 0.45}
 
 
-def choose_tiling_f32(M: int, N: int, batch: int) -> dict:
-    """Tiling of the 3xTF32 GEMM: single CTAs, BN of 128, 64 or 32 by the same
+def choose_tiling_f32(M: int, N: int, batch: int, split3: bool = True) -> dict:
+    """Tiling of the tf32 GEMM: single CTAs, BN of 128, 64 or 32 by the same
     waves x tile-work estimate as ``choose_tiling``; as many stages as fit (a stage
-    holds the f32 tiles and their lo parts: 2 x (16 KB + BN x 128 B))."""
+    holds the f32 tiles, 16 KB + BN x 128 B, and with 3xTF32 their lo parts as much)."""
     best = None
     for bn in (128, 64, 32):
         tiles = batch * (-(-M // 128)) * (-(-N // bn))
@@ -1040,23 +1102,28 @@ def choose_tiling_f32(M: int, N: int, batch: int) -> dict:
         if best is None or cost < best[0]:
             best = (cost, bn)
     bn = best[1]
-    stage = 2 * (128 * 128 + bn * 128)
+    stage = (2 if split3 else 1) * (128 * 128 + bn * 128)
     return {"pair": False, "BN": bn, "stages": min(4, (232448 - 256 - 1024) // stage)}
 
 
 def analyze_f32(spec) -> GemmConfig:
     """emmy's SIMT matmul family with f32 operands: ``problems/m01_matmul_512`` (a
     cp.async-staged 32x64 CTA tile, ``k_matmul_2967be.ir.txt:1-38``), the split-K form
-    with atomic partial sums (``problems/m02_matmul_rect/k_matmul.ir.txt:1-24``), and
-    ``tests/problems/x_m_*`` (batched, bias + relu and constant-scale tails).  Each
-    accumulator adds products of two values loaded -- from global memory or from a
-    shared buffer that a ``CpAsyncCopy`` filled -- from the operands A [.., M, K] and
-    B [.., K, N] (or [.., N, K]); the statements between the accumulator and the Write
-    of C become the epilogue.  The whole K runs in one pass (a split-K ``*_ks`` axis and
-    its atomic adds into the zeroed C give the same sum), on the 3xTF32 template."""
+    with atomic partial sums (``problems/m02_matmul_rect/k_matmul.ir.txt:1-24``),
+    ``tests/problems/x_m_*`` (batched, bias + relu and constant-scale tails) and the
+    operands cast to bf16 before a product kept exact (``tests/problems/x_q_bf16_mm_t``,
+    a warp-shuffle dot product per output, and ``x_q_bf16_mm_odd``, a register tile
+    writing split-K partial slices).  Each accumulator adds products of two values
+    loaded -- from global memory or from a shared buffer a ``CpAsyncCopy`` filled -- from
+    the operands A [.., M, K] and B [.., K, N] (or [.., N, K]), possibly masked to zero
+    past the end of K, or adds another such accumulator; the statements between the
+    accumulator and the Write of C become the epilogue.  The whole K runs in one pass (a
+    split-K ``*_ks`` axis and its atomic adds into the zeroed C, or its partial slices,
+    give the same sum), on the 3xTF32 template or, for cast operands, on one exact tf32
+    MMA of the rounded values."""
     stmts = list(_walk(spec.body))
     kinds = {type(s).__name__ for s in stmts}
-    if kinds & {"MmaSyncPtx", "WarpShuffle", "FragmentRowReduce"}:
+    if kinds & {"MmaSyncPtx", "FragmentRowReduce"}:
         raise NotImplementedError("not the SIMT matmul form")
     accs = [s for s in stmts if type(s).__name__ == "Accum"]
     if not accs:
@@ -1068,7 +1135,7 @@ def analyze_f32(spec) -> GemmConfig:
         if k == "Load":
             for n in s.names:
                 defs[n] = s
-        elif k == "Assign":
+        elif k in ("Assign", "Select", "Init"):
             defs[s.name] = s
     staged = {}
     for s in stmts:
@@ -1077,37 +1144,69 @@ def analyze_f32(spec) -> GemmConfig:
                 raise NotImplementedError("a shared buffer staged from two sources")
 
     def source(name):
-        d = defs.get(name)
+        """(buffer, Load, cast) of an operand value: copies followed to a Load; a
+        narrowing copy (to bf16 / f16) is the IR's cast of the operand."""
+        d, cast = defs.get(name), None
         while d is not None and type(d).__name__ == "Assign" and d.op.name == "copy" and len(d.args) == 1:
+            dt = getattr(d.dtype, "name", None)
+            if dt in ("bf16", "f16"):
+                if cast not in (None, dt):
+                    raise NotImplementedError("an operand cast twice")
+                cast = dt
             d = defs.get(d.args[0])
         if d is None or type(d).__name__ != "Load":
             raise NotImplementedError(f"matmul operand {name} is not a loaded value")
         if d.input in staged:
-            return staged[d.input], d
+            return staged[d.input], d, cast
         if d.input in spec.buffers and d.input not in spec.constants:
-            return d.input, d
+            return d.input, d, cast
         raise NotImplementedError(f"cannot trace operand {name} to a buffer")
 
-    acc_names = {a.name for a in accs}
-    kvars, loads = set(), {}
-    for a in accs:
-        v = defs.get(a.value)
-        if a.op.name != "add" or v is None or type(v).__name__ != "Assign" or \
-                v.op.name != "multiply" or len(v.args) != 2:
+    def is_zero(name):
+        d = defs.get(name)
+        return d is not None and type(d).__name__ == "Init" and float(d.identity) == 0.0
+
+    def product(name):
+        """The multiply an accumulated value is, unwrapping a mask (a Select between the
+        product and a zero Init)."""
+        d = defs.get(name)
+        if d is not None and type(d).__name__ == "Select":
+            vals = [br.value for br in d.branches if not is_zero(br.value)]
+            if len(vals) != 1 or len(d.branches) < 2:
+                raise NotImplementedError("a masked value that is not a product or zero")
+            d = defs.get(vals[0])
+        if d is None or type(d).__name__ != "Assign" or d.op.name != "multiply" or len(d.args) != 2:
             raise NotImplementedError("an accumulation that is not a sum of products")
+        return d
+
+    acc_names = {a.name for a in accs}
+    kvars, loads, casts = set(), {}, set()
+    for a in accs:
+        if a.op.name != "add":
+            raise NotImplementedError("an accumulation that is not a sum")
+        if a.value in acc_names:          # partial accumulators combined
+            continue
+        v = product(a.value)
         kvars |= set(a.axes or ())
         for x in v.args:
-            buf, ld = source(x)
+            buf, ld, cast = source(x)
             loads.setdefault(buf, ld)
+            casts.add(cast)
     if len(loads) != 2 or not kvars:
         raise NotImplementedError("products of other than two operands")
+    if len(casts) != 1:
+        raise NotImplementedError("operands cast differently")
+    cast = casts.pop()
 
-    writes = [s for s in stmts if type(s).__name__ == "Write"]
+    # (writes into shared buffers are the schedule's own combine)
+    writes = [s for s in stmts if type(s).__name__ == "Write" and s.output in spec.buffers]
     if not writes or len({w.output for w in writes}) != 1:
         raise NotImplementedError("matmul without a single output")
     first = writes[0]
     cname = first.output
     C = spec.param(cname)
+    if len(first.index) < 2 or len(C.shape) < 2:
+        raise NotImplementedError("an output without rows and columns")
     rvars, cvars = _vars(first.index[-2]), _vars(first.index[-1])
 
     def backslice(name):
@@ -1119,8 +1218,8 @@ def analyze_f32(spec) -> GemmConfig:
                 seeds.add(n)
                 return
             d = defs.get(n)
-            if d is None:
-                raise NotImplementedError(f"{n} is not defined in the kernel")
+            if d is None or type(d).__name__ not in ("Load", "Assign"):
+                raise NotImplementedError(f"{n} is not a loaded or computed value")
             if id(d) in seen:
                 return
             seen.add(id(d))
@@ -1147,7 +1246,7 @@ def analyze_f32(spec) -> GemmConfig:
                 raise NotImplementedError("outputs computed from several accumulators or differently")
 
     def dims(buf, ld):
-        """(K dim, free dim) of an operand, as dims of the global buffer."""
+        """(K dim, free dim, free-dim variables) of an operand, as dims of the global buffer."""
         shape = spec.param(buf).shape
         idx = ld.index
         kd = [i for i, e in enumerate(idx) if _vars(e) & kvars]
@@ -1175,9 +1274,22 @@ def analyze_f32(spec) -> GemmConfig:
     b_kmajor = bk == len(B.shape) - 1
     M, K = A.shape[-2], A.shape[-1]
     N = B.shape[bf]
-    if B.shape[bk] != K or tuple(C.shape[-2:]) != (M, N):
+    if B.shape[bk] != K:
         raise NotImplementedError("operand shapes do not form a matmul")
-    batch = int(math.prod(C.shape[:-2])) if len(C.shape) > 2 else 1
+    # emmy's split-K partial slices: a `*_ks` tile axis picks slice ks of an f32
+    # [S, .., M, N] buffer that a second kernel sums; the full product goes to slice 0
+    tile = spec.body[0] if len(spec.body) == 1 and type(spec.body[0]).__name__ == "Tile" else None
+    ks_axes = [ax for ax in (tile.axes if tile else ()) if ax.name.endswith("_ks")]
+    cdims, split = tuple(C.shape), {}
+    if ks_axes and len(cdims) == len(A.shape) + 1:
+        S = int(ks_axes[0].extent.value)
+        if len(ks_axes) != 1 or cdims[0] != S or _vars(first.index[0]) != {ks_axes[0].name}:
+            raise NotImplementedError("split-K partial slices not addressed by the split axis")
+        cdims = cdims[1:]
+        split = dict(zero_slots=S - 1, slot_stride=int(math.prod(cdims)))
+    if tuple(cdims[-2:]) != (M, N) or not len(A.shape) == len(B.shape) == len(cdims):
+        raise NotImplementedError("operand shapes do not form a matmul")
+    batch = int(math.prod(cdims[:-2])) if len(cdims) > 2 else 1
     if batch > 1 and (math.prod(A.shape[:-2]) != batch or math.prod(B.shape[:-2]) != batch):
         raise NotImplementedError("broadcast batch operands")
     if any(w.atomic for w in writes) and cname not in spec.zero_outputs:
@@ -1187,6 +1299,8 @@ def analyze_f32(spec) -> GemmConfig:
 
     epi = ()
     if chain:
+        if split:
+            raise NotImplementedError("an epilogue on split-K partial slices")
         from types import SimpleNamespace
         operands = []
         for d in chain:
@@ -1206,9 +1320,10 @@ def analyze_f32(spec) -> GemmConfig:
         epi = (("lambda", lam, tuple(operands), tuple(sorted(spec.constants.items()))),)
     od = tuple((q.name, q.dtype) for q in spec.params)
     return GemmConfig(M=M, N=N, K=K, batch=batch, ab="f32", c="f32", b_kmajor=b_kmajor,
-                      **choose_tiling_f32(M, N, batch), epilogue=epi, name=spec.name,
+                      **choose_tiling_f32(M, N, batch, split3=cast is None), epilogue=epi, name=spec.name,
                       a_param=aname, b_param=bname, c_param=cname, arg_params=arg_params(spec),
-                      buffers=tuple(q.name for q in spec.params), operand_dtypes=od)
+                      buffers=tuple(q.name for q in spec.params), operand_dtypes=od,
+                      operand_round=cast, **split)
 
 
 def emit_gemm(spec) -> str:

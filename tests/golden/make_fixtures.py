@@ -81,6 +81,8 @@ FIXTURES = [
     "tests/problems/x_m_tall", "tests/problems/x_m_wide", "tests/problems/x_m_longk",
     "tests/problems/x_m_256", "tests/problems/x_m_batched", "tests/problems/x_m_bias_relu",
     "tests/problems/x_m_scaled",
+    # f32 operands cast to bf16 before the product (tensor-core and warp-shuffle forms)
+    "tests/problems/x_q_bf16_mm", "tests/problems/x_q_bf16_mm_t",
 ]
 
 

@@ -10,7 +10,9 @@ import pytest
 from conftest import GOLDEN
 
 F32_MM = ["m01_matmul_512", "m02_matmul_rect", "x_m_small", "x_m_tall", "x_m_wide", "x_m_longk",
-          "x_m_256", "x_m_batched", "x_m_bias_relu", "x_m_scaled"]
+          "x_m_256", "x_m_batched", "x_m_bias_relu", "x_m_scaled",
+          # f32 operands cast to bf16 / f16: one exact tf32 MMA of the rounded values
+          "x_q_bf16_mm", "x_q_bf16_mm_t", "x_q_f16_mm_t"]
 
 
 @pytest.mark.gpu
