@@ -69,6 +69,9 @@ class GemmConfig:
     slot_stride: int = 0             # these many further slices (slot_stride elements apart) are zeroed
     operand_round: str | None = None  # f32 operands cast to "bf16" / "f16" before the product: one
                                       # exact tf32 MMA on the rounded values instead of 3xTF32
+    direct: bool = False             # converter warps load A and B from global memory (rows that
+    a_dtype: str = "f32"             # are not 16-byte aligned, 16-bit or mixed sources), with
+    b_dtype: str = "f32"             # these element types, instead of TMA
 
     BM = 128                         # accumulator rows per CTA
 
@@ -163,6 +166,7 @@ def _tile_coords(p: Ptx, cfg: GemmConfig, t: str) -> tuple[str, str, str]:
 
 def emit_gemm_module(cfg: GemmConfig) -> str:
     p = Ptx()
+    split, conv = cfg.split3, cfg.converts
     M, N, K, BM, BN, BK, S = cfg.M, cfg.N, cfg.K, cfg.BM, cfg.BN, cfg.BK, cfg.stages
     eb = ELEM_BYTES[cfg.ab]
     cb = ELEM_BYTES[cfg.c]
@@ -174,7 +178,6 @@ def emit_gemm_module(cfg: GemmConfig) -> str:
     a_bytes = BM * BK * eb                  # 16 KB
     b_bytes = BNc * BK * eb                 # 32 KB at BN = 256 (16 KB per CTA of a pair)
     raw_bytes = a_bytes + b_bytes           # what the TMA copies write per stage and CTA
-    split, conv = cfg.split3, cfg.converts
     if conv and pair:
         raise NotImplementedError("converted f32 operands on CTA pairs")
     # 3xTF32: the stage holds the tf32 hi parts (in place of the loaded f32 values)
@@ -212,13 +215,17 @@ def emit_gemm_module(cfg: GemmConfig) -> str:
         ptr[name] = load_pointer(p, name)
     status = p.reg("b64")
     p.emit(f"ld.param.u64 {status}, [param__status]\ncvta.to.global.u64 {status}, {status}")
+    direct = cfg.direct
+    if direct and not conv:
+        raise NotImplementedError("direct operand loads need the converter warps")
     tma_a, tma_b = p.reg("b64"), p.reg("b64")
-    p.emit(f"""
-        mov.u64 {tma_a}, param__tmap_a
-        cvta.param.u64 {tma_a}, {tma_a}
-        mov.u64 {tma_b}, param__tmap_b
-        cvta.param.u64 {tma_b}, {tma_b}
-    """)
+    if not direct:
+        p.emit(f"""
+            mov.u64 {tma_a}, param__tmap_a
+            cvta.param.u64 {tma_a}, {tma_a}
+            mov.u64 {tma_b}, param__tmap_b
+            cvta.param.u64 {tma_b}, {tma_b}
+        """)
     tid, warp, lane = p.reg("u32"), p.reg("u32"), p.reg("u32")
     p.emit(f"""
         mov.u32 {tid}, %tid.x
@@ -299,6 +306,8 @@ def emit_gemm_module(cfg: GemmConfig) -> str:
     p.emit(f"setp.ne.u32 {pr}, {warp}, 0\n@{pr} bra {role_mma}")
     pl = p.reg("pred")
     p.emit(f"setp.ne.u32 {pl}, {lane}, 0\n@{pl} bra {finish}")
+    if direct:      # the converter warps fetch the operands themselves
+        p.emit(f"bra {finish}")
     p.emit(f"prefetch.tensormap [{tma_a}]\nprefetch.tensormap [{tma_b}]")
     t, s, ph = p.reg("u32"), p.reg("u32"), p.reg("u32")
     p.emit(f"mov.u32 {t}, {cta}\nmov.u32 {s}, 0\nmov.u32 {ph}, 0")
@@ -458,8 +467,12 @@ def emit_gemm_module(cfg: GemmConfig) -> str:
                    waits, finish, crank if pair else None, ltempty if pair else None)
     if conv:
         p.place(role_conv)
-        _emit_split_tf32(p, cfg, tid, ring, bars, full0, conv0, cread, a_bytes, raw_bytes, stage_bytes,
-                         kblocks, cta, nct, ntiles, waits, finish)
+        if direct:
+            _emit_direct_loader(p, cfg, ptr, tid, ring, bars, empty0, conv0, a_bytes, raw_bytes,
+                                stage_bytes, kblocks, cta, nct, ntiles, waits, finish)
+        else:
+            _emit_split_tf32(p, cfg, tid, ring, bars, full0, conv0, cread, a_bytes, raw_bytes,
+                             stage_bytes, kblocks, cta, nct, ntiles, waits, finish)
 
     # -------------------------------------------------------------- finish
     p.place(finish)
@@ -482,8 +495,9 @@ def emit_gemm_module(cfg: GemmConfig) -> str:
     p.emit("ret")
 
     params = list(cfg.arg_params or [f".param .u64 {param_symbol(n)}" for n in cfg.buffers])
-    params += [".param .align 64 .b8 param__tmap_a[128]", ".param .align 64 .b8 param__tmap_b[128]",
-               ".param .u64 param__status"]
+    if not direct:
+        params += [".param .align 64 .b8 param__tmap_a[128]", ".param .align 64 .b8 param__tmap_b[128]"]
+    params += [".param .u64 param__status"]
     nthreads = GEMM_THREADS + (CONV_THREADS if conv else 0)
     text = entry(cfg.name, params, p, maxntid=nthreads)
     statics = (f"\t.shared .align 8 .b64 gbars[{nbar}];\n\t.shared .align 4 .u32 gabort;\n"
@@ -503,13 +517,12 @@ def emit_gemm_module(cfg: GemmConfig) -> str:
     launch = {
         "kind": "gemm", "grid": [grid, 1, 1], "block": [nthreads, 1, 1], "cluster": [2 if pair else 1, 1, 1],
         "smem": smem, "flops": 2 * cfg.batch * M * N * K, "tiles": ntiles,
-        "extra_params": [
+        "extra_params": ([] if direct else [
             {"kind": "tmap", "buffer": cfg.a_param, "dtype": cfg.ab, "dims": a_dims, "strides": a_str,
              "box": [BK, BM] + ([1] if rank == 3 else []), "swizzle": 128},
             {"kind": "tmap", "buffer": cfg.b_param, "dtype": cfg.ab, "dims": b_dims, "strides": b_str,
              "box": b_box, "swizzle": 128},
-            {"kind": "status"},
-        ],
+        ]) + [{"kind": "status"}],
     }
     return module([text], launch, globals_=[".extern .shared .align 1024 .b8 dsmem[];"])
 
@@ -659,6 +672,182 @@ def _emit_split_tf32(p: Ptx, cfg: GemmConfig, tid, ring, bars, full0, conv0, cre
             p.emit(f"st.shared.v4.b32 [{ad}], {{{', '.join(h for h, _ in parts)}}}")
             if cfg.split3:
                 p.emit(f"st.shared.v4.b32 [{ad}+{raw_bytes}], {{{', '.join(lo for _, lo in parts)}}}")
+    p.emit(f"""
+        fence.proxy.async.shared::cta
+        mbarrier.arrive.shared::cta.b64 _, [{ca}]
+        add.u32 {s}, {s}, 1
+        setp.eq.u32 {ps}, {s}, {cfg.stages}
+        @{ps} mov.u32 {s}, 0
+        @{ps} xor.b32 {ph}, {ph}, 1
+        add.u32 {kb}, {kb}, 1
+        setp.lt.u32 {ps}, {kb}, {kblocks}
+        @{ps} bra {kl}
+        add.u32 {t}, {t}, {nct}
+        bra {tl}
+    """)
+
+
+def _emit_direct_loader(p: Ptx, cfg: GemmConfig, ptr: dict, tid, ring, bars, empty0, conv0, a_bytes,
+                        raw_bytes, stage_bytes, kblocks, cta, nct, ntiles, waits: Waits, finish: str) -> None:
+    """Converter warps that fetch the operands from global memory themselves (no TMA): for
+    rows that are not 16-byte aligned (emmy's odd-shaped fixtures), 16-bit sources (widened
+    exactly) and mixed operand types.  Per stage each of the 128 threads loads its
+    elements of the 128 x 32 A tile and the BN x 32 B tile (out-of-range rows, columns and
+    K zero-filled: the loads are predicated), converts them like ``_emit_split_tf32`` and
+    writes them into the K-major 128-byte-swizzled layout the MMAs read.  The stage is
+    taken once the MMAs released it (empty[stage]) and handed over on conv[stage]."""
+    M, N, K, BN = cfg.M, cfg.N, cfg.K, cfg.BN
+    ea, eb = ELEM_BYTES[cfg.a_dtype], ELEM_BYTES[cfg.b_dtype]
+    ctid, lane, grp, l4, lw, t1 = (p.reg("u32") for _ in range(6))
+    p.emit(f"""
+        sub.u32 {ctid}, {tid}, {GEMM_THREADS}
+        and.b32 {lane}, {ctid}, 31
+        shr.u32 {grp}, {ctid}, 5
+        shr.u32 {l4}, {lane}, 2
+        and.b32 {lw}, {lane}, 3
+        shl.b32 {lw}, {lw}, 2
+    """)
+    # K-major rows grp + 4j: row & 7 = grp + 4 (j & 1), so two chunk offsets serve all j
+    kmaj = []
+    for par in (0, 1):
+        o = p.reg("u32")
+        p.emit(f"""
+            add.u32 {t1}, {grp}, {4 * par}
+            xor.b32 {t1}, {t1}, {l4}
+            shl.b32 {t1}, {t1}, 4
+            mad.lo.u32 {o}, {grp}, 128, {t1}
+            add.u32 {o}, {o}, {lw}
+        """)
+        kmaj.append(o)
+    # MN-major B columns lane + 32c, K rows grp + 4q: chunk q ^ (lane & 7), word grp
+    mnq = []
+    if not cfg.b_kmajor:
+        l7, gw = p.reg("u32"), p.reg("u32")
+        p.emit(f"and.b32 {l7}, {lane}, 7\nshl.b32 {gw}, {grp}, 2")
+        for q in range(8):
+            o = p.reg("u32")
+            p.emit(f"""
+                xor.b32 {t1}, {l7}, {q}
+                shl.b32 {t1}, {t1}, 4
+                mad.lo.u32 {o}, {lane}, 128, {t1}
+                add.u32 {o}, {o}, {gw}
+            """)
+            mnq.append(o)
+    nbb = BN // 32
+    t, s, ph, kb = (p.reg("u32") for _ in range(4))
+    p.emit(f"mov.u32 {t}, {cta}\nmov.u32 {s}, 0\nmov.u32 {ph}, 0")
+    tl, kl = p.label("d_tile"), p.label("d_k")
+    pt, ps = p.reg("pred"), p.reg("pred")
+    p.place(tl)
+    p.emit(f"setp.ge.u32 {pt}, {t}, {ntiles}\n@{pt} bra {finish}\nmov.u32 {kb}, 0")
+    bt, mt, nt = _tile_coords(p, cfg, t)
+    m0, n0 = p.reg("u32"), p.reg("u32")
+    p.emit(f"mul.lo.u32 {m0}, {mt}, {cfg.MT}\nmul.lo.u32 {n0}, {nt}, {BN}")
+    p.place(kl)
+    ea_, ca, par, base, k0 = (p.reg("u32") for _ in range(5))
+    p.emit(f"""
+        mad.lo.u32 {ea_}, {s}, 8, {bars}
+        add.u32 {ca}, {ea_}, {conv0}
+        add.u32 {ea_}, {ea_}, {empty0}
+        xor.b32 {par}, {ph}, 1
+        mul.lo.u32 {k0}, {kb}, 32
+    """)
+    waits.wait(ea_, par, "convert", finish)
+    p.emit(f"mad.lo.u32 {base}, {s}, {stage_bytes}, {ring}")
+
+    def load(dtype, adr, off, pred):
+        v = p.reg("b32")
+        p.emit(f"mov.b32 {v}, 0")
+        if dtype == "f32":
+            p.emit(f"@{pred} ld.global.b32 {v}, [{adr}+{off}]")
+        else:
+            h = p.reg("b16")
+            up = "cvt.f32.f16" if dtype == "f16" else "cvt.f32.bf16"
+            p.emit(f"mov.b16 {h}, 0\n@{pred} ld.global.b16 {h}, [{adr}+{off}]\n{up} {v}, {h}")
+        return v
+
+    def store(items):
+        for x, off in items:
+            (hi, lo), = _convert(p, cfg, [x])
+            ad = p.reg("u32")
+            p.emit(f"add.u32 {ad}, {base}, {off[0]}")
+            p.emit(f"st.shared.b32 [{ad}+{off[1]}], {hi}")
+            if cfg.split3:
+                p.emit(f"st.shared.b32 [{ad}+{off[1] + raw_bytes}], {lo}")
+
+    def limit(x):
+        if x >= 2 ** 31:
+            raise NotImplementedError("operand offsets beyond 32 bits")
+        return x
+
+    # A [batch, M, K]: rows m0 + grp + 4j, K k0 + lane
+    ra, kk, pk = p.reg("u32"), p.reg("u32"), p.reg("pred")
+    aad, w = p.reg("b64"), p.reg("b64")
+    p.emit(f"""
+        add.u32 {ra}, {m0}, {grp}
+        add.u32 {kk}, {k0}, {lane}
+        setp.lt.u32 {pk}, {kk}, {K}
+        mad.lo.u32 {t1}, {bt}, {M}, {ra}
+        mul.wide.u32 {aad}, {t1}, {K}
+        cvt.u64.u32 {w}, {kk}
+        add.s64 {aad}, {aad}, {w}
+        mad.lo.s64 {aad}, {aad}, {ea}, {ptr[cfg.a_param]}
+    """)
+    for g0 in range(0, 32, 8):
+        items = []
+        for j in range(g0, g0 + 8):
+            pj = p.reg("pred")
+            if M - 4 * j <= 0:
+                continue
+            p.emit(f"setp.lt.and.u32 {pj}, {ra}, {M - 4 * j}, {pk}")
+            items.append((load(cfg.a_dtype, aad, limit(j * 4 * K * ea), pj), (kmaj[j & 1], j * 512)))
+        store(items)
+    bad, rb = p.reg("b64"), p.reg("u32")
+    if cfg.b_kmajor:
+        # B [batch, N, K]: rows n0 + grp + 4i, K k0 + lane
+        p.emit(f"""
+            add.u32 {rb}, {n0}, {grp}
+            mad.lo.u32 {t1}, {bt}, {N}, {rb}
+            mul.wide.u32 {bad}, {t1}, {K}
+            cvt.u64.u32 {w}, {kk}
+            add.s64 {bad}, {bad}, {w}
+            mad.lo.s64 {bad}, {bad}, {eb}, {ptr[cfg.b_param]}
+        """)
+        for g0 in range(0, BN // 4, 8):
+            items = []
+            for i in range(g0, min(BN // 4, g0 + 8)):
+                pi = p.reg("pred")
+                if N - 4 * i <= 0:
+                    continue
+                p.emit(f"setp.lt.and.u32 {pi}, {rb}, {N - 4 * i}, {pk}")
+                items.append((load(cfg.b_dtype, bad, limit(i * 4 * K * eb), pi), (kmaj[i & 1], a_bytes + i * 512)))
+            store(items)
+    else:
+        # B [batch, K, N]: K rows k0 + grp + 4q, columns n0 + lane + 32c
+        kb_, cn = p.reg("u32"), p.reg("u32")
+        p.emit(f"""
+            add.u32 {kb_}, {k0}, {grp}
+            add.u32 {cn}, {n0}, {lane}
+            mad.lo.u32 {t1}, {bt}, {K}, {kb_}
+            mul.wide.u32 {bad}, {t1}, {N}
+            cvt.u64.u32 {w}, {cn}
+            add.s64 {bad}, {bad}, {w}
+            mad.lo.s64 {bad}, {bad}, {eb}, {ptr[cfg.b_param]}
+        """)
+        pq = [p.reg("pred") for _ in range(8)]
+        pc = [p.reg("pred") for _ in range(nbb)]
+        for q in range(8):
+            p.emit(f"setp.lt.u32 {pq[q]}, {kb_}, {K - 4 * q}" if K - 4 * q > 0 else f"setp.ne.u32 {pq[q]}, 0, 0")
+        for c in range(nbb):
+            p.emit(f"setp.lt.u32 {pc[c]}, {cn}, {N - 32 * c}" if N - 32 * c > 0 else f"setp.ne.u32 {pc[c]}, 0, 0")
+        for q in range(8):
+            items = []
+            for c in range(nbb):
+                pi = p.reg("pred")
+                p.emit(f"and.pred {pi}, {pq[q]}, {pc[c]}")
+                items.append((load(cfg.b_dtype, bad, limit((4 * q * N + 32 * c) * eb), pi),
+                              (mnq[q], a_bytes + c * 4096)))
+            store(items)
     p.emit(f"""
         fence.proxy.async.shared::cta
         mbarrier.arrive.shared::cta.b64 _, [{ca}]
@@ -997,18 +1186,20 @@ def analyze(spec) -> GemmConfig:
     if batch > 1 and (math.prod(A.shape[:-2]) != batch or math.prod(B.shape[:-2]) != batch):
         raise NotImplementedError("broadcast batch operands")
     eb = 4 if f32_cast else 2
-    if (K * eb) % 16 or (not b_kmajor and (N * eb) % 16):
-        raise NotImplementedError("operand rows are not 16-byte aligned (TMA)")
+    aligned = not ((K * eb) % 16 or (not b_kmajor and (N * eb) % 16))
     epi = _epilogue_ops(spec, stores[0])
-    if f32_cast:
-        if C.dtype != "f32":
+    if f32_cast or not aligned:
+        # the tf32 template: f32 operands rounded as the IR casts them, or 16-bit operands
+        # (exact in tf32) fetched by the converter warps where TMA cannot address the rows
+        if f32_cast and C.dtype != "f32":
             raise NotImplementedError("cast-operand matmul with a 16-bit output")
         od = tuple((q.name, q.dtype) for q in spec.params)
-        return GemmConfig(M=M, N=N, K=K, batch=batch, ab="f32", c="f32", b_kmajor=b_kmajor,
+        return GemmConfig(M=M, N=N, K=K, batch=batch, ab="f32", c=C.dtype, b_kmajor=b_kmajor,
                           **choose_tiling_f32(M, N, batch, split3=False), epilogue=epi, name=spec.name,
                           a_param=aname, b_param=bname, c_param=cname, arg_params=arg_params(spec),
                           buffers=tuple(q.name for q in spec.params), operand_dtypes=od,
-                          operand_round=role_cast["a"], **split)
+                          operand_round=role_cast["a"] if f32_cast else A.dtype, direct=not aligned,
+                          a_dtype=A.dtype, b_dtype=B.dtype, **split)
     od = tuple((q.name, q.dtype) for q in spec.params if q.dtype in ("f16", "bf16"))
     tiling = choose_tiling(M, N, batch, 32 if b_kmajor else 64)
     return GemmConfig(M=M, N=N, K=K, batch=batch, ab=A.dtype, c=C.dtype, b_kmajor=b_kmajor, **tiling,
@@ -1267,8 +1458,10 @@ def analyze_f32(spec) -> GemmConfig:
     else:
         raise NotImplementedError("operand roles not identifiable")
     A, B = spec.param(aname), spec.param(bname)
-    if A.dtype != "f32" or B.dtype != "f32" or C.dtype != "f32":
+    if A.dtype not in ("f32", "f16", "bf16") or B.dtype not in ("f32", "f16", "bf16") or C.dtype != "f32":
         raise NotImplementedError(f"SIMT matmul {A.dtype} x {B.dtype} -> {C.dtype}")
+    if cast is None and A.dtype == B.dtype and A.dtype != "f32":
+        cast = A.dtype          # 16-bit operands: exact in tf32, one MMA
     if ak != len(A.shape) - 1:
         raise NotImplementedError("A operand is not K-major")
     b_kmajor = bk == len(B.shape) - 1
@@ -1294,8 +1487,8 @@ def analyze_f32(spec) -> GemmConfig:
         raise NotImplementedError("broadcast batch operands")
     if any(w.atomic for w in writes) and cname not in spec.zero_outputs:
         raise NotImplementedError("atomic partial sums into an output that is not zeroed")
-    if (K * 4) % 16 or (not b_kmajor and (N * 4) % 16):
-        raise NotImplementedError("operand rows are not 16-byte aligned (TMA)")
+    # TMA needs f32 operands with 16-byte rows; anything else is fetched by the converters
+    direct = A.dtype != "f32" or B.dtype != "f32" or bool((K * 4) % 16 or (not b_kmajor and (N * 4) % 16))
 
     epi = ()
     if chain:
@@ -1323,7 +1516,7 @@ def analyze_f32(spec) -> GemmConfig:
                       **choose_tiling_f32(M, N, batch, split3=cast is None), epilogue=epi, name=spec.name,
                       a_param=aname, b_param=bname, c_param=cname, arg_params=arg_params(spec),
                       buffers=tuple(q.name for q in spec.params), operand_dtypes=od,
-                      operand_round=cast, **split)
+                      operand_round=cast, direct=direct, a_dtype=A.dtype, b_dtype=B.dtype, **split)
 
 
 def emit_gemm(spec) -> str:

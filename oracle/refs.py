@@ -370,6 +370,11 @@ PROBLEM_REFS = {
     "x_q_f16_mm_t": lambda a, b: [f32(mm_f16(f16(a), f16(b).T))],
     "x_q_bf16_mm": lambda a, b: [mm_bf16(bf16_round(a), bf16_round(b))],
     "x_q_bf16_mm_t": lambda a, b: [mm_bf16(bf16_round(a), bf16_round(b).T)],
+    "x_q_bf16_mm_odd": lambda a, b: [mm_bf16(bf16_round(a), bf16_round(b))],
+    "x_h_mm_odd": lambda a, b: [mm_f16(a, b)],
+    "x_h_mm_odd2": lambda a, b: [mm_f16(a, b)],
+    "x_h_mm_mixed": lambda a, b: [mm_f32(a, b)],
+    "x_m_odd": lambda a, b: [mm_f32(a, b)],
     "x_d_f16_dot": lambda a, b: [f16_dot(a, b, f16)],
     "x_d_f16_dot_f32": lambda a, b: [f16_dot(a, b, f32)],
     "x_l_swiglu": lambda x, w1, w3: [swiglu(x, w1, w3)],

@@ -12,7 +12,9 @@ from conftest import GOLDEN
 F32_MM = ["m01_matmul_512", "m02_matmul_rect", "x_m_small", "x_m_tall", "x_m_wide", "x_m_longk",
           "x_m_256", "x_m_batched", "x_m_bias_relu", "x_m_scaled",
           # f32 operands cast to bf16 / f16: one exact tf32 MMA of the rounded values
-          "x_q_bf16_mm", "x_q_bf16_mm_t", "x_q_f16_mm_t"]
+          "x_q_bf16_mm", "x_q_bf16_mm_t", "x_q_f16_mm_t",
+          # rows not 16-byte aligned, 16-bit and mixed operands: loaded by the converter warps
+          "x_q_bf16_mm_odd", "x_h_mm_odd", "x_h_mm_odd2", "x_h_mm_mixed", "x_m_odd"]
 
 
 @pytest.mark.gpu
@@ -89,4 +91,54 @@ def test_3xtf32_accuracy(runtime, m, n, k, b_kmajor, batch, BN):
 @pytest.mark.gpu
 def test_3xtf32_bias_on_ragged_tiles(runtime):
     out, ref, scale = _run_f32(130, 100, 64, bias=True, BN=64)
+    assert np.max(np.abs(out - ref) / scale) <= 2.0 ** -16
+
+
+def _run_direct(m, n, k, a_dt, b_dt, b_kmajor, rnd, seed=1):
+    """The converter warps' own operand loads (no TMA) on odd shapes: several tiles, several
+    stages, partial tiles on every edge."""
+    import emmyrt
+    from compiler.kernels.gemm import GemmConfig, choose_tiling_f32, emit_gemm_module
+    from emmyrt import DeviceBuffer
+    from emmyrt.runner import CompiledKernel, f32_to_bf16_bits, bf16_bits_to_f32
+    cfg = GemmConfig(M=m, N=n, K=k, ab="f32", c="f32", b_kmajor=b_kmajor,
+                     **choose_tiling_f32(m, n, 1, split3=rnd is None), name="k_gemm_direct",
+                     buffers=("a", "b", "c"), operand_round=rnd, direct=True, a_dtype=a_dt, b_dtype=b_dt)
+    ck = CompiledKernel.from_module(emit_gemm_module(cfg), "k_gemm_direct", ["a", "b", "c"])
+    rng = np.random.default_rng(seed)
+
+    def host(shape, dt):
+        x = rng.standard_normal(shape).astype(np.float32)
+        if dt == "f16":
+            return x.astype(np.float16), x.astype(np.float16).astype(np.float64)
+        if dt == "bf16":
+            bits = f32_to_bf16_bits(x)
+            return bits, bf16_bits_to_f32(bits).astype(np.float64)
+        return x, x.astype(np.float64)
+    A, Af = host((m, k), a_dt)
+    B, Bf = host((n, k) if b_kmajor else (k, n), b_dt)
+    da, db, dc = DeviceBuffer(A.nbytes), DeviceBuffer(B.nbytes), DeviceBuffer(m * n * 4)
+    da.upload(A)
+    db.upload(B)
+    dc.zero()
+    ck({"a": da.ptr, "b": db.ptr, "c": dc.ptr})
+    emmyrt.stream_wait(0, 60)
+    assert ck.status() == 0
+    out = np.zeros((m, n), np.float32)
+    dc.download(out)
+    Bm = Bf.T if b_kmajor else Bf
+    return out, Af @ Bm, np.abs(Af) @ np.abs(Bm)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("m,n,k,a_dt,b_dt,b_kmajor,rnd", [
+    (300, 173, 229, "f32", "f32", False, None),     # 3xTF32, every row length odd
+    (257, 130, 101, "f32", "f32", True, None),
+    (200, 77, 135, "f16", "f16", False, "f16"),     # 16-bit rows of 154 / 270 bytes
+    (129, 95, 67, "bf16", "bf16", True, "bf16"),
+    (70, 50, 45, "f16", "f32", False, None),        # mixed: f16 A exact, f32 B split
+])
+def test_direct_loads_on_odd_shapes(runtime, m, n, k, a_dt, b_dt, b_kmajor, rnd):
+    out, ref, scale = _run_direct(m, n, k, a_dt, b_dt, b_kmajor, rnd)
+    # 16-bit operands are exact in tf32: only the f32 accumulation differs
     assert np.max(np.abs(out - ref) / scale) <= 2.0 ** -16

@@ -14,7 +14,7 @@ PROBLEMS = sorted(p.name for p in GOLDEN.iterdir())
 # bf16 matmul results: torch adds the f32 products in its own order before rounding to
 # bf16, so a sum that lands next to a bf16 rounding boundary may round the other way
 # (1 of 4096 outputs of x_q_bf16_mm); these agree to one bf16 ulp
-ONE_BF16_ULP = {"x_q_bf16_mm", "x_q_bf16_mm_t"}
+ONE_BF16_ULP = {"x_q_bf16_mm", "x_q_bf16_mm_t", "x_q_bf16_mm_odd"}
 
 
 @pytest.mark.parametrize("pid", PROBLEMS)
@@ -27,8 +27,9 @@ def test_oracle_matches_golden(pid):
     for name, ref in exp.items():
         g = np.asarray(got[name]).reshape(ref.shape)
         if pid in ONE_BF16_ULP:
-            # one ulp of a bf16 value: 2^-7 of it at most (just below a power of two)
-            assert np.all(np.abs(g - ref) <= np.abs(ref) * 2.0 ** -7), f"{pid}:{name}"
+            # one ulp of a bf16 value: 2^-7 of it at most (just below a power of two); sums
+            # that cancel to near zero keep the f32 adding order's own error (~1e-6)
+            assert np.all(np.abs(g - ref) <= np.abs(ref) * 2.0 ** -7 + 2.0 ** -16), f"{pid}:{name}"
             continue
         # same formula at the same precision: bit-identical
         assert np.array_equal(g.astype(ref.dtype), ref), f"{pid}:{name}"
