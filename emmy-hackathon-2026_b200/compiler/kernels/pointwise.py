@@ -46,6 +46,9 @@ class MapKernel:
             k = type(s).__name__
             if k == "Loop":
                 self._check(s.body)
+            elif k == "Cond":
+                self._check(s.body)
+                self._check(s.else_body or ())
             elif k == "Write":
                 if s.atomic:
                     raise NotImplementedError("element map: atomic Write")
@@ -113,6 +116,18 @@ class MapKernel:
         p = ctx.ptx
         for s in body:
             k = type(s).__name__
+            if k == "Cond":
+                # a guard over the element's indices (emmy's bounds checks on partial tiles):
+                # each branch in its own scope, accumulators updated in place
+                c, pc = self._index(p, s.cond), p.reg("pred")
+                l_else, l_end = p.label("cond_else"), p.label("cond_end")
+                p.emit(f"setp.ne.s32 {pc}, {c}, 0\n@!{pc} bra {l_else}")
+                self._body_scope(ctx, s.body)
+                p.emit(f"bra {l_end}")
+                p.place(l_else)
+                self._body_scope(ctx, s.else_body or ())
+                p.place(l_end)
+                continue
             if k != "Loop":
                 lower_body(ctx, [s])
                 continue

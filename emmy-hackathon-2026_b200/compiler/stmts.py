@@ -99,8 +99,19 @@ class ScalarCtx:
 
     def f32(self, name: str) -> str:
         v = self.get(name)
+        if v.kind == "pred":
+            # a bool in arithmetic is 1.0 / 0.0 (torch promotes bool to the float type)
+            r = self.ptx.reg("f32")
+            self.ptx.emit(f"selp.f32 {r}, 0f3F800000, 0f00000000, {v.text}")
+            return r
         if v.kind != "f32":
             raise NotImplementedError(f"{name!r} is {v.kind}, expected f32")
+        return v.text
+
+    def pred(self, name: str) -> str:
+        v = self.get(name)
+        if v.kind != "pred":
+            raise NotImplementedError(f"{name!r} is {v.kind}, expected bool")
         return v.text
 
 
@@ -172,6 +183,41 @@ def emit_erf(p: Ptx, dst: str, x: str) -> None:
     """)
 
 
+# tanh x = x + c3 x^3 + ... + c17 x^17 + ...: its Taylor series, c(2n-1) =
+# 2^(2n) (2^(2n) - 1) B(2n) / (2n)! with B the Bernoulli numbers (-1/3, 2/15, -17/315, ...)
+_TANH_C = (-0.3333333333333333, 0.13333333333333333, -0.05396825396825397, 0.021869488536155203, -0.008863235529902197, 0.003592128036572481, -0.0014558343870513183, 0.000590027440945586)
+_TANH_SERIES_MAX = 0.55      # below: the series (next term < 1e-8 relative); above: via exp
+
+
+def emit_tanh(p: Ptx, dst: str, x: str) -> None:
+    """tanh x: for |x| < 0.55 the odd Taylor series to x^17 (Horner in x^2, error a few
+    ulp); above, 1 - 2 / (exp(2|x|) + 1) with this back end's exp (no cancellation:
+    the subtracted term is at most 1/2 of the result); the sign restored last."""
+    ax, x2, q, e, r, big = (p.reg("f32") for _ in range(6))
+    ps = p.reg("pred")
+    p.emit(f"abs.f32 {ax}, {x}\nmul.rn.f32 {x2}, {x}, {x}\nmov.f32 {q}, {f32_hex(_TANH_C[-1])}")
+    for c in reversed(_TANH_C[:-1]):
+        p.emit(f"fma.rn.f32 {q}, {q}, {x2}, {f32_hex(c)}")
+    p.emit(f"mul.rn.f32 {q}, {q}, {x2}\nfma.rn.f32 {q}, {q}, {ax}, {ax}\nadd.rn.f32 {e}, {ax}, {ax}")
+    emit_exp(p, e, e)
+    p.emit(f"""
+        add.rn.f32 {e}, {e}, 0f3F800000
+        div.rn.f32 {big}, 0f40000000, {e}
+        sub.rn.f32 {big}, 0f3F800000, {big}
+        setp.lt.f32 {ps}, {ax}, {f32_hex(_TANH_SERIES_MAX)}
+        selp.f32 {r}, {q}, {big}, {ps}
+        copysign.f32 {dst}, {x}, {r}
+    """)
+
+
+def emit_sigmoid(p: Ptx, dst: str, x: str) -> None:
+    """1 / (1 + exp(-x)): exp(-x) overflows to inf for x < -88, giving 0 as it should."""
+    n = p.reg("f32")
+    p.emit(f"neg.f32 {n}, {x}")
+    emit_exp(p, n, n)
+    p.emit(f"add.rn.f32 {n}, {n}, 0f3F800000\nrcp.rn.f32 {dst}, {n}")
+
+
 def _unary(p: Ptx, op: str, dst: str, a: str) -> None:
     if op == "copy":
         p.emit(f"mov.f32 {dst}, {a}")
@@ -196,6 +242,10 @@ def _unary(p: Ptx, op: str, dst: str, a: str) -> None:
         p.emit(f"mul.rn.f32 {dst}, {a}, {a}")
     elif op == "erf":
         emit_erf(p, dst, a)
+    elif op == "tanh":
+        emit_tanh(p, dst, a)
+    elif op == "sigmoid":
+        emit_sigmoid(p, dst, a)
     elif op == "log":
         # ln x = log2(x) * ln 2 on the MUFU lg2 unit (about 2^-22 absolute error for
         # x in [1/2, 2], a few ulp relative elsewhere)
@@ -324,8 +374,58 @@ def _contraction(ctx: ScalarCtx, args) -> bool:
     return bool(a and b and a - b and b - a)
 
 
+# comparisons as ordered PTX compares (false with a NaN operand, as torch's), except
+# not_equal (true with a NaN)
+_CMP_OPS = {"greater": "gt", "greater_equal": "ge", "less": "lt", "less_equal": "le",
+            "equal": "eq", "not_equal": "neu"}
+_BOOL_OPS = {"bitwise_and": "and", "bitwise_or": "or", "bitwise_xor": "xor",
+             "logical_and": "and", "logical_or": "or", "logical_xor": "xor"}
+
+
+def _lower_bool(ctx: ScalarCtx, s) -> bool:
+    """Comparisons, logic on bools and ``where``: the bool values live in predicates."""
+    op, p = s.op.name, ctx.ptx
+    if op in _CMP_OPS:
+        a, b = (ctx.f32(x) for x in s.args)
+        r = p.reg("pred")
+        p.emit(f"setp.{_CMP_OPS[op]}.f32 {r}, {a}, {b}")
+        ctx.env[s.name] = Val(r, "pred")
+        return True
+    if op in _BOOL_OPS and all(ctx.get(x).kind == "pred" for x in s.args):
+        a, b = (ctx.pred(x) for x in s.args)
+        r = p.reg("pred")
+        p.emit(f"{_BOOL_OPS[op]}.pred {r}, {a}, {b}")
+        ctx.env[s.name] = Val(r, "pred")
+        return True
+    if op in ("bitwise_not", "logical_not") and ctx.get(s.args[0]).kind == "pred":
+        r = p.reg("pred")
+        p.emit(f"not.pred {r}, {ctx.pred(s.args[0])}")
+        ctx.env[s.name] = Val(r, "pred")
+        return True
+    if op == "where":
+        c = ctx.pred(s.args[0])
+        a, b = ctx.f32(s.args[1]), ctx.f32(s.args[2])
+        r = p.reg("f32")
+        p.emit(f"selp.f32 {r}, {a}, {b}, {c}")
+        val = Val(r, "f32")
+        if dtype_name(s.dtype) in NARROW:
+            val = Val(round_half(ctx, s.dtype, r), "f32")
+        target = ctx.env[s.name].text if (s.name in ctx.mutable and s.name in ctx.env) else None
+        if target is not None:
+            p.emit(f"mov.f32 {target}, {val.text}")
+        else:
+            ctx.env[s.name] = val
+        return True
+    if op == "copy" and dtype_name(s.dtype) == "bool" and ctx.get(s.args[0]).kind == "pred":
+        ctx.env[s.name] = ctx.get(s.args[0])
+        return True
+    return False
+
+
 @handles("Assign")
 def lower_assign(ctx: ScalarCtx, s) -> None:
+    if _lower_bool(ctx, s):
+        return
     _check_f32(s.dtype, "Assign", ctx)
     target = ctx.env[s.name].text if (s.name in ctx.mutable and s.name in ctx.env) else None
     val = compute_f32(ctx, s.op.name, list(s.args), dst=None)

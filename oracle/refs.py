@@ -430,6 +430,25 @@ PROBLEM_REFS = {
     "x_l_linattn": lambda q, k, v: [linattn(q, k, v)],
     "a02_attention_128": lambda q, kt, v: [f32(_softmax(f64(q) @ f64(kt) / 5.656854) @ f64(v))],
     "x_a_rect": lambda q, kt, v: [f32(_softmax((f64(q) @ f64(kt)) * 0.17677669) @ f64(v))],
+    # bool masks / where, tanh and sigmoid (expressions_extra.py:106-184; expressions_llm.py:79-80)
+    "x_l_softcap": lambda x: [f32(_softmax(30 * np.tanh(f64(x) / 30)))],
+    "x_p_where": lambda x, y: [np.where(x > 0, x, y)],
+    "x_p_cmp_mask": lambda x, y: [np.where((x >= y) & (x < np.float32(0.5)), x, -y)],
+    "x_p_elu_where": lambda x: [f32(np.where(f64(x) > 0, f64(x), np.exp(f64(x)) - 1.0))],
+    "x_p_leaky_where": lambda x: [np.where(x > 0, x, x * np.float32(0.1))],
+    "x_p_mask_and": lambda x: [np.where((x > -1) & (x < 1), x, np.float32(0))],
+    "x_p_mask_float": lambda x: [(x > 0.5).astype(np.float32) + x],
+    "x_p_mask_mul": lambda x: [x * (x > 0)],
+    "x_p_mask_not": lambda x: [np.where(~(x > 0), x * np.float32(2), x)],
+    "x_p_gelu_tanh": lambda x: [f32(0.5 * f64(x) * (1 + np.tanh(np.sqrt(2 / np.pi) * (f64(x) + 0.044715 * f64(x) ** 3))))],
+    "x_p_mish": lambda x: [f32(f64(x) * np.tanh(np.logaddexp(0.0, f64(x))))],
+    "x_p_sigmoid": lambda x: [f32(1.0 / (1.0 + np.exp(-f64(x))))],
+    "x_p_tanh": lambda x: [f32(np.tanh(f64(x)))],
+    "x_p_tanhshrink": lambda x: [f32(f64(x) - np.tanh(f64(x)))],
+    # (expressions_extra.py:263-274)
+    "x_a_32x16": lambda q, kt, v: [f32(_softmax((f64(q) @ f64(kt)) / 4.0) @ f64(v))],
+    "x_a_256x64": lambda q, kt, v: [f32(_softmax((f64(q) @ f64(kt)) / 8.0) @ f64(v))],
+    "x_a_batched": lambda q, kt, v: [f32(_softmax((f64(q) @ f64(kt)) / 5.656854) @ f64(v))],
     # scans (expressions_extra.py:288-291; expressions_llm.py:27-29, 56-58)
     "x_r_cumsum": lambda x: [f32(np.cumsum(f64(x)))],
     "x_r_cumsum_rows": lambda x: [f32(np.cumsum(f64(x), -1))],

@@ -87,6 +87,15 @@ FIXTURES = [
     # warps load the tiles themselves
     "tests/problems/x_q_bf16_mm_odd", "tests/problems/x_h_mm_odd", "tests/problems/x_h_mm_odd2",
     "tests/problems/x_h_mm_mixed", "tests/problems/x_m_odd",
+    # emmy's register-tiled f32 attention with bounds guards (element maps with Cond)
+    "tests/problems/x_a_32x16", "tests/problems/x_a_256x64", "tests/problems/x_a_batched",
+    # bool masks / where, tanh (this back end's own, from its series and exp), sigmoid; the
+    # soft-capped softmax (Gemma-style logit capping) is a row reduction
+    "tests/problems/x_l_softcap", "tests/problems/x_p_where", "tests/problems/x_p_cmp_mask",
+    "tests/problems/x_p_elu_where", "tests/problems/x_p_leaky_where", "tests/problems/x_p_mask_and",
+    "tests/problems/x_p_mask_float", "tests/problems/x_p_mask_mul", "tests/problems/x_p_mask_not",
+    "tests/problems/x_p_gelu_tanh", "tests/problems/x_p_mish", "tests/problems/x_p_sigmoid",
+    "tests/problems/x_p_tanh", "tests/problems/x_p_tanhshrink",
 ]
 
 

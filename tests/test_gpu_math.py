@@ -70,3 +70,23 @@ def test_log_error(runtime):
     got = _run("log", x).astype(np.float64)
     ref = np.log(x.astype(np.float64))
     assert np.max(np.abs(got - ref) / np.maximum(np.abs(ref), 1.0)) <= 1e-6
+
+
+@pytest.mark.gpu
+def test_tanh_error(runtime):
+    # the series below |x| = 0.55, 1 - 2 / (exp(2|x|) + 1) above: a few ulp relative
+    x = np.concatenate([np.linspace(-12, 12, 1 << 16), np.linspace(-0.6, 0.6, 1 << 14),
+                        [0.0, -0.0, 1e-30, -1e-30, 100.0, -100.0]]).astype(np.float32)
+    got = _run("tanh", x).astype(np.float64)
+    ref = np.tanh(x.astype(np.float64))
+    assert np.max(np.abs(got - ref) / np.maximum(np.abs(ref), 1e-30)) <= 6e-7
+    assert np.array_equal(np.signbit(got[x == 0]), np.signbit(x[x == 0]))
+
+
+@pytest.mark.gpu
+def test_sigmoid_error(runtime):
+    x = np.linspace(-100, 100, 1 << 16, dtype=np.float32)
+    got = _run("sigmoid", x).astype(np.float64)
+    ref = 1.0 / (1.0 + np.exp(-x.astype(np.float64)))
+    tiny = ref > 1e-30
+    assert np.max(np.abs(got[tiny] - ref[tiny]) / ref[tiny]) <= 6e-7

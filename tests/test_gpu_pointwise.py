@@ -19,6 +19,11 @@ MAP = ["x_p_odd7", "x_p_odd1001", "x_q_fp8_e4m3", "x_q_fp8_e4m3_sat", "x_q_fp8_s
        "x_d_f16_gelu", "x_d_f32_to_f16", "x_d_f16_to_f32",
        # f32 attention / causal linear attention lowered as row reductions and element maps
        "a01_attention", "x_l_linattn", "x_l_gqa", "a02_attention_128", "x_a_rect",
+       "x_a_32x16", "x_a_256x64", "x_a_batched",
+       # bool masks and where; tanh and sigmoid from this back end's own exp
+       "x_p_where", "x_p_cmp_mask", "x_p_elu_where", "x_p_leaky_where", "x_p_mask_and", "x_p_mask_float",
+       "x_p_mask_mul", "x_p_mask_not", "x_p_gelu_tanh", "x_p_mish", "x_p_sigmoid", "x_p_tanh",
+       "x_p_tanhshrink",
        # scans written as per-element serial loops
        "x_r_cumsum", "x_r_cumsum_rows", "x_l_ssm_decay"]
 

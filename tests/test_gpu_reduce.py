@@ -18,7 +18,9 @@ REDUCE = ["f01_rmsnorm", "f02_row_softmax", "f03_l2norm", "r01_array_sum", "r02_
           "x_d_f16_softmax", "x_d_f16_sum", "x_d_f16_mean", "x_d_f16_sq_mean", "x_d_f16_dot",
           "x_d_f16_dot_f32",
           # an f32 SwiGLU that emmy lowers as a row reduction over K
-          "x_l_swiglu"]
+          "x_l_swiglu",
+          # softmax of tanh-capped logits (30 tanh(x / 30))
+          "x_l_softcap"]
 
 
 # row reductions that are dot products over K (cancellation in f32 sums): no 1e-5 bar
