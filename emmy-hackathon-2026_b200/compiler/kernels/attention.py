@@ -1003,8 +1003,16 @@ def analyze_simt(spec) -> AttnConfig:
     kl = loops[0]
     kv = kl.axis.name
     inner = [x for x in kl.body if type(x).__name__ in ("Loop", "StridedLoop")]
-    if len(inner) != 1:
+    if not inner:
         raise NotImplementedError("no head-dim loop")
+    # emmy may unroll the key step (keys kv, kv + 32, ... each with its own softmax state,
+    # combined after the loop: ``x_h_attn_mask``): every replica has the same dot product,
+    # and the first one's statements are the score chain
+    sig0 = [(type(x).__name__, getattr(getattr(x, "op", None), "name", None)) for x in inner[0].body]
+    for other in inner[1:]:
+        if [(type(x).__name__, getattr(getattr(x, "op", None), "name", None)) for x in other.body] != sig0 \
+                or int(other.axis.extent.value) != int(inner[0].axis.extent.value):
+            raise NotImplementedError("unrolled key steps that differ")
     dv = inner[0].axis.name
     body_in = list(inner[0].body)
     loads_in = {x.names[0]: x for x in body_in if type(x).__name__ == "Load" and len(x.names) == 1}
@@ -1036,11 +1044,20 @@ def analyze_simt(spec) -> AttnConfig:
         raise NotImplementedError("key operand layout")
     env = _constants(spec, list(_walk(spec.body)))
     stm = list(kl.body)
-    scaled = [x for x in stm if type(x).__name__ == "Assign" and acc in x.args]
+    if len(inner) > 1:
+        stm = stm[:next(i for i, x in enumerate(stm) if x is inner[1])]
+    # the dot product may be rounded first (``f16 v4 = copy(acc0)``)
+    src = acc
+    while True:
+        cps = [x for x in stm if type(x).__name__ == "Assign" and x.op.name == "copy" and tuple(x.args) == (src,)]
+        if len(cps) != 1:
+            break
+        src = cps[0].name
+    scaled = [x for x in stm if type(x).__name__ == "Assign" and src in x.args]
     if len(scaled) != 1 or scaled[0].op.name != "multiply" or \
-            not all(a == acc or a in env for a in scaled[0].args):
+            not all(a == src or a in env for a in scaled[0].args):
         raise NotImplementedError("score is not a scaled dot product")
-    scale = math.prod(env[a] for a in scaled[0].args if a != acc)
+    scale = math.prod(env[a] for a in scaled[0].args if a != src)
     score = scaled[0].name
     loads = {x.names[0]: x for x in stm if type(x).__name__ == "Load" and len(x.names) == 1}
     mask_ld = None

@@ -59,7 +59,7 @@ class MapKernel:
                     self._buffer(s.input)
                 elif len(s.names) != 1:
                     raise NotImplementedError("element map: multi-value constant Load")
-            elif k not in ("Assign", "Let", "Init", "Accum"):
+            elif k not in ("Assign", "Let", "Init", "Accum", "Select"):
                 raise NotImplementedError(f"element map: statement {k}")
 
     def _buffer(self, name):
@@ -128,6 +128,9 @@ class MapKernel:
                 self._body_scope(ctx, s.else_body or ())
                 p.place(l_end)
                 continue
+            if k == "Select":
+                self._select(ctx, s)
+                continue
             if k != "Loop":
                 lower_body(ctx, [s])
                 continue
@@ -158,6 +161,26 @@ class MapKernel:
             self._body_scope(ctx, s.body)
             del self.axis_reg[name], self.ext[name]
             p.emit(f"add.u32 {r}, {r}, 1\nsetp.lt.u32 {pl}, {r}, {ext}\n@{pl} bra {top}")
+
+    def _select(self, ctx, s):
+        """``v = a when c1, b when c2, ..., z when True``: the first branch whose index
+        condition holds (emmy's concatenations, slices and triangular masks).  The values
+        are computed before the Select, as the reference computes them; the conditions are
+        over the element's indices and the serial loop variables."""
+        p = ctx.ptx
+        brs = list(s.branches)
+        last = brs[-1].select
+        if not (type(last).__name__ == "Literal" and bool(last.value)):
+            raise NotImplementedError("element map: Select without a final default branch")
+        out = p.reg("f32")
+        p.emit(f"mov.f32 {out}, {ctx.f32(brs[-1].value)}")
+        for br in reversed(brs[:-1]):
+            c, pc = self._index(p, br.select), p.reg("pred")
+            p.emit(f"setp.ne.s32 {pc}, {c}, 0\nselp.f32 {out}, {ctx.f32(br.value)}, {out}, {pc}")
+        if s.name in ctx.mutable and s.name in ctx.env:
+            p.emit(f"mov.f32 {ctx.env[s.name].text}, {out}")
+        else:
+            ctx.env[s.name] = Val(out, "f32")
 
     def _body_scope(self, ctx, body):
         """Lower a loop body once; its element-local names do not outlive it, the

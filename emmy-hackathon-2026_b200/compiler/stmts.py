@@ -300,7 +300,7 @@ def compute_f32(ctx: ScalarCtx, op: str, args: list[str], dst: str | None = None
 # handlers
 
 
-NARROW = ("f16", "bf16", "f8e4m3")     # result types rounded per op (values stay f32)
+NARROW = ("f16", "bf16", "f8e4m3", "f8e5m2")     # result types rounded per op (values stay f32)
 
 
 def _check_f32(dt, what: str, ctx: ScalarCtx | None = None) -> None:
@@ -320,6 +320,16 @@ def round_half(ctx: ScalarCtx, dt, reg: str) -> str:
         return reg
     p = ctx.ptx
     out = p.reg("f32")
+    if n == "f8e5m2":
+        # nearest even with torch's overflow to +-inf: the saturating convert (no other form
+        # takes f32 to e5m2), then inf from the midpoint above the largest finite (61440)
+        q, hh, lo, hi, big = p.reg("b16"), p.reg("b32"), p.reg("b16"), p.reg("b16"), p.reg("pred")
+        ax, inf = p.reg("f32"), p.reg("f32")
+        p.emit(f"cvt.rn.satfinite.e5m2x2.f32 {q}, 0f00000000, {reg}\n"
+               f"cvt.rn.f16x2.e5m2x2 {hh}, {q}\nmov.b32 {{{lo}, {hi}}}, {hh}\ncvt.f32.f16 {out}, {lo}\n"
+               f"abs.f32 {ax}, {reg}\nsetp.ge.f32 {big}, {ax}, 0f47700000\n"
+               f"copysign.f32 {inf}, {reg}, 0f7F800000\n@{big} mov.f32 {out}, {inf}")
+        return out
     if n == "f8e4m3":
         # e4m3 pair (value, 0) -> f16 pair -> the value's half -> f32; every e4m3 value is
         # exact in f16

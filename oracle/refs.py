@@ -289,6 +289,23 @@ def e4m3_round(a) -> np.ndarray:
     return (sign * out).astype(np.float32)
 
 
+def e5m2_round(a) -> np.ndarray:
+    """Round to float8 e5m2 (nearest even; 2 mantissa bits, exponents down to 2^-14 and
+    subnormals in steps of 2^-16), overflowing to +-inf past the largest finite 57344 as
+    torch's ``float8_e5m2`` cast does (tests/expressions_quant.py:18-24), returned as f32."""
+    x = np.asarray(a, dtype=np.float64)
+    sign = np.where(np.signbit(x), -1.0, 1.0)
+    m = np.abs(x)
+    out = np.zeros_like(m)
+    nz = (m > 0) & np.isfinite(m)
+    e = np.maximum(np.floor(np.log2(m[nz])), -14.0)
+    q = 2.0 ** (e - 2)
+    out[nz] = np.round(m[nz] / q) * q
+    out[~np.isfinite(m)] = m[~np.isfinite(m)]
+    out[out > 57344.0] = np.inf
+    return (sign * out).astype(np.float32)
+
+
 def mm_f32(a, b):
     """f32 matmul: the product in f64, rounded once to f32 (the reference's refs for
     ``m01_matmul_512`` / ``m02_matmul_rect``, tools/expressions_open.py:66-73, and the
@@ -430,6 +447,9 @@ PROBLEM_REFS = {
     "x_l_linattn": lambda q, k, v: [linattn(q, k, v)],
     "a02_attention_128": lambda q, kt, v: [f32(_softmax(f64(q) @ f64(kt) / 5.656854) @ f64(v))],
     "x_a_rect": lambda q, kt, v: [f32(_softmax((f64(q) @ f64(kt)) * 0.17677669) @ f64(v))],
+    # e5m2 casts (expressions_quant.py:18-24)
+    "x_q_fp8_e5m2": lambda x: [e5m2_round(x)],
+    "x_q_fp8_e5m2_inf": lambda x: [np.clip(e5m2_round(x * np.float32(40000.0)), -1e5, 1e5).astype(np.float32)],
     # bool masks / where, tanh and sigmoid (expressions_extra.py:106-184; expressions_llm.py:79-80)
     "x_l_softcap": lambda x: [f32(_softmax(30 * np.tanh(f64(x) / 30)))],
     "x_p_where": lambda x, y: [np.where(x > 0, x, y)],
@@ -453,6 +473,10 @@ PROBLEM_REFS = {
     "x_r_cumsum": lambda x: [f32(np.cumsum(f64(x)))],
     "x_r_cumsum_rows": lambda x: [f32(np.cumsum(f64(x), -1))],
     "x_l_ssm_decay": lambda a, x: [f32(np.exp(np.cumsum(-np.abs(f64(a)) * 0.1, -1)) * f64(x))],
+    # Mamba-2 style scan in matrix form, rotary embedding (expressions_llm.py:27-46, 59-61, 73-75)
+    "x_l_ssm_scan": lambda a, u: [f32(np.tril(np.exp(np.cumsum(-np.abs(f64(a)) * 0.1)[:, None]
+                                                     - np.cumsum(-np.abs(f64(a)) * 0.1)[None, :])) @ f64(u))],
+    "x_l_rope": lambda x, c, s: [f32(f64(x) * c + np.concatenate((-f64(x)[:, 32:], f64(x)[:, :32]), -1) * s)],
     # grouped-query sdpa: key / value heads repeated 4 times (expressions_llm.py:49-51, 81-84)
     "x_l_gqa": lambda q, k, v: [f32(_softmax(f64(q) @ np.swapaxes(np.repeat(f64(k), 4, 1), -1, -2)
                                              / np.sqrt(q.shape[-1])) @ np.repeat(f64(v), 4, 1))],
@@ -469,6 +493,10 @@ PROBLEM_REFS = {
                                                  causal=True)],
     "x_h_sdpa_mask": lambda q, k, v, m: [attn_f16(q, np.swapaxes(k, -1, -2), v, 1 / np.sqrt(32),
                                                   mask=m)],
+    # (expressions_extra.py:424-431)
+    "x_h_attn_mask": lambda q, kt, m, v: [attn_f16(q, kt, v, 1 / 8, mask=m)],
+    "x_h_sdpa_mask_odd": lambda q, k, v, m: [attn_f16(q, np.swapaxes(k, -1, -2), v, 1 / np.sqrt(32),
+                                                      mask=m)],
 }
 
 

@@ -96,6 +96,13 @@ FIXTURES = [
     "tests/problems/x_p_mask_float", "tests/problems/x_p_mask_mul", "tests/problems/x_p_mask_not",
     "tests/problems/x_p_gelu_tanh", "tests/problems/x_p_mish", "tests/problems/x_p_sigmoid",
     "tests/problems/x_p_tanh", "tests/problems/x_p_tanhshrink",
+    # e5m2 casts, overflowing to inf like torch's
+    "tests/problems/x_q_fp8_e5m2", "tests/problems/x_q_fp8_e5m2_inf",
+    # masked attention in emmy's unrolled SIMT form (key steps replicated, one output
+    # element per cooperative tile), on the tcgen05 attention template
+    "tests/problems/x_h_attn_mask", "tests/problems/x_h_sdpa_mask_odd",
+    # element maps with Select (rotary embedding's rotate-half; the SSM scan's triangular mask)
+    "tests/problems/x_l_rope", "tests/problems/x_l_ssm_scan",
 ]
 
 

@@ -8,7 +8,9 @@ import pytest
 
 from conftest import GOLDEN
 
-ATTN = ["x_h_sdpa", "x_h_attn", "x_h_attn_128", "x_h_attn_b", "x_h_sdpa_causal", "x_h_sdpa_mask"]
+ATTN = ["x_h_sdpa", "x_h_attn", "x_h_attn_128", "x_h_attn_b", "x_h_sdpa_causal", "x_h_sdpa_mask",
+        # emmy's unrolled SIMT masked attention (pre-transposed K; odd 100 x 120 with a mask)
+        "x_h_attn_mask", "x_h_sdpa_mask_odd"]
 
 
 @pytest.mark.gpu

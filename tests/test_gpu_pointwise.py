@@ -9,6 +9,7 @@ import pytest
 from conftest import GOLDEN
 
 MAP = ["x_p_odd7", "x_p_odd1001", "x_q_fp8_e4m3", "x_q_fp8_e4m3_sat", "x_q_fp8_scaled", "x_q_bf16_cast",
+       "x_q_fp8_e5m2", "x_q_fp8_e5m2_inf",
        "x_q_bf16_math", "x_q_f16_scalar",
        "p00_scalar_add", "p01_vector_add", "p02_scale_shift", "p03_relu_mul", "x_p_short_launch",
        "x_p_sub1000", "x_p_big", "x_p_bcast_row", "x_p_bcast_col", "x_p_3d", "x_p_3d_bcast", "x_p_odd_2d",
@@ -25,7 +26,9 @@ MAP = ["x_p_odd7", "x_p_odd1001", "x_q_fp8_e4m3", "x_q_fp8_e4m3_sat", "x_q_fp8_s
        "x_p_mask_mul", "x_p_mask_not", "x_p_gelu_tanh", "x_p_mish", "x_p_sigmoid", "x_p_tanh",
        "x_p_tanhshrink",
        # scans written as per-element serial loops
-       "x_r_cumsum", "x_r_cumsum_rows", "x_l_ssm_decay"]
+       "x_r_cumsum", "x_r_cumsum_rows", "x_l_ssm_decay",
+       # Select over index conditions: rotary embedding, the SSM scan in matrix form
+       "x_l_rope", "x_l_ssm_scan"]
 
 
 @pytest.mark.gpu
