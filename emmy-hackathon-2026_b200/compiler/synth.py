@@ -22,6 +22,7 @@ from __future__ import annotations
 
 import copy
 import json
+import os
 import re
 import tempfile
 from pathlib import Path
@@ -85,11 +86,20 @@ def rescale(src_dir: Path, dims: dict, dtypes: dict | None = None, constants: di
     return irs, meta
 
 
+def _write_atomic(path: Path, text: str) -> None:
+    """Write to a file of this process's own, then rename it over ``path``: processes
+    that write the same problem at once (one per GPU under torchrun) never read a
+    half-written file."""
+    tmp = path.with_name(f".{path.name}.{os.getpid()}.tmp")
+    tmp.write_text(text)
+    os.replace(tmp, path)
+
+
 def write_problem(irs: dict, meta: dict, out_dir: Path) -> Path:
     out_dir.mkdir(parents=True, exist_ok=True)
     for entry, ir in irs.items():
-        (out_dir / f"{entry}.ir.json").write_text(json.dumps(ir))
-    (out_dir / "meta.json").write_text(json.dumps(meta, indent=1))
+        _write_atomic(out_dir / f"{entry}.ir.json", json.dumps(ir))
+    _write_atomic(out_dir / "meta.json", json.dumps(meta, indent=1))
     return out_dir
 
 

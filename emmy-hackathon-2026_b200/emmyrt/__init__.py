@@ -306,10 +306,14 @@ def assemble(ptx: str, arch: str = "sm_100a", extra: tuple = ()) -> tuple[bytes,
         if r.returncode != 0:
             raise RuntimeError(f"ptxas rejected the module:\n{r.stderr}")
         data = out.read_bytes()
-    tmp = cub.with_suffix(".tmp")
+    # per-process temporary names and renames, the cubin last: processes assembling the
+    # same module at once (one per GPU) never read a half-written entry
+    tmp = log.with_name(f".{log.name}.{os.getpid()}.tmp")
+    tmp.write_text(r.stderr)
+    tmp.replace(log)
+    tmp = cub.with_name(f".{cub.name}.{os.getpid()}.tmp")
     tmp.write_bytes(data)
     tmp.replace(cub)
-    log.write_text(r.stderr)
     return data, r.stderr
 
 

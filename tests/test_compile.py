@@ -176,3 +176,22 @@ def test_f32_matmul_recognizer_rejects_other_kernels():
     assert taken == {"m01_matmul_512", "m02_matmul_rect", "x_m_small", "x_m_tall", "x_m_wide", "x_m_longk",
                      "x_m_256", "x_m_batched", "x_m_bias_relu", "x_m_scaled", "x_q_f16_mm_t", "x_q_bf16_mm_t",
                      "x_q_bf16_mm_odd", "x_h_mm_mixed", "x_m_odd"}
+
+
+def _synth_and_read(i):
+    import json as _json
+    from compiler.synth import baseline_dir
+    for _ in range(5):
+        d = baseline_dir("gemm_8192")
+        _json.loads((d / "meta.json").read_text())
+        for f in d.glob("*.ir.json"):
+            _json.loads(f.read_text())
+    return i
+
+
+def test_baseline_problems_written_concurrently():
+    # one process per GPU under torchrun synthesises the same BASELINE problem at once:
+    # every reader must see whole files
+    import multiprocessing as mp
+    with mp.get_context("spawn").Pool(8) as pool:
+        assert sorted(pool.map(_synth_and_read, range(8))) == list(range(8))
