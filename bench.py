@@ -51,6 +51,7 @@ WORKLOADS = {
     "gemm_4096x14336x4096": ("gemm_4096x14336x4096", "TFLOP/s", "gemm"),
     "gemm_2048": ("gemm_2048", "TFLOP/s", "gemm"),
     "gemm_512": ("gemm_512", "TFLOP/s", "gemm"),
+    "gemm_f32_4096": ("gemm_f32_4096", "TFLOP/s", "gemm"),     # f32 (3xTF32), not a BASELINE config
     "attention": ("attention", "TFLOP/s", "attention"),
     "fp8_8192": ("fp8_8192", "TFLOP/s", "fp8"),
     "rmsnorm": ("rmsnorm", "GB/s", "row"),
@@ -250,16 +251,18 @@ def cpu_sample_fn(name: str, inputs: dict, meta: dict, target_s: float = 2.0):
         return (lambda: refs.mm_fp8(sub, Bq, sa, sb)), 2.0 * rows * B.shape[0] * B.shape[1], \
             f"{rows} rows of the e4m3-valued A against the full B (oracle mm_fp8, f64 BLAS)"
     if name.startswith("gemm"):
-        A = bf16_bits_to_f32(inputs["x0"])
-        B = bf16_bits_to_f32(inputs["x1"])
+        f32_ops = inputs["x0"].dtype == np.float32
+        A = inputs["x0"] if f32_ops else bf16_bits_to_f32(inputs["x0"])
+        B = inputs["x1"] if f32_ops else bf16_bits_to_f32(inputs["x1"])
+        mm, mm_name = (refs.mm_f32, "mm_f32") if f32_ops else (refs.mm_bf16, "mm_bf16")
         rows = max(1, min(A.shape[0], 256))
         t0 = time.perf_counter()
-        refs.mm_bf16(A[:rows], B)
+        mm(A[:rows], B)
         dt = time.perf_counter() - t0
         rows = int(max(1, min(A.shape[0], rows * max(1.0, target_s / max(dt, 1e-3)))))
         sub = A[:rows]
-        return (lambda: refs.mm_bf16(sub, B)), 2.0 * rows * B.shape[0] * B.shape[1], \
-            f"{rows} rows of A against the full B (oracle mm_bf16, f64 BLAS)"
+        return (lambda: mm(sub, B)), 2.0 * rows * B.shape[0] * B.shape[1], \
+            f"{rows} rows of A against the full B (oracle {mm_name}, f64 BLAS)"
     if name == "attention":
         q, k, v = (bf16_bits_to_f32(inputs[n]) for n in ("x0", "x1", "x2"))
         S, D = q.shape[-2], q.shape[-1]
@@ -509,6 +512,10 @@ def run_ours(args, dist: Dist) -> int:
         # no measured fp8 figure: the dense e4m3 rate is twice bf16's on this part
         bound, peak = "tensor", 2.0 * float(peaks["bf16_tflops"])
         kind_txt = f"derived: 2 x {peak_kind} bf16_tflops burst"
+    elif name == "gemm_f32_4096":
+        # 3xTF32: three kind::tf32 MMAs per f32 product, tf32 at half the bf16 rate
+        bound, peak = "tensor", float(peaks["bf16_tflops"]) / 6.0
+        kind_txt = f"derived: {peak_kind} bf16_tflops burst / 2 (tf32) / 3 (MMAs per product)"
     elif unit == "TFLOP/s":
         bound, peak = "tensor", float(peaks["bf16_tflops"])
         kind_txt = f"{peak_kind} (bf16_tflops burst)"
@@ -531,7 +538,8 @@ def run_ours(args, dist: Dist) -> int:
             "metric": METRIC, "value": round(value, 2), "unit": unit, "n_gpus": dist.world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 4),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": {"gemm": "bf16", "attention": "bf16", "fp8": "e4m3"}.get(family, "f32"),
+            "dtype": "f32" if name == "gemm_f32_4096" else
+                     {"gemm": "bf16", "attention": "bf16", "fp8": "e4m3"}.get(family, "f32"),
             "data": "synthetic",
             "config": {"workload": name, "kernel": k["entry"], "grid": ck.launch["grid"],
                        "block": ck.launch["block"], "smem": ck.launch["smem"],

@@ -124,6 +124,10 @@ def baseline_problem(name: str, golden: Path = GOLDEN) -> tuple[dict, dict]:
         # x_h_mm_1024: x0 is A [M, K], x1 is B [K, N], matmul is C [M, N]
         return rescale(golden / "x_h_mm_1024", {}, dtypes={"f16": "bf16"},
                        shapes={"x0": [m, k], "x1": [k, n], "matmul": [m, n]}, problem_id=name)
+    if name == "gemm_f32_4096":
+        # not a BASELINE config: the reference's own f32 matmul (m01, emmy's SIMT FMA
+        # schedule) at 4096^3, for the 3xTF32 template's measurements
+        return rescale(golden / "m01_matmul_512", {512: 4096}, problem_id=name)
     if name == "attention":
         shp = [8, 32, 4096, 128]
         return rescale(golden / "x_h_sdpa", {}, dtypes={"f16": "bf16"},
