@@ -653,48 +653,111 @@ def _emit_softmax(p: Ptx, cfg: AttnConfig, ptr, bars, B_S, B_P, B_O, tbase, base
     # is free and O_t holds every earlier block
     waits.wait(sbar, par, "softmax", finish)
     p.emit("bar.warp.sync -1\ntcgen05.fence::after_thread_sync")
-    # the whole S row in registers: four loads in flight, one wait
-    sv = [p.reg("b32") for _ in range(128)]
-    for c in range(4):
-        p.emit(f"tcgen05.ld.sync.aligned.32x32b.x32.b32 {{{', '.join(sv[32 * c:32 * c + 32])}}}, "
-               f"[{s_ta}+{c * 32}]")
-    p.emit("tcgen05.wait::ld.sync.aligned")
+    # the whole S row in registers: four loads in flight, one wait; masked and scaled as
+    # the score chain says
     fv = [p.reg("f32") for _ in range(128)]
-    for i in range(128):
-        p.emit(f"mov.b32 {fv[i]}, {sv[i]}")
+    keyb = None
     if masked:
         keyb = p.reg("u32")
         p.emit(f"mul.lo.u32 {keyb}, {jj}, 128")
-    if cfg.mask_param is not None:
-        # scores in the log2 domain with the additive mask: s*scale*log2e + mask*log2e
-        _add_mask(p, cfg, fv, mrow, jj, scale_log2)
-    if masked:
+
+    def load_s():
+        sv = [p.reg("b32") for _ in range(128)]
+        for c in range(4):
+            p.emit(f"tcgen05.ld.sync.aligned.32x32b.x32.b32 {{{', '.join(sv[32 * c:32 * c + 32])}}}, "
+                   f"[{s_ta}+{c * 32}]")
+        p.emit("tcgen05.wait::ld.sync.aligned")
         for i in range(128):
-            pk, kx = p.reg("pred"), p.reg("u32")
-            p.emit(f"add.u32 {kx}, {keyb}, {i}\nsetp.ge.u32 {pk}, {kx}, {cfg.Sk}\n"
-                   f"@{pk} mov.f32 {fv[i]}, 0fFF800000")
-    if cfg.causal:
-        # keys past this thread's query row are out: key 128 jj + i > qrow <=> i > lim
-        lim, pneed, pany_c = p.reg("u32"), p.reg("pred"), p.reg("pred")
-        l_nocausal = p.label("s_nocausal")
-        p.emit(f"""
-            mad.lo.s32 {lim}, {jj}, -128, {qrow}
-            setp.lt.s32 {pneed}, {lim}, 127
-            vote.sync.any.pred {pany_c}, {pneed}, -1
-            @!{pany_c} bra {l_nocausal}
-        """)
-        for i in range(128):
-            pk = p.reg("pred")
-            p.emit(f"setp.lt.s32 {pk}, {lim}, {i}\n@{pk} mov.f32 {fv[i]}, 0fFF800000")
-        p.place(l_nocausal)
-    mx = _max_tree(p, fv)
+            p.emit(f"mov.b32 {fv[i]}, {sv[i]}")
+        if cfg.mask_param is not None:
+            # scores in the log2 domain with the additive mask: s*scale*log2e + mask*log2e
+            _add_mask(p, cfg, fv, mrow, jj, scale_log2)
+        if masked:
+            for i in range(128):
+                pk, kx = p.reg("pred"), p.reg("u32")
+                p.emit(f"add.u32 {kx}, {keyb}, {i}\nsetp.ge.u32 {pk}, {kx}, {cfg.Sk}\n"
+                       f"@{pk} mov.f32 {fv[i]}, 0fFF800000")
+        if cfg.causal:
+            # keys past this thread's query row are out: key 128 jj + i > qrow <=> i > lim
+            lim, pneed, pany_c = p.reg("u32"), p.reg("pred"), p.reg("pred")
+            l_nocausal = p.label("s_nocausal")
+            p.emit(f"""
+                mad.lo.s32 {lim}, {jj}, -128, {qrow}
+                setp.lt.s32 {pneed}, {lim}, 127
+                vote.sync.any.pred {pany_c}, {pneed}, -1
+                @!{pany_c} bra {l_nocausal}
+            """)
+            for i in range(128):
+                pk = p.reg("pred")
+                p.emit(f"setp.lt.s32 {pk}, {lim}, {i}\n@{pk} mov.f32 {fv[i]}, 0fFF800000")
+            p.place(l_nocausal)
+
+    # the packed P chunks and the chunks' row sums, stored / added once the row is done
+    packed = [[p.reg("b32") for _ in range(16)] for _ in range(4)]
+    psum = [p.reg("f32") for _ in range(4)]
+
+    def exps():
+        """p = 2^(s*scale*log2e - m) per 32-key chunk, its row sum and bf16/f16 pack."""
+        negm, nm2 = p.reg("f32"), p.reg("b64")
+        p.emit(f"neg.f32 {negm}, {m}\nmov.b64 {nm2}, {{{negm}, {negm}}}")
+        for c in range(4):
+            ps = []
+            for i in range(32 * c, 32 * c + 32, 2):
+                x2, e2 = p.reg("b64"), p.reg("b64")
+                ea, eb = p.reg("f32"), p.reg("f32")
+                p.emit(f"mov.b64 {x2}, {{{fv[i]}, {fv[i + 1]}}}\n"
+                       f"fma.rn.f32x2 {e2}, {x2}, {sl2}, {nm2}\nmov.b64 {{{ea}, {eb}}}, {e2}")
+                for k, e in ((i, ea), (i + 1, eb)):
+                    if cfg.poly_every and not masked and k % cfg.poly_every == cfg.poly_every - 1:
+                        emit_exp2_poly(p, e, e)     # offload part of the exponentials from MUFU
+                    else:
+                        p.emit(f"ex2.approx.ftz.f32 {e}, {e}")
+                    ps.append(e)
+            # row sum: pairwise f32x2 adds, then the two halves
+            red = []
+            for i in range(0, 32, 2):
+                r = p.reg("b64")
+                p.emit(f"mov.b64 {r}, {{{ps[i]}, {ps[i + 1]}}}")
+                red.append(r)
+            while len(red) > 1:
+                nxt = []
+                for i in range(0, len(red), 2):
+                    r = p.reg("b64")
+                    p.emit(f"add.rn.f32x2 {r}, {red[i]}, {red[i + 1]}")
+                    nxt.append(r)
+                red = nxt
+            h1 = p.reg("f32")
+            p.emit(f"mov.b64 {{{psum[c]}, {h1}}}, {red[0]}\nadd.rn.f32 {psum[c]}, {psum[c]}, {h1}")
+            for i in range(16):
+                p.emit(f"{cvt} {packed[c][i]}, {ps[2 * i + 1]}, {ps[2 * i]}")
+
+    def o_correction(alpha):
+        """O *= alpha (the whole warp, when any of its rows moved its maximum)."""
+        ov = [p.reg("b32") for _ in range(32)]
+        for c in range(DP // 32):
+            p.emit(f"tcgen05.ld.sync.aligned.32x32b.x32.b32 {{{', '.join(ov)}}}, [{o_ta}+{c * 32}]")
+            p.emit("tcgen05.wait::ld.sync.aligned")
+            for i in range(32):
+                f = p.reg("f32")
+                p.emit(f"mov.b32 {f}, {ov[i]}\nmul.rn.f32 {f}, {f}, {alpha}\nmov.b32 {ov[i]}, {f}")
+            p.emit(f"tcgen05.st.sync.aligned.32x32b.x32.b32 [{o_ta}+{c * 32}], {{{', '.join(ov)}}}")
+        p.emit("tcgen05.wait::st.sync.aligned")
+
+    def block_max(vals_max):
+        mx = p.reg("f32")
+        p.emit(f"mov.f32 {mx}, {vals_max}")
+        if cfg.mask_param is None:
+            p.emit(f"mul.rn.f32 {mx}, {mx}, {f32_hex(scale_log2)}")
+        return mx
+
+    load_s()
+    pfirst = p.reg("pred")
+    p.emit(f"setp.eq.u32 {pfirst}, {jj}, 0")
+    mx = block_max(_max_tree(p, fv))
     mn, alpha, thr = p.reg("f32"), p.reg("f32"), p.reg("f32")
-    prs, pfirst = p.reg("pred"), p.reg("pred")
-    if cfg.mask_param is None:
-        p.emit(f"mul.rn.f32 {mx}, {mx}, {f32_hex(scale_log2)}")
+    prs = p.reg("pred")
     p.emit(f"""
         max.f32 {mn}, {m}, {mx}
-        setp.eq.u32 {pfirst}, {jj}, 0
         add.rn.f32 {thr}, {m}, {f32_hex(RESCALE_LOG2)}
         setp.gt.f32 {prs}, {mn}, {thr}
         @{pfirst} mov.f32 {m}, {mn}
@@ -714,57 +777,20 @@ def _emit_softmax(p: Ptx, cfg: AttnConfig, ptr, bars, B_S, B_P, B_O, tbase, base
     pany = p.reg("pred")
     l_nores = p.label("s_nores")
     p.emit(f"vote.sync.any.pred {pany}, {prs}, -1\n@!{pany} bra {l_nores}")
-    ov = [p.reg("b32") for _ in range(32)]
-    for c in range(DP // 32):
-        p.emit(f"tcgen05.ld.sync.aligned.32x32b.x32.b32 {{{', '.join(ov)}}}, [{o_ta}+{c * 32}]")
-        p.emit("tcgen05.wait::ld.sync.aligned")
-        for i in range(32):
-            f = p.reg("f32")
-            p.emit(f"mov.b32 {f}, {ov[i]}\nmul.rn.f32 {f}, {f}, {alpha}\nmov.b32 {ov[i]}, {f}")
-        p.emit(f"tcgen05.st.sync.aligned.32x32b.x32.b32 [{o_ta}+{c * 32}], {{{', '.join(ov)}}}")
-    p.emit("tcgen05.wait::st.sync.aligned")
+    o_correction(alpha)
     p.place(l_nores)
-    # p = 2^(s*scale*log2e - m), row sum, bf16/f16 pack into the swizzled P tile
-    negm, nm2 = p.reg("f32"), p.reg("b64")
-    p.emit(f"neg.f32 {negm}, {m}\nmov.b64 {nm2}, {{{negm}, {negm}}}")
+    exps()
+    tot, t23 = p.reg("f32"), p.reg("f32")
+    p.emit(f"add.rn.f32 {tot}, {psum[0]}, {psum[1]}\nadd.rn.f32 {t23}, {psum[2]}, {psum[3]}\n"
+           f"add.rn.f32 {tot}, {tot}, {t23}\nadd.rn.f32 {l}, {l}, {tot}")
     for c in range(4):
-        ps = []
-        for i in range(32 * c, 32 * c + 32, 2):
-            x2, e2 = p.reg("b64"), p.reg("b64")
-            ea, eb = p.reg("f32"), p.reg("f32")
-            p.emit(f"mov.b64 {x2}, {{{fv[i]}, {fv[i + 1]}}}\n"
-                   f"fma.rn.f32x2 {e2}, {x2}, {sl2}, {nm2}\nmov.b64 {{{ea}, {eb}}}, {e2}")
-            for k, e in ((i, ea), (i + 1, eb)):
-                if cfg.poly_every and not masked and k % cfg.poly_every == cfg.poly_every - 1:
-                    emit_exp2_poly(p, e, e)     # offload part of the exponentials from MUFU
-                else:
-                    p.emit(f"ex2.approx.ftz.f32 {e}, {e}")
-                ps.append(e)
-        # row sum: pairwise f32x2 adds, then the two halves
-        red = []
-        for i in range(0, 32, 2):
-            r = p.reg("b64")
-            p.emit(f"mov.b64 {r}, {{{ps[i]}, {ps[i + 1]}}}")
-            red.append(r)
-        while len(red) > 1:
-            nxt = []
-            for i in range(0, len(red), 2):
-                r = p.reg("b64")
-                p.emit(f"add.rn.f32x2 {r}, {red[i]}, {red[i + 1]}")
-                nxt.append(r)
-            red = nxt
-        h0, h1 = p.reg("f32"), p.reg("f32")
-        p.emit(f"mov.b64 {{{h0}, {h1}}}, {red[0]}\nadd.rn.f32 {h0}, {h0}, {h1}\nadd.rn.f32 {l}, {l}, {h0}")
-        packed = [p.reg("b32") for _ in range(16)]
-        for i in range(16):
-            p.emit(f"{cvt} {packed[i]}, {ps[2 * i + 1]}, {ps[2 * i]}")
         if cfg.p_tmem:
-            # P chunk c (32 keys = 16 packed columns) over S columns already read
-            p.emit(f"tcgen05.st.sync.aligned.32x32b.x16.b32 [{s_ta}+{c * 16}], {{{', '.join(packed)}}}")
+            # P chunk c (32 keys = 16 packed columns) over the S columns read
+            p.emit(f"tcgen05.st.sync.aligned.32x32b.x16.b32 [{s_ta}+{c * 16}], {{{', '.join(packed[c])}}}")
         else:
             for g in range(4):
                 c16 = c * 4 + g
-                p.emit(f"st.shared.v4.b32 [{chunk_addr[c16]}], {{{', '.join(packed[4 * g:4 * g + 4])}}}")
+                p.emit(f"st.shared.v4.b32 [{chunk_addr[c16]}], {{{', '.join(packed[c][4 * g:4 * g + 4])}}}")
     if cfg.p_tmem:
         p.emit("tcgen05.wait::st.sync.aligned")
     else:
