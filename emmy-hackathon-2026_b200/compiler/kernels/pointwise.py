@@ -19,7 +19,8 @@ from ..ptx import Ptx, entry, f32_hex, module
 from ..stmts import ScalarCtx, Val, load_index_vars, lower_body, matmul_kernel
 from .common import affine_offset, arg_params, load_pointer
 
-ELEM = {"f32": 4, "f16": 2, "bf16": 2}
+ELEM = {"f32": 4, "f16": 2, "bf16": 2, "i32": 4, "i64": 8, "f64": 8}
+KIND = {"i32": "s32", "i64": "s64", "f64": "f64"}        # value kinds of the wider buffer types
 UNROLL = 8               # serial loops up to this many iterations are unrolled, longer ones loop
 CTA = 256
 
@@ -99,7 +100,8 @@ class MapKernel:
                 rem = q
             self.axis_reg[a.name] = r
         ctx = ScalarCtx(p, constants=dict(spec.constants), half_results=True,
-                        exact_products=matmul_kernel(spec.name), index_vars=load_index_vars(spec.body))
+                        exact_products=matmul_kernel(spec.name), index_vars=load_index_vars(spec.body),
+                        const_dtypes={q.name: q.dtype for q in spec.params})
         ctx.on_load = self._load
         ctx.on_write = self._write
         self.fixed = {}
@@ -172,15 +174,18 @@ class MapKernel:
         last = brs[-1].select
         if not (type(last).__name__ == "Literal" and bool(last.value)):
             raise NotImplementedError("element map: Select without a final default branch")
-        out = p.reg("f32")
-        p.emit(f"mov.f32 {out}, {ctx.f32(brs[-1].value)}")
+        kinds = {ctx.get(br.value).kind for br in brs}
+        kind = next((k for k in ("f64", "f32", "s64", "s32") if k in kinds), "f32")
+        b = "b64" if kind in ("f64", "s64") else "b32"
+        out = p.reg(kind)
+        p.emit(f"mov.{b} {out}, {ctx.as_kind(brs[-1].value, kind)}")
         for br in reversed(brs[:-1]):
             c, pc = self._index(p, br.select), p.reg("pred")
-            p.emit(f"setp.ne.s32 {pc}, {c}, 0\nselp.f32 {out}, {ctx.f32(br.value)}, {out}, {pc}")
+            p.emit(f"setp.ne.s32 {pc}, {c}, 0\nselp.{b} {out}, {ctx.as_kind(br.value, kind)}, {out}, {pc}")
         if s.name in ctx.mutable and s.name in ctx.env:
-            p.emit(f"mov.f32 {ctx.env[s.name].text}, {out}")
+            p.emit(f"mov.{b} {ctx.env[s.name].text}, {out}")
         else:
-            ctx.env[s.name] = Val(out, "f32")
+            ctx.env[s.name] = Val(out, kind)
 
     def _body_scope(self, ctx, body):
         """Lower a loop body once; its element-local names do not outlive it, the
@@ -270,8 +275,13 @@ class MapKernel:
         dt = self._buffer(s.input)
         addr = self._address(s.input, s.index)
         for k, name in enumerate(s.names):
-            r = ctx.ptx.reg("f32")
             off = k * ELEM[dt]
+            if dt in KIND:
+                r = ctx.ptx.reg(KIND[dt])
+                ctx.ptx.emit(f"ld.global.{KIND[dt]} {r}, [{addr}+{off}]")
+                ctx.env[name] = Val(r, KIND[dt])
+                continue
+            r = ctx.ptx.reg("f32")
             if dt == "f32":
                 ctx.ptx.emit(f"ld.global.f32 {r}, [{addr}+{off}]")
             else:
@@ -285,8 +295,11 @@ class MapKernel:
         dt = self._buffer(w.output)
         addr = self._address(w.output, w.index)
         for k, name in enumerate(w.values):
-            v = ctx.f32(name)
             off = k * ELEM[dt]
+            if dt in KIND:
+                ctx.ptx.emit(f"st.global.{KIND[dt]} [{addr}+{off}], {ctx.as_kind(name, KIND[dt])}")
+                continue
+            v = ctx.f32(name)
             if dt == "f32":
                 ctx.ptx.emit(f"st.global.f32 [{addr}+{off}], {v}")
             else:

@@ -25,7 +25,7 @@ import re
 from dataclasses import dataclass, field
 from typing import Callable
 
-from .ptx import Ptx, f32_hex
+from .ptx import Ptx, f32_hex, f64_hex
 
 HANDLERS: dict[str, Callable] = {}
 
@@ -81,6 +81,7 @@ class ScalarCtx:
     half_results: bool = False                       # f16 / bf16 results rounded per op (else rejected)
     exact_products: bool = False                     # a matmul kernel: 16-bit products stay exact
     index_vars: dict = field(default_factory=dict)   # loaded name -> index variables of its Load
+    const_dtypes: dict = field(default_factory=dict) # constant buffer -> IR dtype (i32 / i64 / f64 ...)
 
     def bind(self, name: str, val: Val) -> None:
         if name in self.mutable and name in self.env:
@@ -104,9 +105,39 @@ class ScalarCtx:
             r = self.ptx.reg("f32")
             self.ptx.emit(f"selp.f32 {r}, 0f3F800000, 0f00000000, {v.text}")
             return r
+        if v.kind in ("s32", "s64", "f64"):
+            return self.as_kind(name, "f32")
         if v.kind != "f32":
             raise NotImplementedError(f"{name!r} is {v.kind}, expected f32")
         return v.text
+
+    def as_kind(self, name: str, kind: str) -> str:
+        """``name``'s value as a ``kind`` register (f32 / f64 / s32 / s64): integers and
+        bools promote to floats exactly where they can (nearest otherwise), floats to
+        integers truncate toward zero (torch's ``.to(int)``), wide integers narrow by
+        dropping high bits."""
+        v, p = self.get(name), self.ptx
+        if v.kind == kind:
+            return v.text
+        r = p.reg(kind)
+        if v.kind == "pred":
+            one, zero = {"f32": ("0f3F800000", "0f00000000"), "f64": ("0d3FF0000000000000", "0d0000000000000000"),
+                         "s32": ("1", "0"), "s64": ("1", "0")}[kind]
+            p.emit(f"selp.{'b32' if kind in ('f32', 's32') else 'b64'} {r}, {one}, {zero}, {v.text}")
+            return r
+        if v.const is not None and kind in ("f32", "f64"):
+            return f32_hex(v.const) if kind == "f32" else f64_hex(v.const)
+        if v.const is not None and kind in ("s32", "s64"):
+            return str(int(v.const))
+        src = {"f32": "f32", "f64": "f64", "s32": "s32", "s64": "s64"}[v.kind]
+        if kind in ("f32", "f64"):
+            rnd = "" if (src == "f32" and kind == "f64") else ".rn"
+            p.emit(f"cvt{rnd}.{kind}.{src} {r}, {v.text}")
+        elif src in ("f32", "f64"):
+            p.emit(f"cvt.rzi.{kind}.{src} {r}, {v.text}")
+        else:
+            p.emit(f"cvt.{kind}.{src} {r}, {v.text}")
+        return r
 
     def pred(self, name: str) -> str:
         v = self.get(name)
@@ -384,6 +415,140 @@ def _contraction(ctx: ScalarCtx, args) -> bool:
     return bool(a and b and a - b and b - a)
 
 
+# f64 exp: e^x = 2^k e^r with k = rint(x / ln 2), r = x - k ln 2 (ln 2 in two parts, so r is
+# exact to f64), |r| <= ln2 / 2 and e^r by its Taylor series to r^13 (the next term is below
+# 2^-60 relative): 1/n! for n = 2 .. 13
+_EXP64_TAYLOR = (0.5, 0.16666666666666666, 0.041666666666666664, 0.008333333333333333, 0.001388888888888889, 0.0001984126984126984, 2.48015873015873e-05, 2.7557319223985893e-06, 2.755731922398589e-07, 2.505210838544172e-08, 2.08767569878681e-09, 1.6059043836821613e-10)
+# ln 2 (from its series sum 1 / (k 2^k)) split at the low 32 mantissa bits: k * _LN2_HI is
+# exact for the |k| < 1100 used here, _LN2_LO the rest to f64
+_LN2_HI = 0.6931467056274414
+_LN2_LO = 4.7493250390316726e-07
+
+
+def emit_exp_f64(p: Ptx, dst: str, x: str) -> None:
+    """e^x in f64, written here from the definition (not a library's exp).  2^k is built in
+    the exponent field; where k is outside the normal exponents (results near the overflow
+    threshold, or subnormal results) q is pre-scaled by 2 or 2^-54 and k moved back into
+    range.  Above log(DBL_MAX) the result is inf, below -745.2 it is 0, NaN stays NaN."""
+    xc, kf, r, q, sc = (p.reg("f64") for _ in range(5))
+    k64, bits = p.reg("s64"), p.reg("b64")
+    plo, phi, pnan, pbig, psmall = (p.reg("pred") for _ in range(5))
+    p.emit(f"""
+        setp.lt.f64 {plo}, {x}, {f64_hex(-745.2)}
+        setp.gt.f64 {phi}, {x}, {f64_hex(709.782712893384)}
+        setp.nan.f64 {pnan}, {x}, {x}
+        max.f64 {xc}, {x}, {f64_hex(-745.2)}
+        min.f64 {xc}, {xc}, {f64_hex(709.782712893384)}
+        mul.rn.f64 {kf}, {xc}, {f64_hex(1.4426950408889634)}
+        cvt.rni.f64.f64 {kf}, {kf}
+        neg.f64 {r}, {kf}
+        fma.rn.f64 {r}, {r}, {f64_hex(_LN2_HI)}, {xc}
+        neg.f64 {q}, {kf}
+        fma.rn.f64 {r}, {q}, {f64_hex(_LN2_LO)}, {r}
+        mov.f64 {q}, {f64_hex(_EXP64_TAYLOR[-1])}
+    """)
+    for c in reversed(_EXP64_TAYLOR[:-1]):
+        p.emit(f"fma.rn.f64 {q}, {q}, {r}, {f64_hex(c)}")
+    p.emit(f"""
+        fma.rn.f64 {q}, {q}, {r}, 0d3FF0000000000000
+        fma.rn.f64 {q}, {q}, {r}, 0d3FF0000000000000
+        cvt.rni.s64.f64 {k64}, {kf}
+        setp.gt.s64 {pbig}, {k64}, 1023
+        @{pbig} add.rn.f64 {q}, {q}, {q}
+        @{pbig} sub.s64 {k64}, {k64}, 1
+        setp.lt.s64 {psmall}, {k64}, -1022
+        @{psmall} mul.rn.f64 {q}, {q}, 0d3C90000000000000
+        @{psmall} add.s64 {k64}, {k64}, 54
+        add.s64 {k64}, {k64}, 1023
+        shl.b64 {bits}, {k64}, 52
+        mov.b64 {sc}, {bits}
+        mul.rn.f64 {dst}, {q}, {sc}
+        @{plo} mov.f64 {dst}, 0d0000000000000000
+        @{phi} mov.f64 {dst}, 0d7FF0000000000000
+        @{pnan} mov.f64 {dst}, {x}
+    """)
+
+
+_KIND = {"i32": "s32", "i64": "s64", "f64": "f64", "f32": "f32"}
+
+
+def _lower_typed(ctx: ScalarCtx, s) -> bool:
+    """Assigns whose result is i32, i64 or f64: the IR's result dtype says the type, the
+    operands promote to it (``ScalarCtx.as_kind``).  Integer ops follow torch: wrap-around
+    arithmetic, floor division and a remainder with the divisor's sign, arithmetic right
+    shift."""
+    kind = _KIND.get(dtype_name(s.dtype))
+    if kind not in ("s32", "s64", "f64"):
+        return False
+    op, p = s.op.name, ctx.ptx
+    w = kind[1:]
+    b = "b" + w
+    r = p.reg(kind)
+    if op == "where":
+        c = ctx.pred(s.args[0])
+        x, y = ctx.as_kind(s.args[1], kind), ctx.as_kind(s.args[2], kind)
+        p.emit(f"selp.{b} {r}, {x}, {y}, {c}")
+    elif op == "copy":
+        r = ctx.as_kind(s.args[0], kind)
+    elif kind == "f64":
+        args = [ctx.as_kind(x, "f64") for x in s.args]
+        binop = {"add": "add.rn.f64", "subtract": "sub.rn.f64", "multiply": "mul.rn.f64",
+                 "divide": "div.rn.f64", "maximum": "max.f64", "minimum": "min.f64"}
+        unop = {"negative": "neg.f64", "abs": "abs.f64", "sqrt": "sqrt.rn.f64", "reciprocal": "rcp.rn.f64"}
+        if op in binop and len(args) == 2:
+            p.emit(f"{binop[op]} {r}, {args[0]}, {args[1]}")
+        elif op in unop and len(args) == 1:
+            p.emit(f"{unop[op]} {r}, {args[0]}")
+        elif op == "exp" and len(args) == 1:
+            emit_exp_f64(p, r, args[0])
+        else:
+            raise NotImplementedError(f"elementwise op {op} (f64)")
+    else:
+        args = [ctx.as_kind(x, kind) for x in s.args]
+        t = kind                       # s32 / s64
+        if op in ("add", "subtract") and len(args) == 2:
+            p.emit(f"{'add' if op == 'add' else 'sub'}.{t} {r}, {args[0]}, {args[1]}")
+        elif op == "multiply" and len(args) == 2:
+            p.emit(f"mul.lo.{t} {r}, {args[0]}, {args[1]}")
+        elif op in ("maximum", "minimum") and len(args) == 2:
+            p.emit(f"{'max' if op == 'maximum' else 'min'}.{t} {r}, {args[0]}, {args[1]}")
+        elif op in ("bitwise_and", "bitwise_or", "bitwise_xor") and len(args) == 2:
+            p.emit(f"{op.split('_')[1]}.{b} {r}, {args[0]}, {args[1]}")
+        elif op == "bitwise_not" and len(args) == 1:
+            p.emit(f"not.{b} {r}, {args[0]}")
+        elif op == "negative" and len(args) == 1:
+            p.emit(f"neg.{t} {r}, {args[0]}")
+        elif op == "abs" and len(args) == 1:
+            p.emit(f"abs.{t} {r}, {args[0]}")
+        elif op in ("right_shift", "bitwise_right_shift", "left_shift", "bitwise_left_shift") and len(args) == 2:
+            n = ctx.as_kind(s.args[1], "s32") if kind == "s64" else args[1]
+            ins = f"shr.{t}" if "right" in op else f"shl.{b}"
+            p.emit(f"{ins} {r}, {args[0]}, {n}")
+        elif op in ("floor_divide", "remainder") and len(args) == 2:
+            # C's truncating quotient / remainder, then moved toward -inf when the signs differ
+            q, m, x, pn, pz = p.reg(kind), p.reg(kind), p.reg(kind), p.reg("pred"), p.reg("pred")
+            p.emit(f"""
+                div.{t} {q}, {args[0]}, {args[1]}
+                rem.{t} {m}, {args[0]}, {args[1]}
+                xor.{b} {x}, {m}, {args[1]}
+                setp.lt.{t} {pn}, {x}, 0
+                setp.ne.{t} {pz}, {m}, 0
+                and.pred {pn}, {pn}, {pz}
+            """)
+            if op == "floor_divide":
+                p.emit(f"mov.{b} {r}, {q}\n@{pn} sub.{t} {r}, {q}, 1")
+            else:
+                p.emit(f"mov.{b} {r}, {m}\n@{pn} add.{t} {r}, {m}, {args[1]}")
+        else:
+            raise NotImplementedError(f"elementwise op {op} ({dtype_name(s.dtype)})")
+    target = ctx.env[s.name].text if (s.name in ctx.mutable and s.name in ctx.env) else None
+    if target is not None:
+        p.emit(f"mov.{b} {target}, {r}")
+    else:
+        ctx.env[s.name] = Val(r, kind)
+    return True
+
+
 # comparisons as ordered PTX compares (false with a NaN operand, as torch's), except
 # not_equal (true with a NaN)
 _CMP_OPS = {"greater": "gt", "greater_equal": "ge", "less": "lt", "less_equal": "le",
@@ -396,9 +561,15 @@ def _lower_bool(ctx: ScalarCtx, s) -> bool:
     """Comparisons, logic on bools and ``where``: the bool values live in predicates."""
     op, p = s.op.name, ctx.ptx
     if op in _CMP_OPS:
-        a, b = (ctx.f32(x) for x in s.args)
+        # compared in the operands' common type (torch's promotion)
+        kinds = {ctx.get(x).kind for x in s.args}
+        kind = next((k for k in ("f64", "f32", "s64", "s32") if k in kinds), "f32")
+        a, b = (ctx.as_kind(x, kind) for x in s.args)
+        cmp = _CMP_OPS[op]
+        if kind in ("s32", "s64") and cmp == "neu":
+            cmp = "ne"
         r = p.reg("pred")
-        p.emit(f"setp.{_CMP_OPS[op]}.f32 {r}, {a}, {b}")
+        p.emit(f"setp.{cmp}.{kind} {r}, {a}, {b}")
         ctx.env[s.name] = Val(r, "pred")
         return True
     if op in _BOOL_OPS and all(ctx.get(x).kind == "pred" for x in s.args):
@@ -434,7 +605,7 @@ def _lower_bool(ctx: ScalarCtx, s) -> bool:
 
 @handles("Assign")
 def lower_assign(ctx: ScalarCtx, s) -> None:
-    if _lower_bool(ctx, s):
+    if _lower_bool(ctx, s) or _lower_typed(ctx, s):
         return
     _check_f32(s.dtype, "Assign", ctx)
     target = ctx.env[s.name].text if (s.name in ctx.mutable and s.name in ctx.env) else None
@@ -489,8 +660,15 @@ def lower_load(ctx: ScalarCtx, s) -> None:
     if all(n in ctx.env for n in s.names):
         return   # bound by the template (vector lane or cached value)
     if len(s.names) == 1 and s.input in ctx.constants:
-        _check_f32(s.dtype, "constant Load", ctx)
+        cdt = ctx.const_dtypes.get(s.input)
         v = float(ctx.constants[s.input])
+        if cdt in ("i32", "i64"):
+            ctx.env[s.names[0]] = Val(str(int(v)), "s32" if cdt == "i32" else "s64", v)
+            return
+        if cdt == "f64":
+            ctx.env[s.names[0]] = Val(f64_hex(v), "f64", v)
+            return
+        _check_f32(s.dtype, "constant Load", ctx)
         ctx.env[s.names[0]] = Val(f32_hex(v), "f32", v)
         return
     if ctx.on_load is None:

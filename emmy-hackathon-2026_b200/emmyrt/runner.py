@@ -64,8 +64,12 @@ def host_array(dtype: str, values) -> np.ndarray:
 
 
 def as_f32(dtype: str, a: np.ndarray) -> np.ndarray:
+    """A downloaded buffer as floats for comparison: f32, except f64 and i64 buffers,
+    which keep their precision as f64."""
     if dtype == "bf16":
         return bf16_bits_to_f32(a)
+    if dtype in ("f64", "i64"):
+        return a.astype(np.float64)
     return a.astype(np.float32)
 
 

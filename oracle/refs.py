@@ -34,6 +34,8 @@ def seeded(seed: int, shape, dtype="f32") -> np.ndarray:
         return a.astype(np.float16)
     if dtype == "f64":
         return a
+    if dtype in ("i32", "i64"):            # truncated toward zero, as numpy's astype
+        return a.astype(np.int32 if dtype == "i32" else np.int64)
     return a.astype(np.float32)
 
 
@@ -447,6 +449,25 @@ PROBLEM_REFS = {
     "x_l_linattn": lambda q, k, v: [linattn(q, k, v)],
     "a02_attention_128": lambda q, kt, v: [f32(_softmax(f64(q) @ f64(kt) / 5.656854) @ f64(v))],
     "x_a_rect": lambda q, kt, v: [f32(_softmax((f64(q) @ f64(kt)) * 0.17677669) @ f64(v))],
+    # integer and f64 element maps (expressions_extra.py:323-368; expressions_quant.py:25-26)
+    "x_d_f64_add": lambda a, b: [a + b],
+    "x_d_f64_div": lambda a, b: [a * b / (np.abs(b) + 1)],
+    "x_d_f64_exp": lambda x: [np.exp(x)],
+    "x_d_i32_add": lambda a, b: [a + b],
+    "x_d_i64_mul_add": lambda a, b: [a * b + b],
+    "x_d_i32_floordiv": lambda a, b: [a // (np.abs(b) + 1)],
+    "x_d_i32_rem": lambda a, b: [a % (np.abs(b) + 1)],
+    "x_d_i32_floordiv_c": lambda a: [a // 2],
+    "x_d_i32_bitwise": lambda a, b: [(a & b) ^ (a | b)],
+    "x_d_i32_rshift": lambda a: [a >> 1],
+    "x_d_i32_cmp": lambda a, b: [f32(a > b)],
+    "x_d_i32_where": lambda a: [np.where(a > 0, a, -a)],
+    "x_d_i32_abs_sub": lambda a: [np.abs(a) - 1],
+    "x_d_i32_mixed": lambda a, b: [f32(a) * np.float32(0.5) + b],
+    "x_d_f32_to_i32": lambda x: [(x * np.float32(10)).astype(np.int32)],
+    "x_d_i32_to_f32": lambda a: [f32(a) / np.float32(3)],
+    "x_d_i64_cumsum": lambda x: [np.cumsum(x, -1)],
+    "x_q_int4_unpack": lambda x: [(((x >> 4) & 15) - 8).astype(np.float32) * np.float32(0.1)],
     # e5m2 casts (expressions_quant.py:18-24)
     "x_q_fp8_e5m2": lambda x: [e5m2_round(x)],
     "x_q_fp8_e5m2_inf": lambda x: [np.clip(e5m2_round(x * np.float32(40000.0)), -1e5, 1e5).astype(np.float32)],

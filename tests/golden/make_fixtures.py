@@ -103,6 +103,13 @@ FIXTURES = [
     "tests/problems/x_h_attn_mask", "tests/problems/x_h_sdpa_mask_odd",
     # element maps with Select (rotary embedding's rotate-half; the SSM scan's triangular mask)
     "tests/problems/x_l_rope", "tests/problems/x_l_ssm_scan",
+    # integer (i32 / i64) and f64 element maps: torch's promotions, floor division, remainder,
+    # shifts, bit operations, casts; f64 exp written here
+    "tests/problems/x_d_f32_to_i32", "tests/problems/x_d_f64_add", "tests/problems/x_d_f64_div", "tests/problems/x_d_f64_exp",
+    "tests/problems/x_d_i32_abs_sub", "tests/problems/x_d_i32_add", "tests/problems/x_d_i32_bitwise", "tests/problems/x_d_i32_cmp",
+    "tests/problems/x_d_i32_floordiv", "tests/problems/x_d_i32_floordiv_c", "tests/problems/x_d_i32_mixed", "tests/problems/x_d_i32_rem",
+    "tests/problems/x_d_i32_rshift", "tests/problems/x_d_i32_to_f32", "tests/problems/x_d_i32_where", "tests/problems/x_d_i64_cumsum",
+    "tests/problems/x_d_i64_mul_add", "tests/problems/x_q_int4_unpack",
 ]
 
 

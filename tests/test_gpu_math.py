@@ -90,3 +90,46 @@ def test_sigmoid_error(runtime):
     ref = 1.0 / (1.0 + np.exp(-x.astype(np.float64)))
     tiny = ref > 1e-30
     assert np.max(np.abs(got[tiny] - ref[tiny]) / ref[tiny]) <= 6e-7
+
+
+F64 = "DataType(name='f64', np=dtype('float64'), nbytes=8)"
+
+
+def _run_f64_exp(x: np.ndarray) -> np.ndarray:
+    import emmyrt
+    from compiler.ir import parse_stmt
+    from compiler.loader import KernelSpec, Param
+    from emmyrt import DeviceBuffer
+    from emmyrt.runner import CompiledKernel
+    n = x.size
+    body = parse_stmt(
+        f"Tile(axes=(Axis(name='a0', extent=Dim({n}), window=None),), body=("
+        f"Load(names=('in0',), input='x', index=(Var(name='a0'),), dtype={F64}), "
+        f"Assign(name='v0', op=ElementwiseImpl('exp'), args=('in0',), dtype={F64}), "
+        f"Write(output='y', index=(Var(name='a0'),), values=('v0',), value_dtype={F64}, atomic=False, "
+        f"swizzle='NONE')), block_threads=256, aux_threads=0, raster_axes=None, raster_group=None, "
+        f"raster_orient='m')")
+    params = (Param("x", "f64", (n,)), Param("y", "f64", (n,)))
+    ck = CompiledKernel.from_spec(KernelSpec("k_exp_f64_sweep", (body,), params, None, None, {},
+                                             buffers={p.name: p for p in params}))
+    dx, dy = DeviceBuffer(x.nbytes), DeviceBuffer(x.nbytes)
+    dx.upload(x)
+    ck({"x": dx.ptr, "y": dy.ptr})
+    emmyrt.stream_wait(0, 60)
+    y = np.zeros_like(x)
+    dy.download(y)
+    return y
+
+
+@pytest.mark.gpu
+def test_exp_f64_error(runtime):
+    # Cody-Waite reduction with ln 2 in two parts and the Taylor series to r^13: a few ulp
+    x = np.concatenate([np.linspace(-708, 709.78, 1 << 16), np.linspace(-1, 1, 1 << 14)])
+    got = _run_f64_exp(x)
+    ref = np.exp(x)
+    assert np.max(np.abs(got - ref) / ref) <= 8 * 2.0 ** -53
+    # subnormal results, the overflow threshold, the limits and NaN
+    edge = np.array([-720.0, -740.0, 709.782, -800.0, 800.0, 0.0, np.nan])
+    g = _run_f64_exp(edge)
+    assert np.allclose(g[:3], np.exp(edge[:3]), rtol=1e-12, atol=2e-323)   # (subnormal spacing 5e-324)
+    assert np.array_equal(g[3:6], [0.0, np.inf, 1.0]) and np.isnan(g[6])
