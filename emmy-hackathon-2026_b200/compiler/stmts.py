@@ -249,6 +249,87 @@ def emit_sigmoid(p: Ptx, dst: str, x: str) -> None:
     p.emit(f"add.rn.f32 {n}, {n}, 0f3F800000\nrcp.rn.f32 {dst}, {n}")
 
 
+# pi / 2 (from Machin's formula pi = 16 atan(1/5) - 4 atan(1/239)) in three parts; the first
+# two keep 12 mantissa bits, so k * part is exact for |k| < 2^11 (|x| below ~3200)
+_PIO2 = (1.570556640625, 0.0002396702766418457, 1.5893254712295857e-08)
+_TWO_OVER_PI = 0.6366197723675814
+# Taylor coefficients: sin r = r + r (r^2 S1 + r^4 S2 + ...), cos r = 1 + r^2 C1 + r^4 C2 + ...
+_SIN_C = (-0.16666666666666666, 0.008333333333333333, -0.0001984126984126984, 2.7557319223985893e-06, -2.505210838544172e-08)          # (-1)^k / (2k+1)!, k = 1..5
+_COS_C = (-0.5, 0.041666666666666664, -0.001388888888888889, 2.48015873015873e-05, -2.755731922398589e-07, 2.08767569878681e-09)          # (-1)^k / (2k)!,   k = 1..6
+
+
+def emit_sincos(p: Ptx, dst: str, x: str, cos: bool) -> None:
+    """sin x / cos x written here from the definitions: x = k pi/2 + r with |r| <= pi/4
+    (Cody-Waite, pi/2 in three parts), then the Taylor series of sin r or cos r (to r^11 /
+    r^12, truncation below 2e-9) picked and signed by the quadrant k mod 4 (cos x =
+    sin(x + pi/2): the quadrant of k + 1)."""
+    kf, r, r2, sp, cp, res = (p.reg("f32") for _ in range(6))
+    k = p.reg("s32")
+    p1, p2, p3 = p.reg("pred"), p.reg("pred"), p.reg("pred")
+    q, qb = p.reg("b32"), p.reg("b32")
+    p.emit(f"""
+        mul.rn.f32 {kf}, {x}, {f32_hex(_TWO_OVER_PI)}
+        cvt.rni.f32.f32 {kf}, {kf}
+        cvt.rni.s32.f32 {k}, {kf}
+        neg.f32 {r}, {kf}
+        fma.rn.f32 {r}, {r}, {f32_hex(_PIO2[0])}, {x}
+        neg.f32 {res}, {kf}
+        fma.rn.f32 {r}, {res}, {f32_hex(_PIO2[1])}, {r}
+        fma.rn.f32 {r}, {res}, {f32_hex(_PIO2[2])}, {r}
+        mul.rn.f32 {r2}, {r}, {r}
+        mov.f32 {sp}, {f32_hex(_SIN_C[-1])}
+    """)
+    for c in reversed(_SIN_C[:-1]):
+        p.emit(f"fma.rn.f32 {sp}, {sp}, {r2}, {f32_hex(c)}")
+    p.emit(f"mul.rn.f32 {sp}, {sp}, {r2}\nfma.rn.f32 {sp}, {sp}, {r}, {r}\nmov.f32 {cp}, {f32_hex(_COS_C[-1])}")
+    for c in reversed(_COS_C[:-1]):
+        p.emit(f"fma.rn.f32 {cp}, {cp}, {r2}, {f32_hex(c)}")
+    p.emit(f"""
+        fma.rn.f32 {cp}, {cp}, {r2}, 0f3F800000
+        add.s32 {q}, {k}, {1 if cos else 0}
+        and.b32 {q}, {q}, 3
+        and.b32 {qb}, {q}, 1
+        setp.ne.b32 {p1}, {qb}, 0
+        selp.f32 {res}, {cp}, {sp}, {p1}
+        and.b32 {q}, {q}, 2
+        setp.ne.b32 {p2}, {q}, 0
+        neg.f32 {dst}, {res}
+        selp.f32 {dst}, {dst}, {res}, {p2}
+        setp.nan.f32 {p3}, {x}, {x}
+        @{p3} mov.f32 {dst}, {x}
+    """)
+
+
+def emit_pow(p: Ptx, dst: str, x: str, y: str) -> None:
+    """x^y = 2^(y log2 |x|) on the MUFU units (error ~ |y log2 x| * 2^-22 relative), with
+    torch's special cases: x^0 = 1 and 1^y = 1, a negative x only with an integral y
+    (negative for an odd one), NaN otherwise."""
+    ax, l, e, yi, hy, hi = (p.reg("f32") for _ in range(6))
+    pint, podd, pneg, pz, p1, pnan = (p.reg("pred") for _ in range(6))
+    p.emit(f"""
+        abs.f32 {ax}, {x}
+        lg2.approx.f32 {l}, {ax}
+        mul.rn.f32 {l}, {l}, {y}
+        ex2.approx.f32 {e}, {l}
+        cvt.rzi.f32.f32 {yi}, {y}
+        setp.eq.f32 {pint}, {yi}, {y}
+        mul.rn.f32 {hy}, {y}, 0f3F000000
+        cvt.rzi.f32.f32 {hi}, {hy}
+        setp.ne.and.f32 {podd}, {hi}, {hy}, {pint}
+        setp.lt.f32 {pneg}, {x}, 0f00000000
+        mov.f32 {dst}, {e}
+        and.pred {podd}, {podd}, {pneg}
+        @{podd} neg.f32 {dst}, {e}
+        not.pred {pnan}, {pint}
+        and.pred {pnan}, {pnan}, {pneg}
+        @{pnan} mov.f32 {dst}, 0f7FFFFFFF
+        setp.eq.f32 {pz}, {y}, 0f00000000
+        setp.eq.f32 {p1}, {x}, 0f3F800000
+        or.pred {pz}, {pz}, {p1}
+        @{pz} mov.f32 {dst}, 0f3F800000
+    """)
+
+
 def _unary(p: Ptx, op: str, dst: str, a: str) -> None:
     if op == "copy":
         p.emit(f"mov.f32 {dst}, {a}")
@@ -275,6 +356,8 @@ def _unary(p: Ptx, op: str, dst: str, a: str) -> None:
         emit_erf(p, dst, a)
     elif op == "tanh":
         emit_tanh(p, dst, a)
+    elif op in ("sin", "cos"):
+        emit_sincos(p, dst, a, op == "cos")
     elif op == "sigmoid":
         emit_sigmoid(p, dst, a)
     elif op == "log":
@@ -299,6 +382,8 @@ def _binary(p: Ptx, op: str, dst: str, a: str, b: str) -> None:
         p.emit(f"max.f32 {dst}, {a}, {b}")
     elif op == "minimum":
         p.emit(f"min.f32 {dst}, {a}, {b}")
+    elif op == "pow":
+        emit_pow(p, dst, a, b)
     else:
         raise NotImplementedError(f"elementwise op {op} (f32, binary)")
 
@@ -318,6 +403,32 @@ def compute_f32(ctx: ScalarCtx, op: str, args: list[str], dst: str | None = None
                 return Val(r, "f32")
         emit_exp_nonpos(p, out, vals[0])
         return Val(out, "f32")
+    if op == "pow" and len(args) == 2 and ctx.get(args[1]).const is not None:
+        n = float(ctx.get(args[1]).const)
+        if n.is_integer() and 1 <= abs(n) <= 16:
+            # x^n by repeated squaring, 1 / x^|n| for a negative n (a few ulp)
+            k, base, acc = int(abs(n)), vals[0], None
+            while k:
+                if k & 1:
+                    if acc is None:
+                        acc = base
+                    else:
+                        t = p.reg("f32")
+                        p.emit(f"mul.rn.f32 {t}, {acc}, {base}")
+                        acc = t
+                k >>= 1
+                if k:
+                    t = p.reg("f32")
+                    p.emit(f"mul.rn.f32 {t}, {base}, {base}")
+                    base = t
+            if n < 0:
+                p.emit(f"rcp.rn.f32 {out}, {acc}")
+            else:
+                p.emit(f"mov.f32 {out}, {acc}")
+            return Val(out, "f32")
+        if n == 0.5:
+            p.emit(f"sqrt.rn.f32 {out}, {vals[0]}")
+            return Val(out, "f32")
     if len(vals) == 1:
         _unary(p, op, out, vals[0])
     elif len(vals) == 2:

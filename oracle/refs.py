@@ -468,6 +468,12 @@ PROBLEM_REFS = {
     "x_d_i32_to_f32": lambda a: [f32(a) / np.float32(3)],
     "x_d_i64_cumsum": lambda x: [np.cumsum(x, -1)],
     "x_q_int4_unpack": lambda x: [(((x >> 4) & 15) - 8).astype(np.float32) * np.float32(0.1)],
+    # pow and sin / cos (expressions_extra.py:136-172)
+    "x_p_pow3": lambda x: [f32(f64(x) ** 3)],
+    "x_p_pow_frac": lambda x: [f32(np.abs(f64(x)) ** 0.7)],
+    "x_p_pow_tensor": lambda a, b: [f32(f64(np.abs(a) + np.float32(0.5)) ** f64(b))],
+    "x_p_neg_pow": lambda x: [f32(f64(np.abs(x) + np.float32(0.5)) ** -2)],
+    "x_p_sin_cos": lambda x: [f32(np.sin(f64(x)) + np.cos(f64(x)))],
     # e5m2 casts (expressions_quant.py:18-24)
     "x_q_fp8_e5m2": lambda x: [e5m2_round(x)],
     "x_q_fp8_e5m2_inf": lambda x: [np.clip(e5m2_round(x * np.float32(40000.0)), -1e5, 1e5).astype(np.float32)],

@@ -103,6 +103,9 @@ FIXTURES = [
     "tests/problems/x_h_attn_mask", "tests/problems/x_h_sdpa_mask_odd",
     # element maps with Select (rotary embedding's rotate-half; the SSM scan's triangular mask)
     "tests/problems/x_l_rope", "tests/problems/x_l_ssm_scan",
+    # pow (constant integer exponents as products) and sin / cos written here
+    "tests/problems/x_p_pow3", "tests/problems/x_p_pow_frac", "tests/problems/x_p_pow_tensor",
+    "tests/problems/x_p_neg_pow", "tests/problems/x_p_sin_cos",
     # integer (i32 / i64) and f64 element maps: torch's promotions, floor division, remainder,
     # shifts, bit operations, casts; f64 exp written here
     "tests/problems/x_d_f32_to_i32", "tests/problems/x_d_f64_add", "tests/problems/x_d_f64_div", "tests/problems/x_d_f64_exp",

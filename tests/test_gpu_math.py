@@ -133,3 +133,14 @@ def test_exp_f64_error(runtime):
     g = _run_f64_exp(edge)
     assert np.allclose(g[:3], np.exp(edge[:3]), rtol=1e-12, atol=2e-323)   # (subnormal spacing 5e-324)
     assert np.array_equal(g[3:6], [0.0, np.inf, 1.0]) and np.isnan(g[6])
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("op,fn", [("sin", np.sin), ("cos", np.cos)])
+def test_sin_cos_error(runtime, op, fn):
+    # Cody-Waite by pi/2 and the Taylor series on |r| <= pi/4: a few ulp of 1 (absolute)
+    x = np.concatenate([np.linspace(-100, 100, 1 << 16), np.linspace(-4, 4, 1 << 14),
+                        [0.0, np.pi / 2, np.pi, 3000.0]]).astype(np.float32)
+    got = _run(op, x).astype(np.float64)
+    ref = fn(x.astype(np.float64))
+    assert np.max(np.abs(got - ref)) <= 4e-7

@@ -29,6 +29,8 @@ MAP = ["x_p_odd7", "x_p_odd1001", "x_q_fp8_e4m3", "x_q_fp8_e4m3_sat", "x_q_fp8_s
        "x_r_cumsum", "x_r_cumsum_rows", "x_l_ssm_decay",
        # Select over index conditions: rotary embedding, the SSM scan in matrix form
        "x_l_rope", "x_l_ssm_scan",
+       # pow and sin / cos
+       "x_p_pow3", "x_p_pow_frac", "x_p_pow_tensor", "x_p_neg_pow", "x_p_sin_cos",
        # integer and f64 element maps
        "x_d_f32_to_i32", "x_d_f64_add", "x_d_f64_div", "x_d_f64_exp", "x_d_i32_abs_sub",
        "x_d_i32_add", "x_d_i32_bitwise", "x_d_i32_cmp", "x_d_i32_floordiv", "x_d_i32_floordiv_c",
