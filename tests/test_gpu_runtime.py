@@ -67,3 +67,57 @@ def test_stream_wait_event_orders_streams(runtime):
     out = np.zeros_like(src)
     d2.download(out)
     assert np.array_equal(out, src)
+
+
+def _stuck_wait_kernel():
+    """One thread waits on an mbarrier that nothing arrives on, through the templates' own
+    bounded wait (2 s of %globaltimer): the wait gives up, records its role's status bit,
+    raises the CTA's abort flag and the kernel returns -- no trap, no fault, no endless
+    spin.  Bit 0x100 would mean the wait returned as if the barrier had completed."""
+    from compiler.kernels.tc import Waits
+    from compiler.ptx import Ptx, entry, module
+    from emmyrt.runner import CompiledKernel
+    p = Ptx()
+    st, bar, ab, tid, pz = p.reg("b64"), p.reg("u32"), p.reg("u32"), p.reg("u32"), p.reg("pred")
+    done = p.label("done")
+    p.emit(f"""
+        ld.param.u64 {st}, [param__status]
+        cvta.to.global.u64 {st}, {st}
+        mov.u32 {bar}, gbar
+        mov.u32 {ab}, gabort
+        mov.u32 {tid}, %tid.x
+        setp.ne.u32 {pz}, {tid}, 0
+        @{pz} bra {done}
+        mbarrier.init.shared::cta.b64 [{bar}], 1
+        st.shared.u32 [{ab}], 0
+        fence.mbarrier_init.release.cluster
+    """)
+    Waits(p, st, ab).wait(bar, "0", "mma", done)
+    p.emit(f"red.global.or.b32 [{st}], 256")
+    p.place(done)
+    p.emit("ret")
+    text = entry("k_stuck_wait", [".param .u64 param__status"], p, maxntid=32)
+    text = text.replace("{\n", "{\n\t.shared .align 8 .b64 gbar;\n\t.shared .align 4 .u32 gabort;\n", 1)
+    launch = {"kind": "probe", "grid": [1, 1, 1], "block": [32, 1, 1], "cluster": [1, 1, 1], "smem": 0,
+              "extra_params": [{"kind": "status"}]}
+    return CompiledKernel.from_module(module([text], launch), "k_stuck_wait", [])
+
+
+@pytest.mark.gpu
+def test_bounded_wait_reports_and_returns(runtime):
+    # failure detection without a GPU fault: a wait that can never complete ends on its
+    # own limit, the host reads the status, and the context keeps working
+    import time
+    import emmyrt
+    from compiler.kernels.tc import STATUS, TIMEOUT_NS
+    ck = _stuck_wait_kernel()
+    t0 = time.perf_counter()
+    ck({}, 0)
+    emmyrt.stream_wait(0, 30)
+    dt = time.perf_counter() - t0
+    assert ck.status() == STATUS["mma"]
+    assert TIMEOUT_NS * 1e-9 * 0.9 <= dt < 30
+    rk, bufs, out = _rmsnorm_kernel()
+    rk({n: b.ptr for n, b in bufs.items()}, 0)
+    emmyrt.stream_wait(0, 30)
+    assert rk.status() == 0
