@@ -72,7 +72,10 @@ class Dist:
         self.pg = None
         if self.world > 1:
             import torch.distributed as td
-            td.init_process_group("gloo", timeout=timedelta(seconds=180))
+            # a rank that dies ends the others' next collective with an error within this
+            # limit instead of a hang
+            limit = float(os.environ.get("EMMY_PG_TIMEOUT_S", 180))
+            td.init_process_group("gloo", timeout=timedelta(seconds=limit))
             self.pg = td
 
     def barrier(self):
