@@ -44,6 +44,10 @@ def select(spec) -> str:
         if gcfg is not None:
             return emit_gemm_module(gcfg)
         from .reduce import emit_reduction
+        if any(q.dtype in ("i32", "i64", "f64") for q in spec.params):
+            # integer / f64 buffers: one thread per output, the reduction serial
+            from .pointwise import emit_map, serialize_cooperative
+            return emit_map(serialize_cooperative(spec))
         return emit_reduction(spec)
     # emmy's SIMT f32 matmuls (FMA over cp.async-staged tiles) run on the tensor cores
     # as 3xTF32

@@ -39,7 +39,7 @@ from .tc import Waits, instr_desc, smem_desc_hi, smem_desc_lo_const
 SMS = 148
 GEMM_THREADS = 192       # warp 0 TMA, warp 1 MMA, warps 2-5 epilogue
 CONV_THREADS = 128       # warps 6-9 with 3xTF32 operands: the hi/lo split
-ELEM_BYTES = {"bf16": 2, "f16": 2, "e4m3": 1, "f32": 4}
+ELEM_BYTES = {"bf16": 2, "f16": 2, "e4m3": 1, "f32": 4, "f64": 8}
 AB_FORMAT = {"f16": 0, "bf16": 1, "e4m3": 0, "e5m2": 1, "f32": 2}   # f32 operands are read as tf32
 
 
@@ -530,6 +530,8 @@ def emit_gemm_module(cfg: GemmConfig) -> str:
 def _tf32_round(p: Ptx, x: str, mode: str) -> str:
     """x rounded to bf16 / f16 (nearest even, as the IR's cast), as an f32 bit pattern: a
     value a tf32 operand holds exactly, so the MMA's products are the 16-bit products."""
+    if mode not in ("bf16", "f16"):
+        raise NotImplementedError(f"operand rounding to {mode}")
     h, r = p.reg("b16"), p.reg("b32")
     if mode == "bf16":
         z = p.reg("b16")
@@ -758,7 +760,11 @@ def _emit_direct_loader(p: Ptx, cfg: GemmConfig, ptr: dict, tid, ring, bars, emp
     def load(dtype, adr, off, pred):
         v = p.reg("b32")
         p.emit(f"mov.b32 {v}, 0")
-        if dtype == "f32":
+        if dtype == "f64":        # an f64 operand whose products the IR takes in f32
+            d = p.reg("f64")
+            p.emit(f"mov.f64 {d}, 0d0000000000000000\n@{pred} ld.global.f64 {d}, [{adr}+{off}]\n"
+                   f"cvt.rn.f32.f64 {v}, {d}")
+        elif dtype == "f32":
             p.emit(f"@{pred} ld.global.b32 {v}, [{adr}+{off}]")
         else:
             h = p.reg("b16")
@@ -987,6 +993,13 @@ def _emit_epilogue(p: Ptx, cfg: GemmConfig, ptr: dict, bars, tfull0, tempty0, tb
                 for sl in range(1, cfg.zero_slots + 1):
                     p.emit(f"@{pg} st.global.v4.f32 [{cadr}+{(sl * cfg.slot_stride + col0 + 4 * g) * 4}], "
                            f"{{{zf}, {zf}, {zf}, {zf}}}")
+        elif cfg.c == "f64":
+            if cfg.zero_slots:
+                raise NotImplementedError("split-K partial slices other than f32")
+            for i in range(32):
+                pg, colr, d = p.reg("pred"), p.reg("u32"), p.reg("f64")
+                p.emit(f"add.u32 {colr}, {n0}, {col0 + i}\nsetp.lt.u32 {pg}, {colr}, {N}\n"
+                       f"cvt.f64.f32 {d}, {vals[i]}\n@{pg} st.global.f64 [{cadr}+{(col0 + i) * 8}], {d}")
         else:
             for i in range(32):
                 pg, colr = p.reg("pred"), p.reg("u32")
@@ -1458,9 +1471,12 @@ def analyze_f32(spec) -> GemmConfig:
     else:
         raise NotImplementedError("operand roles not identifiable")
     A, B = spec.param(aname), spec.param(bname)
-    if A.dtype not in ("f32", "f16", "bf16") or B.dtype not in ("f32", "f16", "bf16") or C.dtype != "f32":
+    if A.dtype not in ("f32", "f16", "bf16", "f64") or B.dtype not in ("f32", "f16", "bf16", "f64") or \
+            C.dtype not in ("f32", "f64"):
         raise NotImplementedError(f"SIMT matmul {A.dtype} x {B.dtype} -> {C.dtype}")
-    if cast is None and A.dtype == B.dtype and A.dtype != "f32":
+    if "f64" in (A.dtype, B.dtype) and any(getattr(a.dtype, "name", None) != "f32" for a in accs):
+        raise NotImplementedError("f64 products accumulated in f64")
+    if cast is None and A.dtype == B.dtype and A.dtype in ("f16", "bf16"):
         cast = A.dtype          # 16-bit operands: exact in tf32, one MMA
     if ak != len(A.shape) - 1:
         raise NotImplementedError("A operand is not K-major")
@@ -1512,7 +1528,7 @@ def analyze_f32(spec) -> GemmConfig:
         lam = SimpleNamespace(params=tuple(lam_seeds), body=tuple(chain), results=(first.values[0],))
         epi = (("lambda", lam, tuple(operands), tuple(sorted(spec.constants.items()))),)
     od = tuple((q.name, q.dtype) for q in spec.params)
-    return GemmConfig(M=M, N=N, K=K, batch=batch, ab="f32", c="f32", b_kmajor=b_kmajor,
+    return GemmConfig(M=M, N=N, K=K, batch=batch, ab="f32", c=C.dtype, b_kmajor=b_kmajor,
                       **choose_tiling_f32(M, N, batch, split3=cast is None), epilogue=epi, name=spec.name,
                       a_param=aname, b_param=bname, c_param=cname, arg_params=arg_params(spec),
                       buffers=tuple(q.name for q in spec.params), operand_dtypes=od,

@@ -15,7 +15,7 @@ from __future__ import annotations
 
 import math
 
-from ..ptx import Ptx, entry, f32_hex, module
+from ..ptx import Ptx, entry, f32_hex, f64_hex, module
 from ..stmts import ScalarCtx, Val, load_index_vars, lower_body, matmul_kernel
 from .common import affine_offset, arg_params, load_pointer
 
@@ -141,13 +141,15 @@ class MapKernel:
             if s.seed:
                 for st in s.body:
                     if type(st).__name__ == "Accum":
+                        kind = KIND.get(getattr(st.dtype, "name", None), "f32")
                         if st.name in ctx.env and st.name in ctx.mutable:
                             r = ctx.env[st.name].text
                         else:
-                            r = p.reg("f32")
-                            ctx.env[st.name] = Val(r, "f32")
+                            r = p.reg(kind)
+                            ctx.env[st.name] = Val(r, kind)
                             ctx.mutable.add(st.name)
-                        p.emit(f"mov.f32 {r}, {f32_hex(float(st.op.identity))}")
+                        p.emit(f"mov.{'b64' if kind in ('s64', 'f64') else 'b32'} {r}, "
+                               f"{_identity(kind, float(st.op.identity))}")
             ext, name = int(s.axis.extent.value), s.axis.name
             if ext <= UNROLL:
                 for v in range(ext):
@@ -305,6 +307,94 @@ class MapKernel:
             else:
                 h = ctx.ptx.reg("b16")
                 ctx.ptx.emit(f"cvt.rn.{dt}.f32 {h}, {v}\nst.global.b16 [{addr}+{off}], {h}")
+
+
+def _identity(kind: str, v: float) -> str:
+    """An accumulator's starting value in its register kind (the IR's f32 identities:
+    0, 1, -1e30 for max, +1e30 for min; integers clamp them to their range)."""
+    if kind == "f64":
+        return f64_hex(v)
+    if kind in ("s32", "s64"):
+        lo, hi = (-(1 << 31), (1 << 31) - 1) if kind == "s32" else (-(1 << 63), (1 << 63) - 1)
+        return str(int(min(max(v, lo), hi)))
+    return f32_hex(v)
+
+
+def serialize_cooperative(spec):
+    """One thread per output instead of a cooperative tile: emmy's warp- and CTA-wide
+    reductions (``Tile[.., a_co]`` with ``for a in a_co..N:W`` strided loops, a
+    WarpShuffle / TreeHalve combine through shared memory and the result written by lane
+    ``a_co == 0``) become serial loops over the whole axis, the combine statements go and
+    the write guard opens.  Only the simple form is taken (every strided loop starts at
+    the cooperative variable and steps by its width; nothing else reads it).  Used for
+    the buffer types the streaming reduction template does not read (i32 / i64 / f64),
+    whose kernels are small."""
+    from dataclasses import replace
+    from ..ir import IR_CLASSES
+    from ..stmts import expr_vars
+    if len(spec.body) != 1 or type(spec.body[0]).__name__ != "Tile":
+        raise NotImplementedError("not a single-tile kernel")
+    tile = spec.body[0]
+    co = [a for a in tile.axes if a.name.endswith("_co")]
+    if len(co) != 1:
+        raise NotImplementedError("not one cooperative axis")
+    cname, width = co[0].name, int(co[0].extent.value)
+
+    def mentions(obj) -> bool:
+        if type(obj).__name__ == "Var":
+            return obj.name == cname
+        if isinstance(obj, (tuple, list)):
+            return any(mentions(x) for x in obj)
+        if hasattr(obj, "__dataclass_fields__"):
+            return any(mentions(getattr(obj, f)) for f in obj.__dataclass_fields__)
+        return False
+
+    def writes_global(stmts) -> bool:
+        for x in stmts:
+            if type(x).__name__ == "Write" and x.output in spec.buffers:
+                return True
+            for attr in ("body", "else_body"):
+                sub = getattr(x, attr, None)
+                if isinstance(sub, tuple) and writes_global(sub):
+                    return True
+        return False
+
+    def conv(stmts) -> tuple:
+        out = []
+        for x in stmts:
+            k = type(x).__name__
+            if k in ("WarpShuffle", "TreeHalve", "Sync", "Smem"):
+                continue
+            if k == "Cond":
+                cv = expr_vars(x.cond)
+                if cv <= {"lane", "warp"} and not writes_global(x.body) and not writes_global(x.else_body or ()):
+                    continue            # the shared-memory leg of the combine
+                c = x.cond
+                if type(c).__name__ == "BinaryExpr" and c.op == "==" and cv == {cname} and \
+                        type(c.right).__name__ == "Literal" and int(c.right.value) == 0 and not x.else_body:
+                    out.extend(conv(x.body))
+                    continue
+                if mentions(x.cond):
+                    raise NotImplementedError("a condition on the cooperative lane")
+                out.append(replace(x, body=conv(x.body), else_body=conv(x.else_body or ())))
+                continue
+            if k == "StridedLoop":
+                st, sp = x.start, x.step
+                if not (type(st).__name__ == "Var" and st.name == cname and type(sp).__name__ == "Literal"
+                        and int(sp.value) == width) or mentions(x.body):
+                    raise NotImplementedError("a strided loop other than the cooperative stride")
+                out.append(IR_CLASSES["Loop"](axis=x.axis, body=conv(x.body), unroll=False, seed=x.seed))
+                continue
+            if k == "Loop":
+                out.append(replace(x, body=conv(x.body)))
+                continue
+            if mentions(x):
+                raise NotImplementedError(f"{k} reads the cooperative lane")
+            out.append(x)
+        return tuple(out)
+
+    new_tile = replace(tile, axes=tuple(a for a in tile.axes if a.name != cname), body=conv(tile.body))
+    return replace(spec, body=(new_tile,))
 
 
 def emit_map(spec) -> str:

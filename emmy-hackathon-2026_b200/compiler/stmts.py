@@ -757,9 +757,19 @@ def lower_accum(ctx: ScalarCtx, s) -> None:
     """``acc = op(base or acc, value)`` into the accumulator's own register
     (the reference: ``compiler/stmts.py:441-467``).  The template seeds the
     accumulator register with the op's identity before the loop."""
-    _check_f32(s.dtype, "Accum", ctx)
     acc = ctx.get(s.name)
     left = s.base or s.name
+    if acc.kind in ("s32", "s64", "f64"):
+        # an accumulator of the IR's integer / f64 type (its register kind set when seeded)
+        a, b = ctx.as_kind(left, acc.kind), ctx.as_kind(s.value, acc.kind)
+        t, op = acc.kind, s.op.name
+        ins = {"add": f"add.{t}" if t != "f64" else "add.rn.f64", "maximum": f"max.{t}",
+               "minimum": f"min.{t}", "multiply": f"mul.lo.{t}" if t != "f64" else "mul.rn.f64"}.get(op)
+        if ins is None:
+            raise NotImplementedError(f"accumulation {op} ({t})")
+        ctx.ptx.emit(f"{ins} {acc.text}, {a}, {b}")
+        return
+    _check_f32(s.dtype, "Accum", ctx)
     a, b = ctx.f32(left), ctx.f32(s.value)
     _binary(ctx.ptx, s.op.name, acc.text, a, b)
     if dtype_name(s.dtype) in NARROW:

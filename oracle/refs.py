@@ -451,6 +451,12 @@ PROBLEM_REFS = {
     "x_a_rect": lambda q, kt, v: [f32(_softmax((f64(q) @ f64(kt)) * 0.17677669) @ f64(v))],
     # integer and f64 element maps (expressions_extra.py:323-368; expressions_quant.py:25-26)
     "x_d_f64_add": lambda a, b: [a + b],
+    "x_d_f64_mm": lambda a, b: [a @ b],
+    "x_d_f64_sum": lambda x: [x.sum()],
+    "x_d_f64_softmax": lambda x: [_softmax(x)],
+    "x_d_i32_max": lambda x: [x.max(-1)],
+    "x_d_i64_max": lambda x: [x.max(-1)],
+    "x_d_i32_sum": lambda x: [x.astype(np.int64).sum()],
     "x_d_f64_div": lambda a, b: [a * b / (np.abs(b) + 1)],
     "x_d_f64_exp": lambda x: [np.exp(x)],
     "x_d_i32_add": lambda a, b: [a + b],

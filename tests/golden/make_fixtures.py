@@ -87,6 +87,8 @@ FIXTURES = [
     # warps load the tiles themselves
     "tests/problems/x_q_bf16_mm_odd", "tests/problems/x_h_mm_odd", "tests/problems/x_h_mm_odd2",
     "tests/problems/x_h_mm_mixed", "tests/problems/x_m_odd",
+    # f64 buffers, products taken in f32 as the IR says (f32 rounding of each operand, 3xTF32)
+    "tests/problems/x_d_f64_mm",
     # emmy's register-tiled f32 attention with bounds guards (element maps with Cond)
     "tests/problems/x_a_32x16", "tests/problems/x_a_256x64", "tests/problems/x_a_batched",
     # bool masks / where, tanh (this back end's own, from its series and exp), sigmoid; the
@@ -106,6 +108,9 @@ FIXTURES = [
     # pow (constant integer exponents as products) and sin / cos written here
     "tests/problems/x_p_pow3", "tests/problems/x_p_pow_frac", "tests/problems/x_p_pow_tensor",
     "tests/problems/x_p_neg_pow", "tests/problems/x_p_sin_cos",
+    # integer / f64 reductions: emmy's cooperative form run one thread per output
+    "tests/problems/x_d_f64_sum", "tests/problems/x_d_f64_softmax", "tests/problems/x_d_i32_max",
+    "tests/problems/x_d_i64_max", "tests/problems/x_d_i32_sum",
     # integer (i32 / i64) and f64 element maps: torch's promotions, floor division, remainder,
     # shifts, bit operations, casts; f64 exp written here
     "tests/problems/x_d_f32_to_i32", "tests/problems/x_d_f64_add", "tests/problems/x_d_f64_div", "tests/problems/x_d_f64_exp",

@@ -175,7 +175,7 @@ def test_f32_matmul_recognizer_rejects_other_kernels():
     # writing split-K partial slices
     assert taken == {"m01_matmul_512", "m02_matmul_rect", "x_m_small", "x_m_tall", "x_m_wide", "x_m_longk",
                      "x_m_256", "x_m_batched", "x_m_bias_relu", "x_m_scaled", "x_q_f16_mm_t", "x_q_bf16_mm_t",
-                     "x_q_bf16_mm_odd", "x_h_mm_mixed", "x_m_odd"}
+                     "x_q_bf16_mm_odd", "x_h_mm_mixed", "x_m_odd", "x_d_f64_mm"}
 
 
 def _synth_and_read(i):

@@ -14,7 +14,9 @@ F32_MM = ["m01_matmul_512", "m02_matmul_rect", "x_m_small", "x_m_tall", "x_m_wid
           # f32 operands cast to bf16 / f16: one exact tf32 MMA of the rounded values
           "x_q_bf16_mm", "x_q_bf16_mm_t", "x_q_f16_mm_t",
           # rows not 16-byte aligned, 16-bit and mixed operands: loaded by the converter warps
-          "x_q_bf16_mm_odd", "x_h_mm_odd", "x_h_mm_odd2", "x_h_mm_mixed", "x_m_odd"]
+          "x_q_bf16_mm_odd", "x_h_mm_odd", "x_h_mm_odd2", "x_h_mm_mixed", "x_m_odd",
+          # f64 buffers whose products the IR takes in f32
+          "x_d_f64_mm"]
 
 
 @pytest.mark.gpu

@@ -31,6 +31,8 @@ MAP = ["x_p_odd7", "x_p_odd1001", "x_q_fp8_e4m3", "x_q_fp8_e4m3_sat", "x_q_fp8_s
        "x_l_rope", "x_l_ssm_scan",
        # pow and sin / cos
        "x_p_pow3", "x_p_pow_frac", "x_p_pow_tensor", "x_p_neg_pow", "x_p_sin_cos",
+       # integer / f64 reductions, serialised per output
+       "x_d_f64_sum", "x_d_f64_softmax", "x_d_i32_max", "x_d_i64_max", "x_d_i32_sum",
        # integer and f64 element maps
        "x_d_f32_to_i32", "x_d_f64_add", "x_d_f64_div", "x_d_f64_exp", "x_d_i32_abs_sub",
        "x_d_i32_add", "x_d_i32_bitwise", "x_d_i32_cmp", "x_d_i32_floordiv", "x_d_i32_floordiv_c",
