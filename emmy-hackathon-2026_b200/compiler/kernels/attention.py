@@ -1139,5 +1139,86 @@ def analyze_simt(spec) -> AttnConfig:
                       arg_params=arg_params(spec), buffers=tuple(x.name for x in spec.params), **extra)
 
 
+_DT_REPR = {"f32": "DataType(name='f32', np=dtype('float32'), nbytes=4)",
+            "f16": "DataType(name='f16', np=dtype('float16'), nbytes=2)",
+            "bf16": "DataType(name='bf16', np=dtype('uint16'), nbytes=2)"}
+
+
+def score_input_spec(spec):
+    """``softmax(S) @ V`` with the scores an input buffer (``tests/problems/x_h_softmax_mm``:
+    emmy's tensor-core form reads each score fragment from global memory,
+    ``FragmentApply(_s += s[__frow, __fcol])``, and has only the P V MMA).  Returned as an
+    element-map kernel over (row, column) of O with the same arithmetic: the row maximum,
+    the f32 sum of exp(s - max), P rounded to the operands' 16-bit type times V summed in
+    f32 (the MMA's exact products), and O = acc * (1 / l) rounded on the store."""
+    from dataclasses import replace
+    from ..ir import parse_stmt
+    stmts = list(_walk(spec.body))
+    gm = [x for x in stmts if type(x).__name__ == "FragmentApply" and "gmem" in (x.kinds or ())]
+    if not gm or not any(type(x).__name__ == "FragmentRowReduce" for x in stmts):
+        raise NotImplementedError("no score fragment read from memory")
+    srcs = {x.args[list(x.kinds).index("gmem")][0] for x in gm}
+    if len(srcs) != 1 or any(x.op.name != "add" or x.args[0] != x.out for x in gm):
+        raise NotImplementedError("scores other than one input buffer")
+    sname = next(iter(srcs))
+    staged = {x.smem: x.src for x in stmts if type(x).__name__ == "CpAsyncCopy"}
+    bsrc = {staged.get(x.src_buffer, x.src_buffer) for x in stmts
+            if type(x).__name__ == "LdmatrixLoad" and x.role == "b"}
+    stores = {x.dst_buffer for x in stmts if type(x).__name__ == "RegStore"}
+    # the score fragments see nothing but the input, the softmax and (odd sizes) the mask of
+    # the tile's padding past the last key, where(__fcol >= Sk, -1e30, s)
+    S = spec.param(sname)
+    tail = [x for x in stmts if type(x).__name__ == "FragmentApply" and x.op.name == "where"]
+    for x in tail:
+        c = x.args[0]
+        if not (type(c).__name__ == "BinaryExpr" and c.op == ">=" and getattr(c.left, "name", None) == "__fcol"
+                and type(c.right).__name__ == "Literal" and int(c.right.value) == S.shape[-1]):
+            raise NotImplementedError("a score mask other than the padding past the last key")
+    ops = {x.op.name for x in stmts if type(x).__name__ == "FragmentApply" and "gmem" not in (x.kinds or ())
+           and x.op.name != "where"}
+    if len(bsrc) != 1 or len(stores) != 1 or not ops <= {"subtract", "exp", "multiply"}:
+        raise NotImplementedError("not softmax(S) @ V")
+    V, O = spec.param(next(iter(bsrc))), spec.param(next(iter(stores)))
+    if len(S.shape) != 2 or len(V.shape) != 2 or tuple(O.shape) != (S.shape[0], V.shape[1]) or \
+            V.shape[0] != S.shape[1] or V.dtype not in ("f16", "bf16") or O.dtype not in ("f16", "bf16"):
+        raise NotImplementedError("softmax(S) @ V shapes / types")
+    Sq, Sk, D = S.shape[0], S.shape[1], V.shape[1]
+    f32, pdt, odt = _DT_REPR["f32"], _DT_REPR[V.dtype], _DT_REPR[O.dtype]
+
+    def loop(k, body):
+        return (f"Loop(axis=Axis(name='{k}', extent=Dim({Sk}), window=None), body=({body}), "
+                f"unroll=False, seed=True)")
+    ld_s = "Load(names=('{n}',), input='" + sname + "', index=(Var(name='i'), Var(name='{k}')), dtype=None)"
+    body = ", ".join([
+        loop("k0", ld_s.format(n="s0", k="k0") + ", "
+             f"Accum(name='m', value='s0', op=ElementwiseImpl('maximum'), dtype={f32}, axes=('k0',), base=None)"),
+        loop("k1", ld_s.format(n="s1", k="k1") + ", "
+             f"Assign(name='d1', op=ElementwiseImpl('subtract'), args=('s1', 'm'), dtype={f32}), "
+             f"Assign(name='e1', op=ElementwiseImpl('exp'), args=('d1',), dtype={f32}), "
+             f"Accum(name='l', value='e1', op=ElementwiseImpl('add'), dtype={f32}, axes=('k1',), base=None)"),
+        loop("k2", ld_s.format(n="s2", k="k2") + ", "
+             f"Assign(name='d2', op=ElementwiseImpl('subtract'), args=('s2', 'm'), dtype={f32}), "
+             f"Assign(name='e2', op=ElementwiseImpl('exp'), args=('d2',), dtype={f32}), "
+             f"Assign(name='p2', op=ElementwiseImpl('copy'), args=('e2',), dtype={pdt}), "
+             f"Load(names=('v2',), input='{V.name}', index=(Var(name='k2'), Var(name='c')), dtype=None), "
+             f"Assign(name='t2', op=ElementwiseImpl('multiply'), args=('p2', 'v2'), dtype={f32}), "
+             f"Accum(name='acc', value='t2', op=ElementwiseImpl('add'), dtype={f32}, axes=('k2',), base=None)"),
+        f"Assign(name='rl', op=ElementwiseImpl('reciprocal'), args=('l',), dtype={f32})",
+        f"Assign(name='r', op=ElementwiseImpl('multiply'), args=('acc', 'rl'), dtype={f32})",
+        f"Write(output='{O.name}', index=(Var(name='i'), Var(name='c')), values=('r',), value_dtype={odt}, "
+        f"atomic=False, swizzle='NONE')",
+    ])
+    tile = parse_stmt(f"Tile(axes=(Axis(name='i', extent=Dim({Sq}), window=None), "
+                      f"Axis(name='c', extent=Dim({D}), window=None)), body=({body},), block_threads=256, "
+                      f"aux_threads=0, raster_axes=None, raster_group=None, raster_orient='m')")
+    return replace(spec, body=(tile,))
+
+
 def emit_attention(spec) -> str:
-    return emit_attention_module(analyze(spec))
+    try:
+        cfg = analyze(spec)
+    except NotImplementedError:
+        # softmax(S) @ V over an input S: an element map of the same arithmetic
+        from .pointwise import emit_map
+        return emit_map(score_input_spec(spec))
+    return emit_attention_module(cfg)

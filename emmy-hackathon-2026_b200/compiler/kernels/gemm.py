@@ -1106,9 +1106,12 @@ def analyze(spec) -> GemmConfig:
     stores = [s for s in stmts if type(s).__name__ == "RegStore"]
     if not stores or len({s.dst_buffer for s in stores}) != 1:
         raise NotImplementedError("matmul without a single RegStore output")
-    if any(s.atomic for s in stores):
-        raise NotImplementedError("split-K partial matmul (atomic RegStore)")
     cname = stores[0].dst_buffer
+    # emmy's split-K with atomic partial sums into the zeroed C (``x_h_attn_odd``): the whole
+    # K in one pass gives the same sum
+    atomic = any(s.atomic for s in stores)
+    if atomic and cname not in spec.zero_outputs:
+        raise NotImplementedError("split-K partial matmul (atomic RegStore) into a C that is not zeroed")
     # emmy's split-K schedule: a `*_ks` tile axis gives each CTA one K slice and the
     # partial products go to slice ks of an f32 [S, ..., M, N] buffer that a second
     # kernel sums; here the whole K runs in one pass into slice 0, the others are zeroed
@@ -1186,7 +1189,7 @@ def analyze(spec) -> GemmConfig:
         raise NotImplementedError("operand shapes do not form a matmul")
     split = {}
     cdims = C.shape
-    if ks is not None:
+    if ks is not None and not atomic:
         S = int(ks.extent.value)
         kloop = next(x for x in stmts if type(x).__name__ in ("Loop", "StridedLoop") and x.axis.name == kvar)
         first = stores[0].dst_index[0] if stores[0].dst_index else None
@@ -1201,6 +1204,8 @@ def analyze(spec) -> GemmConfig:
     eb = 4 if f32_cast else 2
     aligned = not ((K * eb) % 16 or (not b_kmajor and (N * eb) % 16))
     epi = _epilogue_ops(spec, stores[0])
+    if atomic and epi:
+        raise NotImplementedError("an epilogue on atomic partial sums")
     if f32_cast or not aligned:
         # the tf32 template: f32 operands rounded as the IR casts them, or 16-bit operands
         # (exact in tf32) fetched by the converter warps where TMA cannot address the rows

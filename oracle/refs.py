@@ -528,6 +528,10 @@ PROBLEM_REFS = {
                                                   mask=m)],
     # (expressions_extra.py:424-431)
     "x_h_attn_mask": lambda q, kt, m, v: [attn_f16(q, kt, v, 1 / 8, mask=m)],
+    "x_h_attn_odd": lambda q, kt, v: [attn_f16(q, kt, v, 1 / 6)],
+    # softmax of input scores @ V (expressions_extra.py:434-439)
+    "x_h_softmax_mm": lambda s, v: [f16(f64(f16(_softmax(f64(s)))) @ f64(v))],
+    "x_h_softmax_mm_odd": lambda s, v: [f16(f64(f16(_softmax(f64(s)))) @ f64(v))],
     "x_h_sdpa_mask_odd": lambda q, k, v, m: [attn_f16(q, np.swapaxes(k, -1, -2), v, 1 / np.sqrt(32),
                                                       mask=m)],
 }

@@ -103,6 +103,11 @@ FIXTURES = [
     # masked attention in emmy's unrolled SIMT form (key steps replicated, one output
     # element per cooperative tile), on the tcgen05 attention template
     "tests/problems/x_h_attn_mask", "tests/problems/x_h_sdpa_mask_odd",
+    # odd attention split in two kernels: Q K^T (split-K atomics into a zeroed buffer, one
+    # pass here on the tf32 template) and emmy's serial online softmax @ V (element map)
+    "tests/problems/x_h_attn_odd",
+    # softmax of input scores @ V (no Q K^T): an element map of the same arithmetic
+    "tests/problems/x_h_softmax_mm", "tests/problems/x_h_softmax_mm_odd",
     # element maps with Select (rotary embedding's rotate-half; the SSM scan's triangular mask)
     "tests/problems/x_l_rope", "tests/problems/x_l_ssm_scan",
     # pow (constant integer exponents as products) and sin / cos written here

@@ -10,7 +10,9 @@ from conftest import GOLDEN
 
 ATTN = ["x_h_sdpa", "x_h_attn", "x_h_attn_128", "x_h_attn_b", "x_h_sdpa_causal", "x_h_sdpa_mask",
         # emmy's unrolled SIMT masked attention (pre-transposed K; odd 100 x 120 with a mask)
-        "x_h_attn_mask", "x_h_sdpa_mask_odd"]
+        "x_h_attn_mask", "x_h_sdpa_mask_odd",
+        # Q K^T and softmax @ V as two kernels (50 x 70 keys); softmax of input scores @ V
+        "x_h_attn_odd", "x_h_softmax_mm", "x_h_softmax_mm_odd"]
 
 
 @pytest.mark.gpu
