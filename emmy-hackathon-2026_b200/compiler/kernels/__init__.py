@@ -23,7 +23,19 @@ def select(spec) -> str:
             from .attention import emit_attention
             return emit_attention(spec)
         from .gemm import emit_gemm
-        return emit_gemm(spec)
+        try:
+            return emit_gemm(spec)
+        except NotImplementedError as err:
+            # two contractions in one kernel (a shared-A pair, or a chain through an A
+            # tile computed in the kernel): an element map of the same arithmetic
+            from .fused import chained_gemm_spec, dual_gemm_spec
+            from .pointwise import emit_map
+            for synth in (dual_gemm_spec, chained_gemm_spec):
+                try:
+                    return emit_map(synth(spec))
+                except NotImplementedError:
+                    continue
+            raise err
     if _has(body, {"WarpShuffle"}):
         # emmy's SIMT form of attention (an online softmax over streamed keys) runs on the
         # tensor-core attention template; every other cooperative reduction on the

@@ -1106,6 +1106,8 @@ def analyze(spec) -> GemmConfig:
     stores = [s for s in stmts if type(s).__name__ == "RegStore"]
     if not stores or len({s.dst_buffer for s in stores}) != 1:
         raise NotImplementedError("matmul without a single RegStore output")
+    if any(getattr(s, "extra_frags", None) for s in stores):
+        raise NotImplementedError("a store combining several accumulators (two matmuls)")
     cname = stores[0].dst_buffer
     # emmy's split-K with atomic partial sums into the zeroed C (``x_h_attn_odd``): the whole
     # K in one pass gives the same sum

@@ -529,6 +529,10 @@ PROBLEM_REFS = {
     # (expressions_extra.py:424-431)
     "x_h_attn_mask": lambda q, kt, m, v: [attn_f16(q, kt, v, 1 / 8, mask=m)],
     "x_h_attn_odd": lambda q, kt, v: [attn_f16(q, kt, v, 1 / 6)],
+    # two contractions in one kernel (expressions_extra.py:396-400; expressions_llm.py:23-24, 69-72)
+    "x_h_mlp": lambda x, w1, w2: [mm_f16(np.maximum(mm_f16(x, w1), f16(0)), w2)],
+    "x_l_swiglu_h": lambda x, w1, w3: [f16((lambda h: h / (1 + np.exp(-h)))(f64(f16(f64(x) @ f64(w1))))
+                                           * f64(f16(f64(x) @ f64(w3))))],
     # softmax of input scores @ V (expressions_extra.py:434-439)
     "x_h_softmax_mm": lambda s, v: [f16(f64(f16(_softmax(f64(s)))) @ f64(v))],
     "x_h_softmax_mm_odd": lambda s, v: [f16(f64(f16(_softmax(f64(s)))) @ f64(v))],

@@ -108,6 +108,8 @@ FIXTURES = [
     "tests/problems/x_h_attn_odd",
     # softmax of input scores @ V (no Q K^T): an element map of the same arithmetic
     "tests/problems/x_h_softmax_mm", "tests/problems/x_h_softmax_mm_odd",
+    # two contractions in one kernel: relu(x W1) W2 and silu(x W1) * (x W3)
+    "tests/problems/x_h_mlp", "tests/problems/x_l_swiglu_h",
     # element maps with Select (rotary embedding's rotate-half; the SSM scan's triangular mask)
     "tests/problems/x_l_rope", "tests/problems/x_l_ssm_scan",
     # pow (constant integer exponents as products) and sin / cos written here

@@ -10,7 +10,9 @@ from conftest import GOLDEN
 GEMM = ["x_h_mm_1024", "x_h_mm_256", "x_h_mm_relu", "x_h_mm_residual", "x_h_mm_t_n8", "x_h_mm_t_odd",
         "x_h_mm_rect", "x_h_bmm", "x_h_mm_bias", "x_h_linear_bias_gelu",
         "x_h_mm_16", "x_h_mm_64", "x_h_mm_128", "x_h_mm_t", "x_h_mm_vec", "x_q_f16_mm_t",
-        "x_h_bmm_t", "x_h_linear"]
+        "x_h_bmm_t", "x_h_linear",
+        # two contractions in one kernel (element maps of the same arithmetic)
+        "x_h_mlp", "x_l_swiglu_h"]
 
 
 @pytest.mark.gpu
