@@ -528,6 +528,13 @@ def run_ours(args, dist: Dist) -> int:
     roofline = {"bound": bound, "achieved": round(achieved, 2), "peak": peak,
                 "peak_kind": kind_txt,
                 "unit": unit, "frac": round(achieved / peak, 4), "traffic": traffic_from_profile(name)}
+    if bound == "tensor" and "bf16_tflops_sustained" in peaks:
+        # the same measured GEMM run seconds-long under the power cap: the denominator for a
+        # timed region long enough to settle at the cap (sw_power_cap in "clocks")
+        scale = peak / float(peaks["bf16_tflops"])
+        ps = float(peaks["bf16_tflops_sustained"]) * scale
+        roofline["peak_sustained"] = round(ps, 2)
+        roofline["frac_sustained"] = round(achieved / ps, 4)
 
     cpu = None
     if dist.rank == 0 and dist.world == 1 and not args.no_cpu:
