@@ -75,13 +75,17 @@ class MapKernel:
         p = Ptx()
         p.comment(f"element map: {self.n} elements over {[a.name for a in self.axes]}")
         self.ptrs = {q.name: load_pointer(p, q.name) for q in spec.params if not q.scalar}
+        # small maps (emmy's register tiles of a few hundred threads, long serial loops in
+        # each) spread over every SM in CTAs of down to one warp; large ones 256 per CTA
+        cta = CTA if self.n >= CTA * 148 else max(32, -(-self.n // (148 * 32)) * 32)
+        self.cta = cta
         i, step = p.reg("u32"), p.reg("u32")
         p.emit(f"""
             mov.u32 {i}, %ctaid.x
             mov.u32 {step}, %tid.x
-            mad.lo.u32 {i}, {i}, {CTA}, {step}
+            mad.lo.u32 {i}, {i}, {cta}, {step}
             mov.u32 {step}, %nctaid.x
-            mul.lo.u32 {step}, {step}, {CTA}
+            mul.lo.u32 {step}, {step}, {cta}
         """)
         top, done = p.label("elem"), p.label("elem_done")
         p.place(top)
@@ -109,10 +113,10 @@ class MapKernel:
         p.emit(f"add.u32 {i}, {i}, {step}\nbra {top}")
         p.place(done)
         p.emit("ret")
-        blocks = max(1, min(-(-self.n // CTA), 148 * 8))
-        launch = {"kind": "map", "grid": [blocks, 1, 1], "block": [CTA, 1, 1], "cluster": [1, 1, 1],
+        blocks = max(1, min(-(-self.n // cta), 148 * 8))
+        launch = {"kind": "map", "grid": [blocks, 1, 1], "block": [cta, 1, 1], "cluster": [1, 1, 1],
                   "smem": 0, "extra_params": []}
-        return module([entry(spec.name, arg_params(spec), p, maxntid=CTA)], launch)
+        return module([entry(spec.name, arg_params(spec), p, maxntid=cta)], launch)
 
     def _lower(self, ctx, body):
         p = ctx.ptx
@@ -157,14 +161,30 @@ class MapKernel:
                     self._body_scope(ctx, s.body)
                 del self.fixed[name]
                 continue
+            # an innermost loop runs UNROLL copies of its body per trip (their loads issue
+            # back to back instead of one load latency per element; accumulators still
+            # update in the loop's order), then the remainder
+            u = UNROLL if not _has_loop(s.body) else 1
+            main = ext // u * u
             r, pl = p.reg("u32"), p.reg("pred")
             top = p.label("serial")
             p.emit(f"mov.u32 {r}, 0")
-            p.place(top)
-            self.axis_reg[name], self.ext[name] = r, ext
-            self._body_scope(ctx, s.body)
+            self.ext[name] = ext
+
+            def copies(n):
+                for c in range(n):
+                    rc = r
+                    if c:
+                        rc = p.reg("u32")
+                        p.emit(f"add.u32 {rc}, {r}, {c}")
+                    self.axis_reg[name] = rc
+                    self._body_scope(ctx, s.body)
+            if main:
+                p.place(top)
+                copies(u)
+                p.emit(f"add.u32 {r}, {r}, {u}\nsetp.lt.u32 {pl}, {r}, {main}\n@{pl} bra {top}")
+            copies(ext - main)
             del self.axis_reg[name], self.ext[name]
-            p.emit(f"add.u32 {r}, {r}, 1\nsetp.lt.u32 {pl}, {r}, {ext}\n@{pl} bra {top}")
 
     def _select(self, ctx, s):
         """``v = a when c1, b when c2, ..., z when True``: the first branch whose index
@@ -307,6 +327,17 @@ class MapKernel:
             else:
                 h = ctx.ptx.reg("b16")
                 ctx.ptx.emit(f"cvt.rn.{dt}.f32 {h}, {v}\nst.global.b16 [{addr}+{off}], {h}")
+
+
+def _has_loop(body) -> bool:
+    for x in body:
+        if type(x).__name__ in ("Loop", "StridedLoop"):
+            return True
+        for attr in ("body", "else_body"):
+            sub = getattr(x, attr, None)
+            if isinstance(sub, tuple) and _has_loop(sub):
+                return True
+    return False
 
 
 def _identity(kind: str, v: float) -> str:
