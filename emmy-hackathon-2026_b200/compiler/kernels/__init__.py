@@ -61,6 +61,15 @@ def select(spec) -> str:
             from .pointwise import emit_map, serialize_cooperative
             return emit_map(serialize_cooperative(spec))
         return emit_reduction(spec)
+    # emmy's register-tiled f32 attention (an online softmax per output element): one
+    # warp per query row over keys staged in shared memory
+    from .attention_f32 import analyze as analyze_attn_f32, emit_module as emit_attn_f32
+    try:
+        acfg = analyze_attn_f32(spec)
+    except NotImplementedError:
+        acfg = None
+    if acfg is not None:
+        return emit_attn_f32(spec, acfg)
     # emmy's SIMT f32 matmuls (FMA over cp.async-staged tiles) run on the tensor cores
     # as 3xTF32
     from .gemm import analyze_f32, emit_gemm_module

@@ -1,0 +1,505 @@
+"""emmy's f32 attention ``softmax(q @ kt * c) @ v`` as one warp-per-query-row SIMT kernel.
+
+The reference lowers f32 attention (problems/a01_attention, problems/a02_attention_128,
+tests/problems/x_a_*) to a register-tiled Tile over the OUTPUT elements: every thread owns
+a few (row, column) outputs and, for each of them, walks all keys with an online softmax,
+recomputing the full ``q . k`` dot product per key and per output column
+(compiler/codegen.py's tiled lowering; the IR: ``Loop(key) { Loop(d) { Accum(q*kt) } ;
+max / exp / rescale ; Accum(p * v) }``).  Run as written, that is Sk x D x Dv FMAs per row
+on a few hundred threads.
+
+Here the same arithmetic is reorganised around the query row:
+
+* one CTA of W warps per block of W x R query rows of one batch entry; a warp owns R rows;
+* keys stream through shared memory in chunks of KC (32 or 64) keys: the chunk of kt
+  (``[D][KC]``, staged along the key axis, which is contiguous in kt) and of v
+  (``[KC][Dv]``, one contiguous span of v), zero-filled past Sk so padding keys give
+  p = 0 and never NaN;
+* scores: lane j owns keys j and j + 32 of the chunk, ``s = sum_d q[d] kt[d][j]`` with q
+  broadcast from shared memory (128-bit loads) -- each kt element read once per warp
+  serves R rows;
+* online softmax per row: chunk max by warp butterfly, ``alpha = 2^((m - m') log2 e)``,
+  ``p = 2^((s c - m') log2 e)``; the row sum stays a per-lane partial until the end;
+* ``o += p v``: p goes through a per-warp shared row (128-bit broadcast loads), lane c
+  owns output columns c, c + 32, ...;
+* epilogue: the row sum by butterfly, ``o / l`` (IEEE division), predicated stores.
+
+Everything is f32; the exponentials use ``ex2.approx`` (relative error ~2^-22), inside the
+fixtures' rtol 1e-3.  No global synchronisation, no atomics: deterministic.
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+from ..ptx import Ptx, entry, f32_hex, module
+from ..stmts import expr_vars
+from .common import arg_params, load_pointer
+
+LOG2E = 1.4426950408889634
+WARPS = 4
+
+
+@dataclass
+class F32AttnConfig:
+    name: str
+    B: int
+    Sq: int
+    Sk: int
+    D: int
+    Dv: int
+    q: str
+    k: str
+    v: str
+    o: str
+    scale_param: str | None        # 1-element buffer holding the multiplier (or its inverse)
+    scale_recip: bool              # multiplier = 1 / param[0]
+    scale_const: float             # used when scale_param is None
+    R: int = 1                     # query rows per warp
+    KC: int = 64                   # keys per staged chunk
+
+    @property
+    def KPL(self) -> int:          # keys per lane per chunk
+        return self.KC // 32
+
+    @property
+    def NC(self) -> int:           # output columns per lane
+        return -(-self.Dv // 32)
+
+    @property
+    def DP(self) -> int:           # q row stride in shared memory (16-byte rows)
+        return -(-self.D // 4) * 4
+
+    @property
+    def vec(self) -> bool:         # 128-bit staging: key and value rows in whole float4s
+        return self.Sk % 4 == 0 and self.Dv % 4 == 0
+
+
+def _walk_loops(body, loops=()):
+    """(statement, enclosing loop axes outermost first) over a statement tree."""
+    for s in body:
+        yield s, loops
+        k = type(s).__name__
+        inner = loops + ((s.axis.name,) if k == "Loop" else ())
+        for attr in ("body", "else_body"):
+            sub = getattr(s, attr, None)
+            if isinstance(sub, tuple):
+                yield from _walk_loops(sub, inner)
+
+
+_ALLOWED = {"Tile", "Load", "Assign", "Accum", "Loop", "Let", "Write", "Cond"}
+
+
+def analyze(spec) -> F32AttnConfig:
+    """Recognise ``softmax(q @ kt * c, -1) @ v`` in f32 from the statements.
+
+    Raises NotImplementedError for anything else (masks, 16-bit operands, k stored
+    key-major, broadcast batch dims, ...), which then lowers as an element map."""
+    if len(spec.body) != 1 or type(spec.body[0]).__name__ != "Tile":
+        raise NotImplementedError("not a single Tile")
+    walk = list(_walk_loops(spec.body))
+    kinds = {type(s).__name__ for s, _ in walk}
+    if not kinds <= _ALLOWED:
+        raise NotImplementedError(f"statements {sorted(kinds - _ALLOWED)}")
+    defs = {}
+    for s, _ in walk:
+        k = type(s).__name__
+        if k == "Load":
+            for n in s.names:
+                defs[n] = s
+        elif k in ("Assign", "Let"):
+            defs[s.name] = s
+    # the contraction: Accum(add) of a product of two loads, in a loop nested in the key loop
+    dots = []
+    for s, loops in walk:
+        if type(s).__name__ == "Accum" and s.op.name == "add" and len(loops) >= 2:
+            prod = defs.get(s.value)
+            if prod is not None and type(prod).__name__ == "Assign" and prod.op.name == "multiply" \
+                    and all(type(defs.get(a)).__name__ == "Load" for a in prod.args):
+                dots.append((s, loops, [defs[a] for a in prod.args]))
+    if not dots:
+        raise NotImplementedError("no dot product in a nested loop")
+    key, red = dots[0][1][-2], dots[0][1][-1]
+    q_in = k_in = None
+    for acc, loops, lds in dots:
+        if loops[-2:] != (key, red) or tuple(acc.axes or ()) != (red,):
+            raise NotImplementedError("dot products over different loops")
+        for ld in lds:
+            last = expr_vars(ld.index[-1])
+            if last == {red} and not any(key in expr_vars(i) for i in ld.index):
+                q_in = q_in or ld.input
+                if ld.input != q_in:
+                    raise NotImplementedError("two q buffers")
+            elif last == {key} and len(ld.index) >= 2 and expr_vars(ld.index[-2]) == {red}:
+                k_in = k_in or ld.input
+                if ld.input != k_in:
+                    raise NotImplementedError("two k buffers")
+            else:
+                raise NotImplementedError("dot product operands not (q row, kt column)")
+    if q_in is None or k_in is None:
+        raise NotImplementedError("q / kt not identified")
+    # v: read in the key loop (outside the dot product), key index on its rows
+    v_in = None
+    for s, loops in walk:
+        if type(s).__name__ == "Load" and s.input not in (q_in, k_in):
+            if len(s.index) >= 2 and key in loops and red not in loops and \
+                    expr_vars(s.index[-2]) == {key} and key not in expr_vars(s.index[-1]):
+                v_in = v_in or s.input
+                if s.input != v_in:
+                    raise NotImplementedError("two v buffers")
+    if v_in is None:
+        raise NotImplementedError("no v operand")
+    # the softmax: an exp and a running max over the key axis; the score times a scale
+    if not any(type(s).__name__ == "Assign" and s.op.name == "exp" for s, _ in walk):
+        raise NotImplementedError("no exp")
+    if not any(type(s).__name__ == "Accum" and s.op.name == "maximum" and key in (s.axes or ())
+               for s, _ in walk):
+        raise NotImplementedError("no running max over the keys")
+    dot_names = {d[0].name for d in dots}
+    scale_param, recip, const = None, False, 1.0
+    scaled = [s for s, _ in walk if type(s).__name__ == "Assign" and set(s.args) & dot_names]
+    if not scaled or any(s.op.name != "multiply" or len(s.args) != 2 for s in scaled):
+        raise NotImplementedError("score not scaled by a multiply")
+    others = {a for s in scaled for a in s.args if a not in dot_names}
+    if len(others) != 1:
+        raise NotImplementedError("scores scaled by different values")
+    sd = defs.get(next(iter(others)))
+
+    def scalar_param(ld):
+        if ld is None or type(ld).__name__ != "Load":
+            return None
+        p = spec.param(ld.input)
+        if p.dtype != "f32" or p.scalar or math.prod(p.shape) != 1:
+            return None
+        return p.name
+    if type(sd).__name__ == "Load" and scalar_param(sd):
+        scale_param = scalar_param(sd)
+    elif type(sd).__name__ == "Assign" and sd.op.name == "reciprocal" and len(sd.args) == 1 \
+            and scalar_param(defs.get(sd.args[0])):
+        scale_param, recip = scalar_param(defs.get(sd.args[0])), True
+    elif type(sd).__name__ == "Let" and type(sd.value).__name__ == "Literal":
+        const = float(sd.value.value)
+    else:
+        raise NotImplementedError("scale is not a constant or a 1-element buffer")
+    # guards only: no condition may look at the key or reduction axis (a mask would)
+    for s, _ in walk:
+        if type(s).__name__ == "Cond" and expr_vars(s.cond) & {key, red}:
+            raise NotImplementedError("a condition on the key axis (mask)")
+    loaded = {s.input for s, _ in walk if type(s).__name__ == "Load"}
+    if loaded - {q_in, k_in, v_in, scale_param}:
+        raise NotImplementedError(f"extra inputs {sorted(loaded - {q_in, k_in, v_in})}")
+    outs = {s.output for s, _ in walk if type(s).__name__ == "Write"}
+    if len(outs) != 1:
+        raise NotImplementedError("not one output")
+    Q, K, V, O = (spec.param(n) for n in (q_in, k_in, v_in, next(iter(outs))))
+    if any(p.dtype != "f32" or p.scalar for p in (Q, K, V, O)):
+        raise NotImplementedError("f32 buffers only")
+    if len(Q.shape) < 2 or not (len(Q.shape) == len(K.shape) == len(V.shape) == len(O.shape)):
+        raise NotImplementedError("operand ranks")
+    lead = tuple(Q.shape[:-2])
+    if any(tuple(p.shape[:-2]) != lead for p in (K, V, O)):
+        raise NotImplementedError("batch dims differ (broadcast)")
+    Sq, D = Q.shape[-2:]
+    Sk, Dv = V.shape[-2:]
+    if tuple(K.shape[-2:]) != (D, Sk) or tuple(O.shape[-2:]) != (Sq, Dv):
+        raise NotImplementedError("operand shapes")
+    B = math.prod(lead) if lead else 1
+    if D > 256 or Dv > 256 or B > 65535 or min(Sq, Sk, D, Dv) < 1:
+        raise NotImplementedError("head dims above 256")
+    cfg = F32AttnConfig(spec.name, B, Sq, Sk, D, Dv, Q.name, K.name, V.name, O.name,
+                        scale_param, recip, const)
+    cfg.KC = 32 if Sk <= 32 else 64
+    # rows per warp: reuse each staged key across rows once the grid covers the SMs
+    for R in (4, 2):
+        if B * -(-Sq // (WARPS * R)) >= 148:
+            cfg.R = R
+            break
+    return cfg
+
+
+def smem_layout(cfg: F32AttnConfig) -> dict:
+    """Byte offsets in dynamic shared memory (each region 16-byte aligned)."""
+    ks = 0
+    vs = ks + cfg.D * cfg.KC * 4
+    qs = vs + cfg.KC * cfg.Dv * 4
+    qs = -(-qs // 16) * 16
+    ps = qs + WARPS * cfg.R * cfg.DP * 4
+    end = ps + WARPS * cfg.R * cfg.KC * 4
+    return {"ks": ks, "vs": vs, "qs": qs, "ps": ps, "bytes": end}
+
+
+def emit_attention_f32(spec) -> str:
+    return emit_module(spec, analyze(spec))
+
+
+def emit_module(spec, cfg: F32AttnConfig) -> str:
+    p = Ptx()
+    T, R, KC, KPL, NC, D, Dv, DP = WARPS * 32, cfg.R, cfg.KC, cfg.KPL, cfg.NC, cfg.D, cfg.Dv, cfg.DP
+    lay = smem_layout(cfg)
+    NEG_INF = "0fFF800000"
+
+    tid, lane, warp = p.reg("u32"), p.reg("u32"), p.reg("u32")
+    bidx, row0 = p.reg("u32"), p.reg("u32")
+    p.emit(f"""
+        mov.u32 {tid}, %tid.x
+        and.b32 {lane}, {tid}, 31
+        shr.u32 {warp}, {tid}, 5
+        mov.u32 {bidx}, %ctaid.y
+        mov.u32 {row0}, %ctaid.x
+        mad.lo.u32 {row0}, {row0}, {WARPS}, {warp}
+        mul.lo.u32 {row0}, {row0}, {R}
+    """)
+    ptr = {n: load_pointer(p, n) for n in (cfg.q, cfg.k, cfg.v, cfg.o)}
+
+    def batch_base(name, per):
+        off = p.reg("u64")
+        p.emit(f"mul.wide.u32 {off}, {bidx}, {per * 4}\nadd.s64 {ptr[name]}, {ptr[name]}, {off}")
+    batch_base(cfg.q, cfg.Sq * D)
+    batch_base(cfg.k, D * cfg.Sk)
+    batch_base(cfg.v, cfg.Sk * Dv)
+    batch_base(cfg.o, cfg.Sq * Dv)
+
+    # the score multiplier c
+    sc = p.reg("f32")
+    if cfg.scale_param is not None:
+        sp = load_pointer(p, cfg.scale_param)
+        p.emit(f"ld.global.nc.f32 {sc}, [{sp}]")
+        if cfg.scale_recip:
+            p.emit(f"rcp.rn.f32 {sc}, {sc}")
+    else:
+        p.emit(f"mov.f32 {sc}, {f32_hex(cfg.scale_const)}")
+
+    # shared-memory bases (32-bit shared addresses)
+    sbase = p.reg("u32")
+    p.emit(f"mov.u32 {sbase}, dsmem")
+    ks_lane, vs_lane, qw, pw, pwl = (p.reg("u32") for _ in range(5))
+    t0 = p.reg("u32")
+    p.emit(f"""
+        shl.b32 {t0}, {lane}, 2
+        add.u32 {ks_lane}, {sbase}, {lay['ks']}
+        add.u32 {ks_lane}, {ks_lane}, {t0}
+        add.u32 {vs_lane}, {sbase}, {lay['vs']}
+        add.u32 {vs_lane}, {vs_lane}, {t0}
+        mad.lo.u32 {qw}, {warp}, {R * DP * 4}, {sbase}
+        add.u32 {qw}, {qw}, {lay['qs']}
+        mad.lo.u32 {pw}, {warp}, {R * KC * 4}, {sbase}
+        add.u32 {pw}, {pw}, {lay['ps']}
+        add.u32 {pwl}, {pw}, {t0}
+    """)
+
+    # ---- the warp's q rows into shared memory (zero past Sq and past D)
+    for r in range(R):
+        row, prow = p.reg("u32"), p.reg("pred")
+        p.emit(f"add.u32 {row}, {row0}, {r}\nsetp.lt.u32 {prow}, {row}, {cfg.Sq}")
+        for i in range(-(-DP // 32)):
+            d = p.reg("u32")
+            val, pd, pst, a64 = p.reg("f32"), p.reg("pred"), p.reg("pred"), p.reg("u64")
+            p.emit(f"""
+                add.u32 {d}, {lane}, {32 * i}
+                setp.lt.and.u32 {pd}, {d}, {D}, {prow}
+                setp.lt.u32 {pst}, {d}, {DP}
+                mov.f32 {val}, 0f00000000
+                mad.lo.u32 {t0}, {row}, {D}, {d}
+                mul.wide.u32 {a64}, {t0}, 4
+                add.s64 {a64}, {ptr[cfg.q]}, {a64}
+                @{pd} ld.global.nc.f32 {val}, [{a64}]
+                shl.b32 {t0}, {d}, 2
+                add.u32 {t0}, {t0}, {qw}
+                @{pst} st.shared.f32 [{t0}+{r * DP * 4}], {val}
+            """)
+
+    # running state
+    m = [p.reg("f32") for _ in range(R)]
+    l = [p.reg("f32") for _ in range(R)]
+    o = [[p.reg("f32") for _ in range(NC)] for _ in range(R)]
+    for r in range(R):
+        p.emit(f"mov.f32 {m[r]}, {NEG_INF}\nmov.f32 {l[r]}, 0f00000000")
+        for i in range(NC):
+            p.emit(f"mov.f32 {o[r][i]}, 0f00000000")
+    pcol = []
+    for i in range(NC):
+        pc = p.reg("pred")
+        p.emit(f"add.u32 {t0}, {lane}, {32 * i}\nsetp.lt.u32 {pc}, {t0}, {Dv}")
+        pcol.append(pc)
+    vv = [p.reg("f32") for _ in range(NC)]
+    for i in range(NC):
+        p.emit(f"mov.f32 {vv[i]}, 0f00000000")
+
+    # staging geometry: kt chunk [D][KC] and v chunk [KC][Dv]
+    key0 = p.reg("u32")
+    p.emit(f"mov.u32 {key0}, 0")
+    top = p.label("chunk")
+    p.place(top)
+    p.emit("bar.sync 0")
+    _stage(p, cfg, ptr, tid, key0, sbase, lay, T)
+    p.emit("bar.sync 0")
+
+    # ---- scores for the chunk: acc[r][k] = q_r . kt[:, key0 + lane + 32k]
+    acc = [[p.reg("f32") for _ in range(KPL)] for _ in range(R)]
+    for r in range(R):
+        for k in range(KPL):
+            p.emit(f"mov.f32 {acc[r][k]}, 0f00000000")
+    kv = [p.reg("f32") for _ in range(KPL)]
+    qv = [[p.reg("f32") for _ in range(4)] for _ in range(R)]
+    for d0 in range(0, D, 4):
+        for r in range(R):
+            p.emit(f"ld.shared.v4.f32 {{{', '.join(qv[r])}}}, [{qw}+{(r * DP + d0) * 4}]")
+        for dd in range(min(4, D - d0)):
+            d = d0 + dd
+            for k in range(KPL):
+                p.emit(f"ld.shared.f32 {kv[k]}, [{ks_lane}+{(d * KC + 32 * k) * 4}]")
+            for r in range(R):
+                for k in range(KPL):
+                    p.emit(f"fma.rn.f32 {acc[r][k]}, {qv[r][dd]}, {kv[k]}, {acc[r][k]}")
+
+    # ---- online softmax per row; p to the warp's shared row
+    kvalid = []
+    for k in range(KPL):
+        pk = p.reg("pred")
+        p.emit(f"add.u32 {t0}, {key0}, {lane}\nadd.u32 {t0}, {t0}, {32 * k}\nsetp.lt.u32 {pk}, {t0}, {cfg.Sk}")
+        kvalid.append(pk)
+    l2e = f32_hex(LOG2E)
+    for r in range(R):
+        t = [p.reg("f32") for _ in range(KPL)]
+        cm, sh, mn, alpha, ps_sum = p.reg("f32"), p.reg("f32"), p.reg("f32"), p.reg("f32"), p.reg("f32")
+        for k in range(KPL):
+            p.emit(f"mul.rn.f32 {t[k]}, {acc[r][k]}, {sc}\nselp.f32 {t[k]}, {t[k]}, {NEG_INF}, {kvalid[k]}")
+        p.emit(f"mov.f32 {cm}, {t[0]}")
+        for k in range(1, KPL):
+            p.emit(f"max.f32 {cm}, {cm}, {t[k]}")
+        for off in (16, 8, 4, 2, 1):
+            p.emit(f"shfl.sync.bfly.b32 {sh}, {cm}, {off}, 31, 0xffffffff\nmax.f32 {cm}, {cm}, {sh}")
+        p.emit(f"""
+            max.f32 {mn}, {m[r]}, {cm}
+            sub.f32 {alpha}, {m[r]}, {mn}
+            mul.rn.f32 {alpha}, {alpha}, {l2e}
+            ex2.approx.f32 {alpha}, {alpha}
+            mov.f32 {m[r]}, {mn}
+            mov.f32 {ps_sum}, 0f00000000
+        """)
+        for k in range(KPL):
+            p.emit(f"""
+                sub.f32 {t[k]}, {t[k]}, {mn}
+                mul.rn.f32 {t[k]}, {t[k]}, {l2e}
+                ex2.approx.f32 {t[k]}, {t[k]}
+                add.f32 {ps_sum}, {ps_sum}, {t[k]}
+                st.shared.f32 [{pwl}+{(r * KC + 32 * k) * 4}], {t[k]}
+            """)
+        p.emit(f"fma.rn.f32 {l[r]}, {l[r]}, {alpha}, {ps_sum}")
+        for i in range(NC):
+            p.emit(f"mul.rn.f32 {o[r][i]}, {o[r][i]}, {alpha}")
+    p.emit("bar.warp.sync 0xffffffff")
+
+    # ---- o += p v over the chunk's keys
+    pv = [[p.reg("f32") for _ in range(4)] for _ in range(R)]
+    for j0 in range(0, KC, 4):
+        for r in range(R):
+            p.emit(f"ld.shared.v4.f32 {{{', '.join(pv[r])}}}, [{pw}+{(r * KC + j0) * 4}]")
+        for jj in range(4):
+            j = j0 + jj
+            for i in range(NC):
+                p.emit(f"@{pcol[i]} ld.shared.f32 {vv[i]}, [{vs_lane}+{(j * Dv + 32 * i) * 4}]")
+            for r in range(R):
+                for i in range(NC):
+                    p.emit(f"fma.rn.f32 {o[r][i]}, {pv[r][jj]}, {vv[i]}, {o[r][i]}")
+    pl = p.reg("pred")
+    p.emit(f"add.u32 {key0}, {key0}, {KC}\nsetp.lt.u32 {pl}, {key0}, {cfg.Sk}\n@{pl} bra {top}")
+
+    # ---- epilogue: o / l
+    for r in range(R):
+        sh, row, prow = p.reg("f32"), p.reg("u32"), p.reg("pred")
+        for off in (16, 8, 4, 2, 1):
+            p.emit(f"shfl.sync.bfly.b32 {sh}, {l[r]}, {off}, 31, 0xffffffff\nadd.f32 {l[r]}, {l[r]}, {sh}")
+        p.emit(f"add.u32 {row}, {row0}, {r}\nsetp.lt.u32 {prow}, {row}, {cfg.Sq}")
+        for i in range(NC):
+            ps_, a64, res = p.reg("pred"), p.reg("u64"), p.reg("f32")
+            p.emit(f"""
+                and.pred {ps_}, {prow}, {pcol[i]}
+                div.rn.f32 {res}, {o[r][i]}, {l[r]}
+                mad.lo.u32 {t0}, {row}, {Dv}, {lane}
+                add.u32 {t0}, {t0}, {32 * i}
+                mul.wide.u32 {a64}, {t0}, 4
+                add.s64 {a64}, {ptr[cfg.o]}, {a64}
+                @{ps_} st.global.f32 [{a64}], {res}
+            """)
+    p.emit("ret")
+
+    grid = [-(-cfg.Sq // (WARPS * R)), cfg.B, 1]
+    flops = 2 * cfg.B * cfg.Sq * cfg.Sk * (D + Dv)
+    launch = {"kind": "attention_f32", "grid": grid, "block": [T, 1, 1], "cluster": [1, 1, 1],
+              "smem": lay["bytes"], "extra_params": [], "flops": flops}
+    return module([entry(spec.name, arg_params(spec), p, maxntid=T)], launch,
+                  globals_=[".extern .shared .align 16 .b8 dsmem[];"])
+
+
+def _stage(p: Ptx, cfg: F32AttnConfig, ptr: dict, tid: str, key0: str, sbase: str, lay: dict,
+           T: int) -> None:
+    """Copy the chunk's kt columns [key0, key0 + KC) and v rows into shared memory, zero
+    past Sk.  128-bit accesses when rows are whole float4s; loads batched 16 deep."""
+    KC, D, Dv, Sk = cfg.KC, cfg.D, cfg.Dv, cfg.Sk
+    w = 4 if cfg.vec else 1
+    sfx = ".v4.f32" if w == 4 else ".f32"
+    ops = []        # (pred-setup text, pred, global address reg, shared address reg)
+    # kt: unit e = tid + T it over [D][KC / w]; T is a multiple of KC / w
+    per_row = KC // w
+    rows_per_pass = T // per_row
+    dt, jt, nk = p.reg("u32"), p.reg("u32"), p.reg("u32")
+    p.emit(f"""
+        shr.u32 {dt}, {tid}, {per_row.bit_length() - 1}
+        and.b32 {jt}, {tid}, {per_row - 1}
+        mul.lo.u32 {jt}, {jt}, {w}
+        sub.u32 {nk}, {Sk}, {key0}
+    """)
+    pkey = p.reg("pred")
+    p.emit(f"setp.lt.u32 {pkey}, {jt}, {nk}")
+    gk = p.reg("u32")
+    p.emit(f"add.u32 {gk}, {key0}, {jt}")
+    for it in range(-(-D // rows_per_pass)):
+        d = p.reg("u32")
+        pr = p.reg("pred")
+        p.emit(f"add.u32 {d}, {dt}, {it * rows_per_pass}\nsetp.lt.and.u32 {pr}, {d}, {D}, {pkey}")
+        ga, sa, t = p.reg("u64"), p.reg("u32"), p.reg("u32")
+        p.emit(f"""
+            mad.lo.u32 {t}, {d}, {Sk}, {gk}
+            mul.wide.u32 {ga}, {t}, 4
+            add.s64 {ga}, {ptr[cfg.k]}, {ga}
+            mad.lo.u32 {sa}, {d}, {KC}, {jt}
+            shl.b32 {sa}, {sa}, 2
+            add.u32 {sa}, {sa}, {sbase}
+        """)
+        pst = p.reg("pred")
+        p.emit(f"setp.lt.u32 {pst}, {d}, {D}")
+        ops.append((pr, pst, ga, sa + f"+{lay['ks']}"))
+    # v: the chunk is one contiguous span of min(KC, Sk - key0) x Dv floats
+    nv = p.reg("u32")
+    p.emit(f"min.u32 {nv}, {nk}, {KC}\nmul.lo.u32 {nv}, {nv}, {Dv}")
+    units = KC * Dv // w
+    vbase = p.reg("u64")
+    p.emit(f"mul.wide.u32 {vbase}, {key0}, {Dv * 4}\nadd.s64 {vbase}, {ptr[cfg.v]}, {vbase}")
+    for it in range(-(-units // T)):
+        e = p.reg("u32")
+        pr, pst = p.reg("pred"), p.reg("pred")
+        ga, sa = p.reg("u64"), p.reg("u32")
+        p.emit(f"""
+            add.u32 {e}, {tid}, {it * T}
+            mul.lo.u32 {e}, {e}, {w}
+            setp.lt.u32 {pr}, {e}, {nv}
+            setp.lt.u32 {pst}, {e}, {KC * Dv}
+            mul.wide.u32 {ga}, {e}, 4
+            add.s64 {ga}, {vbase}, {ga}
+            shl.b32 {sa}, {e}, 2
+            add.u32 {sa}, {sa}, {sbase}
+        """)
+        ops.append((pr, pst, ga, sa + f"+{lay['vs']}"))
+    for b0 in range(0, len(ops), 16):
+        batch = ops[b0:b0 + 16]
+        vals = []
+        for pr, _, ga, _ in batch:
+            v = [p.reg("f32") for _ in range(w)]
+            p.emit("\n".join(f"mov.f32 {x}, 0f00000000" for x in v))
+            tgt = "{" + ", ".join(v) + "}" if w == 4 else v[0]
+            p.emit(f"@{pr} ld.global.nc{sfx} {tgt}, [{ga}]")
+            vals.append(tgt)
+        for (_, pst, _, sa), tgt in zip(batch, vals):
+            p.emit(f"@{pst} st.shared{sfx} [{sa}], {tgt}")

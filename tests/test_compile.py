@@ -139,6 +139,28 @@ def test_simt_attention_recognizer():
                 analyze_simt(load(ir))
 
 
+F32_ATTN = {"a01_attention": (1, 64, 64, 64, 64, True), "a02_attention_128": (1, 128, 128, 32, 32, True),
+            "x_a_256x64": (1, 256, 256, 64, 64, True), "x_a_32x16": (1, 32, 32, 16, 16, True),
+            "x_a_batched": (4, 64, 64, 32, 32, True), "x_a_rect": (1, 64, 192, 32, 48, False)}
+
+
+def test_f32_attention_recognizer():
+    """The register-tiled f32 attention forms (q @ kt scaled by a 1-element buffer or its
+    inverse) go to the warp-per-row template; nothing else in the fixtures does."""
+    from compiler.kernels.attention_f32 import analyze
+    for ir in sorted(GOLDEN.glob("*/*.ir.json")):
+        pid = ir.parent.name
+        if pid in F32_ATTN:
+            cfg = analyze(load(ir))
+            b, sq, sk, d, dv, recip = F32_ATTN[pid]
+            assert (cfg.B, cfg.Sq, cfg.Sk, cfg.D, cfg.Dv, cfg.scale_recip) == (b, sq, sk, d, dv, recip)
+            assert (cfg.q, cfg.k, cfg.v) == ("q", "kt", "v") and cfg.scale_param is not None
+            assert parse_launch(compile_kernel(load(ir)))["kind"] == "attention_f32"
+        else:
+            with pytest.raises(NotImplementedError):
+                analyze(load(ir))
+
+
 @pytest.mark.parametrize("pid,mnk,batch,a,b,epi", [
     ("m01_matmul_512", (512, 512, 512), 1, "x0", "x1", None),
     ("m02_matmul_rect", (128, 64, 256), 1, "x0", "x1", None),      # split-K atomics: one pass
