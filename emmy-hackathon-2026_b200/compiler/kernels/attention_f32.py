@@ -12,9 +12,12 @@ Here the same arithmetic is reorganised around the query row:
 
 * one CTA of W warps per block of W x R query rows of one batch entry; a warp owns R rows;
 * keys stream through shared memory in chunks of KC (32 or 64) keys: the chunk of kt
-  (``[D][KC]``, staged along the key axis, which is contiguous in kt) and of v
-  (``[KC][Dv]``, one contiguous span of v), zero-filled past Sk so padding keys give
-  p = 0 and never NaN;
+  (``[D][KC]``, staged along the key axis, which is contiguous in kt) -- or of a
+  key-major k (sdpa's ``[.., Sk, D]``: one contiguous span, rows stored with the odd
+  stride D + 1 so the lanes' key rows fall in different banks) -- and of v (``[KC][Dv]``,
+  one contiguous span), zero-filled past Sk so padding keys give p = 0 and never NaN;
+* grouped-query heads (``k.repeat_interleave(G, dim=1)``, tests/problems/x_l_gqa): query
+  entry y reads k / v entry y // G, checked over every entry from the loads' indices;
 * scores: lane j owns keys j and j + 32 of the chunk, ``s = sum_d q[d] kt[d][j]`` with q
   broadcast from shared memory (128-bit loads) -- each kt element read once per warp
   serves R rows;
@@ -56,6 +59,8 @@ class F32AttnConfig:
     scale_param: str | None        # 1-element buffer holding the multiplier (or its inverse)
     scale_recip: bool              # multiplier = 1 / param[0]
     scale_const: float             # used when scale_param is None
+    kt: bool = True                # k stored [.., D, Sk] (kt); False: [.., Sk, D] (sdpa's k)
+    group: int = 1                 # query batch entries per k / v entry (grouped-query heads)
     R: int = 1                     # query rows per warp
     KC: int = 64                   # keys per staged chunk
 
@@ -72,8 +77,12 @@ class F32AttnConfig:
         return -(-self.D // 4) * 4
 
     @property
+    def DK(self) -> int:           # shared row stride of a key-major k chunk (odd: no conflicts)
+        return self.D + 1
+
+    @property
     def vec(self) -> bool:         # 128-bit staging: key and value rows in whole float4s
-        return self.Sk % 4 == 0 and self.Dv % 4 == 0
+        return (self.Sk % 4 == 0 if self.kt else self.D % 4 == 0) and self.Dv % 4 == 0
 
 
 def _walk_loops(body, loops=()):
@@ -94,8 +103,8 @@ _ALLOWED = {"Tile", "Load", "Assign", "Accum", "Loop", "Let", "Write", "Cond"}
 def analyze(spec) -> F32AttnConfig:
     """Recognise ``softmax(q @ kt * c, -1) @ v`` in f32 from the statements.
 
-    Raises NotImplementedError for anything else (masks, 16-bit operands, k stored
-    key-major, broadcast batch dims, ...), which then lowers as an element map."""
+    Raises NotImplementedError for anything else (masks, 16-bit operands, batch maps
+    other than y -> y // G, ...), which then lowers as an element map."""
     if len(spec.body) != 1 or type(spec.body[0]).__name__ != "Tile":
         raise NotImplementedError("not a single Tile")
     walk = list(_walk_loops(spec.body))
@@ -122,30 +131,37 @@ def analyze(spec) -> F32AttnConfig:
         raise NotImplementedError("no dot product in a nested loop")
     key, red = dots[0][1][-2], dots[0][1][-1]
     q_in = k_in = None
+    q_ld = k_ld = None
+    kt_layout = set()
     for acc, loops, lds in dots:
         if loops[-2:] != (key, red) or tuple(acc.axes or ()) != (red,):
             raise NotImplementedError("dot products over different loops")
         for ld in lds:
             last = expr_vars(ld.index[-1])
+            prev = expr_vars(ld.index[-2]) if len(ld.index) >= 2 else set()
             if last == {red} and not any(key in expr_vars(i) for i in ld.index):
-                q_in = q_in or ld.input
+                q_in, q_ld = q_in or ld.input, q_ld or ld
                 if ld.input != q_in:
                     raise NotImplementedError("two q buffers")
-            elif last == {key} and len(ld.index) >= 2 and expr_vars(ld.index[-2]) == {red}:
-                k_in = k_in or ld.input
-                if ld.input != k_in:
-                    raise NotImplementedError("two k buffers")
+                continue
+            if last == {key} and prev == {red}:
+                kt_layout.add(True)
+            elif last == {red} and prev == {key}:
+                kt_layout.add(False)
             else:
-                raise NotImplementedError("dot product operands not (q row, kt column)")
-    if q_in is None or k_in is None:
-        raise NotImplementedError("q / kt not identified")
+                raise NotImplementedError("dot product operands not (q row, k row / kt column)")
+            k_in, k_ld = k_in or ld.input, k_ld or ld
+            if ld.input != k_in:
+                raise NotImplementedError("two k buffers")
+    if q_in is None or k_in is None or len(kt_layout) != 1:
+        raise NotImplementedError("q / k not identified")
     # v: read in the key loop (outside the dot product), key index on its rows
-    v_in = None
+    v_in = v_ld = None
     for s, loops in walk:
         if type(s).__name__ == "Load" and s.input not in (q_in, k_in):
             if len(s.index) >= 2 and key in loops and red not in loops and \
                     expr_vars(s.index[-2]) == {key} and key not in expr_vars(s.index[-1]):
-                v_in = v_in or s.input
+                v_in, v_ld = v_in or s.input, v_ld or s
                 if s.input != v_in:
                     raise NotImplementedError("two v buffers")
     if v_in is None:
@@ -189,26 +205,26 @@ def analyze(spec) -> F32AttnConfig:
     loaded = {s.input for s, _ in walk if type(s).__name__ == "Load"}
     if loaded - {q_in, k_in, v_in, scale_param}:
         raise NotImplementedError(f"extra inputs {sorted(loaded - {q_in, k_in, v_in})}")
-    outs = {s.output for s, _ in walk if type(s).__name__ == "Write"}
-    if len(outs) != 1:
+    writes = [s for s, _ in walk if type(s).__name__ == "Write"]
+    if len({w.output for w in writes}) != 1:
         raise NotImplementedError("not one output")
-    Q, K, V, O = (spec.param(n) for n in (q_in, k_in, v_in, next(iter(outs))))
+    Q, K, V, O = (spec.param(n) for n in (q_in, k_in, v_in, writes[0].output))
     if any(p.dtype != "f32" or p.scalar for p in (Q, K, V, O)):
         raise NotImplementedError("f32 buffers only")
     if len(Q.shape) < 2 or not (len(Q.shape) == len(K.shape) == len(V.shape) == len(O.shape)):
         raise NotImplementedError("operand ranks")
-    lead = tuple(Q.shape[:-2])
-    if any(tuple(p.shape[:-2]) != lead for p in (K, V, O)):
-        raise NotImplementedError("batch dims differ (broadcast)")
+    kt = kt_layout.pop()
     Sq, D = Q.shape[-2:]
     Sk, Dv = V.shape[-2:]
-    if tuple(K.shape[-2:]) != (D, Sk) or tuple(O.shape[-2:]) != (Sq, Dv):
+    if tuple(K.shape[-2:]) != ((D, Sk) if kt else (Sk, D)) or tuple(O.shape[-2:]) != (Sq, Dv) \
+            or tuple(O.shape) != tuple(Q.shape[:-1]) + (Dv,):
         raise NotImplementedError("operand shapes")
-    B = math.prod(lead) if lead else 1
+    B = math.prod(Q.shape[:-2])
+    group = _lead_group(spec, q_ld, [w.index for w in writes], k_ld, v_ld)
     if D > 256 or Dv > 256 or B > 65535 or min(Sq, Sk, D, Dv) < 1:
         raise NotImplementedError("head dims above 256")
     cfg = F32AttnConfig(spec.name, B, Sq, Sk, D, Dv, Q.name, K.name, V.name, O.name,
-                        scale_param, recip, const)
+                        scale_param, recip, const, kt=kt, group=group)
     cfg.KC = 32 if Sk <= 32 else 64
     # rows per warp: reuse each staged key across rows once the grid covers the SMs
     for R in (4, 2):
@@ -218,10 +234,58 @@ def analyze(spec) -> F32AttnConfig:
     return cfg
 
 
+def _lead_group(spec, q_ld, out_indices, k_ld, v_ld) -> int:
+    """The batch map between q / o entries and k / v entries, from the loads' leading
+    coordinates: every query entry y (row-major over q's leading dims) must read k and v
+    entry ``y // G`` for one G (1 for plain attention; the head group of grouped-query
+    attention, ``k.repeat_interleave(G, dim=1)``, which the IR indexes as ``h / G``)."""
+    from ..stmts import eval_index
+    Q, K, V = (spec.param(ld.input) for ld in (q_ld, k_ld, v_ld))
+    ql, nl = tuple(Q.shape[:-2]), len(Q.shape) - 2
+    if tuple(K.shape[:-2]) != tuple(V.shape[:-2]) or len(K.shape) - 2 != nl:
+        raise NotImplementedError("k / v batch dims differ")
+    qe = q_ld.index[:nl]
+    if any(repr(tuple(ix[:nl])) != repr(tuple(qe)) for ix in out_indices):
+        raise NotImplementedError("output rows not q's rows")
+    nq, nk = math.prod(ql), math.prod(K.shape[:-2])
+    if nq % nk:
+        raise NotImplementedError("query entries not a multiple of key entries")
+    G = nq // nk
+    for y in range(nq):
+        coords, r = [], y
+        for d in reversed(ql):
+            coords.append(r % d)
+            r //= d
+        coords.reverse()
+        env = {}
+        for e, c in zip(qe, coords):
+            k = type(e).__name__
+            if k == "Var":
+                if env.get(e.name, c) != c:
+                    raise NotImplementedError("q's leading index repeats a variable")
+                env[e.name] = c
+            elif not (k == "Literal" and int(e.value) == c):
+                raise NotImplementedError("q's leading index is not one variable per dim")
+        for ld in (k_ld, v_ld):
+            try:
+                kc = [eval_index(e, env) for e in ld.index[:nl]]
+            except KeyError:
+                raise NotImplementedError("k / v leading index uses other variables") from None
+            flat = 0
+            for c, d in zip(kc, K.shape[:-2]):
+                if not 0 <= c < d:
+                    raise NotImplementedError("k / v leading index out of range")
+                flat = flat * d + c
+            if flat != y // G:
+                raise NotImplementedError("k / v entries not y // G")
+    return G
+
+
 def smem_layout(cfg: F32AttnConfig) -> dict:
     """Byte offsets in dynamic shared memory (each region 16-byte aligned)."""
     ks = 0
-    vs = ks + cfg.D * cfg.KC * 4
+    vs = ks + (cfg.D * cfg.KC if cfg.kt else cfg.KC * cfg.DK) * 4
+    vs = -(-vs // 16) * 16
     qs = vs + cfg.KC * cfg.Dv * 4
     qs = -(-qs // 16) * 16
     ps = qs + WARPS * cfg.R * cfg.DP * 4
@@ -256,9 +320,11 @@ def emit_module(spec, cfg: F32AttnConfig) -> str:
         off = p.reg("u64")
         p.emit(f"mul.wide.u32 {off}, {bidx}, {per * 4}\nadd.s64 {ptr[name]}, {ptr[name]}, {off}")
     batch_base(cfg.q, cfg.Sq * D)
+    batch_base(cfg.o, cfg.Sq * Dv)
+    if cfg.group > 1:
+        p.emit(f"div.u32 {bidx}, {bidx}, {cfg.group}")
     batch_base(cfg.k, D * cfg.Sk)
     batch_base(cfg.v, cfg.Sk * Dv)
-    batch_base(cfg.o, cfg.Sq * Dv)
 
     # the score multiplier c
     sc = p.reg("f32")
@@ -275,10 +341,12 @@ def emit_module(spec, cfg: F32AttnConfig) -> str:
     p.emit(f"mov.u32 {sbase}, dsmem")
     ks_lane, vs_lane, qw, pw, pwl = (p.reg("u32") for _ in range(5))
     t0 = p.reg("u32")
+    # a lane's key column: kt chunk [D][KC] -> 4 lane; key-major chunk [KC][DK] -> 4 DK lane
     p.emit(f"""
-        shl.b32 {t0}, {lane}, 2
+        mul.lo.u32 {t0}, {lane}, {4 if cfg.kt else 4 * cfg.DK}
         add.u32 {ks_lane}, {sbase}, {lay['ks']}
         add.u32 {ks_lane}, {ks_lane}, {t0}
+        shl.b32 {t0}, {lane}, 2
         add.u32 {vs_lane}, {sbase}, {lay['vs']}
         add.u32 {vs_lane}, {vs_lane}, {t0}
         mad.lo.u32 {qw}, {warp}, {R * DP * 4}, {sbase}
@@ -348,7 +416,8 @@ def emit_module(spec, cfg: F32AttnConfig) -> str:
         for dd in range(min(4, D - d0)):
             d = d0 + dd
             for k in range(KPL):
-                p.emit(f"ld.shared.f32 {kv[k]}, [{ks_lane}+{(d * KC + 32 * k) * 4}]")
+                off = d * KC + 32 * k if cfg.kt else 32 * k * cfg.DK + d
+                p.emit(f"ld.shared.f32 {kv[k]}, [{ks_lane}+{off * 4}]")
             for r in range(R):
                 for k in range(KPL):
                     p.emit(f"fma.rn.f32 {acc[r][k]}, {qv[r][dd]}, {kv[k]}, {acc[r][k]}")
@@ -435,71 +504,90 @@ def emit_module(spec, cfg: F32AttnConfig) -> str:
 
 def _stage(p: Ptx, cfg: F32AttnConfig, ptr: dict, tid: str, key0: str, sbase: str, lay: dict,
            T: int) -> None:
-    """Copy the chunk's kt columns [key0, key0 + KC) and v rows into shared memory, zero
-    past Sk.  128-bit accesses when rows are whole float4s; loads batched 16 deep."""
-    KC, D, Dv, Sk = cfg.KC, cfg.D, cfg.Dv, cfg.Sk
+    """Copy the chunk's keys [key0, key0 + KC) of k and v into shared memory, zero past
+    Sk.  128-bit global loads when rows are whole float4s; loads batched 16 deep."""
+    KC, D, Sk = cfg.KC, cfg.D, cfg.Sk
     w = 4 if cfg.vec else 1
+    nk = p.reg("u32")
+    p.emit(f"sub.u32 {nk}, {Sk}, {key0}")
+    ops = []        # (load predicate, store predicate, global address, [shared addresses])
+    if cfg.kt:
+        # kt [D][Sk]: unit e = tid + T it over [D][KC / w]; T is a multiple of KC / w
+        per_row = KC // w
+        rows_per_pass = T // per_row
+        dt, jt = p.reg("u32"), p.reg("u32")
+        p.emit(f"""
+            shr.u32 {dt}, {tid}, {per_row.bit_length() - 1}
+            and.b32 {jt}, {tid}, {per_row - 1}
+            mul.lo.u32 {jt}, {jt}, {w}
+        """)
+        pkey, gk = p.reg("pred"), p.reg("u32")
+        p.emit(f"setp.lt.u32 {pkey}, {jt}, {nk}\nadd.u32 {gk}, {key0}, {jt}")
+        for it in range(-(-D // rows_per_pass)):
+            d, pr, pst = p.reg("u32"), p.reg("pred"), p.reg("pred")
+            ga, sa, t = p.reg("u64"), p.reg("u32"), p.reg("u32")
+            p.emit(f"""
+                add.u32 {d}, {dt}, {it * rows_per_pass}
+                setp.lt.and.u32 {pr}, {d}, {D}, {pkey}
+                setp.lt.u32 {pst}, {d}, {D}
+                mad.lo.u32 {t}, {d}, {Sk}, {gk}
+                mul.wide.u32 {ga}, {t}, 4
+                add.s64 {ga}, {ptr[cfg.k]}, {ga}
+                mad.lo.u32 {sa}, {d}, {KC}, {jt}
+                shl.b32 {sa}, {sa}, 2
+                add.u32 {sa}, {sa}, {sbase}
+            """)
+            ops.append((pr, pst, ga, [f"{sa}+{lay['ks']}"]))
+    else:
+        # key-major k: rows of D floats, stored with the odd stride DK
+        ops += _span(p, cfg, ptr[cfg.k], tid, key0, nk, sbase, lay["ks"], D, cfg.DK, T, w)
+    ops += _span(p, cfg, ptr[cfg.v], tid, key0, nk, sbase, lay["vs"], cfg.Dv, cfg.Dv, T, w)
     sfx = ".v4.f32" if w == 4 else ".f32"
-    ops = []        # (pred-setup text, pred, global address reg, shared address reg)
-    # kt: unit e = tid + T it over [D][KC / w]; T is a multiple of KC / w
-    per_row = KC // w
-    rows_per_pass = T // per_row
-    dt, jt, nk = p.reg("u32"), p.reg("u32"), p.reg("u32")
-    p.emit(f"""
-        shr.u32 {dt}, {tid}, {per_row.bit_length() - 1}
-        and.b32 {jt}, {tid}, {per_row - 1}
-        mul.lo.u32 {jt}, {jt}, {w}
-        sub.u32 {nk}, {Sk}, {key0}
-    """)
-    pkey = p.reg("pred")
-    p.emit(f"setp.lt.u32 {pkey}, {jt}, {nk}")
-    gk = p.reg("u32")
-    p.emit(f"add.u32 {gk}, {key0}, {jt}")
-    for it in range(-(-D // rows_per_pass)):
-        d = p.reg("u32")
-        pr = p.reg("pred")
-        p.emit(f"add.u32 {d}, {dt}, {it * rows_per_pass}\nsetp.lt.and.u32 {pr}, {d}, {D}, {pkey}")
-        ga, sa, t = p.reg("u64"), p.reg("u32"), p.reg("u32")
-        p.emit(f"""
-            mad.lo.u32 {t}, {d}, {Sk}, {gk}
-            mul.wide.u32 {ga}, {t}, 4
-            add.s64 {ga}, {ptr[cfg.k]}, {ga}
-            mad.lo.u32 {sa}, {d}, {KC}, {jt}
-            shl.b32 {sa}, {sa}, 2
-            add.u32 {sa}, {sa}, {sbase}
-        """)
-        pst = p.reg("pred")
-        p.emit(f"setp.lt.u32 {pst}, {d}, {D}")
-        ops.append((pr, pst, ga, sa + f"+{lay['ks']}"))
-    # v: the chunk is one contiguous span of min(KC, Sk - key0) x Dv floats
-    nv = p.reg("u32")
-    p.emit(f"min.u32 {nv}, {nk}, {KC}\nmul.lo.u32 {nv}, {nv}, {Dv}")
-    units = KC * Dv // w
-    vbase = p.reg("u64")
-    p.emit(f"mul.wide.u32 {vbase}, {key0}, {Dv * 4}\nadd.s64 {vbase}, {ptr[cfg.v]}, {vbase}")
-    for it in range(-(-units // T)):
-        e = p.reg("u32")
-        pr, pst = p.reg("pred"), p.reg("pred")
-        ga, sa = p.reg("u64"), p.reg("u32")
-        p.emit(f"""
-            add.u32 {e}, {tid}, {it * T}
-            mul.lo.u32 {e}, {e}, {w}
-            setp.lt.u32 {pr}, {e}, {nv}
-            setp.lt.u32 {pst}, {e}, {KC * Dv}
-            mul.wide.u32 {ga}, {e}, 4
-            add.s64 {ga}, {vbase}, {ga}
-            shl.b32 {sa}, {e}, 2
-            add.u32 {sa}, {sa}, {sbase}
-        """)
-        ops.append((pr, pst, ga, sa + f"+{lay['vs']}"))
     for b0 in range(0, len(ops), 16):
         batch = ops[b0:b0 + 16]
         vals = []
         for pr, _, ga, _ in batch:
             v = [p.reg("f32") for _ in range(w)]
             p.emit("\n".join(f"mov.f32 {x}, 0f00000000" for x in v))
-            tgt = "{" + ", ".join(v) + "}" if w == 4 else v[0]
-            p.emit(f"@{pr} ld.global.nc{sfx} {tgt}, [{ga}]")
-            vals.append(tgt)
-        for (_, pst, _, sa), tgt in zip(batch, vals):
-            p.emit(f"@{pst} st.shared{sfx} [{sa}], {tgt}")
+            p.emit(f"@{pr} ld.global.nc{sfx} {'{' + ', '.join(v) + '}' if w == 4 else v[0]}, [{ga}]")
+            vals.append(v)
+        for (_, pst, _, sas), v in zip(batch, vals):
+            if len(sas) == 1 and w == 4:
+                p.emit(f"@{pst} st.shared.v4.f32 [{sas[0]}], {{{', '.join(v)}}}")
+            else:
+                for sa, x in zip(sas, v):
+                    p.emit(f"@{pst} st.shared.f32 [{sa}], {x}")
+
+
+def _span(p: Ptx, cfg: F32AttnConfig, gptr: str, tid: str, key0: str, nk: str, sbase: str,
+          soff: int, width: int, sstride: int, T: int, w: int) -> list:
+    """Staging ops for rows [key0, key0 + KC) of a [.., Sk, width] buffer: one contiguous
+    span of global memory; in shared memory row j starts at j * sstride (floats)."""
+    KC = cfg.KC
+    nv = p.reg("u32")
+    p.emit(f"min.u32 {nv}, {nk}, {KC}\nmul.lo.u32 {nv}, {nv}, {width}")
+    base = p.reg("u64")
+    p.emit(f"mul.wide.u32 {base}, {key0}, {width * 4}\nadd.s64 {base}, {gptr}, {base}")
+    ops = []
+    for it in range(-(-(KC * width // w) // T)):
+        e, pr, pst = p.reg("u32"), p.reg("pred"), p.reg("pred")
+        ga, sa = p.reg("u64"), p.reg("u32")
+        p.emit(f"""
+            add.u32 {e}, {tid}, {it * T}
+            mul.lo.u32 {e}, {e}, {w}
+            setp.lt.u32 {pr}, {e}, {nv}
+            setp.lt.u32 {pst}, {e}, {KC * width}
+            mul.wide.u32 {ga}, {e}, 4
+            add.s64 {ga}, {base}, {ga}
+        """)
+        if sstride == width:
+            p.emit(f"shl.b32 {sa}, {e}, 2\nadd.u32 {sa}, {sa}, {sbase}")
+            ops.append((pr, pst, ga, [f"{sa}+{soff}"]))
+        else:
+            # element e sits in row e / width: shift it by that many pad floats (a float4
+            # never straddles rows: width is a multiple of w)
+            j = p.reg("u32")
+            p.emit(f"div.u32 {j}, {e}, {width}\nmad.lo.u32 {sa}, {j}, {sstride - width}, {e}\n"
+                   f"shl.b32 {sa}, {sa}, 2\nadd.u32 {sa}, {sa}, {sbase}")
+            ops.append((pr, pst, ga, [f"{sa}+{soff + 4 * c}" for c in range(w)]))
+    return ops

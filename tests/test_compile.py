@@ -141,7 +141,8 @@ def test_simt_attention_recognizer():
 
 F32_ATTN = {"a01_attention": (1, 64, 64, 64, 64, True), "a02_attention_128": (1, 128, 128, 32, 32, True),
             "x_a_256x64": (1, 256, 256, 64, 64, True), "x_a_32x16": (1, 32, 32, 16, 16, True),
-            "x_a_batched": (4, 64, 64, 32, 32, True), "x_a_rect": (1, 64, 192, 32, 48, False)}
+            "x_a_batched": (4, 64, 64, 32, 32, True), "x_a_rect": (1, 64, 192, 32, 48, False),
+            "x_l_gqa": (8, 64, 64, 32, 32, False)}
 
 
 def test_f32_attention_recognizer():
@@ -154,7 +155,11 @@ def test_f32_attention_recognizer():
             cfg = analyze(load(ir))
             b, sq, sk, d, dv, recip = F32_ATTN[pid]
             assert (cfg.B, cfg.Sq, cfg.Sk, cfg.D, cfg.Dv, cfg.scale_recip) == (b, sq, sk, d, dv, recip)
-            assert (cfg.q, cfg.k, cfg.v) == ("q", "kt", "v") and cfg.scale_param is not None
+            if pid == "x_l_gqa":      # sdpa: key-major k, 4 query heads per k / v head
+                assert (cfg.kt, cfg.group, cfg.k) == (False, 4, "x1")
+            else:
+                assert (cfg.q, cfg.k, cfg.v, cfg.kt, cfg.group) == ("q", "kt", "v", True, 1)
+            assert cfg.scale_param is not None
             assert parse_launch(compile_kernel(load(ir)))["kind"] == "attention_f32"
         else:
             with pytest.raises(NotImplementedError):
