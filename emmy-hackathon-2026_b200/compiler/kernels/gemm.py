@@ -164,6 +164,35 @@ def _tile_coords(p: Ptx, cfg: GemmConfig, t: str) -> tuple[str, str, str]:
     return bt, mt, nt
 
 
+def _emit_zero_slices(p: Ptx, cfg: GemmConfig, cptr: str, tid: str, nthreads: int) -> None:
+    """Split-K partial slices 1 .. zero_slots of C (the whole product goes to slice 0) are
+    one contiguous range; every thread of the grid zeroes part of it with coalesced
+    stores before the roles start (16-byte stores when the slices are whole float4s)."""
+    w = 4 if cfg.slot_stride % 4 == 0 else 1
+    units = cfg.zero_slots * cfg.slot_stride // w
+    gi, gs, a = p.reg("u32"), p.reg("u32"), p.reg("b64")
+    pz = p.reg("pred")
+    top, done = p.label("zero_slices"), p.label("zero_done")
+    zero = "{0f00000000, 0f00000000, 0f00000000, 0f00000000}" if w == 4 else "0f00000000"
+    p.emit(f"""
+        mov.u32 {gi}, %ctaid.x
+        mad.lo.u32 {gi}, {gi}, {nthreads}, {tid}
+        mov.u32 {gs}, %nctaid.x
+        mul.lo.u32 {gs}, {gs}, {nthreads}
+    """)
+    p.place(top)
+    p.emit(f"""
+        setp.ge.u32 {pz}, {gi}, {units}
+        @{pz} bra {done}
+        mul.wide.u32 {a}, {gi}, {4 * w}
+        add.s64 {a}, {a}, {cptr}
+        st.global{'.v4' if w == 4 else ''}.f32 [{a}+{cfg.slot_stride * 4}], {zero}
+        add.u32 {gi}, {gi}, {gs}
+        bra {top}
+    """)
+    p.place(done)
+
+
 def emit_gemm_module(cfg: GemmConfig) -> str:
     p = Ptx()
     split, conv = cfg.split3, cfg.converts
@@ -232,6 +261,8 @@ def emit_gemm_module(cfg: GemmConfig) -> str:
         shr.u32 {warp}, {tid}, 5
         and.b32 {lane}, {tid}, 31
     """)
+    if cfg.zero_slots:
+        _emit_zero_slices(p, cfg, ptr[cfg.c_param], tid, GEMM_THREADS + (CONV_THREADS if conv else 0))
     ring, bars, abort, tslot = p.reg("u32"), p.reg("u32"), p.reg("u32"), p.reg("u32")
     p.emit(f"""
         mov.u32 {ring}, dsmem
@@ -950,8 +981,6 @@ def _emit_epilogue(p: Ptx, cfg: GemmConfig, ptr: dict, bars, tfull0, tempty0, tb
         res_adr[name] = a
     nchunks = BN // 32
     regs = [p.reg("b32") for _ in range(32)]
-    zf = p.reg("f32")
-    p.emit(f"mov.f32 {zf}, 0f00000000")
     if cfg.zero_slots and cfg.c != "f32":
         raise NotImplementedError("split-K partial slices other than f32")
     for ch in range(nchunks):
@@ -990,9 +1019,6 @@ def _emit_epilogue(p: Ptx, cfg: GemmConfig, ptr: dict, bars, tfull0, tempty0, tb
                 p.emit(f"add.u32 {colr}, {n0}, {col0 + 4 * g}\nsetp.lt.u32 {pg}, {colr}, {N}")
                 p.emit(f"@{pg} st.global.v4.f32 [{cadr}+{(col0 + 4 * g) * 4}], "
                        f"{{{', '.join(vals[4 * g:4 * g + 4])}}}")
-                for sl in range(1, cfg.zero_slots + 1):
-                    p.emit(f"@{pg} st.global.v4.f32 [{cadr}+{(sl * cfg.slot_stride + col0 + 4 * g) * 4}], "
-                           f"{{{zf}, {zf}, {zf}, {zf}}}")
         elif cfg.c == "f64":
             if cfg.zero_slots:
                 raise NotImplementedError("split-K partial slices other than f32")
@@ -1006,8 +1032,6 @@ def _emit_epilogue(p: Ptx, cfg: GemmConfig, ptr: dict, bars, tfull0, tempty0, tb
                 p.emit(f"add.u32 {colr}, {n0}, {col0 + i}\nsetp.lt.u32 {pg}, {colr}, {N}")
                 if cfg.c == "f32":
                     p.emit(f"@{pg} st.global.f32 [{cadr}+{(col0 + i) * 4}], {vals[i]}")
-                    for sl in range(1, cfg.zero_slots + 1):
-                        p.emit(f"@{pg} st.global.f32 [{cadr}+{(sl * cfg.slot_stride + col0 + i) * 4}], {zf}")
                 else:
                     h = p.reg("b16")
                     cvt = "cvt.rn.bf16.f32" if cfg.c == "bf16" else "cvt.rn.f16.f32"
