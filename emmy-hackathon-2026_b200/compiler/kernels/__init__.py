@@ -28,8 +28,12 @@ def select(spec) -> str:
         except NotImplementedError as err:
             # two contractions in one kernel (a shared-A pair, or a chain through an A
             # tile computed in the kernel): an element map of the same arithmetic
-            from .fused import chained_gemm_spec, dual_gemm_spec
+            from .fused import chained_gemm_spec, dual_gemm_spec, emit_chained_rows
             from .pointwise import emit_map
+            try:
+                return emit_chained_rows(spec)
+            except NotImplementedError:
+                pass
             for synth in (dual_gemm_spec, chained_gemm_spec):
                 try:
                     return emit_map(synth(spec))

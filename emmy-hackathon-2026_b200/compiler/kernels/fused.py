@@ -104,6 +104,33 @@ def chained_gemm_spec(spec):
     """``out = g(H) W2`` with ``H = f(x W1)`` computed in the kernel: the shared A tile of
     the MMAs is written from values computed from a dot product of two global buffers.  The
     first written value's statements (back to its accumulator) are the per-element f."""
+    X, W1, W2, O, a0, chain, hname = chained_parts(spec)
+    M, K1 = X.shape
+    J, N = W1.shape[1], W2.shape[1]
+    f32 = _DT["f32"]
+    inner = (f"Loop(axis=Axis(name='k', extent=Dim({K1}), window=None), body=("
+             f"Load(names=('_x',), input='{X.name}', index=(Var(name='i'), Var(name='k')), dtype=None), "
+             f"Load(names=('_w1',), input='{W1.name}', index=(Var(name='k'), Var(name='j')), dtype=None), "
+             f"Assign(name='_p1', op=ElementwiseImpl('multiply'), args=('_x', '_w1'), dtype={f32}), "
+             f"Accum(name='{a0}', value='_p1', op=ElementwiseImpl('add'), dtype={f32}, axes=('k',), "
+             f"base=None)), unroll=False, seed=True)")
+    tail = (f"Load(names=('_w2',), input='{W2.name}', index=(Var(name='j'), Var(name='n')), dtype=None), "
+            f"Assign(name='_p2', op=ElementwiseImpl('multiply'), args=('{hname}', '_w2'), dtype={f32}), "
+            f"Accum(name='_acc2', value='_p2', op=ElementwiseImpl('add'), dtype={f32}, axes=('j',), base=None)")
+    outer = parse_stmt(f"Loop(axis=Axis(name='j', extent=Dim({J}), window=None), body=({inner}, {tail}), "
+                       f"unroll=False, seed=True)")
+    # H's own statements (16-bit rounding, the activation) between the two contractions
+    outer = replace(outer, body=(outer.body[0],) + tuple(chain) + outer.body[1:])
+    tile = _tile([("i", M), ("n", N)], "Let(name='_unused', value=Literal(value=0, dtype='int'), dtype=None)")
+    write = parse_stmt(f"Write(output='{O.name}', index=(Var(name='i'), Var(name='n')), values=('_acc2',), "
+                       f"value_dtype={_DT[O.dtype]}, atomic=False, swizzle='NONE')")
+    tile = replace(tile, body=(outer, write))
+    return replace(spec, body=(tile,))
+
+
+def chained_parts(spec):
+    """(x, W1, W2, out, H's accumulator name, H's statements in program order, H's name)
+    of a chained GEMM; NotImplementedError for anything else."""
     stmts = list(_walk(spec.body))
     src = _sources(stmts, spec)
     mmas = [x for x in stmts if type(x).__name__ == "MmaSyncPtx"]
@@ -170,25 +197,114 @@ def chained_gemm_spec(spec):
     if tuple(W1.shape[:1]) != (K1,) or len(W1.shape) != 2 or W2.shape[0] != W1.shape[1] or \
             tuple(O.shape) != (M, W2.shape[1]) or O.dtype not in _DT:
         raise NotImplementedError("chained GEMM shapes")
+    chain = sorted(chain, key=lambda d: order[id(d)])
+    return X, W1, W2, O, a0.name, chain, writes[0].values[0]
+
+
+ROW_THREADS = 256
+_LD_BATCH = 16
+
+
+def emit_chained_rows(spec) -> str:
+    """The chained GEMM ``out = g(f(x W1)) W2`` as one CTA per output row: x's row is staged
+    in shared memory; thread j computes ``H[j] = f(x_row . W1[:, j])`` (W1 read along its
+    rows, coalesced across the threads) with the IR's own statements for f (16-bit rounding,
+    the activation) and writes it to shared memory; after one barrier thread n computes
+    ``out[n] = H . W2[:, n]``.  Each H row is computed once instead of once per output
+    element.  Products of 16-bit values are exact in f32 (the MMA's), sums in f32 in index
+    order; loads issue 16 deep.  Contractions are unrolled in full, so K and J are capped
+    (larger chains stay element maps)."""
+    from ..ptx import Ptx, entry, module
+    from ..stmts import ScalarCtx, Val, load_index_vars, lower_body, matmul_kernel
+    from .common import arg_params, load_pointer
+    X, W1, W2, O, a0, chain, hname = chained_parts(spec)
+    M, K = X.shape
     J, N = W1.shape[1], W2.shape[1]
-    f32 = _DT["f32"]
-    hname = writes[0].values[0]
-    inner = (f"Loop(axis=Axis(name='k', extent=Dim({K1}), window=None), body=("
-             f"Load(names=('_x',), input='{X.name}', index=(Var(name='i'), Var(name='k')), dtype=None), "
-             f"Load(names=('_w1',), input='{W1.name}', index=(Var(name='k'), Var(name='j')), dtype=None), "
-             f"Assign(name='_p1', op=ElementwiseImpl('multiply'), args=('_x', '_w1'), dtype={f32}), "
-             f"Accum(name='{a0.name}', value='_p1', op=ElementwiseImpl('add'), dtype={f32}, axes=('k',), "
-             f"base=None)), unroll=False, seed=True)")
-    tail = (f"Load(names=('_w2',), input='{W2.name}', index=(Var(name='j'), Var(name='n')), dtype=None), "
-            f"Assign(name='_p2', op=ElementwiseImpl('multiply'), args=('{hname}', '_w2'), dtype={f32}), "
-            f"Accum(name='_acc2', value='_p2', op=ElementwiseImpl('add'), dtype={f32}, axes=('j',), base=None)")
-    outer = parse_stmt(f"Loop(axis=Axis(name='j', extent=Dim({J}), window=None), body=({inner}, {tail}), "
-                       f"unroll=False, seed=True)")
-    # H's own statements (16-bit rounding, the activation) between the two contractions
-    outer = replace(outer, body=(outer.body[0],) + tuple(sorted(chain, key=lambda d: order[id(d)]))
-                    + outer.body[1:])
-    tile = _tile([("i", M), ("n", N)], "Let(name='_unused', value=Literal(value=0, dtype='int'), dtype=None)")
-    write = parse_stmt(f"Write(output='{O.name}', index=(Var(name='i'), Var(name='n')), values=('_acc2',), "
-                       f"value_dtype={_DT[O.dtype]}, atomic=False, swizzle='NONE')")
-    tile = replace(tile, body=(outer, write))
-    return replace(spec, body=(tile,))
+    if K > 1024 or J > 1024 or any(b.dtype not in _DT for b in (X, W1, W2)):
+        raise NotImplementedError("chained GEMM: contraction above 1024 or operand type")
+    T = ROW_THREADS
+    p = Ptx()
+    p.comment(f"chained GEMM {M}x{K} . {K}x{J} -> f -> . {J}x{N}, one CTA per row")
+    ptr = {b.name: load_pointer(p, b.name) for b in (X, W1, W2, O)}
+    row, tid = p.reg("u32"), p.reg("u32")
+    xs, hs = p.reg("u32"), p.reg("u32")
+    p.emit(f"mov.u32 {row}, %ctaid.x\nmov.u32 {tid}, %tid.x\nmov.u32 {xs}, chain_xs\nmov.u32 {hs}, chain_hs")
+
+    def load(buf, addr, dst):
+        if buf.dtype == "f32":
+            p.emit(f"ld.global.nc.f32 {dst}, [{addr}]")
+        else:
+            h = p.reg("b16")
+            p.emit(f"ld.global.nc.b16 {h}, [{addr}]\ncvt.f32.{buf.dtype} {dst}, {h}")
+
+    def eb(buf):
+        return 4 if buf.dtype == "f32" else 2
+
+    # x's row -> shared (f32)
+    for it in range(-(-K // T)):
+        k, pk, a = p.reg("u32"), p.reg("pred"), p.reg("b64")
+        v = p.reg("f32")
+        skip = p.label("xs_skip")
+        p.emit(f"add.u32 {k}, {tid}, {it * T}\nsetp.ge.u32 {pk}, {k}, {K}\n@{pk} bra {skip}")
+        p.emit(f"mad.lo.u32 {k}, {row}, {K}, {k}\nmul.wide.u32 {a}, {k}, {eb(X)}\nadd.s64 {a}, {ptr[X.name]}, {a}")
+        load(X, a, v)
+        sa = p.reg("u32")
+        p.emit(f"add.u32 {sa}, {tid}, {it * T}\nshl.b32 {sa}, {sa}, 2\nadd.u32 {sa}, {sa}, {xs}\nst.shared.f32 [{sa}], {v}")
+        p.place(skip)
+    p.emit("bar.sync 0")
+
+    def dot(n_terms, lhs_smem, col_reg, buf, ncols):
+        """sum_t lhs[t] * buf[t, col] over t < n_terms, loads 16 deep; returns the f32 sum."""
+        acc = p.reg("f32")
+        p.emit(f"mov.f32 {acc}, 0f00000000")
+        base = p.reg("b64")
+        p.emit(f"mul.wide.u32 {base}, {col_reg}, {eb(buf)}\nadd.s64 {base}, {ptr[buf.name]}, {base}")
+        for t0 in range(0, n_terms, _LD_BATCH):
+            ts = range(t0, min(n_terms, t0 + _LD_BATCH))
+            vals = {}
+            for t in ts:
+                vals[t] = p.reg("f32")
+                load(buf, f"{base}+{t * ncols * eb(buf)}", vals[t])
+            for t in ts:
+                lv = p.reg("f32")
+                p.emit(f"ld.shared.f32 {lv}, [{lhs_smem}+{4 * t}]\nfma.rn.f32 {acc}, {lv}, {vals[t]}, {acc}")
+        return acc
+
+    ctx = ScalarCtx(p, constants=dict(spec.constants), half_results=True,
+                    exact_products=matmul_kernel(spec.name), index_vars=load_index_vars(spec.body),
+                    const_dtypes={q.name: q.dtype for q in spec.params})
+    for it in range(-(-J // T)):
+        j, pj = p.reg("u32"), p.reg("pred")
+        skip = p.label("h_skip")
+        p.emit(f"add.u32 {j}, {tid}, {it * T}\nsetp.ge.u32 {pj}, {j}, {J}\n@{pj} bra {skip}")
+        acc = dot(K, xs, j, W1, J)
+        saved = dict(ctx.env)
+        ctx.env[a0] = Val(acc, "f32")
+        try:
+            lower_body(ctx, chain)
+            h = ctx.f32(hname)
+        except ValueError as err:      # H's statements read something other than the dot product
+            raise NotImplementedError(f"chained GEMM: {err}") from None
+        ctx.env = saved
+        sa = p.reg("u32")
+        p.emit(f"shl.b32 {sa}, {j}, 2\nadd.u32 {sa}, {sa}, {hs}\nst.shared.f32 [{sa}], {h}")
+        p.place(skip)
+    p.emit("bar.sync 0")
+    for it in range(-(-N // T)):
+        n, pn = p.reg("u32"), p.reg("pred")
+        skip = p.label("o_skip")
+        p.emit(f"add.u32 {n}, {tid}, {it * T}\nsetp.ge.u32 {pn}, {n}, {N}\n@{pn} bra {skip}")
+        acc = dot(J, hs, n, W2, N)
+        a, off = p.reg("b64"), p.reg("u32")
+        p.emit(f"mad.lo.u32 {off}, {row}, {N}, {n}\nmul.wide.u32 {a}, {off}, {eb(O)}\nadd.s64 {a}, {ptr[O.name]}, {a}")
+        if O.dtype == "f32":
+            p.emit(f"st.global.f32 [{a}], {acc}")
+        else:
+            h = p.reg("b16")
+            p.emit(f"cvt.rn.{O.dtype}.f32 {h}, {acc}\nst.global.b16 [{a}], {h}")
+        p.place(skip)
+    p.emit("ret")
+    launch = {"kind": "chained_rows", "grid": [M, 1, 1], "block": [T, 1, 1], "cluster": [1, 1, 1],
+              "smem": 0, "extra_params": [], "flops": 2 * M * J * (K + N)}
+    return module([entry(spec.name, arg_params(spec), p, maxntid=T)], launch,
+                  globals_=[f".shared .align 16 .f32 chain_xs[{K}];", f".shared .align 16 .f32 chain_hs[{J}];"])
