@@ -198,6 +198,34 @@ def analyze(spec) -> F32AttnConfig:
         const = float(sd.value.value)
     else:
         raise NotImplementedError("scale is not a constant or a 1-element buffer")
+    # the scaled score feeds the online softmax and nothing else: the running maximum and
+    # the differences taken against it (a softcap, a bias or a mask in between would sit
+    # here, and this template does not compute them)
+    scaled_names = {s.name for s in scaled}
+    for s, _ in walk:
+        k = type(s).__name__
+        uses = set(s.args) if k == "Assign" else {s.value} if k == "Accum" else set()
+        if uses & scaled_names:
+            if not ((k == "Assign" and s.op.name in ("maximum", "subtract")) or
+                    (k == "Accum" and s.op.name == "maximum")):
+                raise NotImplementedError(f"the scaled score also feeds {s.op.name}")
+    # every written value is (sum of p v) * 1 / (sum of p), both accumulated over the keys
+    key_sums = {s.name for s, _ in walk if type(s).__name__ == "Accum" and s.op.name == "add"
+                and key in (s.axes or ())}
+    for w, _ in ((s, l) for s, l in walk if type(s).__name__ == "Write"):
+        for val in w.values:
+            d = defs.get(val)
+            if type(d).__name__ != "Assign" or d.op.name != "multiply" or len(d.args) != 2:
+                raise NotImplementedError("output is not a normalised sum")
+            a, b = (defs.get(x) for x in d.args)
+            if type(b).__name__ == "Assign" and b.op.name == "reciprocal":
+                num, den = d.args[0], b.args[0]
+            elif type(a).__name__ == "Assign" and a.op.name == "reciprocal":
+                num, den = d.args[1], a.args[0]
+            else:
+                raise NotImplementedError("output is not a normalised sum")
+            if num not in key_sums or den not in key_sums:
+                raise NotImplementedError("output is not a normalised sum")
     # guards only: no condition may look at the key or reduction axis (a mask would)
     for s, _ in walk:
         if type(s).__name__ == "Cond" and expr_vars(s.cond) & {key, red}:

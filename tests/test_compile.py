@@ -166,6 +166,27 @@ def test_f32_attention_recognizer():
                 analyze(load(ir))
 
 
+def test_f32_attention_rejects_score_transforms():
+    """A softcap between the scaled score and the softmax (planted into a01's statements)
+    is not computed by the template, so the recogniser must hand the kernel back."""
+    from dataclasses import replace
+    from compiler.kernels.attention_f32 import analyze
+    spec = load(next((GOLDEN / "a01_attention").glob("*.ir.json")))
+
+    def plant(body):
+        out = []
+        for x in body:
+            if type(x).__name__ == "Assign" and x.name == "v4__gn__c0_0":
+                out.append(parse_stmt("Assign(name='tc', op=ElementwiseImpl('tanh'), args=('v4__c0_0',), "
+                                      "dtype=None)"))
+                x = replace(x, args=("acc1__c0_0", "tc"))
+            sub = getattr(x, "body", None)
+            out.append(replace(x, body=plant(sub)) if isinstance(sub, tuple) else x)
+        return tuple(out)
+    with pytest.raises(NotImplementedError, match="tanh"):
+        analyze(replace(spec, body=plant(spec.body)))
+
+
 @pytest.mark.parametrize("pid,mnk,batch,a,b,epi", [
     ("m01_matmul_512", (512, 512, 512), 1, "x0", "x1", None),
     ("m02_matmul_rect", (128, 64, 256), 1, "x0", "x1", None),      # split-K atomics: one pass
