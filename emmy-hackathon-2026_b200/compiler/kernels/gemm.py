@@ -65,6 +65,7 @@ class GemmConfig:
     buffers: tuple = ()              # pointer params to load (name list) for IR kernels
     pair: bool = False               # CTA pair (cta_group::2): 256-row tiles, B split by column
     operand_dtypes: tuple = ()       # (buffer, dtype) of epilogue operands
+    ksplit: int = 0                  # K slices per tile (0: chosen from the shape; 1: none)
     zero_slots: int = 0              # split-K partials: the full product goes to slice 0 of C and
     slot_stride: int = 0             # these many further slices (slot_stride elements apart) are zeroed
     operand_round: str | None = None  # f32 operands cast to "bf16" / "f16" before the product: one
@@ -143,8 +144,13 @@ def choose_tiling(M: int, N: int, batch: int, min_bn: int = 64, pairs: bool = Tr
     return best
 
 
-def _tile_coords(p: Ptx, cfg: GemmConfig, t: str) -> tuple[str, str, str]:
-    """Grouped raster: tile index -> (batch, m tile, n tile), all u32 registers."""
+def _tile_coords(p: Ptx, cfg: GemmConfig, t: str, ks: int = 1) -> tuple[str, str, str]:
+    """Grouped raster: tile index -> (batch, m tile, n tile), all u32 registers.  With
+    ``ks`` K slices per tile, ``t`` is a work unit: tile t / ks, slice t % ks."""
+    if ks > 1:
+        tt = p.reg("u32")
+        p.emit(f"div.u32 {tt}, {t}, {ks}")
+        t = tt
     tm, tn = cfg.tiles
     per_batch = tm * tn
     gsz = cfg.group_m * tn
@@ -162,6 +168,25 @@ def _tile_coords(p: Ptx, cfg: GemmConfig, t: str) -> tuple[str, str, str]:
         div.u32 {nt}, {w}, {gm}
     """)
     return bt, mt, nt
+
+
+def choose_ksplit(cfg: GemmConfig, ntiles: int, kblocks: int, pair: bool) -> int:
+    """K slices per tile when the tiles alone leave most SMs idle.  Splitting adds a fixed
+    chain of about 5 us (the partial's stores, a GPU-scope fence, the ticket, the last
+    slice's L2 reads), so it is taken only where it removes at least 8 K stages from the
+    critical path of the converter-fed kernels (3xTF32 / direct loads, ~0.75 us a stage;
+    a 16-bit TMA stage is ~0.15 us and never gains on B200, measured): the largest power of
+    two that keeps the units within one wave, at least four K blocks per unit, and the
+    last slice's reduction read (slices x one f32 tile) within 512 KB."""
+    if cfg.ksplit:
+        return cfg.ksplit
+    if pair or cfg.zero_slots or not cfg.converts or 2 * ntiles > SMS:
+        return 1
+    ks = 1
+    while (ntiles * ks * 2 <= SMS and kblocks % (ks * 2) == 0 and kblocks // (ks * 2) >= 4
+           and ks * 2 * cfg.MT * cfg.BN * 4 <= 512 * 1024):
+        ks *= 2
+    return ks if kblocks - kblocks // ks >= 8 else 1
 
 
 def _emit_zero_slices(p: Ptx, cfg: GemmConfig, cptr: str, tid: str, nthreads: int) -> None:
@@ -203,6 +228,10 @@ def emit_gemm_module(cfg: GemmConfig) -> str:
     ntiles = cfg.batch * tm * tn
     kblocks = -(-K // BK)
     pair = cfg.pair
+    KS = choose_ksplit(cfg, ntiles, kblocks, pair)
+    if KS > 1 and (pair or kblocks % KS):
+        raise NotImplementedError("K slices need 1-CTA tiles and whole K blocks per slice")
+    kps, nunits = kblocks // KS, ntiles * KS
     BNc = BN // 2 if pair else BN           # B columns held by one CTA
     a_bytes = BM * BK * eb                  # 16 KB
     b_bytes = BNc * BK * eb                 # 32 KB at BN = 256 (16 KB per CTA of a pair)
@@ -345,8 +374,10 @@ def emit_gemm_module(cfg: GemmConfig) -> str:
     tl, td = p.label("p_tile"), p.label("p_done")
     p.place(tl)
     pt = p.reg("pred")
-    p.emit(f"setp.ge.u32 {pt}, {t}, {ntiles}\n@{pt} bra {td}")
-    bt, mt, nt = _tile_coords(p, cfg, t)
+    p.emit(f"setp.ge.u32 {pt}, {t}, {nunits}\n@{pt} bra {td}")
+    bt, mt, nt = _tile_coords(p, cfg, t, KS)
+    kb0 = p.reg("u32")         # the unit's first K block
+    p.emit(f"rem.u32 {kb0}, {t}, {KS}\nmul.lo.u32 {kb0}, {kb0}, {kps}")
     m0, n0 = p.reg("u32"), p.reg("u32")
     p.emit(f"mul.lo.u32 {m0}, {mt}, {cfg.MT}\nmul.lo.u32 {n0}, {nt}, {BN}")
     if pair:    # this CTA's rows of the 256-row tile and its half of the B columns
@@ -378,7 +409,8 @@ def emit_gemm_module(cfg: GemmConfig) -> str:
     p.emit(f"""
         mad.lo.u32 {sa}, {s}, {stage_bytes}, {ring}
         add.u32 {sbb}, {sa}, {a_bytes}
-        mul.lo.u32 {kx}, {kb}, {BK}
+        add.u32 {kx}, {kb}, {kb0}
+        mul.lo.u32 {kx}, {kx}, {BK}
     """)
     zc = f", {bt}" if rank == 3 else ""
     p.emit(f"{tma} [{sa}], [{tma_a}, {{{kx}, {m0}{zc}}}], [{faddr}]")
@@ -397,7 +429,7 @@ def emit_gemm_module(cfg: GemmConfig) -> str:
         @{ps} mov.u32 {s}, 0
         @{ps} xor.b32 {ph}, {ph}, 1
         add.u32 {kb}, {kb}, 1
-        setp.lt.u32 {ps}, {kb}, {kblocks}
+        setp.lt.u32 {ps}, {kb}, {kps}
         @{ps} bra {kl}
         add.u32 {t}, {t}, {nct}
         bra {tl}
@@ -421,7 +453,7 @@ def emit_gemm_module(cfg: GemmConfig) -> str:
     p.emit(f"mov.u32 {t2}, {cta}\nmov.u32 {s2}, 0\nmov.u32 {ph2}, 0\nmov.u32 {tc}, 0")
     ml, md = p.label("m_tile"), p.label("m_done")
     p.place(ml)
-    p.emit(f"setp.ge.u32 {pt}, {t2}, {ntiles}\n@{pt} bra {md}")
+    p.emit(f"setp.ge.u32 {pt}, {t2}, {nunits}\n@{pt} bra {md}")
     ab, aph, tea, tfa, dt = p.reg("u32"), p.reg("u32"), p.reg("u32"), p.reg("u32"), p.reg("u32")
     p.emit(f"""
         rem.u32 {ab}, {tc}, {cfg.acc_bufs}
@@ -479,7 +511,7 @@ def emit_gemm_module(cfg: GemmConfig) -> str:
         @{ps} mov.u32 {s2}, 0
         @{ps} xor.b32 {ph2}, {ph2}, 1
         add.u32 {kb2}, {kb2}, 1
-        setp.lt.u32 {ps}, {kb2}, {kblocks}
+        setp.lt.u32 {ps}, {kb2}, {kps}
         @{ps} bra {mk}
         {commit.format(a=tfa)}
         add.u32 {tc}, {tc}, 1
@@ -494,16 +526,16 @@ def emit_gemm_module(cfg: GemmConfig) -> str:
     if conv:
         role_conv = p.label("role_conv")
         p.emit(f"setp.ge.u32 {pr}, {warp}, {GEMM_THREADS // 32}\n@{pr} bra {role_conv}")
-    _emit_epilogue(p, cfg, ptr, bars, tfull0, tempty0, tbase, warp, lane, cta, nct, ntiles,
-                   waits, finish, crank if pair else None, ltempty if pair else None)
+    _emit_epilogue(p, cfg, ptr, bars, tfull0, tempty0, tbase, warp, lane, cta, nct, nunits,
+                   waits, finish, crank if pair else None, ltempty if pair else None, KS)
     if conv:
         p.place(role_conv)
         if direct:
             _emit_direct_loader(p, cfg, ptr, tid, ring, bars, empty0, conv0, a_bytes, raw_bytes,
-                                stage_bytes, kblocks, cta, nct, ntiles, waits, finish)
+                                stage_bytes, kps, cta, nct, nunits, waits, finish, KS)
         else:
             _emit_split_tf32(p, cfg, tid, ring, bars, full0, conv0, cread, a_bytes, raw_bytes,
-                             stage_bytes, kblocks, cta, nct, ntiles, waits, finish)
+                             stage_bytes, kps, cta, nct, nunits, waits, finish)
 
     # -------------------------------------------------------------- finish
     p.place(finish)
@@ -528,13 +560,15 @@ def emit_gemm_module(cfg: GemmConfig) -> str:
     params = list(cfg.arg_params or [f".param .u64 {param_symbol(n)}" for n in cfg.buffers])
     if not direct:
         params += [".param .align 64 .b8 param__tmap_a[128]", ".param .align 64 .b8 param__tmap_b[128]"]
+    if KS > 1:
+        params += [".param .u64 param__ksplit_ws", ".param .u64 param__ksplit_tickets"]
     params += [".param .u64 param__status"]
     nthreads = GEMM_THREADS + (CONV_THREADS if conv else 0)
     text = entry(cfg.name, params, p, maxntid=nthreads)
     statics = (f"\t.shared .align 8 .b64 gbars[{nbar}];\n\t.shared .align 4 .u32 gabort;\n"
                f"\t.shared .align 4 .u32 gtmem;\n")
     text = text.replace("{\n", "{\n" + statics, 1)
-    grid = 2 * min(ntiles, SMS // 2) if pair else min(ntiles, SMS)
+    grid = 2 * min(ntiles, SMS // 2) if pair else min(nunits, SMS)
     a_dims = [K, M] + ([cfg.batch] if rank == 3 else [])
     a_str = [K * eb] + ([M * K * eb] if rank == 3 else [])
     if cfg.b_kmajor:
@@ -547,13 +581,14 @@ def emit_gemm_module(cfg: GemmConfig) -> str:
         b_box = [128 // eb, BK] + ([1] if rank == 3 else [])
     launch = {
         "kind": "gemm", "grid": [grid, 1, 1], "block": [nthreads, 1, 1], "cluster": [2 if pair else 1, 1, 1],
-        "smem": smem, "flops": 2 * cfg.batch * M * N * K, "tiles": ntiles,
+        "smem": smem, "flops": 2 * cfg.batch * M * N * K, "tiles": ntiles, "ksplit": KS,
         "extra_params": ([] if direct else [
             {"kind": "tmap", "buffer": cfg.a_param, "dtype": cfg.ab, "dims": a_dims, "strides": a_str,
              "box": [BK, BM] + ([1] if rank == 3 else []), "swizzle": 128},
             {"kind": "tmap", "buffer": cfg.b_param, "dtype": cfg.ab, "dims": b_dims, "strides": b_str,
              "box": b_box, "swizzle": 128},
-        ]) + [{"kind": "status"}],
+        ]) + ([{"kind": "scratch", "bytes": nunits * cfg.MT * BN * 4},
+               {"kind": "scratch", "bytes": ntiles * 4 * 4}] if KS > 1 else []) + [{"kind": "status"}],
     }
     return module([text], launch, globals_=[".extern .shared .align 1024 .b8 dsmem[];"])
 
@@ -721,7 +756,7 @@ def _emit_split_tf32(p: Ptx, cfg: GemmConfig, tid, ring, bars, full0, conv0, cre
 
 
 def _emit_direct_loader(p: Ptx, cfg: GemmConfig, ptr: dict, tid, ring, bars, empty0, conv0, a_bytes,
-                        raw_bytes, stage_bytes, kblocks, cta, nct, ntiles, waits: Waits, finish: str) -> None:
+                        raw_bytes, stage_bytes, kblocks, cta, nct, ntiles, waits: Waits, finish: str, ks: int = 1) -> None:
     """Converter warps that fetch the operands from global memory themselves (no TMA): for
     rows that are not 16-byte aligned (emmy's odd-shaped fixtures), 16-bit sources (widened
     exactly) and mixed operand types.  Per stage each of the 128 threads loads its
@@ -773,9 +808,10 @@ def _emit_direct_loader(p: Ptx, cfg: GemmConfig, ptr: dict, tid, ring, bars, emp
     pt, ps = p.reg("pred"), p.reg("pred")
     p.place(tl)
     p.emit(f"setp.ge.u32 {pt}, {t}, {ntiles}\n@{pt} bra {finish}\nmov.u32 {kb}, 0")
-    bt, mt, nt = _tile_coords(p, cfg, t)
-    m0, n0 = p.reg("u32"), p.reg("u32")
-    p.emit(f"mul.lo.u32 {m0}, {mt}, {cfg.MT}\nmul.lo.u32 {n0}, {nt}, {BN}")
+    bt, mt, nt = _tile_coords(p, cfg, t, ks)
+    m0, n0, kb0 = p.reg("u32"), p.reg("u32"), p.reg("u32")
+    p.emit(f"mul.lo.u32 {m0}, {mt}, {cfg.MT}\nmul.lo.u32 {n0}, {nt}, {BN}\n"
+           f"rem.u32 {kb0}, {t}, {ks}\nmul.lo.u32 {kb0}, {kb0}, {kblocks}")
     p.place(kl)
     ea_, ca, par, base, k0 = (p.reg("u32") for _ in range(5))
     p.emit(f"""
@@ -783,7 +819,8 @@ def _emit_direct_loader(p: Ptx, cfg: GemmConfig, ptr: dict, tid, ring, bars, emp
         add.u32 {ca}, {ea_}, {conv0}
         add.u32 {ea_}, {ea_}, {empty0}
         xor.b32 {par}, {ph}, 1
-        mul.lo.u32 {k0}, {kb}, 32
+        add.u32 {k0}, {kb}, {kb0}
+        mul.lo.u32 {k0}, {k0}, 32
     """)
     waits.wait(ea_, par, "convert", finish)
     p.emit(f"mad.lo.u32 {base}, {s}, {stage_bytes}, {ring}")
@@ -901,7 +938,12 @@ def _emit_direct_loader(p: Ptx, cfg: GemmConfig, ptr: dict, tid, ring, bars, emp
 
 
 def _emit_epilogue(p: Ptx, cfg: GemmConfig, ptr: dict, bars, tfull0, tempty0, tbase, warp, lane,
-                   cta, nct, ntiles, waits: Waits, finish: str, crank=None, ltempty=None) -> None:
+                   cta, nct, ntiles, waits: Waits, finish: str, crank=None, ltempty=None,
+                   ks: int = 1) -> None:
+    """TMEM accumulator -> fused epilogue ops -> C, one thread per row.  With ``ks`` K slices
+    per tile, each unit first writes its f32 partial to a workspace; per warp quarter of the
+    tile a ticket counts the slices in, and the warp that takes the last one sums the
+    slices in slice order (deterministic), applies the epilogue and writes C."""
     M, N, BM, BN = cfg.M, cfg.N, cfg.BM, cfg.BN
     cb = ELEM_BYTES[cfg.c]
     q, row_t = p.reg("u32"), p.reg("u32")
@@ -941,7 +983,7 @@ def _emit_epilogue(p: Ptx, cfg: GemmConfig, ptr: dict, bars, tfull0, tempty0, tb
     """)
     waits.wait(tfa, aph, "epilogue", finish)
     p.emit("bar.warp.sync -1\ntcgen05.fence::after_thread_sync")
-    bt, mt, nt = _tile_coords(p, cfg, t)
+    bt, mt, nt = _tile_coords(p, cfg, t, ks)
     row, n0, taddr = p.reg("u32"), p.reg("u32"), p.reg("u32")
     prow = p.reg("pred")
     if crank is not None:   # the CTA's 128 rows of the pair's 256-row tile
@@ -983,7 +1025,7 @@ def _emit_epilogue(p: Ptx, cfg: GemmConfig, ptr: dict, bars, tfull0, tempty0, tb
     regs = [p.reg("b32") for _ in range(32)]
     if cfg.zero_slots and cfg.c != "f32":
         raise NotImplementedError("split-K partial slices other than f32")
-    for ch in range(nchunks):
+    def load_chunk(ch):
         p.emit(f"tcgen05.ld.sync.aligned.32x32b.x32.b32 {{{', '.join(regs)}}}, [{taddr}+{ch * 32}]")
         p.emit("tcgen05.wait::ld.sync.aligned")
         if ch == nchunks - 1:
@@ -994,9 +1036,8 @@ def _emit_epilogue(p: Ptx, cfg: GemmConfig, ptr: dict, bars, tfull0, tempty0, tb
                        f"mbarrier.arrive.release.cluster.shared::cluster.b64 _, [{ra}]")
             else:
                 p.emit(f"tcgen05.fence::before_thread_sync\nmbarrier.arrive.shared::cta.b64 _, [{tea}]")
-        vals = [p.reg("f32") for _ in range(32)]
-        for i in range(32):
-            p.emit(f"mov.b32 {vals[i]}, {regs[i]}")
+
+    def store_chunk(ch, vals):
         vals = _apply_epilogue(p, cfg, vals, scale, res_adr, ch, prow, n0)
         skip = p.label("st_skip")
         col0 = ch * 32
@@ -1037,6 +1078,21 @@ def _emit_epilogue(p: Ptx, cfg: GemmConfig, ptr: dict, bars, tfull0, tempty0, tb
                     cvt = "cvt.rn.bf16.f32" if cfg.c == "bf16" else "cvt.rn.f16.f32"
                     p.emit(f"{cvt} {h}, {vals[i]}\n@{pg} st.global.b16 [{cadr}+{(col0 + i) * 2}], {h}")
         p.place(skip)
+
+    if ks > 1:
+        l_next = _emit_ksplit_partial(p, cfg, ks, t, row_t, lane, q, regs, nchunks, load_chunk)
+        for ch in range(nchunks):
+            store_chunk(ch, _ksplit_sum(p, cfg, ks, t, row_t, ch))
+    else:
+        l_next = None
+        for ch in range(nchunks):
+            load_chunk(ch)
+            vals = [p.reg("f32") for _ in range(32)]
+            for i in range(32):
+                p.emit(f"mov.b32 {vals[i]}, {regs[i]}")
+            store_chunk(ch, vals)
+    if l_next is not None:
+        p.place(l_next)
     p.emit(f"""
         add.u32 {tc}, {tc}, 1
         add.u32 {t}, {t}, {nct}
@@ -1044,6 +1100,69 @@ def _emit_epilogue(p: Ptx, cfg: GemmConfig, ptr: dict, bars, tfull0, tempty0, tb
     """)
     p.place(ed)
     p.emit(f"bra {finish}")
+
+
+def _emit_ksplit_partial(p: Ptx, cfg: GemmConfig, ks: int, t: str, row_t: str, lane: str,
+                         q: str, regs: list, nchunks: int, load_chunk) -> str:
+    """Write this unit's accumulator rows to the workspace and take the warp quarter's
+    ticket; returns the label the warps that are not last jump to (the next unit)."""
+    BN, MT = cfg.BN, cfg.MT
+    ws, tk = p.reg("b64"), p.reg("b64")
+    p.emit(f"ld.param.u64 {ws}, [param__ksplit_ws]\ncvta.to.global.u64 {ws}, {ws}\n"
+           f"ld.param.u64 {tk}, [param__ksplit_tickets]\ncvta.to.global.u64 {tk}, {tk}")
+    # row (unit t, row_t) of the workspace: [tile][slice][row][BN] f32 = [unit][row][BN]
+    wrow, w = p.reg("b64"), p.reg("u32")
+    p.emit(f"mad.lo.u32 {w}, {t}, {MT}, {row_t}\nmul.wide.u32 {wrow}, {w}, {BN * 4}\nadd.s64 {wrow}, {wrow}, {ws}")
+    for ch in range(nchunks):
+        load_chunk(ch)
+        for g in range(8):
+            p.emit(f"st.global.v4.b32 [{wrow}+{(ch * 32 + 4 * g) * 4}], {{{', '.join(regs[4 * g:4 * g + 4])}}}")
+    # every lane's stores before lane 0's ticket; the ticket of (tile, warp quarter)
+    tile, ta, old, last = p.reg("u32"), p.reg("b64"), p.reg("u32"), p.reg("u32")
+    p0, pl = p.reg("pred"), p.reg("pred")
+    l_next = p.label("ks_next")
+    p.emit(f"""
+        fence.acq_rel.gpu
+        bar.warp.sync -1
+        div.u32 {tile}, {t}, {ks}
+        mad.lo.u32 {tile}, {tile}, 4, {q}
+        mul.wide.u32 {ta}, {tile}, 4
+        add.s64 {ta}, {ta}, {tk}
+        setp.eq.u32 {p0}, {lane}, 0
+        mov.u32 {last}, 0
+        @{p0} atom.acq_rel.gpu.global.add.u32 {old}, [{ta}], 1
+        @{p0} setp.eq.u32 {pl}, {old}, {ks - 1}
+        @{p0} selp.u32 {last}, 1, 0, {pl}
+        shfl.sync.idx.b32 {last}, {last}, 0, 31, -1
+        setp.eq.u32 {pl}, {last}, 0
+        @{pl} bra {l_next}
+        @{p0} st.relaxed.gpu.global.u32 [{ta}], 0
+        fence.acq_rel.gpu
+    """)
+    return l_next
+
+
+def _ksplit_sum(p: Ptx, cfg: GemmConfig, ks: int, t: str, row_t: str, ch: int) -> list:
+    """Columns 32 ch .. 32 ch + 31 of the thread's row summed over the tile's slices in
+    slice order (L2 loads: the other slices were written by other CTAs)."""
+    BN, MT = cfg.BN, cfg.MT
+    ws = p.reg("b64")
+    p.emit(f"ld.param.u64 {ws}, [param__ksplit_ws]\ncvta.to.global.u64 {ws}, {ws}")
+    u0, w, a = p.reg("u32"), p.reg("u32"), p.reg("b64")
+    # unit of slice 0 of this tile: t - t % ks
+    p.emit(f"rem.u32 {u0}, {t}, {ks}\nsub.u32 {u0}, {t}, {u0}")
+    acc = [p.reg("f32") for _ in range(32)]
+    tmp = [p.reg("f32") for _ in range(32)]
+    for sl in range(ks):
+        p.emit(f"add.u32 {w}, {u0}, {sl}\nmad.lo.u32 {w}, {w}, {MT}, {row_t}\n"
+               f"mul.wide.u32 {a}, {w}, {BN * 4}\nadd.s64 {a}, {a}, {ws}")
+        dst = acc if sl == 0 else tmp
+        for g in range(8):
+            p.emit(f"ld.global.cg.v4.f32 {{{', '.join(dst[4 * g:4 * g + 4])}}}, [{a}+{(ch * 32 + 4 * g) * 4}]")
+        if sl:
+            for i in range(32):
+                p.emit(f"add.rn.f32 {acc[i]}, {acc[i]}, {tmp[i]}")
+    return acc
 
 
 def _load_operand(p: Ptx, cfg: GemmConfig, buf: str, adr: str, ch: int, i: int, prow, n0) -> str:

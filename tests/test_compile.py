@@ -187,6 +187,19 @@ def test_f32_attention_rejects_score_transforms():
         analyze(replace(spec, body=plant(spec.body)))
 
 
+def test_gemm_ksplit_choice():
+    """K slices only where they remove many converter stages: the f32 512^3 matmul (64
+    tiles, 16 K blocks) takes 2, the 64x64x2048 one (2 tiles) 16; 16-bit GEMMs none."""
+    from compiler.synth import baseline_dir
+    want = {"m01_matmul_512": 2, "x_m_longk": 16, "x_h_mm_256": 1, "m02_matmul_rect": 1}
+    for pid, ks in want.items():
+        ir = sorted((GOLDEN / pid).glob("*.ir.json"))[-1]
+        assert parse_launch(compile_kernel(load(ir))).get("ksplit", 1) == ks, pid
+    for name in ("gemm_512", "gemm_2048"):
+        for ir in baseline_dir(name).glob("*.ir.json"):
+            assert parse_launch(compile_kernel(load(ir)))["ksplit"] == 1
+
+
 @pytest.mark.parametrize("pid,mnk,batch,a,b,epi", [
     ("m01_matmul_512", (512, 512, 512), 1, "x0", "x1", None),
     ("m02_matmul_rect", (128, 64, 256), 1, "x0", "x1", None),      # split-K atomics: one pass
