@@ -36,13 +36,14 @@ def test_gemm_matches_golden(runtime, pid):
         assert np.allclose(got, o, rtol=meta["rtol"], atol=meta["atol"])
 
 
-def _direct_gemm(m, n, k, pair, b_kmajor, seed=0, batch=1):
+def _direct_gemm(m, n, k, pair, b_kmajor, seed=0, batch=1, ksplit=0):
     from compiler.kernels.gemm import GemmConfig, emit_gemm_module
     from emmyrt import DeviceBuffer
     from emmyrt.runner import CompiledKernel, bf16_bits_to_f32, f32_to_bf16_bits
     import emmyrt
     cfg = GemmConfig(M=m, N=n, K=k, batch=batch, ab="bf16", c="bf16", b_kmajor=b_kmajor, BN=256,
-                     stages=6 if pair else 4, pair=pair, name="k_gemm_test", buffers=("a", "b", "c"))
+                     stages=6 if pair else 4, pair=pair, name="k_gemm_test", buffers=("a", "b", "c"),
+                     ksplit=ksplit)
     ck = CompiledKernel.from_module(emit_gemm_module(cfg), "k_gemm_test", ["a", "b", "c"])
     rng = np.random.default_rng(seed)
     A = f32_to_bf16_bits(rng.standard_normal((batch, m, k), dtype=np.float32) * np.float32(0.05))
@@ -70,5 +71,16 @@ def _direct_gemm(m, n, k, pair, b_kmajor, seed=0, batch=1):
 def test_gemm_direct_bf16(runtime, m, n, k, pair, kmaj):
     from oracle.refs import mm_bf16
     got, A, B = _direct_gemm(m, n, k, pair, kmaj)
+    ref = mm_bf16(A[0], B[0])
+    assert np.allclose(got[0], ref, rtol=1e-2, atol=1e-2), f"max abs err {np.max(np.abs(got[0] - ref))}"
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("m,n,k,kmaj,ksplit", [(512, 512, 1024, False, 4), (300, 200, 512, True, 2)])
+def test_gemm_split_k_bf16(runtime, m, n, k, kmaj, ksplit):
+    """K slices forced on 16-bit tiles (the automatic choice keeps them for the f32 path):
+    partials through the workspace, the last slice's ordered sum, ragged M and N tiles."""
+    from oracle.refs import mm_bf16
+    got, A, B = _direct_gemm(m, n, k, False, kmaj, ksplit=ksplit)
     ref = mm_bf16(A[0], B[0])
     assert np.allclose(got[0], ref, rtol=1e-2, atol=1e-2), f"max abs err {np.max(np.abs(got[0] - ref))}"

@@ -36,7 +36,7 @@ def test_f32_matmul_matches_golden(runtime, pid):
         assert np.allclose(got, np.asarray(ora[name]).reshape(ref.shape), rtol=meta["rtol"], atol=meta["atol"])
 
 
-def _run_f32(m, n, k, b_kmajor=False, batch=1, bias=False, seed=0, BN=None):
+def _run_f32(m, n, k, b_kmajor=False, batch=1, bias=False, seed=0, BN=None, ksplit=0):
     import emmyrt
     from compiler.kernels.gemm import GemmConfig, choose_tiling_f32, emit_gemm_module
     from emmyrt import DeviceBuffer
@@ -47,7 +47,7 @@ def _run_f32(m, n, k, b_kmajor=False, batch=1, bias=False, seed=0, BN=None):
     epi = (("bias", "bias"),) if bias else ()
     cfg = GemmConfig(M=m, N=n, K=k, batch=batch, ab="f32", c="f32", b_kmajor=b_kmajor, **tiling,
                      epilogue=epi, name="k_gemm_f32_test", buffers=("a", "b", "c", "bias"),
-                     operand_dtypes=(("bias", "f32"),))
+                     operand_dtypes=(("bias", "f32"),), ksplit=ksplit)
     ck = CompiledKernel.from_module(emit_gemm_module(cfg), "k_gemm_f32_test", ["a", "b", "c", "bias"])
     rng = np.random.default_rng(seed)
     A = rng.standard_normal((batch, m, k)).astype(np.float32)
@@ -88,6 +88,15 @@ def test_3xtf32_accuracy(runtime, m, n, k, b_kmajor, batch, BN):
     # single tf32 products (2^-11 each) would miss it
     err = np.abs(out - ref) / scale
     assert np.max(err) <= 2.0 ** -16, f"max error {np.max(err)} of sum |a||b|"
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("m,n,k,batch,bias,ksplit", [(130, 100, 512, 1, True, 4), (200, 96, 256, 3, False, 2)])
+def test_3xtf32_split_k(runtime, m, n, k, batch, bias, ksplit):
+    """Forced K slices: the bias epilogue runs once, after the ordered sum of the slices;
+    batched tiles take their own tickets."""
+    out, ref, scale = _run_f32(m, n, k, batch=batch, bias=bias, BN=64, ksplit=ksplit)
+    assert np.max(np.abs(out - ref) / scale) <= 2.0 ** -16
 
 
 @pytest.mark.gpu
