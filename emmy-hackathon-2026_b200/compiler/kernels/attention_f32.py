@@ -27,6 +27,13 @@ Here the same arithmetic is reorganised around the query row:
   owns output columns c, c + 32, ...;
 * epilogue: the row sum by butterfly, ``o / l`` (IEEE division), predicated stores.
 
+The same kernel takes the score-input form (the online softmax over a score buffer that the
+reference's split attention runs after its Q K^T kernel, tests/problems/x_h_attn_odd): the
+scores are read from the buffer instead of computed, the IR's per-key transform (its f16
+rounding and f16 scale) and its loop-invariant statements are lowered with the element-map
+statement lowering, and v / the output may be 16-bit (widened to f32 in shared memory,
+rounded on the store).
+
 Everything is f32; the exponentials use ``ex2.approx`` (relative error ~2^-22), inside the
 fixtures' rtol 1e-3.  No global synchronisation, no atomics: deterministic.
 """
@@ -37,7 +44,7 @@ import math
 from dataclasses import dataclass
 
 from ..ptx import Ptx, entry, f32_hex, module
-from ..stmts import expr_vars
+from ..stmts import Val, expr_vars, lower_body
 from .common import arg_params, load_pointer
 
 LOG2E = 1.4426950408889634
@@ -63,6 +70,15 @@ class F32AttnConfig:
     group: int = 1                 # query batch entries per k / v entry (grouped-query heads)
     R: int = 1                     # query rows per warp
     KC: int = 64                   # keys per staged chunk
+    scores: str | None = None      # score-input form: this [.., Sq, Sk] buffer instead of q kt
+    s_name: str = ""               # the name its Load binds
+    s_out: str = ""                # the transformed score the softmax takes
+    s_chain: tuple = ()            # the IR's statements from s_name to s_out, per key
+    prelude: tuple = ()            # the loop-invariant statements before the key loop
+    dtypes: tuple = ()             # (buffer, dtype) of 16-bit buffers (all others f32)
+
+    def dt(self, name: str) -> str:
+        return dict(self.dtypes).get(name, "f32")
 
     @property
     def KPL(self) -> int:          # keys per lane per chunk
@@ -82,7 +98,8 @@ class F32AttnConfig:
 
     @property
     def vec(self) -> bool:         # 128-bit staging: key and value rows in whole float4s
-        return (self.Sk % 4 == 0 if self.kt else self.D % 4 == 0) and self.Dv % 4 == 0
+        return ((self.Sk % 4 == 0 if self.kt else self.D % 4 == 0) and self.Dv % 4 == 0
+                and self.dt(self.v) == "f32")
 
 
 def _walk_loops(body, loops=()):
@@ -128,7 +145,7 @@ def analyze(spec) -> F32AttnConfig:
                     and all(type(defs.get(a)).__name__ == "Load" for a in prod.args):
                 dots.append((s, loops, [defs[a] for a in prod.args]))
     if not dots:
-        raise NotImplementedError("no dot product in a nested loop")
+        return _analyze_scores(spec, walk, defs)
     key, red = dots[0][1][-2], dots[0][1][-1]
     q_in = k_in = None
     q_ld = k_ld = None
@@ -201,35 +218,9 @@ def analyze(spec) -> F32AttnConfig:
     # the scaled score feeds the online softmax and nothing else: the running maximum and
     # the differences taken against it (a softcap, a bias or a mask in between would sit
     # here, and this template does not compute them)
-    scaled_names = {s.name for s in scaled}
-    for s, _ in walk:
-        k = type(s).__name__
-        uses = set(s.args) if k == "Assign" else {s.value} if k == "Accum" else set()
-        if uses & scaled_names:
-            if not ((k == "Assign" and s.op.name in ("maximum", "subtract")) or
-                    (k == "Accum" and s.op.name == "maximum")):
-                raise NotImplementedError(f"the scaled score also feeds {s.op.name}")
-    # every written value is (sum of p v) * 1 / (sum of p), both accumulated over the keys
-    key_sums = {s.name for s, _ in walk if type(s).__name__ == "Accum" and s.op.name == "add"
-                and key in (s.axes or ())}
-    for w, _ in ((s, l) for s, l in walk if type(s).__name__ == "Write"):
-        for val in w.values:
-            d = defs.get(val)
-            if type(d).__name__ != "Assign" or d.op.name != "multiply" or len(d.args) != 2:
-                raise NotImplementedError("output is not a normalised sum")
-            a, b = (defs.get(x) for x in d.args)
-            if type(b).__name__ == "Assign" and b.op.name == "reciprocal":
-                num, den = d.args[0], b.args[0]
-            elif type(a).__name__ == "Assign" and a.op.name == "reciprocal":
-                num, den = d.args[1], a.args[0]
-            else:
-                raise NotImplementedError("output is not a normalised sum")
-            if num not in key_sums or den not in key_sums:
-                raise NotImplementedError("output is not a normalised sum")
-    # guards only: no condition may look at the key or reduction axis (a mask would)
-    for s, _ in walk:
-        if type(s).__name__ == "Cond" and expr_vars(s.cond) & {key, red}:
-            raise NotImplementedError("a condition on the key axis (mask)")
+    _check_softmax_use(walk, {s.name for s in scaled})
+    _check_normalised(walk, defs, key)
+    _check_guards(walk, {key, red})
     loaded = {s.input for s, _ in walk if type(s).__name__ == "Load"}
     if loaded - {q_in, k_in, v_in, scale_param}:
         raise NotImplementedError(f"extra inputs {sorted(loaded - {q_in, k_in, v_in})}")
@@ -255,6 +246,154 @@ def analyze(spec) -> F32AttnConfig:
                         scale_param, recip, const, kt=kt, group=group)
     cfg.KC = 32 if Sk <= 32 else 64
     # rows per warp: reuse each staged key across rows once the grid covers the SMs
+    for R in (4, 2):
+        if B * -(-Sq // (WARPS * R)) >= 148:
+            cfg.R = R
+            break
+    return cfg
+
+
+def _check_softmax_use(walk, scaled_names: set) -> None:
+    """The scaled score feeds the online softmax and nothing else: the running maximum and
+    the differences taken against it (a softcap, a bias or a mask in between would sit
+    here, and this template does not compute them)."""
+    for s, _ in walk:
+        k = type(s).__name__
+        uses = set(s.args) if k == "Assign" else {s.value} if k == "Accum" else set()
+        if uses & scaled_names:
+            if not ((k == "Assign" and s.op.name in ("maximum", "subtract")) or
+                    (k == "Accum" and s.op.name == "maximum")):
+                raise NotImplementedError(f"the scaled score also feeds {s.op.name}")
+
+
+def _check_normalised(walk, defs, key: str) -> None:
+    """Every written value is (sum of p v) * 1 / (sum of p), both accumulated over the keys."""
+    key_sums = {s.name for s, _ in walk if type(s).__name__ == "Accum" and s.op.name == "add"
+                and key in (s.axes or ())}
+    for w, _ in ((s, l) for s, l in walk if type(s).__name__ == "Write"):
+        for val in w.values:
+            d = defs.get(val)
+            if type(d).__name__ != "Assign" or d.op.name != "multiply" or len(d.args) != 2:
+                raise NotImplementedError("output is not a normalised sum")
+            a, b = (defs.get(x) for x in d.args)
+            if type(b).__name__ == "Assign" and b.op.name == "reciprocal":
+                num, den = d.args[0], b.args[0]
+            elif type(a).__name__ == "Assign" and a.op.name == "reciprocal":
+                num, den = d.args[1], a.args[0]
+            else:
+                raise NotImplementedError("output is not a normalised sum")
+            if num not in key_sums or den not in key_sums:
+                raise NotImplementedError("output is not a normalised sum")
+
+
+def _check_guards(walk, axes: set) -> None:
+    """Guards only: no condition may look at the key or reduction axis (a mask would)."""
+    for s, _ in walk:
+        if type(s).__name__ == "Cond" and expr_vars(s.cond) & axes:
+            raise NotImplementedError("a condition on the key axis (mask)")
+
+
+_HALF = ("f16", "bf16")
+
+
+def _analyze_scores(spec, walk, defs) -> F32AttnConfig:
+    """``softmax(f(s), -1) @ v`` over a score buffer s: the second kernel of the reference's
+    split attention (tests/problems/x_h_attn_odd, after a Q K^T kernel wrote s), an online
+    softmax over the key loop whose per-key transform f (the 16-bit rounding and scale the
+    IR states) is lowered from the IR's own statements; the loop-invariant statements before
+    the key loop (a scale read from a 1-element buffer, its reciprocal) run once."""
+    tile = spec.body[0]
+    maxes = [(s, l) for s, l in walk if type(s).__name__ == "Accum" and s.op.name == "maximum"]
+    if not maxes or any(len(s.axes or ()) != 1 for s, _ in maxes):
+        raise NotImplementedError("no running max over one axis")
+    key = maxes[0][0].axes[0]
+    if any(s.axes[0] != key or key not in l for s, l in maxes):
+        raise NotImplementedError("running maxima over different loops")
+    if any(key in l and len(l) > 1 for _, l in walk):
+        raise NotImplementedError("loops nested in the key loop")
+    in_loop = {id(s) for s, l in walk if key in l}
+    s_ld, chain, seen = None, [], set()
+
+    def trace(name):
+        nonlocal s_ld
+        d = defs.get(name)
+        if d is None:
+            raise NotImplementedError(f"{name} not defined")
+        if id(d) not in in_loop or id(d) in seen:
+            return
+        seen.add(id(d))
+        k = type(d).__name__
+        if k == "Load":
+            if s_ld is not None or len(d.names) != 1 or expr_vars(d.index[-1]) != {key} \
+                    or any(key in expr_vars(i) for i in d.index[:-1]):
+                raise NotImplementedError("score not one load of a [.., Sq, Sk] buffer")
+            s_ld = d
+        elif k == "Assign":
+            for a in d.args:
+                trace(a)
+            chain.append(d)
+        elif k == "Let":
+            chain.append(d)
+        else:
+            raise NotImplementedError(f"{k} in the score transform")
+    s_out = maxes[0][0].value
+    trace(s_out)
+    if s_ld is None:
+        raise NotImplementedError("no score load")
+    prelude = []
+    for st in tile.body:
+        k = type(st).__name__
+        if k == "Loop":
+            break
+        if k == "Load" and not any(expr_vars(i) for i in st.index) and len(st.names) == 1:
+            prelude.append(st)
+        elif k in ("Assign", "Let"):
+            prelude.append(st)
+        else:
+            raise NotImplementedError(f"{k} before the key loop")
+    v_ld = None
+    for st, loops in walk:
+        if type(st).__name__ == "Load" and st.input != s_ld.input and key in loops:
+            if len(st.index) < 2 or expr_vars(st.index[-2]) != {key} or key in expr_vars(st.index[-1]):
+                raise NotImplementedError("a load in the key loop that is not s or v")
+            if v_ld is not None and st.input != v_ld.input:
+                raise NotImplementedError("two v buffers")
+            v_ld = v_ld or st
+    if v_ld is None:
+        raise NotImplementedError("no v operand")
+    if not any(type(st).__name__ == "Assign" and st.op.name == "exp" for st, _ in walk):
+        raise NotImplementedError("no exp")
+    _check_softmax_use(walk, {s.value for s, _ in maxes})
+    _check_normalised(walk, defs, key)
+    _check_guards(walk, {key})
+    writes = [st for st, _ in walk if type(st).__name__ == "Write"]
+    if len({w.output for w in writes}) != 1:
+        raise NotImplementedError("not one output")
+    S, V, O = (spec.param(n) for n in (s_ld.input, v_ld.input, writes[0].output))
+    pre_in = {st.input for st in prelude if type(st).__name__ == "Load"}
+    loaded = {st.input for st, _ in walk if type(st).__name__ == "Load"}
+    if loaded - {S.name, V.name} - pre_in:
+        raise NotImplementedError("extra inputs")
+    for n in pre_in:
+        q = spec.param(n)
+        if q.scalar or q.dtype not in ("f32",) + _HALF:
+            raise NotImplementedError("a prelude load that is not a float buffer")
+    if any(q.scalar or q.dtype not in ("f32",) + _HALF for q in (S, V, O)) or len(S.shape) < 2 \
+            or not (len(S.shape) == len(V.shape) == len(O.shape)):
+        raise NotImplementedError("operand types or ranks")
+    Sq, Sk = S.shape[-2:]
+    Dv = V.shape[-1]
+    if V.shape[-2] != Sk or tuple(O.shape) != tuple(S.shape[:-1]) + (Dv,):
+        raise NotImplementedError("operand shapes")
+    B = math.prod(S.shape[:-2])
+    group = _lead_group(spec, s_ld, [w.index for w in writes], v_ld, v_ld)
+    if Dv > 256 or B > 65535 or min(Sq, Sk, Dv) < 1:
+        raise NotImplementedError("value dims above 256")
+    cfg = F32AttnConfig(spec.name, B, Sq, Sk, 0, Dv, "", "", V.name, O.name, None, False, 1.0,
+                        group=group, scores=S.name, s_name=s_ld.names[0], s_out=s_out,
+                        s_chain=tuple(chain), prelude=tuple(prelude),
+                        dtypes=tuple((q.name, q.dtype) for q in (S, V, O) if q.dtype in _HALF))
+    cfg.KC = 32 if Sk <= 32 else 64
     for R in (4, 2):
         if B * -(-Sq // (WARPS * R)) >= 148:
             cfg.R = R
@@ -309,6 +448,39 @@ def _lead_group(spec, q_ld, out_indices, k_ld, v_ld) -> int:
     return G
 
 
+def _esz(dtype: str) -> int:
+    return 2 if dtype in _HALF else 4
+
+
+def _emit_ld(p: Ptx, dtype: str, addr: str, dst: str, pred: str) -> None:
+    """dst = buffer element at addr widened to f32, 0 where pred is false."""
+    if dtype == "f32":
+        p.emit(f"mov.f32 {dst}, 0f00000000\n@{pred} ld.global.nc.f32 {dst}, [{addr}]")
+    else:
+        h = p.reg("b16")
+        p.emit(f"mov.b16 {h}, 0\n@{pred} ld.global.nc.b16 {h}, [{addr}]\ncvt.f32.{dtype} {dst}, {h}")
+
+
+def _score_ctx(p: Ptx, spec):
+    """The element-map statement lowering for the score transform: 16-bit results rounded
+    per op as the IR states; loads are the prelude's 1-element reads."""
+    from ..stmts import ScalarCtx, eval_index, flat_offset
+
+    def on_load(ctx, ld):
+        q = spec.param(ld.input)
+        off = flat_offset(tuple(ld.index), q.shape, {})
+        a, r = p.reg("b64"), p.reg("f32")
+        p.emit(f"add.s64 {a}, {load_pointer(p, q.name)}, {off * _esz(q.dtype)}")
+        t = p.reg("pred")
+        p.emit(f"setp.eq.u32 {t}, 0, 0")
+        _emit_ld(p, q.dtype, a, r, t)
+        ctx.env[ld.names[0]] = Val(r, "f32")
+    ctx = ScalarCtx(p, constants=dict(spec.constants), half_results=True,
+                    const_dtypes={q.name: q.dtype for q in spec.params})
+    ctx.on_load = on_load
+    return ctx
+
+
 def smem_layout(cfg: F32AttnConfig) -> dict:
     """Byte offsets in dynamic shared memory (each region 16-byte aligned)."""
     ks = 0
@@ -342,21 +514,28 @@ def emit_module(spec, cfg: F32AttnConfig) -> str:
         mad.lo.u32 {row0}, {row0}, {WARPS}, {warp}
         mul.lo.u32 {row0}, {row0}, {R}
     """)
-    ptr = {n: load_pointer(p, n) for n in (cfg.q, cfg.k, cfg.v, cfg.o)}
+    score = cfg.scores is not None
+    ptr = {n: load_pointer(p, n) for n in ((cfg.scores,) if score else (cfg.q, cfg.k)) + (cfg.v, cfg.o)}
 
     def batch_base(name, per):
         off = p.reg("u64")
-        p.emit(f"mul.wide.u32 {off}, {bidx}, {per * 4}\nadd.s64 {ptr[name]}, {ptr[name]}, {off}")
-    batch_base(cfg.q, cfg.Sq * D)
+        p.emit(f"mul.wide.u32 {off}, {bidx}, {per * _esz(cfg.dt(name))}\n"
+               f"add.s64 {ptr[name]}, {ptr[name]}, {off}")
+    batch_base(cfg.scores if score else cfg.q, cfg.Sq * (cfg.Sk if score else D))
     batch_base(cfg.o, cfg.Sq * Dv)
     if cfg.group > 1:
         p.emit(f"div.u32 {bidx}, {bidx}, {cfg.group}")
-    batch_base(cfg.k, D * cfg.Sk)
+    if not score:
+        batch_base(cfg.k, D * cfg.Sk)
     batch_base(cfg.v, cfg.Sk * Dv)
 
-    # the score multiplier c
+    # the score multiplier c; or (score input) the IR's loop-invariant statements, run once
     sc = p.reg("f32")
-    if cfg.scale_param is not None:
+    ctx = None
+    if score:
+        ctx = _score_ctx(p, spec)
+        lower_body(ctx, cfg.prelude)
+    elif cfg.scale_param is not None:
         sp = load_pointer(p, cfg.scale_param)
         p.emit(f"ld.global.nc.f32 {sc}, [{sp}]")
         if cfg.scale_recip:
@@ -385,7 +564,7 @@ def emit_module(spec, cfg: F32AttnConfig) -> str:
     """)
 
     # ---- the warp's q rows into shared memory (zero past Sq and past D)
-    for r in range(R):
+    for r in range(R if not score else 0):
         row, prow = p.reg("u32"), p.reg("pred")
         p.emit(f"add.u32 {row}, {row0}, {r}\nsetp.lt.u32 {prow}, {row}, {cfg.Sq}")
         for i in range(-(-DP // 32)):
@@ -431,14 +610,33 @@ def emit_module(spec, cfg: F32AttnConfig) -> str:
     _stage(p, cfg, ptr, tid, key0, sbase, lay, T)
     p.emit("bar.sync 0")
 
-    # ---- scores for the chunk: acc[r][k] = q_r . kt[:, key0 + lane + 32k]
+    # ---- scores for the chunk: acc[r][k] = q_r . kt[:, key0 + lane + 32k] (or read from s)
     acc = [[p.reg("f32") for _ in range(KPL)] for _ in range(R)]
     for r in range(R):
         for k in range(KPL):
             p.emit(f"mov.f32 {acc[r][k]}, 0f00000000")
+    if score:
+        sdt = cfg.dt(cfg.scores)
+        for r in range(R):
+            for k in range(KPL):
+                pk, a64 = p.reg("pred"), p.reg("u64")
+                p.emit(f"""
+                    add.u32 {t0}, {row0}, {r}
+                    setp.lt.u32 {pk}, {t0}, {cfg.Sq}
+                    mad.lo.u32 {t0}, {t0}, {cfg.Sk}, {key0}
+                    add.u32 {t0}, {t0}, {lane}
+                    add.u32 {t0}, {t0}, {32 * k}
+                    mul.wide.u32 {a64}, {t0}, {_esz(sdt)}
+                    add.s64 {a64}, {ptr[cfg.scores]}, {a64}
+                """)
+                # the key index: lane + 32 k past key0 (predicated on the row and the key)
+                pkk = p.reg("pred")
+                p.emit(f"add.u32 {t0}, {key0}, {lane}\nadd.u32 {t0}, {t0}, {32 * k}\n"
+                       f"setp.lt.and.u32 {pkk}, {t0}, {cfg.Sk}, {pk}")
+                _emit_ld(p, sdt, a64, acc[r][k], pkk)
     kv = [p.reg("f32") for _ in range(KPL)]
     qv = [[p.reg("f32") for _ in range(4)] for _ in range(R)]
-    for d0 in range(0, D, 4):
+    for d0 in range(0, D if not score else 0, 4):
         for r in range(R):
             p.emit(f"ld.shared.v4.f32 {{{', '.join(qv[r])}}}, [{qw}+{(r * DP + d0) * 4}]")
         for dd in range(min(4, D - d0)):
@@ -461,7 +659,15 @@ def emit_module(spec, cfg: F32AttnConfig) -> str:
         t = [p.reg("f32") for _ in range(KPL)]
         cm, sh, mn, alpha, ps_sum = p.reg("f32"), p.reg("f32"), p.reg("f32"), p.reg("f32"), p.reg("f32")
         for k in range(KPL):
-            p.emit(f"mul.rn.f32 {t[k]}, {acc[r][k]}, {sc}\nselp.f32 {t[k]}, {t[k]}, {NEG_INF}, {kvalid[k]}")
+            if score:
+                saved = dict(ctx.env)
+                ctx.env[cfg.s_name] = Val(acc[r][k], "f32")
+                lower_body(ctx, cfg.s_chain)
+                p.emit(f"mov.f32 {t[k]}, {ctx.f32(cfg.s_out)}")
+                ctx.env = saved
+            else:
+                p.emit(f"mul.rn.f32 {t[k]}, {acc[r][k]}, {sc}")
+            p.emit(f"selp.f32 {t[k]}, {t[k]}, {NEG_INF}, {kvalid[k]}")
         p.emit(f"mov.f32 {cm}, {t[0]}")
         for k in range(1, KPL):
             p.emit(f"max.f32 {cm}, {cm}, {t[k]}")
@@ -516,10 +722,14 @@ def emit_module(spec, cfg: F32AttnConfig) -> str:
                 div.rn.f32 {res}, {o[r][i]}, {l[r]}
                 mad.lo.u32 {t0}, {row}, {Dv}, {lane}
                 add.u32 {t0}, {t0}, {32 * i}
-                mul.wide.u32 {a64}, {t0}, 4
+                mul.wide.u32 {a64}, {t0}, {_esz(cfg.dt(cfg.o))}
                 add.s64 {a64}, {ptr[cfg.o]}, {a64}
-                @{ps_} st.global.f32 [{a64}], {res}
             """)
+            if cfg.dt(cfg.o) == "f32":
+                p.emit(f"@{ps_} st.global.f32 [{a64}], {res}")
+            else:
+                h = p.reg("b16")
+                p.emit(f"cvt.rn.{cfg.dt(cfg.o)}.f32 {h}, {res}\n@{ps_} st.global.b16 [{a64}], {h}")
     p.emit("ret")
 
     grid = [-(-cfg.Sq // (WARPS * R)), cfg.B, 1]
@@ -539,7 +749,9 @@ def _stage(p: Ptx, cfg: F32AttnConfig, ptr: dict, tid: str, key0: str, sbase: st
     nk = p.reg("u32")
     p.emit(f"sub.u32 {nk}, {Sk}, {key0}")
     ops = []        # (load predicate, store predicate, global address, [shared addresses])
-    if cfg.kt:
+    if cfg.scores is not None:
+        pass                  # scores come from the score buffer, not from k
+    elif cfg.kt:
         # kt [D][Sk]: unit e = tid + T it over [D][KC / w]; T is a multiple of KC / w
         per_row = KC // w
         rows_per_pass = T // per_row
@@ -569,7 +781,15 @@ def _stage(p: Ptx, cfg: F32AttnConfig, ptr: dict, tid: str, key0: str, sbase: st
     else:
         # key-major k: rows of D floats, stored with the odd stride DK
         ops += _span(p, cfg, ptr[cfg.k], tid, key0, nk, sbase, lay["ks"], D, cfg.DK, T, w)
-    ops += _span(p, cfg, ptr[cfg.v], tid, key0, nk, sbase, lay["vs"], cfg.Dv, cfg.Dv, T, w)
+    vops = _span(p, cfg, ptr[cfg.v], tid, key0, nk, sbase, lay["vs"], cfg.Dv, cfg.Dv, T, w,
+                 _esz(cfg.dt(cfg.v)))
+    if cfg.dt(cfg.v) != "f32":      # 16-bit v: element loads widened to f32 in shared memory
+        for pr, pst, ga, sas in vops:
+            x = p.reg("f32")
+            _emit_ld(p, cfg.dt(cfg.v), ga, x, pr)
+            p.emit(f"@{pst} st.shared.f32 [{sas[0]}], {x}")
+        vops = []
+    ops += vops
     sfx = ".v4.f32" if w == 4 else ".f32"
     for b0 in range(0, len(ops), 16):
         batch = ops[b0:b0 + 16]
@@ -588,14 +808,14 @@ def _stage(p: Ptx, cfg: F32AttnConfig, ptr: dict, tid: str, key0: str, sbase: st
 
 
 def _span(p: Ptx, cfg: F32AttnConfig, gptr: str, tid: str, key0: str, nk: str, sbase: str,
-          soff: int, width: int, sstride: int, T: int, w: int) -> list:
+          soff: int, width: int, sstride: int, T: int, w: int, esz: int = 4) -> list:
     """Staging ops for rows [key0, key0 + KC) of a [.., Sk, width] buffer: one contiguous
     span of global memory; in shared memory row j starts at j * sstride (floats)."""
     KC = cfg.KC
     nv = p.reg("u32")
     p.emit(f"min.u32 {nv}, {nk}, {KC}\nmul.lo.u32 {nv}, {nv}, {width}")
     base = p.reg("u64")
-    p.emit(f"mul.wide.u32 {base}, {key0}, {width * 4}\nadd.s64 {base}, {gptr}, {base}")
+    p.emit(f"mul.wide.u32 {base}, {key0}, {width * esz}\nadd.s64 {base}, {gptr}, {base}")
     ops = []
     for it in range(-(-(KC * width // w) // T)):
         e, pr, pst = p.reg("u32"), p.reg("pred"), p.reg("pred")
@@ -605,7 +825,7 @@ def _span(p: Ptx, cfg: F32AttnConfig, gptr: str, tid: str, key0: str, nk: str, s
             mul.lo.u32 {e}, {e}, {w}
             setp.lt.u32 {pr}, {e}, {nv}
             setp.lt.u32 {pst}, {e}, {KC * width}
-            mul.wide.u32 {ga}, {e}, 4
+            mul.wide.u32 {ga}, {e}, {esz}
             add.s64 {ga}, {base}, {ga}
         """)
         if sstride == width:

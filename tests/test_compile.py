@@ -147,11 +147,19 @@ F32_ATTN = {"a01_attention": (1, 64, 64, 64, 64, True), "a02_attention_128": (1,
 
 def test_f32_attention_recognizer():
     """The register-tiled f32 attention forms (q @ kt scaled by a 1-element buffer or its
-    inverse) go to the warp-per-row template; nothing else in the fixtures does."""
+    inverse) go to the warp-per-row template, and so does the online softmax over a score
+    buffer of the split attention (its f16 rounding and f16 scale lowered from the IR);
+    nothing else in the fixtures does."""
     from compiler.kernels.attention_f32 import analyze
     for ir in sorted(GOLDEN.glob("*/*.ir.json")):
         pid = ir.parent.name
-        if pid in F32_ATTN:
+        if pid == "x_h_attn_odd" and "softmax" in ir.name:
+            cfg = analyze(load(ir))
+            assert (cfg.scores, cfg.B, cfg.Sq, cfg.Sk, cfg.Dv) == ("matmul_1__place_03e2a34518_0", 1, 50, 70, 24)
+            assert dict(cfg.dtypes) == {"v": "f16", "matmul_1": "f16"}
+            assert [x.op.name for x in cfg.s_chain] == ["copy", "multiply"]
+            assert parse_launch(compile_kernel(load(ir)))["kind"] == "attention_f32"
+        elif pid in F32_ATTN:
             cfg = analyze(load(ir))
             b, sq, sk, d, dv, recip = F32_ATTN[pid]
             assert (cfg.B, cfg.Sq, cfg.Sk, cfg.D, cfg.Dv, cfg.scale_recip) == (b, sq, sk, d, dv, recip)
