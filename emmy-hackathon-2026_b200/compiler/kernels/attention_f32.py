@@ -220,6 +220,7 @@ def analyze(spec) -> F32AttnConfig:
     # here, and this template does not compute them)
     _check_softmax_use(walk, {s.name for s in scaled})
     _check_normalised(walk, defs, key)
+    _check_pv(walk, defs, key, v_in)
     _check_guards(walk, {key, red})
     loaded = {s.input for s, _ in walk if type(s).__name__ == "Load"}
     if loaded - {q_in, k_in, v_in, scale_param}:
@@ -284,6 +285,32 @@ def _check_normalised(walk, defs, key: str) -> None:
                 raise NotImplementedError("output is not a normalised sum")
             if num not in key_sums or den not in key_sums:
                 raise NotImplementedError("output is not a normalised sum")
+
+
+def _check_pv(walk, defs, key: str, v_input: str) -> None:
+    """Every sum over the keys adds exp(..) times a v element (o) or times 1 (l): the
+    template multiplies the f32 probabilities straight into v, so a p rounded to 16 bits
+    first (or any other step between the exponential and the product) is handed back."""
+    for acc, _ in walk:
+        if type(acc).__name__ != "Accum" or acc.op.name != "add" or key not in (acc.axes or ()):
+            continue
+        d = defs.get(acc.value)
+        if type(d).__name__ != "Assign" or d.op.name != "multiply" or len(d.args) != 2:
+            raise NotImplementedError("a key sum that is not a product")
+        kinds = []
+        for a in d.args:
+            x = defs.get(a)
+            k = type(x).__name__
+            if k == "Assign" and x.op.name == "exp":
+                kinds.append("exp")
+            elif k == "Load" and x.input == v_input:
+                kinds.append("v")
+            elif k == "Let" and type(x.value).__name__ == "Literal" and float(x.value.value) == 1.0:
+                kinds.append("one")
+            else:
+                kinds.append("other")
+        if sorted(kinds) not in (["exp", "v"], ["exp", "one"]):
+            raise NotImplementedError("a key sum other than exp * v or exp * 1")
 
 
 def _check_guards(walk, axes: set) -> None:
@@ -365,6 +392,7 @@ def _analyze_scores(spec, walk, defs) -> F32AttnConfig:
         raise NotImplementedError("no exp")
     _check_softmax_use(walk, {s.value for s, _ in maxes})
     _check_normalised(walk, defs, key)
+    _check_pv(walk, defs, key, v_ld.input)
     _check_guards(walk, {key})
     writes = [st for st, _ in walk if type(st).__name__ == "Write"]
     if len({w.output for w in writes}) != 1:

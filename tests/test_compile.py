@@ -195,6 +195,28 @@ def test_f32_attention_rejects_score_transforms():
         analyze(replace(spec, body=plant(spec.body)))
 
 
+def test_f32_attention_rejects_rounded_p():
+    """p rounded to f16 before it multiplies v (planted into a01's statements) is a step the
+    template does not take, so the recogniser must hand the kernel back."""
+    from dataclasses import replace
+    from compiler.kernels.attention_f32 import analyze
+    spec = load(next((GOLDEN / "a01_attention").glob("*.ir.json")))
+
+    def plant(body):
+        out = []
+        for x in body:
+            if type(x).__name__ == "Assign" and x.name == "v4__acc5__sum_sb__c0_0":
+                out.append(parse_stmt("Assign(name='p16', op=ElementwiseImpl('copy'), "
+                                      "args=('v4__beta__c0_0',), dtype=DataType(name='f16', "
+                                      "np=dtype('float16'), nbytes=2))"))
+                x = replace(x, args=(x.args[0], "p16"))
+            sub = getattr(x, "body", None)
+            out.append(replace(x, body=plant(sub)) if isinstance(sub, tuple) else x)
+        return tuple(out)
+    with pytest.raises(NotImplementedError, match="key sum"):
+        analyze(replace(spec, body=plant(spec.body)))
+
+
 def test_gemm_ksplit_choice():
     """K slices only where they remove many converter stages: the f32 512^3 matmul (64
     tiles, 16 K blocks) takes 2, the 64x64x2048 one (2 tiles) 16; 16-bit GEMMs none."""
