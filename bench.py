@@ -1,34 +1,39 @@
 #!/usr/bin/env python3
 """Benchmark of the B200 back end on BASELINE.json's configurations.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME|all]
+                    [--impl ours|reference] [--no-cpu]
 
-One step = one launch of the kernel compile.py emits for the workload's IR (the
-BASELINE configuration synthesised from the reference's IR family), over inputs
-already resident in HBM.  The default workload is the bf16 GEMM at M=N=K=8192,
-the configuration BASELINE.json's TFLOP/s target is quoted on.
+One step = one launch of the kernel ``compile.py`` emits for a configuration (its IR
+synthesised from the reference's IR family at the configured size), over inputs
+already resident in HBM.  The headline (the line's top-level ``value``) is the bf16
+GEMM at M=N=K=8192, BASELINE.json's TFLOP/s target, timed over exactly K steps.  Every
+other configuration of BASELINE.json (attention, FP8 GEMM, the other GEMM sizes,
+RMSNorm, row softmax, the 2^31 sum) is measured in the same run and reported under
+``workloads``, each with its own value, roofline, CPU baseline, end-to-end figure and
+SM clocks; their timed regions are stretched to at least 0.3 s.
 
-Multi-GPU (torchrun, one process per GPU): the work is partitioned the way the
-reference's problem partitions (GEMM by N-panel, attention by batch x head, row
-kernels by rows): every rank runs its own panel, no data-path collective, weak
-scaling; the global sum's per-rank partials are finished by one NCCL all-reduce.
-Times are CUDA events on the launching stream, the job time is the max over ranks.
+Multi-GPU (torchrun, one process per GPU): each configuration is ONE problem split
+across the GPUs (strong scaling): GEMM and FP8 by N-panel (A replicated), attention by
+batch (batch x head pairs), RMSNorm and softmax by rows, the sum by chunks whose f64
+partials one NCCL all-reduce finishes inside every step.  ``value`` is the whole
+problem's work divided by the slowest rank's time (CUDA events on the launching
+stream, max over ranks).
 
-The JSON line carries the device-resident throughput (``value``), the end-to-end
-throughput through the C-ABI runtime with host buffers (``e2e``: every step copies its
-inputs up from pinned host memory and its result down; steps are pipelined over two
-device buffer sets and three streams, so step i+1's upload and step i-1's download
-overlap step i's kernel), the roofline of
-the kernel, a CPU baseline (the oracle port, timed on a bounded sample), SM clocks
-sampled during the timed region, and the number of our kernel launches timed.
-``--impl reference`` times the reference path's CPU evaluation (the numpy oracle the
-reference's harness computes expected outputs with) on the same configuration.
+``e2e`` is the same metric through the C-ABI runtime with host buffers: every step
+copies its inputs up from pinned host memory and its result down (pipelined over two
+device buffer sets and three streams).  ``cpu_baseline`` and ``--impl reference`` time
+the torch-CPU evaluation of the configuration (the reference harness's own form of
+the problem) on the host's cores, on the same bounded sample; the reference arm loads
+none of this repository's native code.
 """
 
 from __future__ import annotations
 
 import argparse
+import gc
 import json
+import math
 import os
 import sys
 import threading
@@ -42,26 +47,18 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT / "emmy-hackathon-2026_b200"))
 sys.path.insert(0, str(ROOT))
 
-METRIC = "GEMM/attention TFLOP/s & reduction HBM GB/s vs B200 peak at 1/2/4/8 GPUs"
-L2_BYTES = 126 * 2 ** 20
+import baseline_configs as bc  # noqa: E402  (pure numpy: no native library)
 
-# workload -> (synthesised problem, unit, kernel family)
-WORKLOADS = {
-    "gemm_8192": ("gemm_8192", "TFLOP/s", "gemm"),
-    "gemm_4096x14336x4096": ("gemm_4096x14336x4096", "TFLOP/s", "gemm"),
-    "gemm_2048": ("gemm_2048", "TFLOP/s", "gemm"),
-    "gemm_512": ("gemm_512", "TFLOP/s", "gemm"),
-    "gemm_f32_4096": ("gemm_f32_4096", "TFLOP/s", "gemm"),     # f32 (3xTF32), not a BASELINE config
-    "attention": ("attention", "TFLOP/s", "attention"),
-    "fp8_8192": ("fp8_8192", "TFLOP/s", "fp8"),
-    "rmsnorm": ("rmsnorm", "GB/s", "row"),
-    "softmax": ("softmax", "GB/s", "row"),
-    "sum": ("sum", "GB/s", "sum"),
-}
+METRIC = "GEMM/attention TFLOP/s & reduction HBM GB/s vs B200 peak at 1/2/4/8 GPUs"
+HEADLINE = "gemm_8192"
+L2_BYTES = 126 * 2 ** 20
+MIN_REGION_S = 0.3          # timed region of each non-headline workload
+MAX_LAUNCHES = 50000
+EXTRA = ("gemm_f32_4096",)  # measurable on request, not BASELINE configurations
 
 
 # ---------------------------------------------------------------------------
-# distributed plumbing
+# distributed plumbing (host side: gloo barrier / max; NCCL lives in the runtime)
 
 
 class Dist:
@@ -74,7 +71,7 @@ class Dist:
             import torch.distributed as td
             # a rank that dies ends the others' next collective with an error within this
             # limit instead of a hang
-            limit = float(os.environ.get("EMMY_PG_TIMEOUT_S", 180))
+            limit = float(os.environ.get("EMMY_PG_TIMEOUT_S", 300))
             td.init_process_group("gloo", timeout=timedelta(seconds=limit))
             self.pg = td
 
@@ -90,7 +87,7 @@ class Dist:
         self.pg.all_reduce(t, op=self.pg.ReduceOp.MAX)
         return float(t.item())
 
-    def broadcast_bytes(self, b: bytes | None) -> bytes:
+    def broadcast_bytes(self, b):
         if not self.pg:
             return b
         obj = [b]
@@ -103,15 +100,16 @@ class Dist:
 
 
 # ---------------------------------------------------------------------------
-# clocks (read-only NVML sampling during the timed region)
+# clocks (read-only NVML sampling during a timed region, every millisecond)
 
 
 class ClockSampler:
     REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown",
                0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown"}
 
-    def __init__(self, device: int):
-        self.samples, self.reasons, self.max_mhz = [], set(), None
+    def __init__(self, device: int, period_s: float = 0.001):
+        self.samples, self.power, self.reasons, self.max_mhz = [], [], set(), None
+        self.period = period_s
         self._stop = threading.Event()
         try:
             import pynvml
@@ -122,18 +120,22 @@ class ClockSampler:
         except Exception:
             self.nv = None
 
-    def _run(self):
+    def _sample(self):
         nv = self.nv
+        try:
+            self.samples.append(nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM))
+            bits = nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+            for b, n in self.REASONS.items():
+                if bits & b:
+                    self.reasons.add(n)
+            self.power.append(nv.nvmlDeviceGetPowerUsage(self.h) / 1000.0)
+        except Exception:
+            pass
+
+    def _run(self):
         while not self._stop.is_set():
-            try:
-                self.samples.append(nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM))
-                bits = nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
-                for b, n in self.REASONS.items():
-                    if bits & b:
-                        self.reasons.add(n)
-            except Exception:
-                pass
-            time.sleep(0.01)
+            self._sample()
+            time.sleep(self.period)
 
     def __enter__(self):
         if self.nv:
@@ -145,85 +147,22 @@ class ClockSampler:
         self._stop.set()
         if self.nv:
             self.t.join()
+            self._sample()
 
     def summary(self) -> dict:
         s = sorted(self.samples)
         return {"sm_mhz": float(np.median(s)) if s else None, "sm_max_mhz": self.max_mhz,
-                "samples": len(s), "reasons": sorted(self.reasons)}
+                "samples": len(s), "period_ms": self.period * 1e3,
+                "power_w_max": round(max(self.power), 1) if self.power else None,
+                "reasons": sorted(self.reasons)}
 
 
 # ---------------------------------------------------------------------------
-# workload construction
+# shared helpers
 
 
-def problem(name: str):
-    if name == "fp8_8192":
-        # no IR family (the reference has no FP8 GEMM): the pipeline is built from the
-        # templates directly; the "meta" describes its graph inputs and output
-        n = 8192
-        return None, {"kernels": [{"entry": "k_gemm_e4m3", "args": [
-            {"name": "a", "dtype": "f32", "shape": [n, n], "seed": 0},
-            {"name": "b", "dtype": "f32", "shape": [n, n], "seed": 1},
-            {"name": "c", "dtype": "bf16", "shape": [n, n], "output": True}]}]}
-    from compiler.synth import baseline_dir
-    d = baseline_dir(name)
-    meta = json.loads((d / "meta.json").read_text())
-    return d, meta
-
-
-def host_inputs(name: str, meta: dict, rank: int) -> dict:
-    """Seeded synthetic inputs with BASELINE.json's distributions (rank-distinct
-    panels under multi-GPU runs)."""
-    from emmyrt.runner import f32_to_bf16_bits, NP_DTYPE
-    k = meta["kernels"][0]
-    rng = np.random.default_rng(1000 * rank + 7)
-    out = {}
-    for a in k["args"]:
-        shape = tuple(a["shape"]) or (1,)
-        if a.get("output"):
-            out[a["name"]] = np.zeros(shape, dtype=NP_DTYPE[a["dtype"]])
-            continue
-        if "data" in a:
-            out[a["name"]] = np.asarray(a["data"], dtype=NP_DTYPE[a["dtype"]])
-            continue
-        if name.startswith("gemm"):
-            v = rng.standard_normal(shape, dtype=np.float32) * np.float32(0.05)
-        elif name == "sum":
-            v = rng.random(shape, dtype=np.float32) * np.float32(2) - np.float32(1)
-        elif name == "softmax":
-            v = rng.standard_normal(shape, dtype=np.float32) * np.float32(np.sqrt(2.0))
-        elif name == "rmsnorm" and len(shape) == 1:
-            v = rng.random(shape, dtype=np.float32) + np.float32(0.5)
-        else:
-            v = rng.standard_normal(shape, dtype=np.float32)
-        out[a["name"]] = f32_to_bf16_bits(v) if a["dtype"] == "bf16" else v.astype(NP_DTYPE[a["dtype"]])
-    return out
-
-
-def work_units(name: str, ck, meta: dict) -> float:
-    """Algorithmic work of one launch: flops for tensor-core kernels, bytes read once
-    + written once for streaming kernels."""
-    L = ck.launch
-    if "flops" in L:
-        return float(L["flops"])
-    k = meta["kernels"][0]
-    nbytes = 0
-    for a in k["args"]:
-        n = int(np.prod(a["shape"] or [1]))
-        if n > 1:
-            nbytes += n * {"f32": 4, "bf16": 2, "f16": 2}[a["dtype"]]
-    return float(nbytes)
-
-
-def traffic_from_profile(workload: str):
-    """DRAM bytes per launch from the committed ncu summary, if one exists."""
-    p = ROOT / "profiles" / f"{workload}.md"
-    if not p.exists():
-        return None
-    for line in p.read_text().splitlines():
-        if line.strip().startswith("dram_bytes_per_launch:"):
-            return float(line.split(":", 1)[1].strip().split()[0])
-    return None
+def to_rate(units: float, seconds: float, unit: str) -> float:
+    return units / seconds / (1e12 if unit == "TFLOP/s" else 1e9)
 
 
 def measured_peaks() -> tuple[dict, str]:
@@ -233,266 +172,347 @@ def measured_peaks() -> tuple[dict, str]:
     return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
 
 
-# ---------------------------------------------------------------------------
-# CPU side: the oracle port (reference arm and cpu_baseline)
+def traffic_from_profile(workload: str):
+    """DRAM bytes per launch of the whole problem from the committed ncu summary."""
+    p = ROOT / "profiles" / f"{workload}.md"
+    if not p.exists():
+        return None
+    for line in p.read_text().splitlines():
+        if line.strip().startswith("dram_bytes_per_launch:"):
+            return float(line.split(":", 1)[1].strip().split()[0])
+    return None
 
 
-def cpu_sample_fn(name: str, inputs: dict, meta: dict, target_s: float = 2.0):
-    """(fn, units, description) for one bounded CPU sample of the workload, computed
-    by the oracle; GEMM samples are sized to take about ``target_s`` seconds."""
-    from oracle import refs
-    from emmyrt.runner import bf16_bits_to_f32
-    if name == "fp8_8192":
-        from emmyrt.fp8 import e4m3_decode  # noqa: F401
-        A, B = inputs["a"], inputs["b"]
-        sa = np.float32(np.abs(A).max()) / np.float32(448.0)
-        sb = np.float32(np.abs(B).max()) / np.float32(448.0)
-        Aq = refs.e4m3_round(A / sa)
-        Bq = refs.e4m3_round(B / sb)
-        rows = 128
-        sub = Aq[:rows]
-        return (lambda: refs.mm_fp8(sub, Bq, sa, sb)), 2.0 * rows * B.shape[0] * B.shape[1], \
-            f"{rows} rows of the e4m3-valued A against the full B (oracle mm_fp8, f64 BLAS)"
-    if name.startswith("gemm"):
-        f32_ops = inputs["x0"].dtype == np.float32
-        A = inputs["x0"] if f32_ops else bf16_bits_to_f32(inputs["x0"])
-        B = inputs["x1"] if f32_ops else bf16_bits_to_f32(inputs["x1"])
-        mm, mm_name = (refs.mm_f32, "mm_f32") if f32_ops else (refs.mm_bf16, "mm_bf16")
-        rows = max(1, min(A.shape[0], 256))
-        t0 = time.perf_counter()
-        mm(A[:rows], B)
-        dt = time.perf_counter() - t0
-        rows = int(max(1, min(A.shape[0], rows * max(1.0, target_s / max(dt, 1e-3)))))
-        sub = A[:rows]
-        return (lambda: mm(sub, B)), 2.0 * rows * B.shape[0] * B.shape[1], \
-            f"{rows} rows of A against the full B (oracle {mm_name}, f64 BLAS)"
+def config_of(name: str, world: int) -> dict:
+    """The line's ``config`` (identical in both arms)."""
+    c = bc.CONFIGS[name] if name in bc.CONFIGS else None
+    if c is None:
+        return {"workload": name}
+    in_bytes = _input_bytes(name, 0, world)
+    copies = 1 if in_bytes > L2_BYTES else -(-2 * L2_BYTES // max(1, in_bytes))
+    return {"workload": name, "problem": list(c.dims), "dtype": c.dtype,
+            "parallelism": f"{world} GPU(s); split by {c.shard_by}" if world > 1 else "1 GPU",
+            "l2": ("inputs larger than L2" if copies == 1 else
+                   f"inputs rotated over {copies} device copies ({copies * in_bytes >> 20} MiB, > L2)")}
+
+
+def _input_bytes(name: str, rank: int, world: int) -> int:
+    c = bc.CONFIGS[name]
+    d = bc.shard_dims(name, rank, world)
+    if c.family == "gemm":
+        return 2 * (d["m"] * d["k"] + d["k"] * d["n"])
+    if c.family == "fp8":
+        return d["m"] * d["k"] + d["k"] * d["n"]      # the e4m3 operands the GEMM reads
     if name == "attention":
-        q, k, v = (bf16_bits_to_f32(inputs[n]) for n in ("x0", "x1", "x2"))
-        S, D = q.shape[-2], q.shape[-1]
-        scale = 1.0 / np.sqrt(D)
-        rows = 64
-        t0 = time.perf_counter()
-        refs.attn_bf16(q[0, 0, :rows], k[0, 0], v[0, 0], scale)
-        dt = time.perf_counter() - t0
-        rows = int(max(1, min(S, rows * max(1.0, target_s / max(dt, 1e-3)))))
-        sub = q[0, 0, :rows]
-        return (lambda: refs.attn_bf16(sub, k[0, 0], v[0, 0], scale)), 4.0 * rows * S * D, \
-            f"{rows} query rows of one batch x head pair against its {S} keys (oracle attn_bf16, f64)"
-    if name == "rmsnorm":
-        x, w = inputs["x0"], inputs["x1"]
-        return (lambda: refs.rmsnorm(x, w, 1e-6)), float(2 * x.nbytes + w.nbytes), "full 4096x4096"
-    if name == "softmax":
-        x = inputs["x"][:4096]
-        return (lambda: refs.softmax(x)), float(2 * x.nbytes), "4096 of the 65536 rows"
+        return 3 * 2 * d["b"] * d["h"] * d["s"] * d["d"]
+    if c.family == "row":
+        r = d["rows"][1] - d["rows"][0]
+        return 4 * r * d["cols"] + (4 * d["cols"] if name == "rmsnorm" else 0)
     if name == "sum":
-        x = inputs["x"][: 1 << 28]
-        return (lambda: refs.total_sum(x)), float(x.nbytes), "first 2^28 of the 2^31 elements"
+        return 4 * (d["rows"][1] - d["rows"][0])
     raise KeyError(name)
 
 
-def time_cpu(fn, reps: int) -> float:
-    best = float("inf")
-    for _ in range(reps):
-        t0 = time.perf_counter()
-        fn()
-        best = min(best, time.perf_counter() - t0)
-    return best
+def regime_of(region_s: float, clocks: dict) -> str:
+    """burst: a short region at full clock; sustained: long enough to sit at the power cap."""
+    if region_s >= 1.0 or "sw_power_cap" in clocks.get("reasons", []):
+        return "sustained"
+    return "burst"
 
 
-def to_rate(units: float, seconds: float, unit: str) -> float:
-    return units / seconds / (1e12 if unit == "TFLOP/s" else 1e9)
+def roofline(name: str, unit: str, units_per_launch: float, launch_s: float, clocks: dict,
+             region_s: float, world: int) -> dict:
+    peaks, kind = measured_peaks()
+    achieved = to_rate(units_per_launch, launch_s, unit)
+    regime = regime_of(region_s, clocks)
+    if name == "fp8_8192":
+        # no measured fp8 figure: the dense e4m3 rate is twice bf16's on this part
+        burst, sust = 2 * float(peaks["bf16_tflops"]), 2 * float(peaks["bf16_tflops_sustained"])
+        what = f"derived: 2 x {kind} bf16_tflops"
+    elif name == "gemm_f32_4096":
+        burst, sust = float(peaks["bf16_tflops"]) / 6, float(peaks["bf16_tflops_sustained"]) / 6
+        what = f"derived: {kind} bf16_tflops / 2 (tf32) / 3 (MMAs per product)"
+    elif unit == "TFLOP/s":
+        burst, sust = float(peaks["bf16_tflops"]), float(peaks["bf16_tflops_sustained"])
+        what = f"{kind} bf16_tflops"
+    else:
+        burst = sust = float(peaks["hbm_gbs"])
+        what = f"{kind} hbm_gbs (copy)"
+    peak = burst if regime == "burst" else sust
+    out = {"bound": "tensor" if unit == "TFLOP/s" else "hbm", "achieved": round(achieved, 2),
+           "peak": peak, "unit": unit, "frac": round(achieved / peak, 4),
+           "peak_kind": f"{what} ({regime})", "regime": regime,
+           "frac_of_burst": round(achieved / burst, 4),
+           "traffic": traffic_from_profile(name) if world == 1 else None}
+    if unit == "TFLOP/s" and clocks.get("sm_mhz") and clocks.get("sm_max_mhz"):
+        # tensor-bound kernels scale with the SM clock: the rate the same launches would
+        # reach at the maximum clock (time x median MHz / max MHz)
+        out["achieved_at_max_clock"] = round(achieved * clocks["sm_max_mhz"] / clocks["sm_mhz"], 2)
+    return out
 
 
 # ---------------------------------------------------------------------------
+# CPU side: the torch-CPU evaluation (cpu_baseline leg and the reference arm)
+
+
+def cpu_measure(name: str, reps: int, warmup: int = 1) -> dict:
+    from oracle import torch_cpu
+    cores = torch_cpu.threads()
+    inputs, units, sample = bc.cpu_sample_inputs(name)
+    fn = torch_cpu.sample_fn(name, inputs)
+    for _ in range(max(1, warmup)):
+        fn()
+    times = []
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        fn()
+        times.append(time.perf_counter() - t0)
+    dt = float(np.median(times))
+    unit = bc.CONFIGS[name].unit
+    return {"value": round(to_rate(units, dt, unit), 4), "unit": unit, "cores": cores, "kind": "port",
+            "sample": f"{sample}; torch-CPU evaluation of the problem's torch expression, "
+                      f"median of {reps}", "ms_per_sample": round(dt * 1e3, 3), "_dt": dt,
+            "_units": units}
 
 
 def run_reference(args, dist: Dist) -> int:
-    name = args.workload
-    _, unit, _ = WORKLOADS[name]
+    """The reference's CPU evaluation (torch on the host cores) of the same configurations."""
     if dist.rank != 0:
         return 0
-    pname = WORKLOADS[name][0]
-    _, meta = problem(pname)
-    inputs = host_inputs(pname, meta, 0)
-    # each step a bounded sample, so the whole run stays within a couple of minutes
-    fn, units, sample = cpu_sample_fn(pname, inputs, meta,
-                                      target_s=min(1.0, 90.0 / (args.steps + args.warmup)))
-    for _ in range(args.warmup):
-        fn()
-    t0 = time.perf_counter()
-    for _ in range(args.steps):
-        fn()
-    dt = (time.perf_counter() - t0) / args.steps
-    v = to_rate(units, dt, unit)
-    line = {"metric": METRIC, "impl": "reference", "value": round(v, 3), "unit": unit,
+    names = _names(args)
+    head = names[0]
+    workloads = {}
+    for name in names:
+        steps = args.steps if name == head else 3
+        warm = args.warmup if name == head else 1
+        r = cpu_measure(name, steps, warm)
+        dt, units = r.pop("_dt"), r.pop("_units")
+        unit = bc.CONFIGS[name].unit
+        workloads[name] = {"value": r["value"], "unit": unit, "ms_per_step": r["ms_per_sample"],
+                           "steps": steps, "cpu_baseline": r,
+                           "e2e": {"value": r["value"], "unit": unit, "h2d_bytes_per_step": 0,
+                                   "d2h_bytes_per_step": 0}}
+        gc.collect()
+    h = workloads[head]
+    line = {"metric": METRIC, "impl": "reference", "value": h["value"], "unit": h["unit"],
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": round(dt * 1e3, 3), "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "f64", "data": "synthetic",
-            "config": {"workload": name, "sample": sample},
-            "cpu_baseline": {"value": round(v, 3), "unit": unit, "cores": os.cpu_count(),
-                             "kind": "port", "sample": sample},
-            "e2e": {"value": round(v, 3), "unit": unit, "h2d_bytes_per_step": 0,
-                    "d2h_bytes_per_step": 0}}
+            "ms_per_step": h["ms_per_step"], "higher_is_better": True,
+            "scaling": "strong" if args.gpus > 1 else "weak", "vs_baseline": None,
+            "dtype": bc.CONFIGS[head].dtype, "data": "synthetic",
+            "config": config_of(head, args.gpus), "cpu_baseline": h["cpu_baseline"],
+            "e2e": h["e2e"], "workloads": workloads}
     print(json.dumps(line), flush=True)
     return 0
 
 
-def run_ours(args, dist: Dist) -> int:
+# ---------------------------------------------------------------------------
+# our arm
+
+
+class Workload:
+    """One configuration's shard on this rank: compiled kernel, pinned host inputs,
+    device buffer sets, and the prepared launches."""
+
+    def __init__(self, name: str, dist: Dist, comm):
+        import emmyrt
+        from emmyrt import DeviceBuffer, HostBuffer
+        from emmyrt.runner import CompiledKernel
+        from compiler import synth
+        self.name, self.dist, self.comm = name, dist, comm
+        self.cfg = bc.CONFIGS[name] if name in bc.CONFIGS else None
+        self.unit = self.cfg.unit if self.cfg else "TFLOP/s"
+        if self.cfg is None:               # a non-BASELINE workload (e.g. the f32 GEMM)
+            irs, meta = synth.baseline_problem(name)
+        else:
+            irs, meta = bc.shard_problem(name, dist.rank, dist.world)
+        self.meta = meta
+        k = meta["kernels"][0]
+        self.fp8 = None
+        if self.cfg is not None and self.cfg.family == "fp8":
+            from emmyrt.fp8 import Fp8Gemm
+            (m, kk), n = k["args"][0]["shape"], k["args"][1]["shape"][1]
+            self.fp8 = Fp8Gemm(m, n, kk)
+            self.ck = self.fp8.gemm
+        else:
+            d = synth.problem_dir(irs, meta)
+            self.ck = CompiledKernel.from_ir(d / f"{k['entry']}.ir.json")
+        self.host_bufs = []
+
+        def pinned(nb):
+            hb = HostBuffer(max(16, nb))
+            self.host_bufs.append(hb)
+            return hb.array(np.uint8, (max(16, nb),))[:nb]
+        if self.cfg is not None:
+            self.inputs = bc.shard_inputs(name, meta, dist.rank, dist.world, alloc=pinned)
+        else:
+            from hostfmt import NP_DTYPE
+            self.inputs = {}
+            for a in k["args"]:
+                arr = pinned(int(np.prod(a["shape"] or [1])) * np.dtype(NP_DTYPE[a["dtype"]]).itemsize)
+                arr = arr.view(NP_DTYPE[a["dtype"]]).reshape(tuple(a["shape"]) or (1,))
+                arr[...] = (np.random.default_rng(a.get("seed", 0)).standard_normal(arr.shape)
+                            if not a.get("output") else 0)
+                self.inputs[a["name"]] = arr
+        self.args = k["args"]
+        self.in_names = [a["name"] for a in k["args"] if not a.get("output") and "data" not in a]
+        self.out_names = [a["name"] for a in k["args"] if a.get("output")]
+        self.in_bytes = sum(self.inputs[n].nbytes for n in self.in_names)
+        dev_in = (_input_bytes(name, dist.rank, dist.world) if self.cfg is not None else self.in_bytes)
+        self.copies = 1 if dev_in > L2_BYTES else -(-2 * L2_BYTES // max(1, dev_in))
+        if self.fp8 is not None:
+            self.copies = 1                 # the quantised operands are one set (> L2)
+        self.bufsets = []
+        for _ in range(self.copies):
+            bufs = {}
+            for a in k["args"]:
+                h = self.inputs[a["name"]]
+                b = DeviceBuffer(h.nbytes)
+                b.upload(h)
+                bufs[a["name"]] = b
+            self.bufsets.append(bufs)
+        if self.fp8 is not None:
+            # quantisation is outside the timed region (BASELINE: "quantised before timing");
+            # a sharded B needs the amax of all of B: one all-reduce (max) of the panels' amax
+            bs = self.bufsets[0]
+            self.fp8.quantize(bs["a"].ptr, bs["b"].ptr, amax_b_hook=self._amax_hook())
+            self.params = [self.fp8.gemm_params(bs["c"].ptr)]
+        else:
+            self.params = [self.ck.params({n: b.ptr for n, b in bs.items()}) for bs in self.bufsets]
+        self.fire = [self.ck.prepare(pp) for pp in self.params]
+        # the sharded sum: f64 totals (scratch + 8) all-reduced into one f64 per rank
+        self.total = None
+        if self.cfg is not None and self.cfg.family == "sum" and comm is not None:
+            ex = [i for i, e in enumerate(self.ck.launch["extra_params"]) if e["kind"] == "scratch"]
+            off = self.ck.launch["extra_params"][ex[0]]["f64_total_offset"]
+            self.partial_ptr = self.ck.scratch[ex[0]].ptr + off
+            self.total = DeviceBuffer(16)
+        emmyrt.synchronize()
+
+    def _amax_hook(self):
+        if self.comm is None:
+            return None
+        from emmyrt.dist import NCCL_FLOAT32, NCCL_MAX
+        comm = self.comm
+        return lambda ptr, stream: comm.allreduce(ptr, ptr, 1, NCCL_FLOAT32, NCCL_MAX, stream)
+
+    def step(self, i: int, stream: int) -> None:
+        self.fire[i % len(self.fire)](stream)
+        if self.total is not None:
+            from emmyrt.dist import NCCL_FLOAT64
+            self.comm.allreduce(self.partial_ptr, self.total.ptr, 1, NCCL_FLOAT64, stream=stream)
+
+    @property
+    def launches_per_step(self) -> int:
+        return 1
+
+    def free(self):
+        for bs in self.bufsets:
+            for b in bs.values():
+                b.free()
+        self.bufsets = []
+        for hb in self.host_bufs:
+            hb.free()
+        self.host_bufs = []
+        if self.total is not None:
+            self.total.free()
+
+
+def _time_region(w: Workload, steps: int, dist: Dist, stream: int = 0) -> tuple[float, dict, str]:
+    """Time `steps` steps on one stream (a CUDA graph of the launches when no collective
+    is in the step); returns (max-over-ranks ms, clock summary, launch form)."""
     import emmyrt
-    from emmyrt import DeviceBuffer, Event, HostBuffer, check, lib
-    from emmyrt.runner import CompiledKernel, NP_DTYPE
-    name = args.workload
-    pname, unit, family = WORKLOADS[name]
-    emmyrt.init(dist.local)
-    d, meta = problem(pname)
-    k = meta["kernels"][0]
-    inputs = host_inputs(pname, meta, dist.rank)
-    fp8 = None
-    if family == "fp8":
-        from emmyrt.fp8 import Fp8Gemm
-        n = k["args"][0]["shape"][0]
-        fp8 = Fp8Gemm(n, n, n)
-        ck = fp8.gemm
-    else:
-        ck = CompiledKernel.from_ir(d / f"{k['entry']}.ir.json")
-    in_names = [a["name"] for a in k["args"] if not a.get("output") and "data" not in a]
-    out_names = [a["name"] for a in k["args"] if a.get("output")]
-    in_bytes = sum(inputs[n].nbytes for n in in_names)
-    # inputs larger than L2 (or rotated over enough copies to exceed it)
-    copies = 1 if in_bytes > L2_BYTES else -(-2 * L2_BYTES // max(1, in_bytes))
-    bufsets = []
-    for c in range(copies):
-        bufs = {}
-        for a in k["args"]:
-            h = inputs[a["name"]]
-            b = DeviceBuffer(h.nbytes)
-            b.upload(h)
-            bufs[a["name"]] = b
-        bufsets.append(bufs)
-    if fp8 is not None:
-        # quantisation is outside the timed region (BASELINE: "quantised before timing")
-        fp8.quantize(bufsets[0]["a"].ptr, bufsets[0]["b"].ptr)
-        params = [fp8.gemm_params(bufsets[0]["c"].ptr)]
-    else:
-        params = [ck.params({n: b.ptr for n, b in bs.items()}) for bs in bufsets]
-    stream = 0
-    comm = None
-    if family == "sum" and dist.world > 1:
-        # each rank reduces its own 2^31-element chunk; one NCCL all-reduce (sum) of the
-        # per-rank f32 results finishes the global sum in every step
-        from emmyrt.dist import NcclComm, share_unique_id
-        uid = share_unique_id(dist.rank, dist.broadcast_bytes)
-        comm = NcclComm(uid, dist.world, dist.rank)
-        out_ptrs = [bs[[a["name"] for a in k["args"] if a.get("output")][0]].ptr for bs in bufsets]
-
-    fire = [ck.prepare(pp) for pp in params]
-
-    def step(i):
-        fire[i % copies](stream)
-        if comm is not None:
-            o = out_ptrs[i % copies]
-            comm.allreduce(o, o, 1, stream=stream)
-
-    # warm-up, including one checked launch
-    for i in range(max(1, args.warmup)):
-        step(i)
-    emmyrt.stream_wait(stream, 120)
-    if ck.status():
-        raise RuntimeError(f"kernel status {ck.status()}")
-    # The K timed launches are captured once into a CUDA graph and replayed as one: a
-    # 20-microsecond kernel is not starved by per-launch host work (every launch still
-    # runs; NCCL-finished steps keep stream launches).  It is uploaded before timing.
+    from emmyrt import Event, Graph, Stream
     graph = None
-    if comm is None:
-        from emmyrt import Graph, Stream
+    if w.total is None:
         cap = Stream()
-        graph = Graph.capture(cap, lambda: [fire[i % copies](cap.handle) for i in range(args.steps)])
+        graph = Graph.capture(cap, lambda: [w.fire[i % len(w.fire)](cap.handle) for i in range(steps)])
         graph.upload(stream)
-        emmyrt.stream_wait(stream, 60)
+        emmyrt.stream_wait(stream, 120)
     dist.barrier()
     emmyrt.synchronize()
-    ev = [Event() for _ in range(args.steps + 1)]
+    e0, e1 = Event(), Event()
     with ClockSampler(dist.local) as clocks:
-        ev[0].record(stream)
+        e0.record(stream)
         if graph is not None:
             graph.launch(stream)
-            ev[-1].record(stream)
         else:
-            for i in range(args.steps):
-                step(i)
-                ev[i + 1].record(stream)
-        ev[-1].synchronize()
+            for i in range(steps):
+                w.step(i, stream)
+        e1.record(stream)
+        e1.synchronize()
     emmyrt.synchronize()
+    ms = e0.elapsed_ms(e1)
     dist.barrier()
-    total_ms = ev[0].elapsed_ms(ev[-1])
-    per_launch = ([total_ms / args.steps] * args.steps if graph is not None else
-                  [ev[i].elapsed_ms(ev[i + 1]) for i in range(args.steps)])
-    total_ms = dist.max(total_ms)
-    ms_step = total_ms / args.steps
-    units = work_units(pname, ck, meta)
-    value = to_rate(units * dist.world, ms_step / 1e3, unit)
+    ms = dist.max(ms)
+    del graph
+    return ms, clocks.summary(), ("one CUDA graph of the timed launches" if w.total is None else
+                                  "stream launches, kernel + NCCL all-reduce (f64) per step")
 
-    # end to end through the C-ABI runtime: pinned host inputs -> HBM -> kernel -> host result
-    host_in = {}
-    for n in in_names:
-        hb = HostBuffer(inputs[n].nbytes)
-        hb.array(inputs[n].dtype, inputs[n].shape)[...] = inputs[n]
-        host_in[n] = hb
-    host_out = {n: HostBuffer(inputs[n].nbytes) for n in out_names}
-    e2e_steps = max(2, min(args.steps, 20))
-    # Steps are pipelined over two device buffer sets and three streams: the inputs of
-    # step i+1 go up while step i computes and step i-1's result comes down (every step
-    # still copies its own inputs and result).  The FP8 pipeline (shared quantised
-    # operands) and the NCCL-finished sum keep one stream.
-    pipelined = fp8 is None and comm is None
+
+def _e2e(w: Workload, steps: int, dist: Dist) -> dict:
+    """Same metric through the C-ABI runtime with host buffers: every step copies its
+    inputs up from pinned host memory and its result down."""
+    import emmyrt
+    from emmyrt import DeviceBuffer, Event, Stream, check, lib
+    outs = {n: np.empty_like(w.inputs[n]) for n in w.out_names}
+    from emmyrt import HostBuffer
+    host_out = {n: HostBuffer(max(16, w.inputs[n].nbytes)) for n in w.out_names}
+    pipelined = w.fp8 is None and w.total is None
+    extra = None
     if pipelined:
-        from emmyrt import Stream
-        if copies >= 2:
-            e2e_sets, e2e_fire = bufsets[:2], fire[:2]
+        if w.copies >= 2:
+            sets, fires = w.bufsets[:2], w.fire[:2]
         else:
             extra = {}
-            for a in k["args"]:
-                h = inputs[a["name"]]
+            for a in w.args:
+                h = w.inputs[a["name"]]
                 extra[a["name"]] = DeviceBuffer(h.nbytes)
                 extra[a["name"]].upload(h)
-            e2e_sets = [bufsets[0], extra]
-            e2e_fire = [fire[0], ck.prepare(ck.params({n: b.ptr for n, b in extra.items()}))]
+            sets = [w.bufsets[0], extra]
+            fires = [w.fire[0], w.ck.prepare(w.ck.params({n: b.ptr for n, b in extra.items()}))]
         s_in, s_run, s_out = Stream(), Stream(), Stream()
         ev_in, ev_run, ev_out = [Event(), Event()], [Event(), Event()], [Event(), Event()]
-        t_stream = s_in.handle
+        t_stream, end_stream = s_in.handle, s_out.handle
 
         def e2e_step(i):
             b = i % 2
-            bs = e2e_sets[b]
+            bs = sets[b]
             if i >= 2:
                 s_in.wait(ev_run[b])          # step i-2's kernel has read this set's inputs
-            for n in in_names:
-                check(lib.emmy_rt_memcpy_htod(bs[n].ptr, host_in[n].ptr, inputs[n].nbytes, s_in.handle),
-                      "htod")
+            for n in w.in_names:
+                check(lib.emmy_rt_memcpy_htod(bs[n].ptr, w.inputs[n].ctypes.data, w.inputs[n].nbytes,
+                                              s_in.handle), "htod")
             ev_in[b].record(s_in.handle)
             s_run.wait(ev_in[b])
             if i >= 2:
                 s_run.wait(ev_out[b])         # step i-2's result has left this set's output
-            e2e_fire[b](s_run.handle)
+            fires[b](s_run.handle)
             ev_run[b].record(s_run.handle)
             s_out.wait(ev_run[b])
-            for n in out_names:
-                check(lib.emmy_rt_memcpy_dtoh(host_out[n].ptr, bs[n].ptr, inputs[n].nbytes, s_out.handle),
+            for n in w.out_names:
+                check(lib.emmy_rt_memcpy_dtoh(host_out[n].ptr, bs[n].ptr, w.inputs[n].nbytes, s_out.handle),
                       "dtoh")
             ev_out[b].record(s_out.handle)
-        end_stream = s_out.handle
+        d2h = sum(w.inputs[n].nbytes for n in w.out_names)
     else:
-        bufs = bufsets[0]
-        t_stream = end_stream = stream
+        bufs = w.bufsets[0]
+        t_stream = end_stream = 0
+        res = w.total if w.total is not None else None
 
         def e2e_step(i):
-            for n in in_names:
-                check(lib.emmy_rt_memcpy_htod(bufs[n].ptr, host_in[n].ptr, inputs[n].nbytes, stream), "htod")
-            if fp8 is not None:
-                fp8.quantize(bufs["a"].ptr, bufs["b"].ptr, stream)
-            step(0)
-            for n in out_names:
-                check(lib.emmy_rt_memcpy_dtoh(host_out[n].ptr, bufs[n].ptr, inputs[n].nbytes, stream), "dtoh")
+            for n in w.in_names:
+                check(lib.emmy_rt_memcpy_htod(bufs[n].ptr, w.inputs[n].ctypes.data, w.inputs[n].nbytes, 0),
+                      "htod")
+            if w.fp8 is not None:
+                w.fp8.quantize(bufs["a"].ptr, bufs["b"].ptr, 0, amax_b_hook=w._amax_hook())
+            w.step(0, 0)
+            if res is not None:       # the all-reduced f64 sum is the step's result
+                check(lib.emmy_rt_memcpy_dtoh(host_out[w.out_names[0]].ptr, res.ptr, 8, 0), "dtoh")
+            else:
+                for n in w.out_names:
+                    check(lib.emmy_rt_memcpy_dtoh(host_out[n].ptr, bufs[n].ptr, w.inputs[n].nbytes, 0),
+                          "dtoh")
+        d2h = 8 if res is not None else sum(w.inputs[n].nbytes for n in w.out_names)
     for i in range(2):
         e2e_step(i)
     emmyrt.synchronize()
@@ -500,93 +520,140 @@ def run_ours(args, dist: Dist) -> int:
     emmyrt.synchronize()
     e0, e1 = Event(), Event()
     e0.record(t_stream)
-    for i in range(e2e_steps):
+    for i in range(steps):
         e2e_step(i)
     e1.record(end_stream)
     e1.synchronize()
-    e2e_ms = dist.max(e0.elapsed_ms(e1) / e2e_steps)
-    e2e_value = to_rate(units * dist.world, e2e_ms / 1e3, unit)
-
-    # roofline of the kernel (average launch duration, measured live above)
-    peaks, peak_kind = measured_peaks()
-    avg_launch_s = float(np.mean(per_launch)) / 1e3
-    achieved = to_rate(units, avg_launch_s, unit)
-    if family == "fp8":
-        # no measured fp8 figure: the dense e4m3 rate is twice bf16's on this part
-        bound, peak = "tensor", 2.0 * float(peaks["bf16_tflops"])
-        kind_txt = f"derived: 2 x {peak_kind} bf16_tflops burst"
-    elif name == "gemm_f32_4096":
-        # 3xTF32: three kind::tf32 MMAs per f32 product, tf32 at half the bf16 rate
-        bound, peak = "tensor", float(peaks["bf16_tflops"]) / 6.0
-        kind_txt = f"derived: {peak_kind} bf16_tflops burst / 2 (tf32) / 3 (MMAs per product)"
-    elif unit == "TFLOP/s":
-        bound, peak = "tensor", float(peaks["bf16_tflops"])
-        kind_txt = f"{peak_kind} (bf16_tflops burst)"
-    else:
-        bound, peak = "hbm", float(peaks["hbm_gbs"])
-        kind_txt = f"{peak_kind} (hbm_gbs)"
-    roofline = {"bound": bound, "achieved": round(achieved, 2), "peak": peak,
-                "peak_kind": kind_txt,
-                "unit": unit, "frac": round(achieved / peak, 4), "traffic": traffic_from_profile(name)}
-    if bound == "tensor" and "bf16_tflops_sustained" in peaks:
-        # the same measured GEMM run seconds-long under the power cap: the denominator for a
-        # timed region long enough to settle at the cap (sw_power_cap in "clocks")
-        scale = peak / float(peaks["bf16_tflops"])
-        ps = float(peaks["bf16_tflops_sustained"]) * scale
-        roofline["peak_sustained"] = round(ps, 2)
-        roofline["frac_sustained"] = round(achieved / ps, 4)
-
-    cpu = None
-    if dist.rank == 0 and dist.world == 1 and not args.no_cpu:
-        fn, cunits, sample = cpu_sample_fn(pname, inputs, meta)
-        cdt = time_cpu(fn, 2)
-        cpu = {"value": round(to_rate(cunits, cdt, unit), 4), "unit": unit, "cores": os.cpu_count(),
-               "kind": "port", "sample": sample}
-
-    if dist.rank == 0:
-        line = {
-            "metric": METRIC, "value": round(value, 2), "unit": unit, "n_gpus": dist.world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 4),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": "f32" if name == "gemm_f32_4096" else
-                     {"gemm": "bf16", "attention": "bf16", "fp8": "e4m3"}.get(family, "f32"),
-            "data": "synthetic",
-            "config": {"workload": name, "kernel": k["entry"], "grid": ck.launch["grid"],
-                       "block": ck.launch["block"], "smem": ck.launch["smem"],
-                       "l2": ("inputs larger than L2" if copies == 1 else
-                              f"inputs rotated over {copies} copies ({copies * in_bytes >> 20} MiB)"),
-                       "parallelism": f"{dist.world} GPU(s), one panel per rank, no collective"
-                       if family != "sum" else f"{dist.world} GPU(s)"},
-            "e2e": {"value": round(e2e_value, 3), "unit": unit, "h2d_bytes_per_step": int(in_bytes),
-                    "d2h_bytes_per_step": int(sum(inputs[n].nbytes for n in out_names)),
-                    "steps": e2e_steps, "pipelined": pipelined},
-            "roofline": roofline,
-            "cpu_baseline": cpu,
-            "clocks": clocks.summary(),
-            "gpu_launches": args.steps,
-            "launch": "one CUDA graph of the timed launches" if graph is not None else "stream launches",
-        }
-        print(json.dumps(line), flush=True)
-    if comm is not None:
-        emmyrt.synchronize()
-        dist.barrier()
-        comm.destroy()
-    for bs in bufsets:
-        for b in bs.values():
+    ms = dist.max(e0.elapsed_ms(e1) / steps)
+    if extra:
+        for b in extra.values():
             b.free()
+    for hb in host_out.values():
+        hb.free()
+    del outs
+    total = bc.work(w.name, 0, 1) if w.cfg is not None else _units_of(w)
+    return {"value": round(to_rate(total, ms / 1e3, w.unit), 3), "unit": w.unit,
+            "h2d_bytes_per_step": int(w.in_bytes), "d2h_bytes_per_step": int(d2h),
+            "ms_per_step": round(ms, 4), "steps": steps, "pipelined": pipelined,
+            "quantise_in_step": w.fp8 is not None}
+
+
+def _units_of(w: Workload) -> float:
+    L = w.ck.launch
+    return float(L["flops"]) if "flops" in L else float(w.in_bytes)
+
+
+def measure(name: str, args, dist: Dist, comm, headline: bool) -> dict:
+    import emmyrt
+    w = Workload(name, dist, comm)
+    try:
+        unit = w.unit
+        # warm-up (one checked launch first)
+        for i in range(max(1, args.warmup)):
+            w.step(i, 0)
+        emmyrt.stream_wait(0, 300)
+        if w.ck.status():
+            raise RuntimeError(f"{name}: kernel status {w.ck.status()}")
+        # steps: exactly K for the headline; others stretched to >= MIN_REGION_S
+        from emmyrt import Event
+        e0, e1 = Event(), Event()
+        e0.record(0)
+        for i in range(3):
+            w.step(i, 0)
+        e1.record(0)
+        e1.synchronize()
+        est_s = dist.max(e0.elapsed_ms(e1) / 3) / 1e3
+        steps = args.steps if headline else \
+            int(min(MAX_LAUNCHES, max(args.steps, math.ceil(MIN_REGION_S / max(est_s, 1e-7)))))
+        ms, clocks, form = _time_region(w, steps, dist)
+        if w.ck.status():
+            raise RuntimeError(f"{name}: kernel status {w.ck.status()} after the timed region")
+        ms_step = ms / steps
+        total = bc.work(name, 0, 1) if w.cfg is not None else _units_of(w)
+        mine = bc.work(name, dist.rank, dist.world) if w.cfg is not None else total
+        value = to_rate(total, ms_step / 1e3, unit)
+        rec = {"value": round(value, 2), "unit": unit, "ms_per_step": round(ms_step, 5),
+               "steps": steps, "region_ms": round(ms, 3),
+               "roofline": roofline(name, unit, dist.max(mine) if dist.world > 1 else mine,
+                                    ms_step / 1e3, clocks, ms / 1e3, dist.world),
+               "clocks": clocks,
+               "ms_x_sm_mhz": round(ms_step * clocks["sm_mhz"], 3) if clocks.get("sm_mhz") else None,
+               "gpu_launches": steps * w.launches_per_step, "launch": form,
+               "kernel": {"entry": w.ck.spec.name, "grid": w.ck.launch["grid"],
+                          "block": w.ck.launch["block"], "smem": w.ck.launch.get("smem", 0)},
+               "config": config_of(name, dist.world) if w.cfg is not None else {"workload": name}}
+        rec["e2e"] = _e2e(w, max(3, min(args.steps, 10)), dist)
+        if dist.rank == 0 and dist.world == 1 and not args.no_cpu and w.cfg is not None:
+            c = cpu_measure(name, 3)
+            c.pop("_dt"), c.pop("_units")
+            rec["cpu_baseline"] = c
+        else:
+            rec["cpu_baseline"] = None
+        return rec
+    finally:
+        w.free()
+        del w
+        gc.collect()
+
+
+def _names(args) -> list:
+    if args.workload == "all":
+        return list(bc.ORDER)
+    return [args.workload]
+
+
+def run_ours(args, dist: Dist) -> int:
+    import emmyrt
+    emmyrt.init(dist.local)
+    comm = None
+    if dist.world > 1:
+        from emmyrt.dist import NcclComm, share_unique_id
+        uid = share_unique_id(dist.rank, dist.broadcast_bytes)
+        comm = NcclComm(uid, dist.world, dist.rank)
+    names = _names(args)
+    results = {}
+    try:
+        for name in names:
+            if name in EXTRA and dist.world > 1:
+                continue
+            results[name] = measure(name, args, dist, comm, headline=(name == names[0]))
+    finally:
+        if comm is not None:
+            emmyrt.synchronize()
+            dist.barrier()
+            comm.destroy()
+    if dist.rank == 0:
+        head = names[0]
+        h = results[head]
+        line = {"metric": METRIC, "value": h["value"], "unit": h["unit"], "n_gpus": dist.world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": h["ms_per_step"],
+                "higher_is_better": True, "scaling": "strong" if dist.world > 1 else "weak",
+                "vs_baseline": None,
+                "dtype": bc.CONFIGS[head].dtype if head in bc.CONFIGS else "f32",
+                "data": "synthetic (seeded, BASELINE.json distributions)",
+                "config": h["config"], "e2e": h["e2e"], "roofline": h["roofline"],
+                "cpu_baseline": h["cpu_baseline"], "clocks": h["clocks"],
+                "gpu_launches": h["gpu_launches"], "launch": h["launch"], "kernel": h["kernel"]}
+        if len(results) > 1:
+            line["workloads"] = results
+        print(json.dumps(line), flush=True)
     return 0
 
 
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="gemm_8192")
-    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    ap.add_argument("--workload", choices=["all", *bc.ORDER, *EXTRA], default="all")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline samples")
     args = ap.parse_args(argv)
     args.warmup = max(3, args.warmup)
+    if args.workload in EXTRA and args.impl == "reference":
+        print(json.dumps({"impl": "reference", "unavailable": f"{args.workload} is not a BASELINE "
+                          "configuration; no CPU evaluation is defined for it"}))
+        return 0
     dist = Dist()
     try:
         if args.impl == "reference":

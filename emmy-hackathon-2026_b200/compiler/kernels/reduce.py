@@ -1055,7 +1055,9 @@ class FullReduce:
             p.emit(self._combine_f64(tot, q))
             pk = p.reg("pred")
             p.emit(f"add.s64 {ia}, {ia}, 8\nadd.u32 {k}, {k}, 1\nsetp.lt.u32 {pk}, {k}, {self.grid}\n@{pk} bra {lp}")
-        # reset the ticket for the next launch
+        # keep the f64 total beside the ticket (scratch bytes 8..16): a sharded reduction
+        # all-reduces these per-GPU totals in f64; then reset the ticket for the next launch
+        p.emit(f"st.global.f64 [{scratch}+8], {tot}")
         p.emit(f"st.global.u32 [{scratch}], 0")
         fin = p.reg("f32")
         p.emit(f"cvt.rn.f32.f64 {fin}, {tot}")
@@ -1076,7 +1078,8 @@ class FullReduce:
         text = text.replace("{\n", "{\n" + f"\t.shared .align 8 .f64 wpart[{nw}];\n", 1)
         launch = {"kind": "full_reduce", "grid": [self.grid, 1, 1], "block": [self.CTA, 1, 1],
                   "cluster": [1, 1, 1], "smem": 0, "count": self.count,
-                  "extra_params": [{"kind": "scratch", "bytes": self.scratch_bytes, "zero_once": True}]}
+                  "extra_params": [{"kind": "scratch", "bytes": self.scratch_bytes, "zero_once": True,
+                                    "f64_total_offset": 8}]}
         return module([text], launch)
 
     def _combine_f64(self, a: str, b: str) -> str:

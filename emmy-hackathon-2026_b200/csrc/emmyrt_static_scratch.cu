@@ -18,12 +18,17 @@
  *   - the array holds EMMY_RT_STATIC_SCRATCH_BYTES (64 KiB); it is zero-filled when
  *     the library is loaded, and every GPU that loads this library keeps its own
  *     copy until the process exits;
- *   - a launch whose scratch would exceed the array is rejected with
- *     EMMY_RT_ESCRATCH before anything is enqueued;
+ *   - the kernel writes a 16-byte ticket and one 8-byte partial per CTA, so a launch
+ *     of `grid` CTAs needs 16 + 8 * grid bytes whatever the caller claims in
+ *     `scratch_bytes`; a launch whose need (the larger of the two) exceeds the array
+ *     is rejected with EMMY_RT_ESCRATCH before anything is enqueued (at most 8190
+ *     CTAs fit);
  *   - the array's device address is looked up once per device with
  *     cudaGetSymbolAddress on that device's first call (with that device current).
  *     That first call on a device therefore does the set-up; make it before any
- *     stream capture;
+ *     stream capture.  The address belongs to the device's primary context: after
+ *     a reset of that context (cudaDeviceReset) the cached address is stale, so a
+ *     process that resets a device must not call this entry point on it again;
  *   - every call shares the one array and it keeps the last call's contents.  The
  *     ticket word at its head must start at zero, so each call clears it on the
  *     stream (cudaMemsetAsync, which allocates nothing) before the launch.  Two
@@ -39,8 +44,12 @@
 
 static __device__ __align__(256) unsigned char g_reduce_scratch[EMMY_RT_STATIC_SCRATCH_BYTES];
 
-/* device address of g_reduce_scratch per device ordinal, filled on first use */
+/* device address of g_reduce_scratch per device ordinal, filled on first use; host
+ * threads that race on the first call store the same value, atomically */
 static void *g_scratch_addr[64];
+
+/* bytes the whole-array reduction kernel writes for a launch of `grid` CTAs */
+static size_t scratch_need(unsigned grid) { return 16 + 8 * (size_t)grid; }
 
 #define MAX_ARGS 62
 
@@ -50,20 +59,22 @@ int emmy_rt_full_reduce_static_scratch(uint64_t function, unsigned grid, unsigne
                                        uint64_t stream) {
     if (nargs < 0 || nargs > MAX_ARGS || (nargs > 0 && args == NULL) || grid == 0 || block == 0)
         return EMMY_RT_EINVAL;
-    if (scratch_bytes > EMMY_RT_STATIC_SCRATCH_BYTES)
+    size_t need = scratch_need(grid);
+    if (scratch_bytes > need) need = scratch_bytes;
+    if (need > EMMY_RT_STATIC_SCRATCH_BYTES)
         return EMMY_RT_ESCRATCH;
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return (int)e;
     if (dev < 0 || dev >= 64) return EMMY_RT_EINVAL;
-    if (g_scratch_addr[dev] == NULL) {
-        void *p = NULL;
-        e = cudaGetSymbolAddress(&p, g_reduce_scratch);
+    void *base = __atomic_load_n(&g_scratch_addr[dev], __ATOMIC_ACQUIRE);
+    if (base == NULL) {
+        e = cudaGetSymbolAddress(&base, g_reduce_scratch);
         if (e != cudaSuccess) return (int)e;
-        g_scratch_addr[dev] = p;
+        __atomic_store_n(&g_scratch_addr[dev], base, __ATOMIC_RELEASE);
     }
     /* the ticket (first 16 bytes) must read zero when the kernel starts */
-    e = cudaMemsetAsync(g_scratch_addr[dev], 0, 16, (cudaStream_t)(uintptr_t)stream);
+    e = cudaMemsetAsync(base, 0, 16, (cudaStream_t)(uintptr_t)stream);
     if (e != cudaSuccess) return (int)e;
     uint64_t vals[MAX_ARGS + 1];
     void *params[MAX_ARGS + 1];
@@ -71,7 +82,7 @@ int emmy_rt_full_reduce_static_scratch(uint64_t function, unsigned grid, unsigne
         vals[i] = args[i];
         params[i] = &vals[i];
     }
-    vals[nargs] = (uint64_t)(uintptr_t)g_scratch_addr[dev];
+    vals[nargs] = (uint64_t)(uintptr_t)base;
     params[nargs] = &vals[nargs];
     const unsigned g[3] = {grid, 1, 1}, b[3] = {block, 1, 1};
     return emmy_rt_launch(function, g, b, NULL, 0, stream, params);

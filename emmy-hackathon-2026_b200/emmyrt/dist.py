@@ -1,8 +1,10 @@
 """Multi-GPU plumbing: one process per GPU, NCCL through the native runtime.
 
 The reference has no multi-GPU path.  Here every partitioned problem shards without
-communication (GEMM by N-panel, attention by batch x head, row kernels by rows), and
-the whole-array reduction finishes with one all-reduce of the per-rank partials:
+communication on the data path (GEMM by N-panel, attention by batch x head, row kernels
+by rows), and the whole-array reduction finishes with one all-reduce of the per-rank
+f64 partials (the FP8 GEMM's per-tensor scale of a sharded B takes one all-reduce with
+max of the panels' amax, before the timed GEMM):
 ``emmy_rt_nccl_*`` wraps ncclGetUniqueId / ncclCommInitRank / ncclAllReduce; rank 0's
 unique id travels to the other ranks over the host process group (``torch.distributed``
 with gloo), which carries no tensor data.
@@ -79,9 +81,4 @@ class NcclComm:
             self.handle = 0
 
 
-def panel(n: int, rank: int, world: int) -> tuple[int, int]:
-    """[start, stop) of rank's share of n units when n is split into contiguous panels
-    (GEMM N-panels, attention batch x head, rows, array chunks)."""
-    base, extra = divmod(n, world)
-    start = rank * base + min(rank, extra)
-    return start, start + base + (1 if rank < extra else 0)
+from baseline_configs import panel  # noqa: E402,F401  (the one definition of the split)

@@ -68,9 +68,14 @@ class Fp8Gemm:
         self.bm = DeviceBuffer(16)
         self.sa, self.sb = DeviceBuffer(16), DeviceBuffer(16)
 
-    def quantize(self, a_ptr: int, b_ptr: int, stream: int = 0) -> None:
+    def quantize(self, a_ptr: int, b_ptr: int, stream: int = 0, amax_b_hook=None) -> None:
+        """Quantise A and B on ``stream``.  When B is one GPU's N-panel of a larger B,
+        ``amax_b_hook(ptr, stream)`` turns the panel's amax (one f32 on the device) into
+        the whole B's before B is quantised (an all-reduce with max over the GPUs)."""
         self.amax_a({"x": a_ptr, "amax": self.am.ptr}, stream)
         self.amax_b({"x": b_ptr, "amax": self.bm.ptr}, stream)
+        if amax_b_hook is not None:
+            amax_b_hook(self.bm.ptr, stream)
         self.quant_a({"x": a_ptr, "amax": self.am.ptr, "q": self.qa.ptr, "scale": self.sa.ptr}, stream)
         self.quant_b({"x": b_ptr, "amax": self.bm.ptr, "q": self.qb.ptr, "scale": self.sb.ptr}, stream)
 

@@ -35,25 +35,7 @@ if str(_PKG) not in sys.path:
 
 from compiler import compile_kernel, load, parse_launch  # noqa: E402
 
-NP_DTYPE = {"f32": np.float32, "f16": np.float16, "f64": np.float64, "i32": np.int32,
-            "i64": np.int64, "bf16": np.uint16, "e4m3": np.uint8, "u8": np.uint8}
-
-
-# ---------------------------------------------------------------------------
-# bf16 / e4m3 host conversions (round to nearest even, as torch does)
-
-
-def f32_to_bf16_bits(a) -> np.ndarray:
-    u = np.ascontiguousarray(a, dtype=np.float32).view(np.uint32)
-    rounding = ((u >> 16) & 1) + 0x7FFF
-    out = ((u + rounding) >> 16).astype(np.uint16)
-    nan = np.isnan(np.asarray(a, dtype=np.float32))
-    out[nan] = 0x7FC0
-    return out
-
-
-def bf16_bits_to_f32(b) -> np.ndarray:
-    return (np.asarray(b, dtype=np.uint16).astype(np.uint32) << 16).view(np.float32)
+from hostfmt import NP_DTYPE, bf16_bits_to_f32, f32_to_bf16_bits  # noqa: E402,F401
 
 
 def host_array(dtype: str, values) -> np.ndarray:

@@ -183,9 +183,11 @@ int emmy_rt_nccl_comm_destroy(uint64_t comm);
  * (`function`, from emmy_rt_module_function; grid and block from its launch descriptor)
  * with `args` = its nargs pointer arguments in meta.json arg_order and its scratch taken
  * from a file-scope device array of EMMY_RT_STATIC_SCRATCH_BYTES instead of an allocation.
- * Rejects scratch_bytes above that size with EMMY_RT_ESCRATCH.  The first call on a
- * device looks the array up (cudaGetSymbolAddress) and should come before any stream
- * capture.  Calls share the array: each clears its ticket word on `stream` first, and
+ * The kernel writes 16 + 8 * grid bytes of scratch; a launch whose need (that, or
+ * scratch_bytes if larger) exceeds the array is rejected with EMMY_RT_ESCRATCH.  The first
+ * call on a device looks the array up (cudaGetSymbolAddress) and should come before any
+ * stream capture; the address is cached for the life of the process, so a device whose
+ * primary context was reset (cudaDeviceReset) must not be passed here again.  Calls share the array: each clears its ticket word on `stream` first, and
  * calls whose kernels overlap on the GPU race.  Returns 0, EMMY_RT_EINVAL /
  * EMMY_RT_ESCRATCH, a cudaError_t from the set-up or the clear, or emmy_rt_launch's
  * status. */

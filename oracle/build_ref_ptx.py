@@ -26,7 +26,8 @@ import tempfile
 from pathlib import Path
 
 ROOT = Path(__file__).resolve().parents[1]
-REFERENCE = Path(os.environ.get("REFERENCE", "/root/reference"))
+# the reference checkout: $REFERENCE, else a "reference" folder beside this repository
+REFERENCE = Path(os.environ.get("REFERENCE", ROOT.parent / "reference"))
 OUT = ROOT / "oracle" / "_ref" / "ptx"
 GOLDEN = ROOT / "tests" / "golden" / "problems"
 
@@ -58,12 +59,51 @@ for k in meta["kernels"]:
 '''
 
 
+def bf16_gemm_problem(n: int, problem_id: str) -> tuple[dict, dict]:
+    """The reference's f16 GEMM family (x_h_mm_1024: 32 x 256 CTA tiles, a two-stage
+    cp.async pipeline over K in steps of 32, mma.sync m16n8k16) retyped to bf16 and
+    grown to n^3.  Emmy's schedule for it is fixed by the IR: the row / column block
+    axes (a0_b, a1_b) and the K loop (_ks) grow with n, the per-CTA tile does not, and
+    the launch grows to (n / 32) x (n / 256) CTAs.  The K pipeline's prefetch clamp
+    (``_ks + 32 < K ? _ks + 32 : K - 32``) is rewritten for the new K."""
+    from compiler.synth import FAMILIES, rescale
+    if n % 256:
+        raise ValueError("the x_h_mm_1024 schedule tiles N by 256")
+    irs, meta = rescale(FAMILIES / "x_h_mm_1024",
+                        axes={("a0", 1024): n, ("a1", 1024): n, ("_ks", 1024): n,
+                              ("a0_b", 32): n // 32, ("a1_b", 4): n // 256},
+                        dtypes={"f16": "bf16"},
+                        shapes={"x0": [n, n], "x1": [n, n], "matmul": [n, n]},
+                        problem_id=problem_id)
+    old = ("right=Literal(value=1024, dtype='int')), if_true=BinaryExpr(op='+', left=Var(name='_ks'), "
+           "right=Literal(value=32, dtype='int')), if_false=Literal(value=992, dtype='int')")
+    new = old.replace("value=1024", f"value={n}").replace("value=992", f"value={n - 32}")
+    for ir in irs.values():
+        for node in ir["nodes"].values():
+            if node["op"] == "KernelOp":
+                body = node["op_fields"]["body"]
+                if not any(old in s for s in body):
+                    raise ValueError("x_h_mm_1024: the K prefetch clamp was not found")
+                node["op_fields"]["body"] = [s.replace(old, new) for s in body]
+    meta["kernels"][0]["grid"] = [(n // 32) * (n // 256), 1, 1]
+    return irs, meta
+
+
+def baseline_reference_problems() -> dict:
+    """BASELINE configurations (or the largest size the reference's 32-bit indexing
+    reaches) in the reference's own IR families."""
+    from compiler.synth import rmsnorm_family, sum_family
+    return {"ref_rmsnorm_4096": rmsnorm_family(4096, 4096, "ref_rmsnorm_4096"),
+            "ref_sum_2p30": sum_family(1 << 30, "ref_sum_2p30"),
+            "ref_gemm_bf16_2048": bf16_gemm_problem(2048, "ref_gemm_bf16_2048")}
+
+
 def main() -> int:
     if not (REFERENCE / "compiler").exists():
         print(f"reference checkout not found at {REFERENCE}", file=sys.stderr)
         return 1
     sys.path.insert(0, str(ROOT / "emmy-hackathon-2026_b200"))
-    from compiler.synth import rescale, write_problem
+    from compiler.synth import write_problem
     with tempfile.TemporaryDirectory() as td:
         shim = Path(td) / "shim"
         (shim / "emmy" / "compiler").mkdir(parents=True)
@@ -75,12 +115,8 @@ def main() -> int:
         driver.write_text(DRIVER.format(ref=str(REFERENCE), shim=str(shim)))
         jobs = [(GOLDEN / f, f) for f in FIXTURES]
         # BASELINE-family sizes the reference's 32-bit indexing can address
-        irs, meta = rescale(GOLDEN / "x_l_rmsnorm_w", {64: 4096, 512: 4096},
-                            constants={"mean_count": 4096.0}, problem_id="ref_rmsnorm_4096")
-        jobs.append((write_problem(irs, meta, Path(td) / "rms"), "ref_rmsnorm_4096"))
-        irs, meta = rescale(GOLDEN / "x_r_unpinned_sum", {64: 1 << 20, 65536: 1 << 30},
-                            problem_id="ref_sum_2p30")
-        jobs.append((write_problem(irs, meta, Path(td) / "sum"), "ref_sum_2p30"))
+        for name, (irs, meta) in baseline_reference_problems().items():
+            jobs.append((write_problem(irs, meta, Path(td) / name), name))
         ok = 0
         for src, name in jobs:
             r = subprocess.run([sys.executable, str(driver), str(src), str(OUT / name)],

@@ -10,7 +10,7 @@ outputs, computed by its numpy ``ref`` lambdas from the seeded inputs,
 pretty prints are not copied.
 
 Run from the repository root with the reference checked out at REFERENCE
-(default /root/reference):  python tests/golden/make_fixtures.py
+(default: a "reference" folder beside the repository):  python tests/golden/make_fixtures.py
 """
 
 from __future__ import annotations
@@ -20,7 +20,7 @@ import shutil
 import sys
 from pathlib import Path
 
-REFERENCE = Path(os.environ.get("REFERENCE", "/root/reference"))
+REFERENCE = Path(os.environ.get("REFERENCE", Path(__file__).resolve().parents[3] / "reference"))
 OUT = Path(__file__).resolve().parent / "problems"
 
 # the hot-path families (RMSNorm / softmax / L2 norm / row + global reductions,

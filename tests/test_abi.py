@@ -29,6 +29,19 @@ def test_static_scratch_rejects_oversize_without_touching_the_gpu():
     assert rc == emmyrt.EMMY_RT_ESCRATCH
 
 
+def test_static_scratch_need_follows_the_grid_not_the_claim():
+    """The kernel writes 16 + 8 * grid bytes: a large grid is rejected even when the
+    caller claims a small scratch, before any CUDA call."""
+    import ctypes
+    import emmyrt
+    static = emmyrt.static_scratch_lib()
+    args = (ctypes.c_uint64 * 2)(0, 0)
+    fits = (64 * 1024 - 16) // 8                      # 8190 CTAs fill the 64 KiB exactly
+    for grid in (fits + 1, 1 << 20):
+        rc = static.emmy_rt_full_reduce_static_scratch(0, grid, 32, args, 2, 16 + 8, 0)
+        assert rc == emmyrt.EMMY_RT_ESCRATCH, grid
+
+
 def test_calls_before_init_fail_cleanly():
     import ctypes
     import emmyrt

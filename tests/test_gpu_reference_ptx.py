@@ -4,6 +4,7 @@ end's sm_100a kernels agree with it (GEMM, RMSNorm, L2 norm, row and global sums
 
 import json
 
+
 import numpy as np
 import pytest
 
@@ -32,3 +33,58 @@ def test_reference_ptx_agrees(runtime, pid):
             f"reference PTX misses its own golden vector ({pid}:{name})"
         assert np.allclose(o, r, rtol=meta["rtol"], atol=meta["atol"]), \
             f"{pid}:{name}: max |ours - reference| {np.max(np.abs(o - r))}"
+
+
+# BASELINE configurations in the reference's own IR families, at the largest size its
+# 32-bit indexing reaches: RMSNorm 4096 x 4096, the sum over 2^30 elements, and the bf16
+# GEMM (x_h_mm_1024 retyped to bf16 and grown to 2048^3, mma.sync m16n8k16).
+BASELINE_REF = ["ref_rmsnorm_4096", "ref_sum_2p30", "ref_gemm_bf16_2048"]
+
+
+def _ours(name: str, tmp_path):
+    """This back end on the same IR and meta the reference module was built from."""
+    import build_ref_ptx
+    from compiler.synth import write_problem
+    from emmyrt.runner import run_problem
+    irs, meta = build_ref_ptx.baseline_reference_problems()[name]
+    return run_problem(write_problem(irs, meta, tmp_path / name))["outputs"], meta
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("name", BASELINE_REF)
+def test_reference_ptx_at_baseline_sizes(runtime, name, tmp_path):
+    if not available(name):
+        pytest.skip("reference PTX not built (python oracle/build_ref_ptx.py)")
+    import math
+    import sys
+    from conftest import ROOT
+    sys.path.insert(0, str(ROOT / "oracle"))
+    from emmyrt.runner import seeded_input
+    from hostfmt import bf16_bits_to_f32
+    from oracle import refs
+    from parity import assert_parity, sample_rows
+    ref_out, _ = run_reference(name)
+    ours, meta = _ours(name, tmp_path)
+    args = {a["name"]: a for a in meta["kernels"][0]["args"]}
+    if name == "ref_gemm_bf16_2048":
+        A = bf16_bits_to_f32(seeded_input(args["x0"]))
+        B = bf16_bits_to_f32(seeded_input(args["x1"]))
+        r, o = ref_out["matmul"], ours["matmul"]
+        rows = sample_rows(A.shape[0], 64)
+        oracle = refs.mm_bf16(A[rows], B)
+        assert_parity(r[rows], oracle, rel=1e-2, what="reference PTX vs oracle")
+        assert_parity(o[rows], oracle, rel=1e-2, what="ours vs oracle")
+        assert_parity(o, r, rel=1e-2, what="ours vs reference PTX (whole output)")
+    elif name == "ref_rmsnorm_4096":
+        x, w = seeded_input(args["x0"]), seeded_input(args["x1"])
+        oracle = refs.rmsnorm(x, w, 1e-6).astype(np.float64)
+        for what, got in (("reference PTX", ref_out["mul_1"]), ("ours", ours["mul_1"])):
+            err = np.abs(got.reshape(oracle.shape).astype(np.float64) - oracle)
+            assert np.all(err <= 1e-5 * np.abs(oracle) + 1e-6), f"{what}: max abs err {err.max()}"
+    else:
+        x = seeded_input(args["x"])
+        c = 1 << 24
+        exact = math.fsum(float(x[i:i + c].sum(dtype=np.float64)) for i in range(0, x.size, c))
+        for what, got in (("reference PTX", ref_out["sum_1"]), ("ours", ours["sum_1"])):
+            g = float(np.asarray(got).reshape(-1)[0])
+            assert abs(g - exact) <= 1e-5 * max(abs(exact), 1.0), f"{what}: {g} vs {exact}"

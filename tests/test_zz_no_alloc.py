@@ -6,7 +6,8 @@ failure, a latency-bound loop that must not pay for cudaMalloc).  For them
 ``emmy_rt_full_reduce_static_scratch`` runs the same compiled reduction kernel with
 its scratch in a static device array.  This file runs last (pytest collects it
 last) and checks that entry point, through the C ABI, against the regular path that
-allocates its scratch, on two calls in a row.
+allocates its scratch, against the golden vector (expected.npz) and against the oracle,
+on two calls in a row.
 """
 
 import ctypes
@@ -24,11 +25,14 @@ def test_static_scratch_matches_allocating_path(runtime, pid):
     import emmyrt
     from emmyrt import DeviceBuffer
     from emmyrt.runner import CompiledKernel, run_problem, seeded_input
+    from oracle.refs import problem_expected
 
     d = GOLDEN / pid
     meta = json.loads((d / "meta.json").read_text())
     k = meta["kernels"][0]
     expected = run_problem(d)["outputs"]            # the regular path: allocated scratch
+    golden = dict(np.load(d / "expected.npz"))
+    oracle = problem_expected(meta)
 
     ck = CompiledKernel.from_ir(d / f"{k['entry']}.ir.json")
     scratch = [e for e in ck.launch["extra_params"] if e["kind"] == "scratch"]
@@ -56,6 +60,10 @@ def test_static_scratch_matches_allocating_path(runtime, pid):
             assert np.allclose(got, ref, rtol=meta["rtol"], atol=meta["atol"]), \
                 f"call {call}: {got} vs {ref}"
             assert np.array_equal(got, ref.astype(np.float32))   # same kernel, deterministic order
+            for what, want in (("expected.npz", golden[o]), ("oracle", oracle[o])):
+                want = np.asarray(want, np.float64).reshape(-1)
+                assert np.allclose(got, want, rtol=meta["rtol"], atol=meta["atol"]), \
+                    f"call {call}: {got} vs {what} {want}"
 
 
 @pytest.mark.gpu
