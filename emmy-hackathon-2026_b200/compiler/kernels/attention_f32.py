@@ -394,6 +394,7 @@ def _analyze_scores(spec, walk, defs) -> F32AttnConfig:
     _check_normalised(walk, defs, key)
     _check_pv(walk, defs, key, v_ld.input)
     _check_guards(walk, {key})
+    _check_copies(tile, walk, defs, in_loop, maxes, chain, s_ld, v_ld.input)
     writes = [st for st, _ in walk if type(st).__name__ == "Write"]
     if len({w.output for w in writes}) != 1:
         raise NotImplementedError("not one output")
@@ -427,6 +428,100 @@ def _analyze_scores(spec, walk, defs) -> F32AttnConfig:
             cfg.R = R
             break
     return cfg
+
+
+def _chain_signature(root: str, defs, in_loop: set, s_input: str):
+    """(the score load, a name-free signature of the per-key statements from that load
+    to ``root``): every statement's kind, op, type and where each argument comes from
+    (an earlier statement of the chain, the score load, or a named loop-invariant)."""
+    order, seen, s_lds = [], {}, []
+
+    def visit(name):
+        d = defs.get(name)
+        if d is None or id(d) not in in_loop:
+            return ("outer", name)
+        if id(d) in seen:
+            return ("step", seen[id(d)])
+        k = type(d).__name__
+        if k == "Load":
+            if d.input != s_input:
+                raise NotImplementedError("a load other than the score in the score transform")
+            s_lds.append(d)
+            return ("score",)
+        if k == "Assign":
+            args = tuple(visit(a) for a in d.args)
+            sig = ("Assign", d.op.name, getattr(d.dtype, "name", None), args)
+        elif k == "Let":
+            sig = ("Let", repr(d.value), getattr(d.dtype, "name", None))
+        else:
+            raise NotImplementedError(f"{k} in the score transform")
+        seen[id(d)] = len(order)
+        order.append(sig)
+        return ("step", seen[id(d)])
+    visit(root)
+    if len({id(x) for x in s_lds}) != 1:
+        raise NotImplementedError("a score transform that is not fed by one score load")
+    return s_lds[0], tuple(order)
+
+
+def _tile_points(tile, limit: int = 1 << 14):
+    """Values of the tile's axes to evaluate index expressions at: every combination
+    when there are at most ``limit``, else a seeded sample of them."""
+    import itertools
+    import random
+    names = [a.name for a in tile.axes]
+    ext = [int(a.extent.value) for a in tile.axes]
+    if math.prod(ext) <= limit:
+        return [dict(zip(names, c)) for c in itertools.product(*(range(e) for e in ext))]
+    rng = random.Random(0)
+    return [{n: rng.randrange(e) for n, e in zip(names, ext)} for _ in range(limit)]
+
+
+def _check_copies(tile, walk, defs, in_loop, maxes, chain, s_ld, v_input: str) -> None:
+    """The IR unrolls rows and value columns into register copies (c<row>_<col>); the
+    template lowers the first copy's score transform for every row and writes o[row, c]
+    from s[row, :] and v[:, c].  So every copy must apply the same transform to its score
+    load, and every Write must put row r's result, from v column c, at [r, c]: the Write's
+    row index equals its score load's row index and its column index its v element's
+    column, at every point of the tile."""
+    from ..stmts import eval_index
+    first = _chain_signature(maxes[0][0].value, defs, in_loop, s_ld.input)
+    for acc, _ in maxes[1:]:
+        _, sig = _chain_signature(acc.value, defs, in_loop, s_ld.input)
+        if sig != first[1]:
+            raise NotImplementedError("register copies with different score transforms")
+    accums = {st.name: st for st, _ in walk if type(st).__name__ == "Accum"}
+    points = _tile_points(tile)
+    for w, _ in walk:
+        if type(w).__name__ != "Write":
+            continue
+        s_loads, v_elems, todo, seen = set(), set(), list(w.values), set()
+        while todo:
+            n = todo.pop()
+            if n in seen:
+                continue
+            seen.add(n)
+            d = defs.get(n)
+            if d is None and n in accums:
+                todo.append(accums[n].value)
+                continue
+            k = type(d).__name__
+            if k == "Load":
+                if d.input == s_ld.input:
+                    s_loads.add(id(d))
+                    s_row = d.index[-2]
+                elif d.input == v_input:
+                    v_elems.add((id(d), d.names.index(n)))
+                    v_col, v_pos = d.index[-1], d.names.index(n)
+            elif k == "Assign":
+                todo.extend(d.args)
+        if len(s_loads) != 1 or len(v_elems) != 1:
+            raise NotImplementedError("an output element not fed by one score row and one v column")
+        for env in points:
+            if eval_index(w.index[-2], env) != eval_index(s_row, env) or \
+                    eval_index(w.index[-1], env) != eval_index(v_col, env) + v_pos:
+                raise NotImplementedError("an output element written away from its score row "
+                                          "or value column")
 
 
 def _lead_group(spec, q_ld, out_indices, k_ld, v_ld) -> int:

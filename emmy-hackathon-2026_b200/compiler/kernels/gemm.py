@@ -1117,7 +1117,10 @@ def _emit_ksplit_partial(p: Ptx, cfg: GemmConfig, ks: int, t: str, row_t: str, l
         load_chunk(ch)
         for g in range(8):
             p.emit(f"st.global.v4.b32 [{wrow}+{(ch * 32 + 4 * g) * 4}], {{{', '.join(regs[4 * g:4 * g + 4])}}}")
-    # every lane's stores before lane 0's ticket; the ticket of (tile, warp quarter)
+    # every lane's stores before lane 0's ticket; the ticket of (tile, warp quarter).  Lane
+    # 0 takes it with an acq_rel atom; the warp barrier after the broadcast orders the
+    # other lanes' later reads of the other slices after that acquire (then each lane's
+    # own fence)
     tile, ta, old, last = p.reg("u32"), p.reg("b64"), p.reg("u32"), p.reg("u32")
     p0, pl = p.reg("pred"), p.reg("pred")
     l_next = p.label("ks_next")
@@ -1134,6 +1137,7 @@ def _emit_ksplit_partial(p: Ptx, cfg: GemmConfig, ks: int, t: str, row_t: str, l
         @{p0} setp.eq.u32 {pl}, {old}, {ks - 1}
         @{p0} selp.u32 {last}, 1, 0, {pl}
         shfl.sync.idx.b32 {last}, {last}, 0, 31, -1
+        bar.warp.sync -1
         setp.eq.u32 {pl}, {last}, 0
         @{pl} bra {l_next}
         @{p0} st.relaxed.gpu.global.u32 [{ta}], 0

@@ -154,11 +154,20 @@ class CompiledKernel:
                               d.get("smem", 0), params)
 
     def status(self) -> int:
-        """The kernel's device status word (0 = ok; non-zero = a bounded wait gave up)."""
+        """The kernel's device status word (0 = ok; non-zero = a bounded wait gave up).
+
+        A launch that gave up may leave the counters in its scratch (split-K tickets, a
+        reduction's ticket) partly counted; a non-zero status therefore re-zeroes the
+        module's scratch and status word, so the next launch starts clean (its result is
+        still the caller's to discard)."""
         for i, extra in enumerate(self.launch.get("extra_params", [])):
             if extra["kind"] == "status" and i in self.scratch:
                 out = np.zeros(4, dtype=np.uint32)
                 self.scratch[i].download(out)
+                if out[0]:
+                    for buf in self.scratch.values():
+                        buf.zero()
+                    check(lib.emmy_rt_stream_synchronize(0), "sync")
                 return int(out[0])
         return 0
 

@@ -217,6 +217,76 @@ def test_f32_attention_rejects_rounded_p():
         analyze(replace(spec, body=plant(spec.body)))
 
 
+def _odd_scores_spec():
+    return load(next(p for p in (GOLDEN / "x_h_attn_odd").glob("*.ir.json") if "softmax" in p.name))
+
+
+def _replant(body, fn):
+    from dataclasses import replace
+    out = []
+    for x in body:
+        for y in fn(x):
+            sub = getattr(y, "body", None)
+            out.append(replace(y, body=_replant(sub, fn)) if isinstance(sub, tuple) else y)
+    return tuple(out)
+
+
+def test_f32_attention_scores_reject_rounded_p():
+    """x_h_attn_odd's online softmax over a score buffer with p rounded to f16 before it
+    multiplies v (planted): the template multiplies the f32 p, so it must hand back."""
+    from dataclasses import replace
+    from compiler.kernels.attention_f32 import analyze
+    spec = _odd_scores_spec()
+
+    def fn(x):
+        if type(x).__name__ == "Assign" and x.name == "v5__ws03e2a34518__acc5__sum_sb__c1_0":
+            yield parse_stmt("Assign(name='p16', op=ElementwiseImpl('copy'), "
+                             "args=('v5__ws03e2a34518__beta__c1_0',), dtype=DataType(name='f16', "
+                             "np=dtype('float16'), nbytes=2))")
+            yield replace(x, args=(x.args[0], "p16"))
+        else:
+            yield x
+    with pytest.raises(NotImplementedError, match="key sum"):
+        analyze(replace(spec, body=_replant(spec.body, fn)))
+
+
+def test_f32_attention_scores_reject_a_copy_with_another_transform():
+    """One register copy (row 2, column 1) scales its score twice (planted): the template
+    lowers the first copy's transform for every row, so it must hand back."""
+    from dataclasses import replace
+    from compiler.kernels.attention_f32 import analyze
+    spec = _odd_scores_spec()
+
+    def fn(x):
+        if type(x).__name__ == "Assign" and x.name == "v5__ws03e2a34518__c2_1":
+            yield replace(x, name="tw", args=("v2", "v4__ws03e2a34518__c2_1"))
+            yield replace(x, args=("v2", "tw"))
+        else:
+            yield x
+    with pytest.raises(NotImplementedError, match="different score transforms"):
+        analyze(replace(spec, body=_replant(spec.body, fn)))
+
+
+@pytest.mark.parametrize("axis", [-2, -1])
+def test_f32_attention_scores_reject_a_shifted_output(axis):
+    """A Write one row (or one value column) away from its copy's score row / v column
+    (planted) would be miscompiled by the template, so it must hand back."""
+    from dataclasses import replace
+    from compiler.kernels.attention_f32 import analyze
+    spec = _odd_scores_spec()
+
+    def fn(x):
+        if type(x).__name__ == "Write" and x.values == ("acc5__c1_1",):
+            idx = list(x.index)
+            idx[axis] = parse_stmt(f"BinaryExpr(op='+', left={idx[axis]!r}, "
+                                   "right=Literal(value=1, dtype='int'))")
+            yield replace(x, index=tuple(idx))
+        else:
+            yield x
+    with pytest.raises(NotImplementedError, match="written away"):
+        analyze(replace(spec, body=_replant(spec.body, fn)))
+
+
 def test_gemm_ksplit_choice():
     """K slices only where they remove many converter stages: the f32 512^3 matmul (64
     tiles, 16 K blocks) takes 2, the 64x64x2048 one (2 tiles) 16; 16-bit GEMMs none."""
