@@ -128,19 +128,25 @@ class ClockSampler:
             for b, n in self.REASONS.items():
                 if bits & b:
                     self.reasons.add(n)
-            self.power.append(nv.nvmlDeviceGetPowerUsage(self.h) / 1000.0)
+            if len(self.samples) % 8 == 1:          # power is the slow query
+                self.power.append(nv.nvmlDeviceGetPowerUsage(self.h) / 1000.0)
         except Exception:
             pass
 
     def _run(self):
         while not self._stop.is_set():
             self._sample()
+            self._started.set()
             time.sleep(self.period)
 
     def __enter__(self):
+        self._started = threading.Event()
         if self.nv:
             self.t = threading.Thread(target=self._run, daemon=True)
             self.t.start()
+            # the timed work starts only once sampling runs (a short region would
+            # otherwise end before the thread's first samples)
+            self._started.wait(1.0)
         return self
 
     def __exit__(self, *a):
@@ -584,7 +590,7 @@ def measure(name: str, args, dist: Dist, comm, headline: bool) -> dict:
                "config": config_of(name, dist.world) if w.cfg is not None else {"workload": name}}
         rec["e2e"] = _e2e(w, max(3, min(args.steps, 10)), dist)
         if dist.rank == 0 and dist.world == 1 and not args.no_cpu and w.cfg is not None:
-            c = cpu_measure(name, 3)
+            c = cpu_measure(name, 5, warmup=3)
             c.pop("_dt"), c.pop("_units")
             rec["cpu_baseline"] = c
         else:
