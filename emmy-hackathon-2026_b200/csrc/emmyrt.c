@@ -258,28 +258,47 @@ EXPORT int emmy_rt_function_set_max_dynamic_smem(uint64_t function, int bytes) {
 
 /* ----------------------------------------------------------------- launch */
 
-EXPORT int emmy_rt_launch(uint64_t function, const unsigned grid[3], const unsigned block[3],
-                          const unsigned cluster[3], unsigned smem_bytes, uint64_t stream,
-                          void **params) {
+EXPORT int emmy_rt_launch_ex(uint64_t function, const unsigned grid[3], const unsigned block[3],
+                             const unsigned cluster[3], unsigned smem_bytes, uint64_t stream,
+                             void **params, unsigned flags) {
     NEED_INIT();
     if (!grid || !block) return fail(EMMY_RT_EINVAL, "null grid or block");
+    if (flags & ~(unsigned)EMMY_RT_LAUNCH_PDL) return fail(EMMY_RT_EINVAL, "unknown launch flags %#x", flags);
     CUlaunchConfig cfg;
     memset(&cfg, 0, sizeof cfg);
     cfg.gridDimX = grid[0]; cfg.gridDimY = grid[1]; cfg.gridDimZ = grid[2];
     cfg.blockDimX = block[0]; cfg.blockDimY = block[1]; cfg.blockDimZ = block[2];
     cfg.sharedMemBytes = smem_bytes;
     cfg.hStream = (CUstream)(uintptr_t)stream;
-    CUlaunchAttribute attr[1];
+    CUlaunchAttribute attr[2];
+    memset(attr, 0, sizeof attr);
+    unsigned n = 0;
     if (cluster && (cluster[0] * cluster[1] * cluster[2]) > 1) {
-        attr[0].id = CU_LAUNCH_ATTRIBUTE_CLUSTER_DIMENSION;
-        attr[0].value.clusterDim.x = cluster[0];
-        attr[0].value.clusterDim.y = cluster[1];
-        attr[0].value.clusterDim.z = cluster[2];
+        attr[n].id = CU_LAUNCH_ATTRIBUTE_CLUSTER_DIMENSION;
+        attr[n].value.clusterDim.x = cluster[0];
+        attr[n].value.clusterDim.y = cluster[1];
+        attr[n].value.clusterDim.z = cluster[2];
+        ++n;
+    }
+    if (flags & EMMY_RT_LAUNCH_PDL) {
+        /* the kernel may start while the previous kernel of the stream finishes; it waits
+         * for that kernel (griddepcontrol.wait) before its first global memory access */
+        attr[n].id = CU_LAUNCH_ATTRIBUTE_PROGRAMMATIC_STREAM_SERIALIZATION;
+        attr[n].value.programmaticStreamSerializationAllowed = 1;
+        ++n;
+    }
+    if (n) {
         cfg.attrs = attr;
-        cfg.numAttrs = 1;
+        cfg.numAttrs = n;
     }
     CU(cu.LaunchKernelEx(&cfg, (CUfunction)(uintptr_t)function, params, NULL), "cuLaunchKernelEx");
     return 0;
+}
+
+EXPORT int emmy_rt_launch(uint64_t function, const unsigned grid[3], const unsigned block[3],
+                          const unsigned cluster[3], unsigned smem_bytes, uint64_t stream,
+                          void **params) {
+    return emmy_rt_launch_ex(function, grid, block, cluster, smem_bytes, stream, params, 0);
 }
 
 /* -------------------------------------------------------------------- TMA */

@@ -48,6 +48,8 @@ SIGNATURES = {
     "emmy_rt_function_set_max_dynamic_smem": ([_u64, _int], _int),
     "emmy_rt_launch": ([_u64, _P(ctypes.c_uint), _P(ctypes.c_uint), _P(ctypes.c_uint), ctypes.c_uint,
                         _u64, _P(ctypes.c_void_p)], _int),
+    "emmy_rt_launch_ex": ([_u64, _P(ctypes.c_uint), _P(ctypes.c_uint), _P(ctypes.c_uint), ctypes.c_uint,
+                           _u64, _P(ctypes.c_void_p), ctypes.c_uint], _int),
     "emmy_rt_tensor_map_encode_tiled": ([ctypes.c_void_p, _int, ctypes.c_uint, _u64, _P(_u64), _P(_u64),
                                          _P(ctypes.c_uint), _P(ctypes.c_uint), _int, _int, _int, _int], _int),
     "emmy_rt_mem_alloc": ([_P(_u64), _sz], _int),
@@ -352,8 +354,8 @@ class PreparedLaunch:
     """A launch whose argument arrays are built once: each call is one C call (no
     per-launch Python marshalling), so back-to-back launches keep the GPU fed."""
 
-    def __init__(self, fn: int, grid, block, cluster, smem: int, params: list):
-        self.fn, self.smem = fn, smem
+    def __init__(self, fn: int, grid, block, cluster, smem: int, params: list, flags: int = 0):
+        self.fn, self.smem, self.flags = fn, smem, flags
         self.g = (ctypes.c_uint * 3)(*grid)
         self.b = (ctypes.c_uint * 3)(*block)
         self.c = (ctypes.c_uint * 3)(*(cluster or (1, 1, 1)))
@@ -361,15 +363,18 @@ class PreparedLaunch:
         self.arr = (ctypes.c_void_p * max(1, len(params)))(
             *[ctypes.cast(ctypes.pointer(p), ctypes.c_void_p) if not isinstance(p, ctypes.Array)
               else ctypes.cast(p, ctypes.c_void_p) for p in params])
-        self._launch = lib.emmy_rt_launch
+        self._launch = lib.emmy_rt_launch_ex
 
     def __call__(self, stream: int = 0) -> None:
-        st = self._launch(self.fn, self.g, self.b, self.c, self.smem, stream, self.arr)
+        st = self._launch(self.fn, self.g, self.b, self.c, self.smem, stream, self.arr, self.flags)
         if st:
             check(st, "launch")
 
 
-def launch(fn: int, grid, block, cluster, smem: int, stream: int, params: list) -> None:
+LAUNCH_PDL = 1      # EMMY_RT_LAUNCH_PDL
+
+
+def launch(fn: int, grid, block, cluster, smem: int, stream: int, params: list, flags: int = 0) -> None:
     """``params``: one ctypes object per kernel parameter (c_uint64 pointers, tensor
     map byte arrays, scalars), in signature order."""
     g = (ctypes.c_uint * 3)(*grid)
@@ -378,7 +383,7 @@ def launch(fn: int, grid, block, cluster, smem: int, stream: int, params: list) 
     arr = (ctypes.c_void_p * max(1, len(params)))(
         *[ctypes.cast(ctypes.pointer(p), ctypes.c_void_p) if not isinstance(p, ctypes.Array)
           else ctypes.cast(p, ctypes.c_void_p) for p in params])
-    check(lib.emmy_rt_launch(fn, g, b, c, smem, stream, arr), "launch")
+    check(lib.emmy_rt_launch_ex(fn, g, b, c, smem, stream, arr, flags), "launch")
 
 
 # ---------------------------------------------------------------------------

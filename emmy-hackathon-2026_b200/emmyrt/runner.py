@@ -145,13 +145,19 @@ class CompiledKernel:
     def __call__(self, ptrs: dict, stream: int = 0, params: list | None = None) -> None:
         d = self.launch
         launch(self.function, d["grid"], d["block"], d.get("cluster", [1, 1, 1]), d.get("smem", 0),
-               stream, params if params is not None else self.params(ptrs))
+               stream, params if params is not None else self.params(ptrs), self.launch_flags)
+
+    @property
+    def launch_flags(self) -> int:
+        """Programmatic dependent launch for modules that wait for their predecessor."""
+        from . import LAUNCH_PDL
+        return LAUNCH_PDL if self.launch.get("pdl") else 0
 
     def prepare(self, params: list) -> PreparedLaunch:
         """A ready-to-fire launch of this kernel with fixed parameters."""
         d = self.launch
         return PreparedLaunch(self.function, d["grid"], d["block"], d.get("cluster", [1, 1, 1]),
-                              d.get("smem", 0), params)
+                              d.get("smem", 0), params, self.launch_flags)
 
     def status(self) -> int:
         """The kernel's device status word (0 = ok; non-zero = a bounded wait gave up).

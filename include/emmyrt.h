@@ -98,6 +98,19 @@ int emmy_rt_launch(uint64_t function, const unsigned grid[3], const unsigned blo
                    const unsigned cluster[3], unsigned smem_bytes, uint64_t stream,
                    void **params);
 
+/* Launch flags of emmy_rt_launch_ex. */
+#define EMMY_RT_LAUNCH_PDL 1u   /* programmatic dependent launch (see below) */
+
+/* emmy_rt_launch with flags (same role: the reference runner's POST /run launch,
+ * docs/API.md:26-53).  EMMY_RT_LAUNCH_PDL lets the kernel start while the stream's previous
+ * kernel finishes (CU_LAUNCH_ATTRIBUTE_PROGRAMMATIC_STREAM_SERIALIZATION): only for modules
+ * whose launch descriptor says "pdl": true, which wait for the previous kernel
+ * (griddepcontrol.wait) before their first global memory access.  Unknown flags:
+ * EMMY_RT_EINVAL. */
+int emmy_rt_launch_ex(uint64_t function, const unsigned grid[3], const unsigned block[3],
+                      const unsigned cluster[3], unsigned smem_bytes, uint64_t stream,
+                      void **params, unsigned flags);
+
 /* ---- TMA descriptors (new: the reference never emits TMA, TASK.md:130-136) ------- */
 
 /* cuTensorMapEncodeTiled into the 128-byte, 64-byte-aligned buffer `out`.

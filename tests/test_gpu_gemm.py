@@ -91,3 +91,46 @@ def test_gemm_split_k_bf16(runtime, m, n, k, kmaj, ksplit):
     from parity import assert_parity
     got, A, B = _direct_gemm(m, n, k, False, kmaj, ksplit=ksplit, launches=3)
     assert_parity(got[0], mm_bf16(A[0], B[0]), rel=1e-2, what=f"split-K {ksplit}")
+
+
+@pytest.mark.gpu
+def test_pdl_chain_waits_for_the_previous_gemm(runtime):
+    """Programmatic dependent launch: the second GEMM reads the first one's C as its A,
+    launched right behind it on one stream with no host sync in between; its prologue may
+    overlap the first GEMM, its loads must not (griddepcontrol.wait)."""
+    import emmyrt
+    from compiler.kernels.gemm import GemmConfig, emit_gemm_module
+    from emmyrt import DeviceBuffer
+    from emmyrt.runner import CompiledKernel, bf16_bits_to_f32, f32_to_bf16_bits
+    from oracle.refs import mm_bf16
+    from parity import assert_parity
+    n = 512
+    cks = []
+    for name in ("k_pdl_first", "k_pdl_second"):
+        cfg = GemmConfig(M=n, N=n, K=n, ab="bf16", c="bf16", name=name, buffers=("a", "b", "c"))
+        ck = CompiledKernel.from_module(emit_gemm_module(cfg), name, ["a", "b", "c"])
+        assert ck.launch["pdl"] and ck.launch_flags == emmyrt.LAUNCH_PDL
+        cks.append(ck)
+    rng = np.random.default_rng(3)
+    A = f32_to_bf16_bits(rng.standard_normal((n, n), dtype=np.float32) * np.float32(0.05))
+    B = f32_to_bf16_bits(rng.standard_normal((n, n), dtype=np.float32) * np.float32(0.05))
+    da, db, dc1, dc2 = (DeviceBuffer(n * n * 2) for _ in range(4))
+    da.upload(A)
+    db.upload(B)
+    for rep in range(3):
+        dc1.upload(np.full((n, n), 0x7FC0, np.uint16))          # NaN until the first GEMM writes
+        dc2.zero()
+        first = cks[0].prepare(cks[0].params({"a": da.ptr, "b": db.ptr, "c": dc1.ptr}))
+        second = cks[1].prepare(cks[1].params({"a": dc1.ptr, "b": db.ptr, "c": dc2.ptr}))
+        first(0)
+        second(0)
+        emmyrt.stream_wait(0, 60)
+        assert cks[0].status() == 0 and cks[1].status() == 0
+        c1 = np.zeros((n, n), np.uint16)
+        c2 = np.zeros((n, n), np.uint16)
+        dc1.download(c1)
+        dc2.download(c2)
+        C1, C2 = bf16_bits_to_f32(c1), bf16_bits_to_f32(c2)
+        assert np.isfinite(C2).all(), f"rep {rep}: the second GEMM read the first's C too early"
+        assert_parity(C1, mm_bf16(bf16_bits_to_f32(A), bf16_bits_to_f32(B)), rel=1e-2, what="first")
+        assert_parity(C2, mm_bf16(C1, bf16_bits_to_f32(B)), rel=1e-2, what="second")

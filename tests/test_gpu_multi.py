@@ -64,8 +64,15 @@ def test_shards_reassemble_into_the_one_gpu_result(runtime, shards, name):
     whole = np.concatenate(_pieces(shards, name), axis=axis)
     _, one = _run(name)
     assert whole.shape == one.shape
-    # the same kernel code path per output element: the pieces equal the whole run
-    assert np.array_equal(whole, one), f"{name}: {np.count_nonzero(whole != one)} elements differ"
+    if name == "gemm_8192":
+        # a tile's K order depends on its place in the CTA's tile sequence (the serpentine
+        # order), which differs between a panel and the whole: within one bf16 rounding
+        from hostfmt import bf16_bits_to_f32
+        assert_parity(bf16_bits_to_f32(whole), bf16_bits_to_f32(one), rel=5e-3, ulps=1,
+                      what="2-GPU panels vs 1-GPU gemm_8192")
+    else:
+        # the same kernel code path per output element: the pieces equal the whole run
+        assert np.array_equal(whole, one), f"{name}: {np.count_nonzero(whole != one)} elements differ"
 
 
 @pytest.mark.gpu
