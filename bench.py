@@ -179,8 +179,9 @@ def measured_peaks() -> tuple[dict, str]:
 
 
 def traffic_from_profile(workload: str):
-    """DRAM bytes per launch of the whole problem from the committed ncu summary."""
-    p = ROOT / "profiles" / f"{workload}.md"
+    """DRAM bytes per launch of the whole problem from the committed ncu summary
+    (``profiles/<workload>_traffic.txt``)."""
+    p = ROOT / "profiles" / f"{workload}_traffic.txt"
     if not p.exists():
         return None
     for line in p.read_text().splitlines():
