@@ -125,11 +125,19 @@ def choose_bn(M: int, N: int, batch: int, min_bn: int = 64) -> int:
     return choose_tiling(M, N, batch, min_bn, pairs=False)["BN"]
 
 
+def _stages_fit(bn: int, cap: int = 8) -> int:
+    """Stages of a 16-bit / 8-bit TMA ring that fit in shared memory: a stage holds one
+    128-byte K row of A (128 rows) and of B (bn columns).  Short K loops gain most from a
+    deep ring (every K block of a 512^3 tile in flight: 5.2 us against 6.2 us with 4)."""
+    stage = 128 * 128 + bn * 128
+    return max(4, min(cap, (232448 - 256 - 1024) // stage))
+
+
 def choose_tiling(M: int, N: int, batch: int, min_bn: int = 64, pairs: bool = True) -> dict:
     """The tiling with the least estimated time: persistent waves over the SMs (or SM
     pairs) times one tile's MACs per SM divided by that shape's work rate.  Single
-    CTAs run 128 x BN tiles (BN 256, 128 or 64) with 4 stages, CTA pairs 256 x 256
-    tiles with 6 stages (M and N of 256 or more)."""
+    CTAs run 128 x BN tiles (BN 256, 128 or 64) with as many stages as fit (4, 7 or 8),
+    CTA pairs 256 x 256 tiles with 6 stages (M and N of 256 or more)."""
     cands = []
     if pairs and M >= 256 and N >= 256:
         tiles = batch * (-(-M // 256)) * (-(-N // 256))
@@ -140,11 +148,12 @@ def choose_tiling(M: int, N: int, batch: int, min_bn: int = 64, pairs: bool = Tr
             continue
         tiles = batch * (-(-M // 128)) * (-(-N // bn))
         cands.append(((-(-tiles // SMS)) * 128 * bn / _TILE_RATE[(1, bn)], 1,
-                      {"pair": False, "BN": bn, "stages": 4}))
+                      {"pair": False, "BN": bn, "stages": _stages_fit(bn)}))
     best = min(cands, key=lambda c: (c[0], c[1], -c[2]["BN"]))[2]
     if not best["pair"] and N < best["BN"]:
         bn = max(32, -(-N // 32) * 32)       # the epilogue reads TMEM 32 columns at a time
-        best = dict(best, BN=max(bn, min_bn))
+        bn = max(bn, min_bn)
+        best = dict(best, BN=bn, stages=_stages_fit(bn))
     return best
 
 

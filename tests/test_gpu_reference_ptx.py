@@ -85,6 +85,10 @@ def test_reference_ptx_at_baseline_sizes(runtime, name, tmp_path):
         x = seeded_input(args["x"])
         c = 1 << 24
         exact = math.fsum(float(x[i:i + c].sum(dtype=np.float64)) for i in range(0, x.size, c))
-        for what, got in (("reference PTX", ref_out["sum_1"]), ("ours", ours["sum_1"])):
+        # ours: the BASELINE bar for reductions (1e-5 relative; f32 groups folded in f64).
+        # The reference PTX accumulates f32 partials with f32 atomics in whatever order the
+        # CTAs finish: at 2^30 elements its error reaches about 1e-5 of the sum and varies
+        # from run to run, so it is held to 1e-4 (its own fixtures allow 1e-3 at 2^16)
+        for what, got, bar in (("reference PTX", ref_out["sum_1"], 1e-4), ("ours", ours["sum_1"], 1e-5)):
             g = float(np.asarray(got).reshape(-1)[0])
-            assert abs(g - exact) <= 1e-5 * max(abs(exact), 1.0), f"{what}: {g} vs {exact}"
+            assert abs(g - exact) <= bar * max(abs(exact), 1.0), f"{what}: {g} vs {exact}"
