@@ -70,6 +70,8 @@ class GemmConfig:
     pair: bool = False               # CTA pair (cta_group::2): 256-row tiles, B split by column
     operand_dtypes: tuple = ()       # (buffer, dtype) of epilogue operands
     ksplit: int = 0                  # K slices per tile (0: chosen from the shape; 1: none)
+    tail_split: int = 0              # K slices of the tiles past the last full wave of CTAs / pairs
+                                     # (0: chosen from the shape; 1: none)
     zero_slots: int = 0              # split-K partials: the full product goes to slice 0 of C and
     slot_stride: int = 0             # these many further slices (slot_stride elements apart) are zeroed
     operand_round: str | None = None  # f32 operands cast to "bf16" / "f16" before the product: one
@@ -210,6 +212,73 @@ def choose_ksplit(cfg: GemmConfig, ntiles: int, kblocks: int, pair: bool) -> int
     return ks if kblocks - kblocks // ks >= 8 else 1
 
 
+def choose_tail_split(cfg: GemmConfig, ntiles: int, kblocks: int, workers: int) -> int:
+    """K slices for the tiles of the last, partial wave (the tail), when whole tiles would
+    leave workers (SMs or SM pairs) idle in it.  The first (ntiles // workers) waves run
+    whole tiles; the R tiles left are cut into ts slices each and spread over the workers,
+    so the tail takes ceil(R ts / workers) / ts of a tile's time instead of a whole one.
+    Each sliced unit writes its f32 partial to a workspace and the last slice of a tile
+    (a ticket per warp quarter) sums them in slice order, as with ``ksplit``.  Taken when
+    it saves at least 4 % of the kernel's time (4096 x 14336 x 4096 on one B200: 896 pair
+    tiles = 12 full waves + 8 tiles, which 8 slices each spread over 64 pairs)."""
+    if cfg.tail_split:
+        return cfg.tail_split
+    if cfg.converts or cfg.zero_slots or cfg.ksplit > 1 or cfg.direct:
+        return 1
+    full, rem = divmod(ntiles, workers)
+    if full == 0 or rem == 0:
+        return 1
+    # a tile's time at the tensor rate (7736 flop / clock / SM at ~1.9 GHz) against the
+    # fix-up: every unit writes its f32 partial, the finishing slice reads all of them
+    # (about 300 GB/s per SM pair, 150 GB/s per SM)
+    sms = 2 if cfg.pair else 1
+    tile_s = 2.0 * cfg.MT * cfg.BN * cfg.K / (sms * 7736 * 1.9e9)
+    part = cfg.MT * cfg.BN * 4
+    best, best_t = 1, 1.0
+    for ts in (2, 4):
+        if kblocks % ts or kblocks // ts < 4 or rem * ts * part > 256 * 2 ** 20:
+            continue
+        if ts > 2 and cfg.K > 4096:
+            # measured on pair tiles: 4 slices of 8192-deep tiles lose (8192 x 1024 x 8192:
+            # 97 -> 130 us) where the estimate says they gain; 4 slices of 4096 gain 2-3 %
+            continue
+        fix = (part + ts * part) / (sms * 150e9) / tile_s
+        t = -(-rem * ts // workers) / ts + fix
+        if t < best_t - 1e-9:
+            best, best_t = ts, t
+    return best if (1.0 - best_t) / (full + 1) >= 0.04 else 1
+
+
+def _unit_plan(p: Ptx, cfg: GemmConfig, t: str, ks: int, kps: int, tail):
+    """Work unit t -> (batch, m tile, n tile, first K block, K blocks, sliced pred, tail unit).
+
+    Without a tail split: unit t is slice t % ks of tile t / ks (ks uniform K slices, kps
+    blocks each).  With ``tail = (D, ts, kpt)``: units below D are whole tiles (kps blocks),
+    unit D + v is slice v % ts (kpt blocks) of tile D + v / ts."""
+    if tail is None:
+        bt, mt, nt = _tile_coords(p, cfg, t, ks)
+        kb0 = p.reg("u32")
+        p.emit(f"rem.u32 {kb0}, {t}, {ks}\nmul.lo.u32 {kb0}, {kb0}, {kps}")
+        return bt, mt, nt, kb0, str(kps), None, None
+    D, ts, kpt = tail
+    tile, kb0, nkb, v, sl = p.regs("u32", 5)
+    psl = p.reg("pred")
+    p.emit(f"""
+        setp.ge.u32 {psl}, {t}, {D}
+        mov.u32 {tile}, {t}
+        mov.u32 {kb0}, 0
+        mov.u32 {nkb}, {kps}
+        sub.u32 {v}, {t}, {D}
+        @{psl} div.u32 {tile}, {v}, {ts}
+        @{psl} add.u32 {tile}, {tile}, {D}
+        @{psl} rem.u32 {sl}, {v}, {ts}
+        @{psl} mul.lo.u32 {kb0}, {sl}, {kpt}
+        @{psl} mov.u32 {nkb}, {kpt}
+    """)
+    bt, mt, nt = _tile_coords(p, cfg, tile, 1)
+    return bt, mt, nt, kb0, nkb, psl, v
+
+
 def _emit_zero_slices(p: Ptx, cfg: GemmConfig, cptr: str, tid: str, nthreads: int) -> None:
     """Split-K partial slices 1 .. zero_slots of C (the whole product goes to slice 0) are
     one contiguous range; every thread of the grid zeroes part of it with coalesced
@@ -253,6 +322,15 @@ def emit_gemm_module(cfg: GemmConfig) -> str:
     if KS > 1 and (pair or kblocks % KS):
         raise NotImplementedError("K slices need 1-CTA tiles and whole K blocks per slice")
     kps, nunits = kblocks // KS, ntiles * KS
+    workers = SMS // 2 if pair else SMS
+    TS = choose_tail_split(cfg, ntiles, kblocks, workers) if KS == 1 else 1
+    tail = None
+    if TS > 1:
+        if kblocks % TS or cfg.direct or cfg.converts:
+            raise NotImplementedError("tail K slices need whole K blocks and TMA-fed operands")
+        D = (ntiles // workers) * workers
+        tail = (D, TS, kblocks // TS)
+        nunits = D + (ntiles - D) * TS
     BNc = BN // 2 if pair else BN           # B columns held by one CTA
     a_bytes = BM * BK * eb                  # 16 KB
     b_bytes = BNc * BK * eb                 # 32 KB at BN = 256 (16 KB per CTA of a pair)
@@ -413,9 +491,8 @@ def emit_gemm_module(cfg: GemmConfig) -> str:
     p.place(tl)
     pt = p.reg("pred")
     p.emit(f"setp.ge.u32 {pt}, {t}, {nunits}\n@{pt} bra {td}")
-    bt, mt, nt = _tile_coords(p, cfg, t, KS)
-    kb0 = p.reg("u32")         # the unit's first K block
-    p.emit(f"rem.u32 {kb0}, {t}, {KS}\nmul.lo.u32 {kb0}, {kb0}, {kps}")
+    # the unit's tile, first K block and number of K blocks
+    bt, mt, nt, kb0, nkb, _, _ = _unit_plan(p, cfg, t, KS, kps, tail)
     m0, n0 = p.reg("u32"), p.reg("u32")
     p.emit(f"mul.lo.u32 {m0}, {mt}, {cfg.MT}\nmul.lo.u32 {n0}, {nt}, {BN}")
     if pair:    # this CTA's rows of the 256-row tile and its half of the B columns
@@ -450,7 +527,11 @@ def emit_gemm_module(cfg: GemmConfig) -> str:
         add.u32 {kx}, {kb}, {kb0}
     """)
     if rev is not None:
-        p.emit(f"@{rev} sub.u32 {kx}, {kps - 1}, {kb}\n@{rev} add.u32 {kx}, {kx}, {kb0}")
+        if tail is None:
+            p.emit(f"@{rev} sub.u32 {kx}, {kps - 1}, {kb}\n@{rev} add.u32 {kx}, {kx}, {kb0}")
+        else:
+            p.emit(f"@{rev} sub.u32 {kx}, {nkb}, 1\n@{rev} sub.u32 {kx}, {kx}, {kb}\n"
+                   f"@{rev} add.u32 {kx}, {kx}, {kb0}")
     p.emit(f"mul.lo.u32 {kx}, {kx}, {BK}")
     zc = f", {bt}" if rank == 3 else ""
     p.emit(f"{tma} [{sa}], [{tma_a}, {{{kx}, {m0}{zc}}}], [{faddr}]")
@@ -469,7 +550,7 @@ def emit_gemm_module(cfg: GemmConfig) -> str:
         @{ps} mov.u32 {s}, 0
         @{ps} xor.b32 {ph}, {ph}, 1
         add.u32 {kb}, {kb}, 1
-        setp.lt.u32 {ps}, {kb}, {kps}
+        setp.lt.u32 {ps}, {kb}, {nkb}
         @{ps} bra {kl}
         add.u32 {t}, {t}, {nct}
     """)
@@ -509,6 +590,11 @@ def emit_gemm_module(cfg: GemmConfig) -> str:
     """)
     waits.wait(tea, aph, "mma", finish)
     p.emit("tcgen05.fence::after_thread_sync")
+    nkb2 = str(kps)
+    if tail is not None:           # a sliced tail unit runs kpt K blocks
+        nkb2 = p.reg("u32")
+        ptl = p.reg("pred")
+        p.emit(f"setp.ge.u32 {ptl}, {t2}, {tail[0]}\nselp.u32 {nkb2}, {tail[2]}, {kps}, {ptl}")
     kb2 = p.reg("u32")
     mk = p.label("m_k")
     p.emit(f"mov.u32 {kb2}, 0")
@@ -553,7 +639,7 @@ def emit_gemm_module(cfg: GemmConfig) -> str:
         @{ps} mov.u32 {s2}, 0
         @{ps} xor.b32 {ph2}, {ph2}, 1
         add.u32 {kb2}, {kb2}, 1
-        setp.lt.u32 {ps}, {kb2}, {kps}
+        setp.lt.u32 {ps}, {kb2}, {nkb2}
         @{ps} bra {mk}
         {commit.format(a=tfa)}
         add.u32 {tc}, {tc}, 1
@@ -569,7 +655,7 @@ def emit_gemm_module(cfg: GemmConfig) -> str:
         role_conv = p.label("role_conv")
         p.emit(f"setp.ge.u32 {pr}, {warp}, {GEMM_THREADS // 32}\n@{pr} bra {role_conv}")
     _emit_epilogue(p, cfg, ptr, bars, tfull0, tempty0, tbase, warp, lane, cta, nct, nunits,
-                   waits, finish, crank if pair else None, ltempty if pair else None, KS)
+                   waits, finish, crank if pair else None, ltempty if pair else None, KS, tail)
     if conv:
         p.place(role_conv)
         if direct:
@@ -602,7 +688,7 @@ def emit_gemm_module(cfg: GemmConfig) -> str:
     params = list(cfg.arg_params or [f".param .u64 {param_symbol(n)}" for n in cfg.buffers])
     if not direct:
         params += [".param .align 64 .b8 param__tmap_a[128]", ".param .align 64 .b8 param__tmap_b[128]"]
-    if KS > 1:
+    if KS > 1 or tail is not None:
         params += [".param .u64 param__ksplit_ws", ".param .u64 param__ksplit_tickets"]
     params += [".param .u64 param__status"]
     nthreads = GEMM_THREADS + (CONV_THREADS if conv else 0)
@@ -624,6 +710,7 @@ def emit_gemm_module(cfg: GemmConfig) -> str:
     launch = {
         "kind": "gemm", "grid": [grid, 1, 1], "block": [nthreads, 1, 1], "cluster": [2 if pair else 1, 1, 1],
         "smem": smem, "flops": 2 * cfg.batch * M * N * K, "tiles": ntiles, "ksplit": KS,
+        "tail_split": TS, "tail_tiles": 0 if tail is None else ntiles - tail[0],
         "pdl": bool(cfg.pdl),
         "extra_params": ([] if direct else [
             {"kind": "tmap", "buffer": cfg.a_param, "dtype": cfg.ab, "dims": a_dims, "strides": a_str,
@@ -631,7 +718,10 @@ def emit_gemm_module(cfg: GemmConfig) -> str:
             {"kind": "tmap", "buffer": cfg.b_param, "dtype": cfg.ab, "dims": b_dims, "strides": b_str,
              "box": b_box, "swizzle": 128},
         ]) + ([{"kind": "scratch", "bytes": nunits * cfg.MT * BN * 4},
-               {"kind": "scratch", "bytes": ntiles * 4 * 4}] if KS > 1 else []) + [{"kind": "status"}],
+               {"kind": "scratch", "bytes": ntiles * 4 * 4}] if KS > 1 else []) +
+        ([{"kind": "scratch", "bytes": (nunits - tail[0]) * cfg.MT * BN * 4},
+          {"kind": "scratch", "bytes": (ntiles - tail[0]) * 2 * 4 * 4}] if tail is not None else []) +
+        [{"kind": "status"}],
     }
     return module([text], launch, globals_=[".extern .shared .align 1024 .b8 dsmem[];"])
 
@@ -982,7 +1072,7 @@ def _emit_direct_loader(p: Ptx, cfg: GemmConfig, ptr: dict, tid, ring, bars, emp
 
 def _emit_epilogue(p: Ptx, cfg: GemmConfig, ptr: dict, bars, tfull0, tempty0, tbase, warp, lane,
                    cta, nct, ntiles, waits: Waits, finish: str, crank=None, ltempty=None,
-                   ks: int = 1) -> None:
+                   ks: int = 1, tail=None) -> None:
     """TMEM accumulator -> fused epilogue ops -> C, one thread per row.  With ``ks`` K slices
     per tile, each unit first writes its f32 partial to a workspace; per warp quarter of the
     tile a ticket counts the slices in, and the warp that takes the last one sums the
@@ -1026,7 +1116,11 @@ def _emit_epilogue(p: Ptx, cfg: GemmConfig, ptr: dict, bars, tfull0, tempty0, tb
     """)
     waits.wait(tfa, aph, "epilogue", finish)
     p.emit("bar.warp.sync -1\ntcgen05.fence::after_thread_sync")
-    bt, mt, nt = _tile_coords(p, cfg, t, ks)
+    if tail is None:
+        bt, mt, nt = _tile_coords(p, cfg, t, ks)
+        psl = v = None
+    else:
+        bt, mt, nt, _, _, psl, v = _unit_plan(p, cfg, t, 1, 0, tail)
     row, n0, taddr = p.reg("u32"), p.reg("u32"), p.reg("u32")
     prow = p.reg("pred")
     if crank is not None:   # the CTA's 128 rows of the pair's 256-row tile
@@ -1126,6 +1220,23 @@ def _emit_epilogue(p: Ptx, cfg: GemmConfig, ptr: dict, bars, tfull0, tempty0, tb
         l_next = _emit_ksplit_partial(p, cfg, ks, t, row_t, lane, q, regs, nchunks, load_chunk)
         for ch in range(nchunks):
             store_chunk(ch, _ksplit_sum(p, cfg, ks, t, row_t, ch))
+    elif tail is not None:
+        # whole tiles store straight from TMEM; sliced tail units go through the workspace
+        l_sl, l_join = p.label("e_sliced"), p.label("e_join")
+        p.emit(f"@{psl} bra {l_sl}")
+        for ch in range(nchunks):
+            load_chunk(ch)
+            vals = [p.reg("f32") for _ in range(32)]
+            for i in range(32):
+                p.emit(f"mov.b32 {vals[i]}, {regs[i]}")
+            store_chunk(ch, vals)
+        p.emit(f"bra {l_join}")
+        p.place(l_sl)
+        ts = tail[1]
+        l_next = _emit_ksplit_partial(p, cfg, ts, v, rt2, lane, q, regs, nchunks, load_chunk, crank)
+        for ch in range(nchunks):
+            store_chunk(ch, _ksplit_sum(p, cfg, ts, v, rt2, ch))
+        p.place(l_join)
     else:
         l_next = None
         for ch in range(nchunks):
@@ -1146,20 +1257,21 @@ def _emit_epilogue(p: Ptx, cfg: GemmConfig, ptr: dict, bars, tfull0, tempty0, tb
 
 
 def _emit_ksplit_partial(p: Ptx, cfg: GemmConfig, ks: int, t: str, row_t: str, lane: str,
-                         q: str, regs: list, nchunks: int, load_chunk) -> str:
+                         q: str, regs: list, nchunks: int, load_chunk, crank=None) -> str:
     """Write this unit's accumulator rows to the workspace and take the warp quarter's
     ticket; returns the label the warps that are not last jump to (the next unit)."""
     BN, MT = cfg.BN, cfg.MT
     ws, tk = p.reg("b64"), p.reg("b64")
     p.emit(f"ld.param.u64 {ws}, [param__ksplit_ws]\ncvta.to.global.u64 {ws}, {ws}\n"
            f"ld.param.u64 {tk}, [param__ksplit_tickets]\ncvta.to.global.u64 {tk}, {tk}")
-    # row (unit t, row_t) of the workspace: [tile][slice][row][BN] f32 = [unit][row][BN]
-    wrow, w = p.reg("b64"), p.reg("u32")
-    p.emit(f"mad.lo.u32 {w}, {t}, {MT}, {row_t}\nmul.wide.u32 {wrow}, {w}, {BN * 4}\nadd.s64 {wrow}, {wrow}, {ws}")
+    # the workspace holds one f32 partial per unit, [unit][column / 4][row][4]: the lanes
+    # (consecutive rows) of a warp store consecutive 16-byte pieces, 512 bytes per warp
+    # store, and the slices are summed with the same coalesced loads
+    wrow = _ws_row(p, ws, t, row_t, MT, BN)
     for ch in range(nchunks):
         load_chunk(ch)
         for g in range(8):
-            p.emit(f"st.global.v4.b32 [{wrow}+{(ch * 32 + 4 * g) * 4}], {{{', '.join(regs[4 * g:4 * g + 4])}}}")
+            p.emit(f"st.global.v4.b32 [{wrow}+{(ch * 8 + g) * MT * 16}], {{{', '.join(regs[4 * g:4 * g + 4])}}}")
     # every lane's stores before lane 0's ticket; the ticket of (tile, warp quarter).  Lane
     # 0 takes it with an acq_rel atom; the warp barrier after the broadcast orders the
     # other lanes' later reads of the other slices after that acquire (then each lane's
@@ -1171,6 +1283,7 @@ def _emit_ksplit_partial(p: Ptx, cfg: GemmConfig, ks: int, t: str, row_t: str, l
         fence.acq_rel.gpu
         bar.warp.sync -1
         div.u32 {tile}, {t}, {ks}
+        {f"mad.lo.u32 {tile}, {tile}, 2, {crank}" if crank is not None else ""}
         mad.lo.u32 {tile}, {tile}, 4, {q}
         mul.wide.u32 {ta}, {tile}, 4
         add.s64 {ta}, {ta}, {tk}
@@ -1189,26 +1302,41 @@ def _emit_ksplit_partial(p: Ptx, cfg: GemmConfig, ks: int, t: str, row_t: str, l
     return l_next
 
 
+def _ws_row(p: Ptx, ws: str, unit: str, row: str, MT: int, BN: int) -> str:
+    """Address of (unit, first column group, row) in the [unit][column / 4][row][4] f32
+    workspace; column group g of chunk ch is (ch * 8 + g) * MT * 16 bytes further."""
+    a, r = p.reg("b64"), p.reg("b64")
+    p.emit(f"mul.wide.u32 {a}, {unit}, {MT * BN * 4}\nadd.s64 {a}, {a}, {ws}\n"
+           f"mul.wide.u32 {r}, {row}, 16\nadd.s64 {a}, {a}, {r}")
+    return a
+
+
 def _ksplit_sum(p: Ptx, cfg: GemmConfig, ks: int, t: str, row_t: str, ch: int) -> list:
     """Columns 32 ch .. 32 ch + 31 of the thread's row summed over the tile's slices in
     slice order (L2 loads: the other slices were written by other CTAs)."""
     BN, MT = cfg.BN, cfg.MT
     ws = p.reg("b64")
     p.emit(f"ld.param.u64 {ws}, [param__ksplit_ws]\ncvta.to.global.u64 {ws}, {ws}")
-    u0, w, a = p.reg("u32"), p.reg("u32"), p.reg("b64")
+    u0, w = p.reg("u32"), p.reg("u32")
     # unit of slice 0 of this tile: t - t % ks
     p.emit(f"rem.u32 {u0}, {t}, {ks}\nsub.u32 {u0}, {t}, {u0}")
     acc = [p.reg("f32") for _ in range(32)]
-    tmp = [p.reg("f32") for _ in range(32)]
-    for sl in range(ks):
-        p.emit(f"add.u32 {w}, {u0}, {sl}\nmad.lo.u32 {w}, {w}, {MT}, {row_t}\n"
-               f"mul.wide.u32 {a}, {w}, {BN * 4}\nadd.s64 {a}, {a}, {ws}")
-        dst = acc if sl == 0 else tmp
-        for g in range(8):
-            p.emit(f"ld.global.cg.v4.f32 {{{', '.join(dst[4 * g:4 * g + 4])}}}, [{a}+{(ch * 32 + 4 * g) * 4}]")
-        if sl:
-            for i in range(32):
-                p.emit(f"add.rn.f32 {acc[i]}, {acc[i]}, {tmp[i]}")
+    # the loads of up to four slices are in flight together (their own registers), then
+    # added in slice order: one L2 round trip per group of slices, the same sum
+    for g0 in range(0, ks, 4):
+        group = list(range(g0, min(ks, g0 + 4)))
+        bufs = {sl: (acc if sl == 0 else [p.reg("f32") for _ in range(32)]) for sl in group}
+        for sl in group:
+            p.emit(f"add.u32 {w}, {u0}, {sl}")
+            a = _ws_row(p, ws, w, row_t, MT, BN)
+            dst = bufs[sl]
+            for g in range(8):
+                p.emit(f"ld.global.cg.v4.f32 {{{', '.join(dst[4 * g:4 * g + 4])}}}, "
+                       f"[{a}+{(ch * 8 + g) * MT * 16}]")
+        for sl in group:
+            if sl:
+                for i in range(32):
+                    p.emit(f"add.rn.f32 {acc[i]}, {acc[i]}, {bufs[sl][i]}")
     return acc
 
 

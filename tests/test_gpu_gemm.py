@@ -36,14 +36,17 @@ def test_gemm_matches_golden(runtime, pid):
         assert np.allclose(got, o, rtol=meta["rtol"], atol=meta["atol"])
 
 
-def _direct_gemm(m, n, k, pair, b_kmajor, seed=0, batch=1, ksplit=0, launches=1):
+def _direct_gemm(m, n, k, pair, b_kmajor, seed=0, batch=1, ksplit=0, launches=1, tail_split=0):
     from compiler.kernels.gemm import GemmConfig, emit_gemm_module
     from emmyrt import DeviceBuffer
     from emmyrt.runner import CompiledKernel, bf16_bits_to_f32, f32_to_bf16_bits
     import emmyrt
     cfg = GemmConfig(M=m, N=n, K=k, batch=batch, ab="bf16", c="bf16", b_kmajor=b_kmajor, BN=256,
                      stages=6 if pair else 4, pair=pair, name="k_gemm_test", buffers=("a", "b", "c"),
-                     ksplit=ksplit)
+                     ksplit=ksplit, tail_split=tail_split)
+    if tail_split > 1:
+        from compiler import parse_launch
+        assert parse_launch(emit_gemm_module(cfg))["tail_split"] == tail_split
     ck = CompiledKernel.from_module(emit_gemm_module(cfg), "k_gemm_test", ["a", "b", "c"])
     rng = np.random.default_rng(seed)
     A = f32_to_bf16_bits(rng.standard_normal((batch, m, k), dtype=np.float32) * np.float32(0.05))
@@ -134,3 +137,21 @@ def test_pdl_chain_waits_for_the_previous_gemm(runtime):
         assert np.isfinite(C2).all(), f"rep {rep}: the second GEMM read the first's C too early"
         assert_parity(C1, mm_bf16(bf16_bits_to_f32(A), bf16_bits_to_f32(B)), rel=1e-2, what="first")
         assert_parity(C2, mm_bf16(C1, bf16_bits_to_f32(B)), rel=1e-2, what="second")
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("m,n,k,pair,ts", [(2560, 2048, 1024, True, 4),    # 80 pair tiles: 74 + 6 sliced
+                                            (1280, 4096, 512, False, 2),    # 160 CTA tiles: 148 + 12
+                                            (2560, 2048, 2048, True, 8)])
+def test_gemm_tail_split(runtime, m, n, k, pair, ts):
+    """The tiles past the last full wave cut into K slices (partials through the workspace,
+    the last slice's ordered sum): against the oracle on rows of every M tile, against
+    the same GEMM with whole tiles (within one bf16 rounding: only the tail's order
+    differs), bit-identical over three launches of one module (the tickets reset)."""
+    from oracle.refs import mm_bf16
+    from parity import assert_parity
+    got, A, B = _direct_gemm(m, n, k, pair, False, seed=7, launches=3, tail_split=ts)
+    whole, _, _ = _direct_gemm(m, n, k, pair, False, seed=7, tail_split=1)
+    rows = np.arange(0, m, 37)
+    assert_parity(got[0][rows], mm_bf16(A[0][rows], B[0]), rel=1e-2, what=f"tail split {ts}")
+    assert_parity(got[0], whole[0], rel=5e-3, ulps=1, what="tail split vs whole tiles")
