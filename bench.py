@@ -408,10 +408,6 @@ class Workload:
             from emmyrt.dist import NCCL_FLOAT64
             self.comm.allreduce(self.partial_ptr, self.total.ptr, 1, NCCL_FLOAT64, stream=stream)
 
-    @property
-    def launches_per_step(self) -> int:
-        return 1
-
     def free(self):
         for bs in self.bufsets:
             for b in bs.values():
@@ -461,7 +457,6 @@ def _e2e(w: Workload, steps: int, dist: Dist) -> dict:
     inputs up from pinned host memory and its result down."""
     import emmyrt
     from emmyrt import DeviceBuffer, Event, Stream, check, lib
-    outs = {n: np.empty_like(w.inputs[n]) for n in w.out_names}
     from emmyrt import HostBuffer
     host_out = {n: HostBuffer(max(16, w.inputs[n].nbytes)) for n in w.out_names}
     pipelined = w.fp8 is None and w.total is None
@@ -537,7 +532,6 @@ def _e2e(w: Workload, steps: int, dist: Dist) -> dict:
             b.free()
     for hb in host_out.values():
         hb.free()
-    del outs
     total = bc.work(w.name, 0, 1) if w.cfg is not None else _units_of(w)
     return {"value": round(to_rate(total, ms / 1e3, w.unit), 3), "unit": w.unit,
             "h2d_bytes_per_step": int(w.in_bytes), "d2h_bytes_per_step": int(d2h),
@@ -585,7 +579,7 @@ def measure(name: str, args, dist: Dist, comm, headline: bool) -> dict:
                                     ms_step / 1e3, clocks, ms / 1e3, dist.world),
                "clocks": clocks,
                "ms_x_sm_mhz": round(ms_step * clocks["sm_mhz"], 3) if clocks.get("sm_mhz") else None,
-               "gpu_launches": steps * w.launches_per_step, "launch": form,
+               "gpu_launches": steps, "launch": form,
                "kernel": {"entry": w.ck.spec.name, "grid": w.ck.launch["grid"],
                           "block": w.ck.launch["block"], "smem": w.ck.launch.get("smem", 0)},
                "config": config_of(name, dist.world) if w.cfg is not None else {"workload": name}}

@@ -463,6 +463,11 @@ class RowReduce:
                         p.emit(f"mov.f32 {r}, {f32_hex(float(acc.op.identity))}")
                         ctx.env[acc.name] = Val(r, "f32")
                         ctx.mutable.add(acc.name)
+        # programmatic dependent launch: every CTA of this grid is on an SM once all have
+        # passed here, so the stream's next kernel may launch and set up while this one
+        # finishes; this grid waits for the previous kernel (complete, writes visible)
+        # before its first global load
+        p.emit("griddepcontrol.launch_dependents\ngriddepcontrol.wait")
         # every pass's column loads are independent of the row results: issue them all up
         # front so the second pass's operands (e.g. RMSNorm's weight) are in flight with x
         for ph in self.phases:
@@ -483,7 +488,7 @@ class RowReduce:
                 p.place(skip)
         p.emit("ret")
         launch = {"kind": "row_reduce", "grid": [self.grid, 1, 1], "block": [self.CTA, 1, 1],
-                  "cluster": [1, 1, 1], "smem": 0, "extra_params": [],
+                  "cluster": [1, 1, 1], "smem": 0, "extra_params": [], "pdl": True,
                   "rows": self.rows, "cols": self.L}
         text = entry(spec.name, arg_params(spec), p, maxntid=self.CTA)
         # shared arrays are declared inside the entry body

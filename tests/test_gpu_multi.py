@@ -91,7 +91,6 @@ def test_sharded_gemm_against_the_oracle(runtime, shards):
 @pytest.mark.gpu
 def test_sharded_fp8_uses_the_whole_b_scale(runtime, shards):
     import baseline_configs as bc
-    from emmyrt.fp8 import e4m3_decode  # noqa: F401
     from hostfmt import bf16_bits_to_f32
     from oracle.refs import e4m3_round, mm_fp8
     C = bf16_bits_to_f32(np.concatenate(_pieces(shards, "fp8_8192"), axis=1))

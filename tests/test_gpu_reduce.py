@@ -55,3 +55,42 @@ def test_rerun_is_deterministic(runtime):
     a = run_problem(GOLDEN / "x_r_unpinned_sum")["outputs"]["sum_1"]
     b = run_problem(GOLDEN / "x_r_unpinned_sum")["outputs"]["sum_1"]
     assert np.array_equal(a, b)
+
+
+@pytest.mark.gpu
+def test_row_reduce_pdl_chain(runtime, golden):
+    """Programmatic dependent launch on the row template: y1 = rmsnorm(x, w) and
+    y2 = rmsnorm(y1, w) launched back to back on one stream with no host sync; the second
+    waits (griddepcontrol.wait) for the first before reading y1."""
+    import json
+    import emmyrt
+    from emmyrt import DeviceBuffer
+    from emmyrt.runner import CompiledKernel, seeded_input
+    from oracle.refs import rmsnorm
+    d = golden / "x_l_rmsnorm_w"
+    meta = json.loads((d / "meta.json").read_text())
+    k = meta["kernels"][0]
+    ck = CompiledKernel.from_ir(d / f"{k['entry']}.ir.json")
+    assert ck.launch["pdl"] and ck.launch_flags == emmyrt.LAUNCH_PDL
+    args = {a["name"]: a for a in k["args"]}
+    host = {n: seeded_input(a) for n, a in args.items()}
+    bufs = {n: DeviceBuffer(h.nbytes) for n, h in host.items()}
+    for n, h in host.items():
+        bufs[n].upload(h)
+    y2 = DeviceBuffer(host["mul_1"].nbytes)
+    for rep in range(3):
+        bufs["mul_1"].upload(np.full_like(host["mul_1"], np.nan))
+        y2.zero()
+        first = ck.prepare(ck.params({n: b.ptr for n, b in bufs.items()}))
+        second = ck.prepare(ck.params({**{n: b.ptr for n, b in bufs.items()},
+                                       "x0": bufs["mul_1"].ptr, "mul_1": y2.ptr}))
+        first(0)
+        second(0)
+        emmyrt.stream_wait(0, 60)
+        got1, got2 = np.zeros_like(host["mul_1"]), np.zeros_like(host["mul_1"])
+        bufs["mul_1"].download(got1)
+        y2.download(got2)
+        assert np.isfinite(got2).all(), f"rep {rep}: the second kernel read y1 too early"
+        ref1 = rmsnorm(host["x0"], host["x1"], 1e-6)
+        np.testing.assert_allclose(got1, ref1, rtol=1e-5, atol=1e-6)
+        np.testing.assert_allclose(got2, rmsnorm(got1, host["x1"], 1e-6), rtol=1e-5, atol=1e-6)
