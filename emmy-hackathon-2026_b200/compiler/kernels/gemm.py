@@ -127,12 +127,20 @@ def choose_bn(M: int, N: int, batch: int, min_bn: int = 64) -> int:
     return choose_tiling(M, N, batch, min_bn, pairs=False)["BN"]
 
 
+# shared memory of the epilogue's store staging: per epilogue warp, its 32 rows x 32
+# columns of 16-bit results, rows 80 bytes apart (64 bytes + 16 of padding: the rows' 16-byte
+# pieces fall in distinct banks when each lane writes its own row)
+EPI_ROW = 80
+EPI_STAGE_BYTES = 4 * 32 * EPI_ROW
+
+
 def _stages_fit(bn: int, cap: int = 8) -> int:
-    """Stages of a 16-bit / 8-bit TMA ring that fit in shared memory: a stage holds one
-    128-byte K row of A (128 rows) and of B (bn columns).  Short K loops gain most from a
-    deep ring (every K block of a 512^3 tile in flight: 5.2 us against 6.2 us with 4)."""
+    """Stages of a 16-bit / 8-bit TMA ring that fit in shared memory beside the epilogue's
+    staging: a stage holds one 128-byte K row of A (128 rows) and of B (bn columns).  Short
+    K loops gain most from a deep ring (every K block of a 512^3 tile in flight: 5.2 us
+    against 6.2 us with 4)."""
     stage = 128 * 128 + bn * 128
-    return max(4, min(cap, (232448 - 256 - 1024) // stage))
+    return max(4, min(cap, (232448 - 256 - 1024 - EPI_STAGE_BYTES) // stage))
 
 
 def choose_tiling(M: int, N: int, batch: int, min_bn: int = 64, pairs: bool = True) -> dict:
@@ -346,6 +354,11 @@ def emit_gemm_module(cfg: GemmConfig) -> str:
     smem = S * stage_bytes + 1024           # +1 KB to align the ring to 1024 B
     if smem > 232448 - 256:
         raise NotImplementedError("stage ring exceeds shared memory")
+    # 16-bit results leave through shared memory (see _emit_epilogue) when it has room
+    epi_off = None
+    if cfg.c in ("bf16", "f16") and N % 8 == 0 and smem + EPI_STAGE_BYTES <= 232448 - 256:
+        epi_off = S * stage_bytes
+        smem += EPI_STAGE_BYTES
     # tf32 operands read MN-major need the 32-byte-atom swizzle; the 3xTF32 converter writes
     # B K-major instead (the layout A has), so the MMAs read both operands K-major
     mma_b_kmajor = cfg.b_kmajor or cfg.converts
@@ -655,7 +668,8 @@ def emit_gemm_module(cfg: GemmConfig) -> str:
         role_conv = p.label("role_conv")
         p.emit(f"setp.ge.u32 {pr}, {warp}, {GEMM_THREADS // 32}\n@{pr} bra {role_conv}")
     _emit_epilogue(p, cfg, ptr, bars, tfull0, tempty0, tbase, warp, lane, cta, nct, nunits,
-                   waits, finish, crank if pair else None, ltempty if pair else None, KS, tail)
+                   waits, finish, crank if pair else None, ltempty if pair else None, KS, tail,
+                   None if epi_off is None else (ring, epi_off))
     if conv:
         p.place(role_conv)
         if direct:
@@ -692,7 +706,9 @@ def emit_gemm_module(cfg: GemmConfig) -> str:
         params += [".param .u64 param__ksplit_ws", ".param .u64 param__ksplit_tickets"]
     params += [".param .u64 param__status"]
     nthreads = GEMM_THREADS + (CONV_THREADS if conv else 0)
-    text = entry(cfg.name, params, p, maxntid=nthreads)
+    # one CTA per SM (its shared memory allows no more): registers are not scarce, so
+    # let the allocator keep the epilogue's rows in registers instead of spilling
+    text = entry(cfg.name, params, p, maxntid=nthreads, extra_directives="\n.maxnreg 128")
     statics = (f"\t.shared .align 8 .b64 gbars[{nbar}];\n\t.shared .align 4 .u32 gabort;\n"
                f"\t.shared .align 4 .u32 gtmem;\n")
     text = text.replace("{\n", "{\n" + statics, 1)
@@ -1072,7 +1088,7 @@ def _emit_direct_loader(p: Ptx, cfg: GemmConfig, ptr: dict, tid, ring, bars, emp
 
 def _emit_epilogue(p: Ptx, cfg: GemmConfig, ptr: dict, bars, tfull0, tempty0, tbase, warp, lane,
                    cta, nct, ntiles, waits: Waits, finish: str, crank=None, ltempty=None,
-                   ks: int = 1, tail=None) -> None:
+                   ks: int = 1, tail=None, epi_stage=None) -> None:
     """TMEM accumulator -> fused epilogue ops -> C, one thread per row.  With ``ks`` K slices
     per tile, each unit first writes its f32 partial to a workspace; per warp quarter of the
     tile a ticket counts the slices in, and the warp that takes the last one sums the
@@ -1081,6 +1097,13 @@ def _emit_epilogue(p: Ptx, cfg: GemmConfig, ptr: dict, bars, tfull0, tempty0, tb
     cb = ELEM_BYTES[cfg.c]
     q, row_t = p.reg("u32"), p.reg("u32")
     p.emit(f"and.b32 {q}, {warp}, 3\nmad.lo.u32 {row_t}, {q}, 32, {lane}")
+    wbuf = rsub = csub = None
+    if epi_stage is not None:
+        # this warp's staging rows, and the (row, 16-byte column piece) each lane stores
+        ring_r, epi_off = epi_stage
+        wbuf, rsub, csub = p.reg("u32"), p.reg("u32"), p.reg("u32")
+        p.emit(f"mad.lo.u32 {wbuf}, {q}, {32 * EPI_ROW}, {ring_r}\nadd.u32 {wbuf}, {wbuf}, {epi_off}\n"
+               f"shr.u32 {rsub}, {lane}, 2\nand.b32 {csub}, {lane}, 3")
     lane_off = p.reg("u32")
     p.emit(f"shl.b32 {lane_off}, {q}, 21")           # (q * 32) << 16: the warp's TMEM lane quarter
     cptr = ptr[cfg.c_param]
@@ -1160,6 +1183,19 @@ def _emit_epilogue(p: Ptx, cfg: GemmConfig, ptr: dict, bars, tfull0, tempty0, tb
         res_adr[name] = a
     nchunks = BN // 32
     regs = [p.reg("b32") for _ in range(32)]
+    if wbuf is not None:
+        # the warp's first row (the lane's row minus its lane) and the address of
+        # (row rsub, piece csub) of its chunk 0: lane l stores rows l / 4 + 8 i
+        rowq0, sadr, w64 = p.reg("u32"), p.reg("b64"), p.reg("b64")
+        p.emit(f"""
+            sub.u32 {rowq0}, {row}, {lane}
+            mul.wide.u32 {w64}, {lane}, {N * cb}
+            sub.s64 {sadr}, {cadr}, {w64}
+            mul.wide.u32 {w64}, {rsub}, {N * cb}
+            add.s64 {sadr}, {sadr}, {w64}
+            mul.wide.u32 {w64}, {csub}, 16
+            add.s64 {sadr}, {sadr}, {w64}
+        """)
     if cfg.zero_slots and cfg.c != "f32":
         raise NotImplementedError("split-K partial slices other than f32")
     def load_chunk(ch):
@@ -1174,8 +1210,37 @@ def _emit_epilogue(p: Ptx, cfg: GemmConfig, ptr: dict, bars, tfull0, tempty0, tb
             else:
                 p.emit(f"tcgen05.fence::before_thread_sync\nmbarrier.arrive.shared::cta.b64 _, [{tea}]")
 
+    def store_chunk_staged(ch, vals):
+        """Each lane's row of 32 results into the warp's staging rows, then the warp
+        stores 8 rows x 64 contiguous bytes per instruction (4 instructions a chunk)."""
+        cvt = "cvt.rn.bf16x2.f32" if cfg.c == "bf16" else "cvt.rn.f16x2.f32"
+        packed = [p.reg("b32") for _ in range(16)]
+        for i in range(16):
+            p.emit(f"{cvt} {packed[i]}, {vals[2 * i + 1]}, {vals[2 * i]}")
+        wrow = p.reg("u32")
+        p.emit(f"mad.lo.u32 {wrow}, {lane}, {EPI_ROW}, {wbuf}")
+        for g in range(4):
+            p.emit(f"st.shared.v4.b32 [{wrow}+{16 * g}], {{{', '.join(packed[4 * g:4 * g + 4])}}}")
+        p.emit("bar.warp.sync -1")
+        rd, colr, grow = p.reg("u32"), p.reg("u32"), p.reg("u32")
+        p.emit(f"mad.lo.u32 {rd}, {rsub}, {EPI_ROW}, {wbuf}\nmad.lo.u32 {rd}, {csub}, 16, {rd}\n"
+               f"mad.lo.u32 {colr}, {csub}, 8, {n0}\nadd.u32 {colr}, {colr}, {ch * 32}")
+        pc = p.reg("pred")
+        p.emit(f"setp.lt.u32 {pc}, {colr}, {N}")
+        for i in range(4):
+            x = [p.reg("b32") for _ in range(4)]
+            pg = p.reg("pred")
+            p.emit(f"ld.shared.v4.b32 {{{', '.join(x)}}}, [{rd}+{8 * i * EPI_ROW}]\n"
+                   f"add.u32 {grow}, {rowq0}, {rsub}\nadd.u32 {grow}, {grow}, {8 * i}\n"
+                   f"setp.lt.and.u32 {pg}, {grow}, {M}, {pc}\n"
+                   f"@{pg} st.global.v4.b32 [{sadr}+{8 * i * N * cb + ch * 64}], {{{', '.join(x)}}}")
+        p.emit("bar.warp.sync -1")
+
     def store_chunk(ch, vals):
         vals = _apply_epilogue(p, cfg, vals, scale, res_adr, ch, prow, n0)
+        if wbuf is not None:
+            store_chunk_staged(ch, vals)
+            return
         skip = p.label("st_skip")
         col0 = ch * 32
         p.emit(f"@!{prow} bra {skip}")
