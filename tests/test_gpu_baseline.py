@@ -9,7 +9,7 @@ within 4 bf16 ulps of the output's largest magnitude, no absolute floor):
 
 * GEMM: the whole output at 512^3 and 2048^3, sampled rows at the larger sizes,
   recomputed by the oracle in f64, rel 1e-2;
-* attention: 8 or more query rows of EVERY one of the 256 batch x head pairs, rel 1e-2;
+* attention: 16 or more query rows of EVERY one of the 256 batch x head pairs, rel 1e-2;
 * FP8: sampled rows, rel 5e-2, the quantised operands bit-exact with the oracle's cast;
 * RMSNorm: the whole 4096 x 4096 output within 1e-5 relative per element;
 * row softmax: sampled rows within 1e-5 relative, and every one of the 65536 rows
@@ -83,7 +83,7 @@ def test_attention_full_size_every_head(runtime):
     got, ref = [], []
     for b in range(B):
         for h in range(H):
-            rows = sample_rows(S, 8, seed=b * H + h)
+            rows = sample_rows(S, 16, seed=b * H + h)
             got.append(o[b, h, rows])
             ref.append(attn_bf16(q[b, h, rows], kk[b, h], v[b, h], scale))
             # each pair on its own too: a head-indexing mistake shows up where it happens
