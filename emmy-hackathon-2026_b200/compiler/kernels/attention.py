@@ -77,6 +77,10 @@ class AttnConfig:
     mask_bh_stride: int = 0  # elements between the masks of consecutive batch x heads (0: shared)
     heads: int = 0           # query heads per batch entry (grouped-query attention; 0: no groups)
     kv_group: int = 1        # query heads per key / value head: head h reads K / V head h // kv_group
+    # "tiles": this module's two-tile template; "split_keys": the persistent split-key
+    # schedule of attention_split.py (unmasked, non-causal problems only; measured and
+    # not the default)
+    schedule: str = "tiles"
 
     @property
     def BHKV(self) -> int:               # batch x key / value heads
@@ -109,6 +113,11 @@ def register_split(nq: int) -> tuple[int, int, int]:
 
 
 def emit_attention_module(cfg: AttnConfig) -> str:
+    if cfg.schedule == "split_keys":
+        from .attention_split import emit_attention_split_module
+        return emit_attention_split_module(cfg)
+    if cfg.schedule != "tiles":
+        raise NotImplementedError(f"attention schedule {cfg.schedule}")
     if cfg.dtype not in AB_FORMAT:
         raise NotImplementedError(f"attention in {cfg.dtype}")
     if cfg.scale <= 0:
