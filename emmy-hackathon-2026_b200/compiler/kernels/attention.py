@@ -39,7 +39,8 @@ The online-softmax state (m, l) is f32.  Every mbarrier wait is bounded.
 from __future__ import annotations
 
 import math
-from dataclasses import dataclass
+import os
+from dataclasses import dataclass, replace
 
 from ..ptx import Ptx, entry, f32_hex, module
 from .common import arg_params, load_pointer, param_symbol
@@ -79,7 +80,7 @@ class AttnConfig:
     kv_group: int = 1        # query heads per key / value head: head h reads K / V head h // kv_group
     # "tiles": this module's two-tile template; "split_keys": the persistent split-key
     # schedule of attention_split.py (unmasked, non-causal problems only; measured and
-    # not the default)
+    # not the default; EMMY_ATTENTION_SCHEDULE=split_keys selects it wherever it applies)
     schedule: str = "tiles"
 
     @property
@@ -113,6 +114,12 @@ def register_split(nq: int) -> tuple[int, int, int]:
 
 
 def emit_attention_module(cfg: AttnConfig) -> str:
+    if cfg.schedule == "tiles" and os.environ.get("EMMY_ATTENTION_SCHEDULE") == "split_keys":
+        # the whole compile path (bench.py included) on the split-key schedule wherever
+        # it applies, for measuring it against this template
+        from .attention_split import eligible
+        if eligible(cfg):
+            cfg = replace(cfg, schedule="split_keys")
     if cfg.schedule == "split_keys":
         from .attention_split import emit_attention_split_module
         return emit_attention_split_module(cfg)

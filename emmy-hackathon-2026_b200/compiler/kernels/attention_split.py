@@ -40,7 +40,7 @@ so the ring needs no empty barriers of its own; the shared-memory descriptors of
 ring slots are formed once and a K step adds its offset to the 64-bit descriptor.
 The protocol is checked under random schedules by ``tests/test_attention_split_protocol.py``.
 
-Measured on the B200 (BASELINE 8 x 32 x 4096 x 128): about 0.95x the two-tile template.
+Measured on the B200 (BASELINE 8 x 32 x 4096 x 128, bench.py): 0.87-0.91x the two-tile template.
 Per 128-key block the two 64-key score products read Q twice from shared memory, so the
 block moves 192 KB through shared memory (both operands of 16 N = 64 score MMAs, V for 8
 PV MMAs, 64 KB of TMA writes) against the template's 128 KB per tile and block, and
