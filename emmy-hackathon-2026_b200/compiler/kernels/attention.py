@@ -5,8 +5,18 @@ Replaces the reference's register-fragment flash attention (``compiler/mma.py``:
 row max / sum by 2-step shuffles, ``FragmentRepack`` P -> A fragment; K and V read
 straight from global memory, ``tests/problems/x_h_attn_128``, ``x_h_sdpa``).
 
-Kernel structure (one CTA per NQ = 2 query tiles of 128 rows of one batch x head;
-128 * (NQ + 1) threads, one warpgroup per query tile plus a control warpgroup):
+Kernel structure (128 * (NQ + 1) threads, one warpgroup per query tile plus a control
+warpgroup).  The CTAs are persistent, one per SM: CTA c takes the units c, c + grid, ...,
+a unit being NQ = 2 query tiles of 128 rows of one batch x head (consecutive units share
+the batch x head, so concurrent CTAs share K and V in L2; causal: the units with the
+most keys first).  Every role loops over its CTA's units: the K / V ring streams on
+across unit boundaries, the next unit's Q_t tile is loaded as soon as the last
+``Q_t K^T`` of the current unit is done (``q_empty``), the next unit's ``S_t(0)`` are
+issued right behind the current unit's last ``O_t += P_t V`` of both tiles, and the
+barrier parities count blocks over all units.  Against one CTA per unit this measured
+the same (1240.6 against 1243.2 TFLOP/s at the BASELINE size).  (Issuing a tile's next-unit ``S_t(0)`` straight after its
+own last product instead, before the other tile's, measured 4 % slower: the MMA thread
+then waits for the next Q tile while the other tile's product is still to be issued.)
 
 * softmax warpgroup t (warps 4t .. 4t+3), one thread per query row (TMEM lane):
   reads its whole 128-key S row out of TMEM in one go (four ``tcgen05.ld.32x32b.x32``,
@@ -21,9 +31,9 @@ Kernel structure (one CTA per NQ = 2 query tiles of 128 rows of one batch x head
   either way.  With two query tiles the control warpgroup hands its registers to the
   softmax warpgroups (``setmaxnreg``), so the S row, the probabilities and the
   addresses stay in registers;
-* control warpgroup: warp 4NQ, lane 0 -- TMA: Q tiles once, then K_j and V_j (128 keys
-  each) through a ring of 128-byte-swizzled shared-memory slots (as many as shared
-  memory holds: 5 at D = 128), full/empty mbarrier per slot; warp 4NQ+1 -- TMEM
+* control warpgroup: warp 4NQ, lane 0 -- TMA: per unit the Q tiles, then K_j and V_j
+  (128 keys each) through a ring of 128-byte-swizzled shared-memory slots (as many as
+  shared memory holds: 5 at D = 128), full/empty mbarrier per slot; warp 4NQ+1 -- TMEM
   allocation (S_t: 128 f32 columns, O_t: D columns per tile) and, on lane 0, the MMA
   stream: ``S_t = Q_t K_j^T`` (kind::f16, M=128,
   N=128); per tile ``O_t += P_t V_j`` as soon as softmax t hands P_t over, followed by
@@ -31,9 +41,12 @@ Kernel structure (one CTA per NQ = 2 query tiles of 128 rows of one batch x head
   matrix products.  The commit that signals S_t(j+1) also covers O_t += P_t(j) V_j
   (tcgen05 operations of one thread complete in order), so softmax t may reuse its P
   buffer and rescale O_t as soon as it sees S_t(j+1);
-* epilogue (softmax warps): O row from TMEM, times 1/l, to bf16/f16, 128-bit stores.
+* epilogue (softmax warps, per unit): O row from TMEM, times 1/l, to bf16/f16, 128-bit
+  stores; the next unit's first ``O_t += P_t V`` overwrites O_t only after softmax t
+  has handed over that unit's first P_t, so the read-out needs no barrier of its own.
 
-The online-softmax state (m, l) is f32.  Every mbarrier wait is bounded.
+The online-softmax state (m, l) is f32.  Every mbarrier wait is bounded.  The barrier
+protocol is checked under random schedules by ``tests/test_attention_tiles_protocol.py``.
 """
 
 from __future__ import annotations
@@ -44,6 +57,7 @@ from dataclasses import dataclass, replace
 
 from ..ptx import Ptx, entry, f32_hex, module
 from .common import arg_params, load_pointer, param_symbol
+from .gemm import SMS
 from .tc import Waits, instr_desc, smem_desc_hi, smem_desc_lo_const
 
 LOG2E = 1.4426950408889634
@@ -189,18 +203,24 @@ def emit_attention_module(cfg: AttnConfig) -> str:
         mov.u32 {abort}, gabort
         mov.u32 {tslot}, gtmem
     """)
-    # barrier offsets
+    # barrier offsets: per query tile t the Q slot (full / empty), S_t, P_t and O_t;
+    # full / empty per ring slot.  (A unit's first O_t += P_t V needs no barrier of its
+    # own against the previous unit's epilogue: softmax t reads O_t out before it hands
+    # over that unit's first P_t.)
     B_Q = 0
-    B_KVF = 8
+    B_QE = B_Q + 8 * NQ
+    B_KVF = B_QE + 8 * NQ
     B_KVE = B_KVF + 8 * R
     B_S = B_KVE + 8 * R
     B_P = B_S + 8 * NQ
     B_O = B_P + 8 * NQ
-    nbar = 1 + 2 * R + 3 * NQ
+    nbar = 2 * R + 5 * NQ
     p0 = p.reg("pred")
     l_init = p.label("init_done")
     p.emit(f"setp.ne.u32 {p0}, {tid}, 0\n@{p0} bra {l_init}")
-    p.emit(f"mbarrier.init.shared::cta.b64 [{bars}+{B_Q}], 1")
+    for t in range(NQ):
+        p.emit(f"mbarrier.init.shared::cta.b64 [{bars}+{B_Q + 8 * t}], 1")
+        p.emit(f"mbarrier.init.shared::cta.b64 [{bars}+{B_QE + 8 * t}], 1")
     for s in range(R):
         p.emit(f"mbarrier.init.shared::cta.b64 [{bars}+{B_KVF + 8 * s}], 1")
         p.emit(f"mbarrier.init.shared::cta.b64 [{bars}+{B_KVE + 8 * s}], 1")
@@ -227,23 +247,40 @@ def emit_attention_module(cfg: AttnConfig) -> str:
     finish = p.label("finish")
     ptrue, pfalse, zr = p.reg("pred"), p.reg("pred"), p.reg("u32")
     p.emit(f"mov.u32 {zr}, 0\nsetp.eq.u32 {ptrue}, {zr}, 0\nsetp.ne.u32 {pfalse}, {zr}, 0")
-    bh, q0 = p.reg("u32"), p.reg("u32")
-    p.emit(f"mov.u32 {bh}, %ctaid.y\nmov.u32 {q0}, %ctaid.x")
-    if cfg.causal:
-        # the last query tiles see the most keys: launch them first
-        p.emit(f"sub.u32 {q0}, {-(-cfg.Sq // (128 * NQ)) - 1}, {q0}")
-    p.emit(f"mul.lo.u32 {q0}, {q0}, {128 * NQ}")
-    # key blocks per query tile: all of them, or (causal) up to the tile's last query row
-    nbt = []
-    for t in range(NQ):
+    # persistent CTAs: unit u = NQ query tiles of one batch x head (bh = u / nqp, first
+    # query row 128 NQ (u % nqp); causal: the last tiles, which see the most keys,
+    # first); CTA c takes units c, c + grid, ...; nunit = units this CTA takes
+    nqp = -(-cfg.Sq // (128 * NQ))
+    units = nqp * cfg.BH
+    grid = min(SMS, units)
+    # (%ctaid.x is read where it is needed, so no register holds it across the loops)
+
+    def unit_coords(ui):
+        """(bh, q0, key blocks per tile, key blocks of the unit) of this CTA's ui-th unit."""
+        un, bh, q0 = p.regs("u32", 3)
+        p.emit(f"mov.u32 {un}, %ctaid.x\nmad.lo.u32 {un}, {ui}, {grid}, {un}\n"
+               f"div.u32 {bh}, {un}, {nqp}\nrem.u32 {q0}, {un}, {nqp}")
         if cfg.causal:
-            r = p.reg("u32")
-            p.emit(f"add.u32 {r}, {q0}, {128 * t + 127}\nmin.u32 {r}, {r}, {cfg.Sq - 1}\n"
-                   f"shr.u32 {r}, {r}, 7\nadd.u32 {r}, {r}, 1\nmin.u32 {r}, {r}, {nblk}")
-            nbt.append(r)
-        else:
-            nbt.append(str(nblk))
-    nb_cta = nbt[-1]                      # the last tile needs the most blocks
+            p.emit(f"sub.u32 {q0}, {nqp - 1}, {q0}")
+        p.emit(f"mul.lo.u32 {q0}, {q0}, {128 * NQ}")
+        # key blocks per query tile: all of them, or (causal) up to the tile's last row
+        nbt = []
+        for t in range(NQ):
+            if cfg.causal:
+                r = p.reg("u32")
+                p.emit(f"add.u32 {r}, {q0}, {128 * t + 127}\nmin.u32 {r}, {r}, {cfg.Sq - 1}\n"
+                       f"shr.u32 {r}, {r}, 7\nadd.u32 {r}, {r}, 1\nmin.u32 {r}, {r}, {nblk}")
+                nbt.append(r)
+            else:
+                nbt.append(str(nblk))
+        return bh, q0, nbt, nbt[-1]       # the last tile needs the most blocks
+
+    def unit_loop_end(ui, label):
+        """ui += 1; back to ``label`` while this CTA has units left (unit ctaid + ui grid
+        exists)."""
+        pu, un = p.reg("pred"), p.reg("u32")
+        p.emit(f"add.u32 {ui}, {ui}, 1\nmov.u32 {un}, %ctaid.x\nmad.lo.u32 {un}, {ui}, {grid}, {un}\n"
+               f"setp.lt.u32 {pu}, {un}, {units}\n@{pu} bra {label}")
 
     def ring_advance(slot, ph):
         ps = p.reg("pred")
@@ -263,9 +300,20 @@ def emit_attention_module(cfg: AttnConfig) -> str:
 
     # ------------------------------------------------------------------ producer
     p.emit(f"prefetch.tensormap [{tq}]\nprefetch.tensormap [{tk}]\nprefetch.tensormap [{tv}]")
-    qb = p.reg("u32")
-    p.emit(f"add.u32 {qb}, {bars}, {B_Q}\nmbarrier.arrive.expect_tx.shared::cta.b64 _, [{qb}], {NQ * tile_bytes}")
+    slot, ph, ui = p.regs("u32", 3)
+    p.emit(f"mov.u32 {slot}, 0\nmov.u32 {ph}, 0\nmov.u32 {ui}, 0")
+    l_punit = p.label("p_unit")
+    p.place(l_punit)
+    bh, q0, _, nb_cta = unit_coords(ui)
     for t in range(NQ):
+        # Q_t's slot is free once the previous unit's last Q_t K^T is done (use ui - 1)
+        l_qfree = p.label("p_qfree")
+        pq0, qpar = p.reg("pred"), p.reg("u32")
+        p.emit(f"setp.eq.u32 {pq0}, {ui}, 0\n@{pq0} bra {l_qfree}\nsub.u32 {qpar}, {ui}, 1\nand.b32 {qpar}, {qpar}, 1")
+        waits.wait(_addr(p, bars, B_QE + 8 * t), qpar, "producer", finish)
+        p.place(l_qfree)
+        qb = _addr(p, bars, B_Q + 8 * t)
+        p.emit(f"mbarrier.arrive.expect_tx.shared::cta.b64 _, [{qb}], {tile_bytes}")
         for db in range(DP // 64):
             dst, y = p.reg("u32"), p.reg("u32")
             p.emit(f"add.u32 {dst}, {base}, {q_off + t * tile_bytes + db * 16384}\nadd.u32 {y}, {q0}, {t * 128}")
@@ -277,8 +325,8 @@ def emit_attention_module(cfg: AttnConfig) -> str:
         kvbh, hq = p.reg("u32"), p.reg("u32")
         p.emit(f"div.u32 {kvbh}, {bh}, {cfg.heads}\nrem.u32 {hq}, {bh}, {cfg.heads}\n"
                f"div.u32 {hq}, {hq}, {cfg.kv_group}\nmad.lo.u32 {kvbh}, {kvbh}, {cfg.heads // cfg.kv_group}, {hq}")
-    slot, ph, j = p.reg("u32"), p.reg("u32"), p.reg("u32")
-    p.emit(f"mov.u32 {slot}, 0\nmov.u32 {ph}, 0\nmov.u32 {j}, 0")
+    j = p.reg("u32")
+    p.emit(f"mov.u32 {j}, 0")
     l_pk = p.label("p_kv")
     p.place(l_pk)
     key0 = p.reg("u32")
@@ -309,17 +357,18 @@ def emit_attention_module(cfg: AttnConfig) -> str:
                        f"[{dst}], [{tm}, {{{db * 64}, {key0}, {kvbh}}}], [{fa}]")
         ring_advance(slot, ph)
     pj = p.reg("pred")
-    p.emit(f"add.u32 {j}, {j}, 1\nsetp.lt.u32 {pj}, {j}, {nb_cta}\n@{pj} bra {l_pk}\nbra {finish}")
+    p.emit(f"add.u32 {j}, {j}, 1\nsetp.lt.u32 {pj}, {j}, {nb_cta}\n@{pj} bra {l_pk}")
+    unit_loop_end(ui, l_punit)
+    p.emit(f"bra {finish}")
 
     # ----------------------------------------------------------------------- MMA
     p.place(l_mma)
     p.emit(f"setp.ne.u32 {pr}, {warp}, {W_MMA}\n@{pr} bra {finish}\nsetp.ne.u32 {pl}, {lane}, 0\n@{pl} bra {finish}")
-    zero = p.reg("u32")
-    p.emit(f"mov.u32 {zero}, 0")
-    waits.wait(_addr(p, bars, B_Q), zero, "mma", finish)
-    p.emit("tcgen05.fence::after_thread_sync")
-    cslot, cph = p.reg("u32"), p.reg("u32")
-    p.emit(f"mov.u32 {cslot}, 0\nmov.u32 {cph}, 0")
+    cslot, cph, ui = p.regs("u32", 3)
+    p.emit(f"mov.u32 {cslot}, 0\nmov.u32 {cph}, 0\nmov.u32 {ui}, 0")
+    cntp = [p.reg("u32") for _ in range(NQ)]      # P_t hand-overs taken so far, all units
+    for r in cntp:
+        p.emit(f"mov.u32 {r}, 0")
 
     def wait_slot(sl, ph_):
         fa = p.reg("u32")
@@ -384,12 +433,40 @@ def emit_attention_module(cfg: AttnConfig) -> str:
         p.emit(f"add.u32 {ob}, {bars}, {B_O + 8 * t}\n"
                f"tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [{ob}]")
 
-    # prologue: S_t(0)
+    def q_release_if_last(t, blk):
+        """Q_t's slot is free for the next unit once its last Q_t K^T (block nbt_t - 1) is
+        done; ``blk`` (a register or a constant) is the block whose Q_t K^T was just issued."""
+        l_keep = None
+        if cfg.causal:
+            l_keep, plast, last = p.label("m_qkeep"), p.reg("pred"), p.reg("u32")
+            p.emit(f"sub.u32 {last}, {nbt[t]}, 1\nsetp.ne.u32 {plast}, {last}, {blk}\n@{plast} bra {l_keep}")
+        elif nblk == 1:
+            pass                                    # every Q_t K^T is the unit's last
+        elif isinstance(blk, int):
+            if blk != nblk - 1:
+                return
+        else:
+            l_keep, plast = p.label("m_qkeep"), p.reg("pred")
+            p.emit(f"setp.ne.u32 {plast}, {blk}, {nblk - 1}\n@{plast} bra {l_keep}")
+        p.emit(f"tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 "
+               f"[{_addr(p, bars, B_QE + 8 * t)}]")
+        if l_keep is not None:
+            p.place(l_keep)
+    l_munit = p.label("m_unit")
+    p.place(l_munit)
+    _, _, nbt, nb_cta = unit_coords(ui)
+    upar = p.reg("u32")
+    p.emit(f"and.b32 {upar}, {ui}, 1")
+    # unit prologue: S_t(0) once this unit's Q_t is in (B_Q[t], use ui); on an SM the
+    # previous unit's O_t += P_t V were issued before, so they complete first
     kslot, kph = p.reg("u32"), p.reg("u32")
     p.emit(f"mov.u32 {kslot}, {cslot}\nmov.u32 {kph}, {cph}")
     wait_slot(kslot, kph)
     for t in range(NQ):
+        waits.wait(_addr(p, bars, B_Q + 8 * t), upar, "mma", finish)
+        p.emit("tcgen05.fence::after_thread_sync")
         issue_qk(t, kslot)
+        q_release_if_last(t, 0)
     release_slot(kslot)
     ring_advance(cslot, cph)
     jm = p.reg("u32")
@@ -400,10 +477,9 @@ def emit_attention_module(cfg: AttnConfig) -> str:
     p.emit(f"mov.u32 {vslot}, {cslot}\nmov.u32 {vph}, {cph}")
     ring_advance(cslot, cph)
     wait_slot(vslot, vph)
-    pfirst, pmore, pph = p.reg("pred"), p.reg("pred"), p.reg("u32")
+    pfirst, pmore = p.reg("pred"), p.reg("pred")
     nxt = p.reg("u32")
-    p.emit(f"setp.eq.u32 {pfirst}, {jm}, 0\nadd.u32 {nxt}, {jm}, 1\nsetp.lt.u32 {pmore}, {nxt}, {nb_cta}\n"
-           f"and.b32 {pph}, {jm}, 1")
+    p.emit(f"setp.eq.u32 {pfirst}, {jm}, 0\nadd.u32 {nxt}, {jm}, 1\nsetp.lt.u32 {pmore}, {nxt}, {nb_cta}")
     p.emit(f"mov.u32 {kslot}, {cslot}\nmov.u32 {kph}, {cph}")
     kwait = p.reg("pred")                  # K_{j+1} not yet waited for in this block
     p.emit(f"mov.pred {kwait}, {ptrue}")
@@ -412,8 +488,8 @@ def emit_attention_module(cfg: AttnConfig) -> str:
         if cfg.causal and t < NQ - 1:
             pact = p.reg("pred")           # (causal) this tile may stop before the CTA does
             p.emit(f"setp.lt.u32 {pact}, {jm}, {nbt[t]}\n@!{pact} bra {l_tdone}")
-        pb = p.reg("u32")
-        p.emit(f"add.u32 {pb}, {bars}, {B_P + 8 * t}")
+        pb, pph = p.reg("u32"), p.reg("u32")
+        p.emit(f"add.u32 {pb}, {bars}, {B_P + 8 * t}\nand.b32 {pph}, {cntp[t]}, 1\nadd.u32 {cntp[t]}, {cntp[t]}, 1")
         waits.wait(pb, pph, "mma", finish)
         p.emit("tcgen05.fence::after_thread_sync")
         issue_pv(t, vslot, pfirst)
@@ -429,6 +505,7 @@ def emit_attention_module(cfg: AttnConfig) -> str:
         p.emit(f"mov.pred {kwait}, {pfalse}")
         p.place(l_kw)
         issue_qk(t, kslot)
+        q_release_if_last(t, nxt)
         p.place(skip)
         p.place(l_tdone)
     release_slot(vslot)
@@ -437,14 +514,16 @@ def emit_attention_module(cfg: AttnConfig) -> str:
     release_slot(kslot)
     ring_advance(cslot, cph)
     p.place(l_norel)
-    p.emit(f"mov.u32 {jm}, {nxt}\n@{pmore} bra {l_mj}\nbra {finish}")
+    p.emit(f"mov.u32 {jm}, {nxt}\n@{pmore} bra {l_mj}")
+    unit_loop_end(ui, l_munit)
+    p.emit(f"bra {finish}")
 
     # ------------------------------------------------------------------ softmax
     p.place(l_soft)
     if NQ == 2:
         p.emit(f"setmaxnreg.inc.sync.aligned.u32 {regs_soft}")
     _emit_softmax(p, cfg, ptr, bars, B_S, B_P, B_O, tbase, base, p_off, p_bytes, warp, lane,
-                  q0, bh, nbt, scale_log2, masked, waits, finish)
+                  unit_coords, unit_loop_end, scale_log2, masked, waits, finish)
 
     # ------------------------------------------------------------------- finish
     p.place(finish)
@@ -479,7 +558,7 @@ def emit_attention_module(cfg: AttnConfig) -> str:
             {"dims": [cfg.D, cfg.Sk, cfg.BHKV], "strides": [cfg.D * eb, cfg.Sk * cfg.D * eb],
              "box": [64, 128, 1]})
     launch = {
-        "kind": "attention", "grid": [-(-cfg.Sq // (128 * NQ)), cfg.BH, 1], "block": [nthreads, 1, 1],
+        "kind": "attention", "grid": [grid, 1, 1], "block": [nthreads, 1, 1],
         "cluster": [1, 1, 1], "smem": smem, "flops": 4 * cfg.BH * visible * cfg.D,
         "exps": cfg.BH * visible,
         "extra_params": [
@@ -592,7 +671,7 @@ def _add_mask(p: Ptx, cfg: AttnConfig, fv: list, mrow: str, jj: str, scale_log2:
 
 
 def _emit_softmax(p: Ptx, cfg: AttnConfig, ptr, bars, B_S, B_P, B_O, tbase, base, p_off, p_bytes,
-                  warp, lane, q0, bh, nbt, scale_log2, masked, waits: Waits, finish):
+                  warp, lane, unit_coords, unit_loop_end, scale_log2, masked, waits: Waits, finish):
     NQ, DP = cfg.NQ, cfg.DP
     t, q, row, lanebits = p.regs("u32", 4)
     # warps 0..3 -> tile 0, 4..7 -> tile 1; TMEM lane quarter = warp % 4
@@ -617,6 +696,32 @@ def _emit_softmax(p: Ptx, cfg: AttnConfig, ptr, bars, B_S, B_P, B_O, tbase, base
         add.u32 {obar}, {sbar}, {B_O}
         add.u32 {sbar}, {sbar}, {B_S}
     """)
+    # this thread's P row in smem: tile t, row r; 16-byte chunk c of a 64-key block
+    # lives at chunk (c ^ (r % 8)) of the row (128-byte swizzle)
+    chunk_addr = {}
+    if not cfg.p_tmem:
+        prow, rx = p.reg("u32"), p.reg("u32")
+        p.emit(f"""
+            mad.lo.u32 {prow}, {t}, {p_bytes}, {base}
+            add.u32 {prow}, {prow}, {p_off}
+            mad.lo.u32 {prow}, {row}, 128, {prow}
+            and.b32 {rx}, {row}, 7
+        """)
+        for c16 in range(16):            # 16 chunks of 8 keys = 128 keys
+            blk, c = c16 // 8, c16 % 8
+            a = p.reg("u32")
+            p.emit(f"xor.b32 {a}, {rx}, {c}\nmad.lo.u32 {a}, {a}, 16, {prow}\nadd.u32 {a}, {a}, {blk * 16384}")
+            chunk_addr[c16] = a
+    cvt = "cvt.rn.bf16x2.f32" if cfg.dtype == "bf16" else "cvt.rn.f16x2.f32"
+    sl2, slr = p.reg("b64"), p.reg("f32")
+    pre_scaled = cfg.mask_param is not None
+    p.emit(f"mov.f32 {slr}, {f32_hex(1.0 if pre_scaled else scale_log2)}\nmov.b64 {sl2}, {{{slr}, {slr}}}")
+    # persistent: this CTA's units one after the other; gcnt = S_t hand-overs so far
+    ui, gcnt = p.regs("u32", 2)
+    p.emit(f"mov.u32 {ui}, 0\nmov.u32 {gcnt}, 0")
+    l_sunit = p.label("s_unit")
+    p.place(l_sunit)
+    bh, q0, nbt, _ = unit_coords(ui)
     # this tile's number of key blocks and this thread's query row
     if len(set(nbt)) == 1:
         nbm = nbt[0]
@@ -637,34 +742,14 @@ def _emit_softmax(p: Ptx, cfg: AttnConfig, ptr, bars, B_S, B_P, B_O, tbase, base
             add.s64 {mrow}, {mrow}, {w64}
             add.s64 {mrow}, {mrow}, {ptr[cfg.mask_param]}
         """)
-    # this thread's P row in smem: tile t, row r; 16-byte chunk c of a 64-key block
-    # lives at chunk (c ^ (r % 8)) of the row (128-byte swizzle)
-    chunk_addr = {}
-    if not cfg.p_tmem:
-        prow, rx = p.reg("u32"), p.reg("u32")
-        p.emit(f"""
-            mad.lo.u32 {prow}, {t}, {p_bytes}, {base}
-            add.u32 {prow}, {prow}, {p_off}
-            mad.lo.u32 {prow}, {row}, 128, {prow}
-            and.b32 {rx}, {row}, 7
-        """)
-        for c16 in range(16):            # 16 chunks of 8 keys = 128 keys
-            blk, c = c16 // 8, c16 % 8
-            a = p.reg("u32")
-            p.emit(f"xor.b32 {a}, {rx}, {c}\nmad.lo.u32 {a}, {a}, 16, {prow}\nadd.u32 {a}, {a}, {blk * 16384}")
-            chunk_addr[c16] = a
     m, l = p.reg("f32"), p.reg("f32")
     p.emit(f"mov.f32 {m}, 0fF149F2CA\nmov.f32 {l}, 0f00000000")     # m = -1e30 (log2 domain)
-    cvt = "cvt.rn.bf16x2.f32" if cfg.dtype == "bf16" else "cvt.rn.f16x2.f32"
-    sl2, slr = p.reg("b64"), p.reg("f32")
-    pre_scaled = cfg.mask_param is not None
-    p.emit(f"mov.f32 {slr}, {f32_hex(1.0 if pre_scaled else scale_log2)}\nmov.b64 {sl2}, {{{slr}, {slr}}}")
     jj = p.reg("u32")
     p.emit(f"mov.u32 {jj}, 0")
     l_blk = p.label("s_blk")
     p.place(l_blk)
     par = p.reg("u32")
-    p.emit(f"and.b32 {par}, {jj}, 1")
+    p.emit(f"and.b32 {par}, {gcnt}, 1")
     # S_t(j) complete; its commit also covers O_t += P_t(j-1) V_{j-1}, so the P buffer
     # is free and O_t holds every earlier block
     waits.wait(sbar, par, "softmax", finish)
@@ -815,17 +900,19 @@ def _emit_softmax(p: Ptx, cfg: AttnConfig, ptr, bars, B_S, B_P, B_O, tbase, base
         tcgen05.fence::before_thread_sync
         mbarrier.arrive.shared::cta.b64 _, [{pbar}]
         add.u32 {jj}, {jj}, 1
+        add.u32 {gcnt}, {gcnt}, 1
     """)
     pj = p.reg("pred")
     p.emit(f"setp.lt.u32 {pj}, {jj}, {nbm}\n@{pj} bra {l_blk}")
     # epilogue: O / l once the last O_t += P_t V has landed
     parf = p.reg("u32")
-    p.emit(f"sub.u32 {parf}, {nbm}, 1\nand.b32 {parf}, {parf}, 1")
+    p.emit(f"sub.u32 {parf}, {gcnt}, 1\nand.b32 {parf}, {parf}, 1")
     waits.wait(obar, parf, "softmax", finish)
     p.emit("bar.warp.sync -1\ntcgen05.fence::after_thread_sync")
     inv = p.reg("f32")
     p.emit(f"rcp.rn.f32 {inv}, {l}")
     grow, prow_ok = qrow, p.reg("pred")
+    bh, _, _, _ = unit_coords(ui)
     p.emit(f"setp.lt.u32 {prow_ok}, {grow}, {cfg.Sq}")
     oadr, w64 = p.reg("b64"), p.reg("b64")
     p.emit(f"""
@@ -854,6 +941,9 @@ def _emit_softmax(p: Ptx, cfg: AttnConfig, ptr, bars, B_S, B_P, B_O, tbase, base
                 break
             p.emit(f"@{prow_ok} st.global.v4.b32 [{oadr}+{(c * 32 + 8 * g) * 2}], "
                    f"{{{', '.join(packed[4 * g:4 * g + 4])}}}")
+    # (every O_t load above has completed: the next unit's first P_t hand-over, after
+    # which O_t is overwritten, comes later in this thread)
+    unit_loop_end(ui, l_sunit)
     p.emit(f"bra {finish}")
 
 
