@@ -40,11 +40,11 @@ so the ring needs no empty barriers of its own; the shared-memory descriptors of
 ring slots are formed once and a K step adds its offset to the 64-bit descriptor.
 The protocol is checked under random schedules by ``tests/test_attention_split_protocol.py``.
 
-Measured on the B200 (BASELINE 8 x 32 x 4096 x 128, bench.py): 0.87-0.91x the two-tile template.
-Per 128-key block the two 64-key score products read Q twice from shared memory, so the
-block moves 192 KB through shared memory (both operands of 16 N = 64 score MMAs, V for 8
-PV MMAs, 64 KB of TMA writes) against the template's 128 KB per tile and block, and
-shared-memory bandwidth bounds the schedule.
+Measured on the B200 (BASELINE 8 x 32 x 4096 x 128, bench.py): 0.87-0.91x the two-tile
+template.  The per-half score products are M = 128, N = 64 MMAs, which cost about as much
+per instruction as N = 128 ones (~85 clocks each in %clock64 stamps of the MMA threads),
+so a block takes 24 MMA instructions (~2050 clocks) where the template needs 16 per tile
+and block; shared-memory bank reads stay low (14 % of peak), so that is not the limit.
 
 Every mbarrier wait is bounded (``tc.Waits``); a wait that gives up raises the CTA's
 abort flag and every role leaves through the common exit, which frees TMEM.
