@@ -87,3 +87,20 @@ def test_split_schedule_matches_the_oracle(runtime, bh, sq, sk, sms, seed, q_sca
         refs.append(attn_bf16(f["q"][b, rows], f["k"][kvh], f["v"][kvh], cfg.scale))
         assert_parity(outs[-1], refs[-1], rel=1e-2, what=f"batch x head {b}")
     assert_parity(np.concatenate(outs), np.concatenate(refs), rel=1e-2, what="all heads")
+
+
+def test_schedule_override_applies_only_where_the_split_schedule_serves(monkeypatch):
+    """``EMMY_ATTENTION_SCHEDULE=split_keys`` moves the whole compile path (bench.py
+    included) onto the split-key schedule for unmasked, non-causal problems and leaves
+    every other attention problem on the two-tile template."""
+    from compiler.kernels.attention import AttnConfig, emit_attention_module
+    from compiler.ptx import parse_launch
+
+    def sched(**kw):
+        cfg = AttnConfig(BH=4, Sq=512, Sk=512, D=128, scale=0.1, buffers=("q", "k", "v", "o"), **kw)
+        return parse_launch(emit_attention_module(cfg)).get("schedule", "tiles")
+
+    assert sched() == "tiles"
+    monkeypatch.setenv("EMMY_ATTENTION_SCHEDULE", "split_keys")
+    assert sched() == "split_keys"
+    assert sched(causal=True) == "tiles"
