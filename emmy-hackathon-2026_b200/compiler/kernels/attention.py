@@ -13,8 +13,9 @@ most keys first).  Every role loops over its CTA's units: the K / V ring streams
 across unit boundaries, the next unit's Q_t tile is loaded as soon as the last
 ``Q_t K^T`` of the current unit is done (``q_empty``), the next unit's ``S_t(0)`` are
 issued right behind the current unit's last ``O_t += P_t V`` of both tiles, and the
-barrier parities count blocks over all units.  Against one CTA per unit this measured
-the same (1240.6 against 1243.2 TFLOP/s at the BASELINE size).  (Issuing a tile's next-unit ``S_t(0)`` straight after its
+barrier parities count blocks over all units.  Against one CTA per unit this halves
+the fixed cost per unit: the same speed at the BASELINE key length (4096), +6.8 % at
+2048 keys and +12 % at 1024.  (Issuing a tile's next-unit ``S_t(0)`` straight after its
 own last product instead, before the other tile's, measured 4 % slower: the MMA thread
 then waits for the next Q tile while the other tile's product is still to be issued.)
 
