@@ -2,7 +2,7 @@
 """Benchmark of the B200 back end on BASELINE.json's configurations.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME|all]
-                    [--impl ours|reference] [--no-cpu]
+                    [--impl ours|reference|library] [--no-cpu]
 
 One step = one launch of the kernel ``compile.py`` emits for a configuration (its IR
 synthesised from the reference's IR family at the configured size), over inputs
@@ -309,6 +309,132 @@ def run_reference(args, dist: Dist) -> int:
             "config": config_of(head, args.gpus), "cpu_baseline": h["cpu_baseline"],
             "e2e": h["e2e"], "workloads": workloads}
     print(json.dumps(line), flush=True)
+    return 0
+
+
+# ---------------------------------------------------------------------------
+# vendor-library arm (context only): the same configurations through torch's CUDA kernels
+
+
+def _library_ops(name: str, dev):
+    """Closures that run one step of ``name`` with torch's CUDA kernels (cuBLAS bf16,
+    cuBLASLt FP8 through ``torch._scaled_mm``, cuDNN and flash SDPA, torch's own
+    normalisation / softmax / reduction kernels), output buffers allocated up front.
+    Inputs are rotated over enough copies to exceed L2, like the other arm's."""
+    import torch
+    c = bc.CONFIGS[name]
+    g = torch.Generator(device=dev).manual_seed(0)
+
+    def copies(make, nbytes):
+        n = 1 if nbytes > L2_BYTES else -(-2 * L2_BYTES // nbytes)
+        return [make() for _ in range(n)]
+
+    ops = {}
+    if c.family == "gemm":
+        m, n, k = c.dims
+        ins = copies(lambda: (0.05 * torch.randn(m, k, device=dev, generator=g)).bfloat16(), 2 * m * k)
+        B = (0.05 * torch.randn(k, n, device=dev, generator=g)).bfloat16()
+        out = torch.empty(m, n, device=dev, dtype=torch.bfloat16)
+        ops["cublas"] = lambda i: torch.matmul(ins[i % len(ins)], B, out=out)
+    elif c.family == "fp8":
+        m, n, k = c.dims
+        f8 = torch.float8_e4m3fn
+        ins = copies(lambda: torch.randn(m, k, device=dev, generator=g).to(f8), m * k)
+        Bt = torch.randn(n, k, device=dev, generator=g).to(f8)      # column-major B
+        sa = torch.tensor(1.0, device=dev)
+        sb = torch.tensor(1.0, device=dev)
+        ops["cublaslt_scaled_mm"] = lambda i: torch._scaled_mm(
+            ins[i % len(ins)], Bt.t(), scale_a=sa, scale_b=sb, out_dtype=torch.bfloat16)
+    elif name == "attention":
+        from torch.nn.attention import SDPBackend, sdpa_kernel
+        b, h, s, d = c.dims
+        q, k_, v = (torch.randn(b, h, s, d, device=dev, generator=g).bfloat16() for _ in range(3))
+        F = torch.nn.functional
+        for label, be in (("cudnn_sdpa", SDPBackend.CUDNN_ATTENTION),
+                          ("flash_sdpa", SDPBackend.FLASH_ATTENTION)):
+            def run(i, be=be):
+                with sdpa_kernel([be]):
+                    return F.scaled_dot_product_attention(q, k_, v)
+            ops[label] = run
+    elif name == "rmsnorm":
+        rows, cols = c.dims
+        ins = copies(lambda: torch.randn(rows, cols, device=dev, generator=g), 4 * rows * cols)
+        w = torch.rand(cols, device=dev, generator=g) + 0.5
+        ops["torch_rms_norm"] = lambda i: torch.nn.functional.rms_norm(
+            ins[i % len(ins)], (cols,), w, 1e-6)
+    elif name == "softmax":
+        x = torch.randn(*c.dims, device=dev, generator=g) * math.sqrt(2.0)
+        out = torch.empty_like(x)
+        ops["torch_softmax"] = lambda i: torch.softmax(x, dim=-1, out=out)
+    elif name == "sum":
+        x = torch.rand(c.dims[0], device=dev, generator=g) * 2 - 1
+        out = torch.empty((), device=dev)
+        ops["torch_sum"] = lambda i: torch.sum(x, dim=0, out=out)
+    return ops
+
+
+def run_library(args, dist: Dist) -> int:
+    """``--impl library``: the configurations through NVIDIA's libraries via torch on one
+    GPU (CUDA graphs of the launches, CUDA events, the same stretched regions and clock
+    sampling as this back end's arm).  Context for the roofline fractions, not a
+    reference arm: the reference has no GPU implementation of these kernels."""
+    if dist.world > 1 or dist.rank != 0:
+        if dist.rank == 0:
+            print(json.dumps({"impl": "library", "unavailable": "one GPU only"}))
+        return 0
+    import torch
+    if not torch.cuda.is_available():
+        print(json.dumps({"impl": "library", "unavailable": "no CUDA device"}))
+        return 0
+    dev = torch.device("cuda", dist.local)
+    torch.cuda.set_device(dev)
+    results = {}
+    for name in _names(args):
+        if name not in bc.CONFIGS:
+            continue
+        unit = bc.CONFIGS[name].unit
+        for label, op in _library_ops(name, dev).items():
+            try:
+                for i in range(max(3, args.warmup)):
+                    op(i)
+                torch.cuda.synchronize()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                for i in range(3):
+                    op(i)
+                e1.record()
+                e1.synchronize()
+                est_s = e0.elapsed_time(e1) / 3e3
+                steps = int(min(MAX_LAUNCHES, max(args.steps, math.ceil(MIN_REGION_S / max(est_s, 1e-7)))))
+                s = torch.cuda.Stream()
+                graph = torch.cuda.CUDAGraph()
+                with torch.cuda.stream(s):
+                    op(0)                      # library workspaces allocated outside capture
+                    s.synchronize()
+                    with torch.cuda.graph(graph, stream=s):
+                        for i in range(steps):
+                            op(i)
+                torch.cuda.synchronize()
+                with ClockSampler(dist.local) as clocks:
+                    e0.record()
+                    graph.replay()
+                    e1.record()
+                    e1.synchronize()
+                ms = e0.elapsed_time(e1) / steps
+                del graph
+                value = to_rate(bc.work(name), ms / 1e3, unit)
+                results[f"{name}/{label}"] = {"value": round(value, 2), "unit": unit,
+                                              "ms_per_step": round(ms, 5), "steps": steps,
+                                              "clocks": clocks.summary()}
+            except Exception as e:      # a backend torch does not offer for this shape
+                results[f"{name}/{label}"] = {"unavailable": f"{type(e).__name__}: {str(e)[:160]}"}
+            print(json.dumps({f"{name}/{label}": results[f"{name}/{label}"]}), file=sys.stderr, flush=True)
+        torch.cuda.empty_cache()
+        gc.collect()
+    print(json.dumps({"metric": METRIC, "impl": "library", "n_gpus": 1,
+                      "torch": torch.__version__, "device": torch.cuda.get_device_name(dev),
+                      "data": "synthetic (torch generator, BASELINE.json shapes)",
+                      "workloads": results}), flush=True)
     return 0
 
 
@@ -646,7 +772,7 @@ def main(argv=None) -> int:
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--impl", choices=["ours", "reference", "library"], default="ours")
     ap.add_argument("--workload", choices=["all", *bc.ORDER, *EXTRA], default="all")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline samples")
     args = ap.parse_args(argv)
@@ -659,6 +785,8 @@ def main(argv=None) -> int:
     try:
         if args.impl == "reference":
             return run_reference(args, dist)
+        if args.impl == "library":
+            return run_library(args, dist)
         return run_ours(args, dist)
     finally:
         dist.close()
