@@ -332,19 +332,21 @@ def _library_ops(name: str, dev):
     ops = {}
     if c.family == "gemm":
         m, n, k = c.dims
-        ins = copies(lambda: (0.05 * torch.randn(m, k, device=dev, generator=g)).bfloat16(), 2 * m * k)
-        B = (0.05 * torch.randn(k, n, device=dev, generator=g)).bfloat16()
+        ins = copies(lambda: ((0.05 * torch.randn(m, k, device=dev, generator=g)).bfloat16(),
+                              (0.05 * torch.randn(k, n, device=dev, generator=g)).bfloat16()),
+                     2 * (m * k + k * n))
         out = torch.empty(m, n, device=dev, dtype=torch.bfloat16)
-        ops["cublas"] = lambda i: torch.matmul(ins[i % len(ins)], B, out=out)
+        ops["cublas"] = lambda i: torch.matmul(*ins[i % len(ins)], out=out)
     elif c.family == "fp8":
         m, n, k = c.dims
         f8 = torch.float8_e4m3fn
-        ins = copies(lambda: torch.randn(m, k, device=dev, generator=g).to(f8), m * k)
-        Bt = torch.randn(n, k, device=dev, generator=g).to(f8)      # column-major B
+        # (A, B) with B column-major, as cuBLASLt takes it
+        ins = copies(lambda: (torch.randn(m, k, device=dev, generator=g).to(f8),
+                              torch.randn(n, k, device=dev, generator=g).to(f8).t()), m * k + k * n)
         sa = torch.tensor(1.0, device=dev)
         sb = torch.tensor(1.0, device=dev)
         ops["cublaslt_scaled_mm"] = lambda i: torch._scaled_mm(
-            ins[i % len(ins)], Bt.t(), scale_a=sa, scale_b=sb, out_dtype=torch.bfloat16)
+            *ins[i % len(ins)], scale_a=sa, scale_b=sb, out_dtype=torch.bfloat16)
     elif name == "attention":
         from torch.nn.attention import SDPBackend, sdpa_kernel
         b, h, s, d = c.dims
