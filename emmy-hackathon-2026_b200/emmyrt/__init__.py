@@ -234,14 +234,20 @@ class Graph:
         self.handle = handle
 
     @classmethod
-    def capture(cls, stream: "Stream", enqueue) -> "Graph":
+    def capture(cls, stream: "Stream", enqueue, keep=()) -> "Graph":
+        """The captured launches refer to their buffers, scratch and modules by device
+        address only, so whatever owns them (``DeviceBuffer``, ``CompiledKernel``) must live
+        as long as the graph is replayed: a replay after they are freed reads freed memory.
+        The graph holds ``enqueue`` and the objects in ``keep`` for that purpose."""
         check(lib.emmy_rt_graph_begin(stream.handle), "graph begin")
         try:
             enqueue()
         finally:
             g = _u64()
             check(lib.emmy_rt_graph_end(stream.handle, ctypes.byref(g)), "graph end")
-        return cls(g.value)
+        graph = cls(g.value)
+        graph._keep = (enqueue, tuple(keep))
+        return graph
 
     def launch(self, stream: int = 0) -> None:
         check(lib.emmy_rt_graph_launch(self.handle, stream), "graph launch")
