@@ -50,3 +50,40 @@ def test_calls_before_init_fail_cleanly():
     if not emmyrt._initialised:
         assert emmyrt.lib.emmy_rt_device_count(ctypes.byref(n)) == -5
         assert b"emmy_rt_init" in emmyrt.lib.emmy_rt_last_error()
+
+
+def test_graph_holds_what_its_launches_refer_to(monkeypatch):
+    """A captured graph keeps its enqueue callable and the owners named in ``keep`` alive,
+    so the buffers its launches address are not freed while it can be replayed (the
+    capture calls are faked: no GPU is touched)."""
+    import gc
+    import weakref
+    import emmyrt
+
+    class Owner:                       # stands in for a DeviceBuffer / CompiledKernel
+        pass
+
+    class FakeLib:
+        def emmy_rt_graph_begin(self, stream):
+            return 0
+
+        def emmy_rt_graph_end(self, stream, out):
+            return 0
+
+        def emmy_rt_graph_destroy(self, handle):
+            return 0
+
+    monkeypatch.setattr(emmyrt, "lib", FakeLib())
+    buf, kernel = Owner(), Owner()
+    refs = weakref.ref(buf), weakref.ref(kernel)
+
+    class Stream:
+        handle = 0
+
+    g = emmyrt.Graph.capture(Stream(), lambda k=kernel: None, keep=(buf,))
+    del buf, kernel
+    gc.collect()
+    assert all(r() is not None for r in refs)
+    del g
+    gc.collect()
+    assert all(r() is None for r in refs)
