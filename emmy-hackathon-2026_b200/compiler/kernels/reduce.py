@@ -26,9 +26,10 @@ The sm_100a schedule here keeps the IR's arithmetic and changes the movement:
   through shared memory in a fixed order (every thread ends with the row result);
 * whole-array reductions stream with a grid-stride loop, fold 8-element f32 groups
   into an f64 per-thread accumulator, write one f64 partial per CTA to scratch,
-  and the last CTA to arrive (an ``atom.add`` ticket) sums the partials in index
-  order, runs the IR's leader section (e.g. ``/ count``) and stores the result --
-  deterministic, with 64-bit addressing for 2^31 elements.
+  and the last CTA to arrive (an ``atom.add`` ticket) sums the partials with all its
+  threads in a fixed order (each thread its strided share in CTA order, then the warp
+  butterfly and the warp fold), runs the IR's leader section (e.g. ``/ count``) and
+  stores the result -- deterministic, with 64-bit addressing for 2^31 elements.
 """
 
 from __future__ import annotations
@@ -1029,13 +1030,16 @@ class FullReduce:
             bar.sync 0
         """)
         done2 = p.label("cta_done")
-        p.emit(f"@!{pt0} bra {done2}")
+        l_t0 = p.label("t0_done")
+        flag = p.reg("u32")
+        p.emit(f"@!{pt0} bra {l_t0}")
         ctot, t = p.reg("f64"), p.reg("f64")
         p.emit(f"ld.shared.f64 {ctot}, [wpart]")
         for w in range(1, nw):
             p.emit(f"ld.shared.f64 {t}, [wpart+{w * 8}]")
             p.emit(self._combine_f64(ctot, t))
-        # publish the CTA partial, then take a ticket; the last CTA finishes
+        # publish the CTA partial, then take a ticket; the CTA that takes the last one
+        # finishes (thread 0 tells the others through shared memory)
         paddr, ticket, pl = p.reg("b64"), p.reg("u32"), p.reg("pred")
         p.emit(f"""
             mad.wide.u32 {paddr}, %cta, 8, {scratch}
@@ -1043,23 +1047,48 @@ class FullReduce:
             fence.acq_rel.gpu
             atom.global.acq_rel.gpu.add.u32 {ticket}, [{scratch}], 1
             setp.eq.u32 {pl}, {ticket}, {self.grid - 1}
-            @!{pl} bra {done2}
+            selp.u32 {flag}, 1, 0, {pl}
+            st.shared.u32 [wlast], {flag}
         """)
-        # last CTA (one thread): partials in CTA order, then the IR's leader section
-        tot, q, ia = p.reg("f64"), p.reg("f64"), p.reg("b64")
-        lp, ld_ = p.label("fin"), p.label("fin_done")
-        k = p.reg("u32")
-        p.emit(f"""
-            ld.global.cg.f64 {tot}, [{scratch}+16]
-            mov.u32 {k}, 1
-            add.s64 {ia}, {scratch}, 24
-        """)
-        if self.grid > 1:
-            p.place(lp)
-            p.emit(f"ld.global.cg.f64 {q}, [{ia}]")
-            p.emit(self._combine_f64(tot, q))
-            pk = p.reg("pred")
-            p.emit(f"add.s64 {ia}, {ia}, 8\nadd.u32 {k}, {k}, 1\nsetp.lt.u32 {pk}, {k}, {self.grid}\n@{pk} bra {lp}")
+        p.place(l_t0)
+        plast = p.reg("pred")
+        p.emit(f"bar.sync 0\nld.shared.u32 {flag}, [wlast]\nsetp.eq.u32 {plast}, {flag}, 0\n"
+               f"@{plast} bra {done2}")
+        # last CTA, every thread: the CTA partials strided over the threads (all loads of a
+        # thread in flight together, folded in CTA order), then the same fixed-order warp
+        # butterfly and warp fold as above.  (A single thread walking the partials one
+        # dependent L2 load at a time cost tens of microseconds per launch.)
+        ident64 = f64_hex(0.0 if is_add else (-math.inf if self.op == "maximum" else math.inf))
+        p.emit("fence.acq_rel.gpu")
+        per = -(-self.grid // self.CTA)
+        vals = []
+        for j in range(per):
+            idx, a, v, pj = p.reg("u32"), p.reg("b64"), p.reg("f64"), p.reg("pred")
+            p.emit(f"""
+                mov.f64 {v}, {ident64}
+                add.u32 {idx}, {tid}, {j * self.CTA}
+                setp.lt.u32 {pj}, {idx}, {self.grid}
+                mad.wide.u32 {a}, {idx}, 8, {scratch}
+                @{pj} ld.global.cg.f64 {v}, [{a}+16]
+            """)
+            vals.append(v)
+        tot = vals[0]
+        for v in vals[1:]:
+            p.emit(self._combine_f64(tot, v))
+        for xor in (16, 8, 4, 2, 1):
+            lo, hi, o = p.reg("b32"), p.reg("b32"), p.reg("f64")
+            p.emit(f"""
+                mov.b64 {{{lo}, {hi}}}, {tot}
+                shfl.sync.bfly.b32 {lo}, {lo}, {xor}, 31, -1
+                shfl.sync.bfly.b32 {hi}, {hi}, {xor}, 31, -1
+                mov.b64 {o}, {{{lo}, {hi}}}
+            """)
+            p.emit(self._combine_f64(tot, o))
+        p.emit(f"@{pl0} st.shared.f64 [{sa}], {tot}\nbar.sync 0\n@!{pt0} bra {done2}")
+        p.emit(f"ld.shared.f64 {tot}, [wpart]")
+        for w in range(1, nw):
+            p.emit(f"ld.shared.f64 {t}, [wpart+{w * 8}]")
+            p.emit(self._combine_f64(tot, t))
         # keep the f64 total beside the ticket (scratch bytes 8..16): a sharded reduction
         # all-reduces these per-GPU totals in f64; then reset the ticket for the next launch
         p.emit(f"st.global.f64 [{scratch}+8], {tot}")
@@ -1080,7 +1109,8 @@ class FullReduce:
         p.emit("ret")
         params = arg_params(spec) + [".param .u64 param__scratch"]
         text = entry(spec.name, params, p, maxntid=self.CTA)
-        text = text.replace("{\n", "{\n" + f"\t.shared .align 8 .f64 wpart[{nw}];\n", 1)
+        text = text.replace("{\n", "{\n" + f"\t.shared .align 8 .f64 wpart[{nw}];\n"
+                            "\t.shared .align 4 .u32 wlast;\n", 1)
         launch = {"kind": "full_reduce", "grid": [self.grid, 1, 1], "block": [self.CTA, 1, 1],
                   "cluster": [1, 1, 1], "smem": 0, "count": self.count,
                   "extra_params": [{"kind": "scratch", "bytes": self.scratch_bytes, "zero_once": True,
