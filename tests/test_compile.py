@@ -356,3 +356,27 @@ def test_baseline_problems_written_concurrently():
     import multiprocessing as mp
     with mp.get_context("spawn").Pool(8) as pool:
         assert sorted(pool.map(_synth_and_read, range(8))) == list(range(8))
+
+
+def test_compilation_is_deterministic():
+    """The same IR compiles to the same PTX text in a fresh process (no dependence on hash
+    seeds, set order or the order in which modules were compiled), so a module built here
+    is the one the B200 runs and the judge can rebuild."""
+    import os
+    import random
+    sample = [p for p in IRS if _supported(p) is not None]
+    random.Random(3).shuffle(sample)
+    sample = sample[:24]
+    texts = {str(p): compile_kernel(load(p)) for p in sample}
+    code = ("import sys, json; sys.path[:0] = [%r, %r]\n"
+            "from compiler import compile_kernel, load\n"
+            "paths = json.loads(sys.argv[1])\n"
+            "print(json.dumps({p: compile_kernel(load(p)) for p in reversed(paths)}))"
+            % (str(ROOT / "emmy-hackathon-2026_b200"), str(ROOT)))
+    env = {**os.environ, "PYTHONHASHSEED": "12345"}
+    r = subprocess.run([sys.executable, "-c", code, json.dumps(list(texts))], capture_output=True,
+                       text=True, timeout=600, env=env)
+    assert r.returncode == 0, r.stderr[-2000:]
+    again = json.loads(r.stdout)
+    for p, t in texts.items():
+        assert again[p] == t, f"{p}: PTX differs between runs"
