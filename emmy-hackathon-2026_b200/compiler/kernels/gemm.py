@@ -30,9 +30,9 @@ pipeline records a status bit and the CTA releases its TMEM and exits.
 from __future__ import annotations
 
 import math
-from dataclasses import dataclass, field
+from dataclasses import dataclass
 
-from ..ptx import Ptx, entry, f32_hex, module
+from ..ptx import Ptx, entry, module
 from .common import arg_params, load_pointer, param_symbol
 from .tc import Waits, instr_desc, smem_desc_hi, smem_desc_lo_const
 

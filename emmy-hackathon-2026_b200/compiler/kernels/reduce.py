@@ -38,7 +38,7 @@ import math
 from dataclasses import dataclass, field
 
 from ..ptx import Ptx, entry, f32_hex, f64_hex, module
-from ..stmts import (ScalarCtx, Val, dtype_name, emit_exp_nonpos, expr_vars, load_index_vars,
+from ..stmts import (ScalarCtx, Val, emit_exp_nonpos, expr_vars, load_index_vars,
                      lower_body, matmul_kernel)
 from .common import Affine, affine_offset, arg_params, load_pointer
 
